@@ -1,0 +1,73 @@
+// Device-memory protocol between the host runtime and the persistent
+// kernels.  It restates the reference's kernel-argument "ABI"
+// (src/yield.cu:95-102: nextTask fetch-add counter, generation flag,
+// claim[] CAS array, uqNext[] urgent mini-queue, setGT/obsGT/uGT timestamp
+// arrays, uEndMax) as two structs, plus what the reference does not have:
+// a checkpoint slab, a device status word and a bounded-wait limit.
+#pragma once
+#include <cuda.h>
+#include <stdint.h>
+
+namespace apk {
+
+enum PollMode : int { POLL_OFF = 0, POLL_BOUNDARY = 1, POLL_STAGE = 2 };
+enum Discipline : int { DISC_DRAIN = 0, DISC_POISON = 2 };
+
+// Yield-event side of the protocol (src/yield.cu:95-102,148-195).
+struct EventProto {
+  int* flag;                   // generation counter; -1 = stop.  Device memory
+                               // or mapped pinned host memory.
+  int* abort_word;             // device memory; nonzero makes every CTA exit
+  int* status;                 // device memory; first device-side error code
+  const long long* sched_ns;   // device setter: cumulative offsets (nullptr = host sets)
+  int n_sched;
+  int max_events;
+  long long* set_ns;           // [max_events] globaltimer at the device setter's store
+  long long* obs_ns;           // [max_events * grid] per-CTA observation time
+  int* claim;                  // [max_events] first popper's CTA index + 1
+  int* claim_site;             // [max_events] stage index of the claim, -1 = tile boundary
+  int* inflight;               // [max_events] TMA stages in flight when the claimer yielded
+  long long* claim_ns;         // [max_events] globaltimer of the claim
+  unsigned long long* done_ns; // [max_events] atomicMax of urgent item completion times
+  int* uq_next;                // [max_events] urgent mini-queue pop counter
+  int* udone_cnt;              // [max_events] finished urgent items
+  int* ack;                    // mapped host memory [2*max_events]: claim ack, done ack
+  int* uexec;                  // oracle: [max_events] urgent item executions
+  // count-triggered events: event k fires when the completed-tile counter
+  // reaches count_trig[k] (deterministic yields for verification runs)
+  const unsigned long long* count_trig;
+  int n_count;
+  unsigned long long* completed;
+};
+
+// Background work-queue side (src/persistent.cu:51-79 fetch-add queue).
+struct QueueProto {
+  unsigned long long* next_task;
+  unsigned long long num_tasks;
+  int* exec_count;               // oracle: [num_tasks] executions per task id
+  unsigned long long* tiles_done;  // [grid] completed background tiles per CTA
+  unsigned long long* start_min;   // atomicMin of CTA start globaltimer
+  unsigned long long* end_max;     // atomicMax of CTA exit globaltimer
+  int* exited;
+  unsigned long long* yields;      // checkpoints taken (accumulator spills)
+};
+
+// fp32 CUDA-core persistent SGEMM (tile 128x128, K-tile BK).
+struct F32Params {
+  CUtensorMap tmA;   // background A [M][K]  (box BK-slices of 32 x 128 rows, 128B swizzle)
+  CUtensorMap tmB;   // background B [K][N]  (box 128 cols x BK rows, no swizzle)
+  CUtensorMap tmAu;  // urgent A
+  CUtensorMap tmBu;  // urgent B
+  float* C;
+  int ldc, tiles_n, total_tiles, nk;   // nk = K / BK
+  float* Cu;                           // urgent output, one slot per event
+  long long cu_stride;                 // floats between event slots
+  int ldcu, utiles_n, usplit, unk, uitems;  // unk = stages per urgent item
+  float* slab;                         // [grid][16][256] float4 accumulator checkpoints
+  long long* slab_hdr;                 // [grid][4]: task, stage cursor, event, valid
+  long long wait_limit_ns;
+  EventProto ev;
+  QueueProto q;
+};
+
+}  // namespace apk

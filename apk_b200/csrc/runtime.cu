@@ -1,0 +1,1181 @@
+// Host runtime behind include/apk.h: one context per device owning the
+// persistent kernel's control block, event log, checkpoint slab and
+// operands.  Replaces the per-binary main() drivers of the reference
+// (src/persistent.cu:96-264, src/urgent_baseline.cu:144-380,
+// src/yield.cu:327-960, src/midyield.cu:348-793, src/tcyield.cu:384-842).
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <random>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include <cudaTypedefs.h>
+
+#include "../../include/apk.h"
+#include "common.cuh"
+#include "proto.h"
+
+namespace apk {
+namespace f32 {
+cudaError_t prepare(int poll, int disc, bool oracle, int bk, int* max_ctas_per_sm);
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int bk,
+                   cudaStream_t stream);
+int smem_bytes(int bk);
+}  // namespace f32
+namespace bf16 {
+cudaError_t prepare(int poll, int disc, bool oracle, int* max_ctas_per_sm);
+cudaError_t launch(const void* prm, int grid, int poll, int disc, bool oracle, cudaStream_t stream);
+int smem_bytes();
+int threads();
+}  // namespace bf16
+}  // namespace apk
+
+using namespace apk;
+
+namespace {
+
+long long host_now_ns() {
+  return std::chrono::duration_cast<std::chrono::nanoseconds>(
+             std::chrono::steady_clock::now().time_since_epoch())
+      .count();
+}
+
+void spin_until_ns(long long t) {
+  while (host_now_ns() < t) {
+  }
+}
+
+// Device control block (one per launch target).
+struct Ctrl {
+  unsigned long long next_task;
+  unsigned long long start_min;
+  unsigned long long end_max;
+  unsigned long long yields;
+  unsigned long long completed;  // completed background tiles (count triggers)
+  int exited;
+  int abort_word;
+  int status;
+  int flag_dev;  // yield flag in device memory (DEVICE / HOST_MEMCPY modes)
+  int never_set; // a word no code path writes (failure-path self-test)
+  int pad;
+};
+
+// Host-to-globaltimer visibility probe (src/yield.cu:208-214), bounded.
+__global__ void spin_flag_kernel(const int* flag, int target, long long limit_ns, long long* out,
+                                 int* status) {
+  if (threadIdx.x != 0) return;
+  const long long t0 = globaltimer_ns();
+  while (true) {
+    if (flag_load(flag) == target) {
+      *out = globaltimer_ns();
+      return;
+    }
+    if (globaltimer_ns() - t0 > limit_ns) {
+      *out = 0;
+      atomicCAS(status, 0, DEV_WAIT_TIMEOUT_SPIN);
+      return;
+    }
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+}  // namespace
+
+struct apk_ctx {
+  apk_config cfg{};
+  std::string err;
+  int sms = 0, grid = 0, ctas_per_sm = 0, max_ctas_per_sm = 0;
+  int cc_major = 0, cc_minor = 0;
+  char name[128] = {0};
+  cudaStream_t kstream = nullptr, cstream = nullptr, ustream = nullptr;
+  cudaEvent_t ev_start = nullptr, ev_done = nullptr;
+  bool running = false;
+
+  // background operands
+  int M = 0, N = 0, K = 0;
+  void *dA = nullptr, *dB = nullptr, *dC = nullptr;
+  bool ownA = false, ownB = false, ownC = false;
+  size_t capA = 0, capB = 0, capC = 0;
+  // urgent operands
+  int Mu = 0, Nu = 0, Ku = 0;
+  void *dAu = nullptr, *dBu = nullptr;
+  bool ownAu = false, ownBu = false;
+  float* dCu = nullptr;  // (max_events + 1) slots
+  size_t cu_slot = 0;
+
+  // control
+  Ctrl* d_ctrl = nullptr;   // main launch
+  Ctrl* d_uctrl = nullptr;  // baseline urgent launch
+  int* h_flag = nullptr;    // mapped pinned
+  int* d_flag_mapped = nullptr;
+  int* h_ack = nullptr;     // mapped pinned [2*max_events]
+  int* d_ack_mapped = nullptr;
+  int* h_gen = nullptr;     // pinned sources for HOST_MEMCPY stores [max_events + 2]
+
+  // event log (device)
+  long long *d_sched = nullptr, *d_set = nullptr, *d_obs = nullptr, *d_claim_ns = nullptr;
+  unsigned long long* d_done = nullptr;
+  int *d_claim = nullptr, *d_site = nullptr, *d_inflight = nullptr, *d_uq = nullptr,
+      *d_udone = nullptr, *d_uexec = nullptr;
+  int n_sched = 0;
+  unsigned long long* d_count = nullptr;
+  int n_count = 0;
+  // event log (host)
+  std::vector<long long> host_set, host_ack, host_done;
+  std::atomic<int> n_injected{0};
+
+  // checkpoint slab, per-CTA counters
+  float* d_slab = nullptr;
+  long long* d_slab_hdr = nullptr;
+  unsigned long long* d_tiles = nullptr;
+  unsigned long long* d_utiles = nullptr;
+  int* d_exec = nullptr;
+  size_t exec_cap = 0;
+  unsigned long long last_tasks = 0;
+  int last_grid = 0;
+
+  // bf16 parameter block lives in the bf16 translation unit; opaque here
+  std::vector<unsigned char> bf16_params;
+};
+
+namespace {
+
+apk_status fail(apk_ctx* c, apk_status s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (c) c->err = buf;
+  return s;
+}
+
+#define APK_CU(call)                                                                   \
+  do {                                                                                 \
+    cudaError_t e_ = (call);                                                           \
+    if (e_ != cudaSuccess)                                                             \
+      return fail(ctx, APK_ECUDA, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                  __FILE__, __LINE__);                                                 \
+  } while (0)
+
+apk_status ensure_encoder(apk_ctx* ctx) {
+  if (g_encode) return APK_OK;
+  cudaDriverEntryPointQueryResult q;
+  void* fn = nullptr;
+  APK_CU(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q));
+  if (q != cudaDriverEntryPointSuccess || !fn)
+    return fail(ctx, APK_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return APK_OK;
+}
+
+// 2-D row-major tensor map: rows x cols elements, box box_cols x box_rows.
+apk_status make_tmap(apk_ctx* ctx, CUtensorMap* tm, const void* base, CUtensorMapDataType dt,
+                     int esize, long long rows, long long cols, int box_cols, int box_rows,
+                     CUtensorMapSwizzle sw) {
+  if (ensure_encoder(ctx) != APK_OK) return APK_ECUDA;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * esize};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(tm, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(ctx, APK_ECUDA, "cuTensorMapEncodeTiled failed (%d) rows=%lld cols=%lld box=%dx%d",
+                (int)r, rows, cols, box_cols, box_rows);
+  return APK_OK;
+}
+
+size_t esize_of(apk_dtype d) { return d == APK_BF16 ? 2 : 4; }
+
+apk_status upload(apk_ctx* ctx, void** dst, bool* own, size_t* cap, const void* src, size_t bytes,
+                  apk_mem_kind kind) {
+  if (kind == APK_MEM_DEVICE) {
+    if (*own && *dst) cudaFree(*dst);
+    *dst = const_cast<void*>(src);
+    *own = false;
+    *cap = 0;
+    return APK_OK;
+  }
+  if (!*own || *cap < bytes) {
+    if (*own && *dst) cudaFree(*dst);
+    *dst = nullptr;
+    APK_CU(cudaMalloc(dst, bytes));
+    *own = true;
+    *cap = bytes;
+  }
+  if (src) APK_CU(cudaMemcpyAsync(*dst, src, bytes, cudaMemcpyHostToDevice, ctx->kstream));
+  return APK_OK;
+}
+
+int kernel_poll(const apk_ctx* c) { return (int)c->cfg.poll; }
+
+apk_status prepare_kernel(apk_ctx* ctx, int poll) {
+  int maxc = 0;
+  cudaError_t e;
+  if (ctx->cfg.dtype == APK_F32)
+    e = f32::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->cfg.k_tile, &maxc);
+  else
+    e = bf16::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, &maxc);
+  if (e != cudaSuccess)
+    return fail(ctx, APK_EUNSUPPORTED, "kernel variant unavailable (dtype %d poll %d disc %d oracle %d k_tile %d): %s",
+                ctx->cfg.dtype, poll, ctx->cfg.discipline, ctx->cfg.oracle, ctx->cfg.k_tile,
+                cudaGetErrorString(e));
+  if (maxc < 1) return fail(ctx, APK_EUNSUPPORTED, "kernel does not fit on an SM");
+  ctx->max_ctas_per_sm = maxc;
+  return APK_OK;
+}
+
+}  // namespace
+
+// bf16 parameter building lives beside its kernel.
+namespace apk {
+namespace bf16 {
+size_t params_size();
+apk_status build_params(void* out, const void* A, const void* B, void* C, int M, int N, int K,
+                        const void* Au, const void* Bu, float* Cu, int Mu, int Nu, int Ku,
+                        int usplit, size_t cu_stride, const EventProto& ev, const QueueProto& q,
+                        long long wait_limit_ns, int grid, std::string* err);
+}  // namespace bf16
+}  // namespace apk
+
+extern "C" {
+
+int apk_abi_version(void) { return APK_ABI_VERSION; }
+
+void apk_config_default(apk_config* c) {
+  memset(c, 0, sizeof *c);
+  c->device = 0;
+  c->dtype = APK_F32;
+  c->ctas_per_sm = 0;
+  c->grid = 0;
+  c->k_tile = 32;
+  c->poll = APK_POLL_STAGE;
+  c->discipline = APK_DISC_DRAIN;
+  c->set_mode = APK_SET_HOST_MAPPED;
+  c->max_events = 4096;
+  c->oracle = 0;
+  c->urgent_split_k = 4;
+  c->wait_limit_ns = 2000000000LL;
+}
+
+const char* apk_last_error(const apk_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
+  if (!cfg || !out) return APK_EINVAL;
+  *out = nullptr;
+  apk_ctx* ctx = new apk_ctx();
+  ctx->cfg = *cfg;
+  apk_config& c = ctx->cfg;
+  if (c.max_events < 1) c.max_events = 1;
+  if (c.urgent_split_k < 1) c.urgent_split_k = 1;
+  if (c.wait_limit_ns <= 0) c.wait_limit_ns = 2000000000LL;
+  if (c.dtype == APK_F32 && c.k_tile != 32 && c.k_tile != 64) {
+    fail(ctx, APK_EINVAL, "fp32 k_tile must be 32 or 64");
+    *out = ctx;
+    return APK_EINVAL;
+  }
+  if (c.dtype == APK_BF16) c.k_tile = 64;
+  if (c.discipline == APK_DISC_POISON && c.poll == APK_POLL_OFF) {
+    fail(ctx, APK_EINVAL, "the poison discipline needs a poll mode");
+    *out = ctx;
+    return APK_EINVAL;
+  }
+  *out = ctx;
+  APK_CU(cudaSetDevice(c.device));
+  cudaDeviceProp prop;
+  APK_CU(cudaGetDeviceProperties(&prop, c.device));
+  ctx->sms = prop.multiProcessorCount;
+  ctx->cc_major = prop.major;
+  ctx->cc_minor = prop.minor;
+  snprintf(ctx->name, sizeof ctx->name, "%s", prop.name);
+  if (prop.major != 10)
+    return fail(ctx, APK_EUNSUPPORTED, "device %s is sm_%d%d; this build targets sm_100a", prop.name,
+                prop.major, prop.minor);
+  apk_status s = prepare_kernel(ctx, kernel_poll(ctx));
+  if (s != APK_OK) return s;
+  // the POLL_OFF variant is used by the overhead and baseline modes
+  if (c.poll != APK_POLL_OFF && c.discipline == APK_DISC_DRAIN) {
+    const int keep = ctx->max_ctas_per_sm;
+    s = prepare_kernel(ctx, APK_POLL_OFF);
+    if (s != APK_OK) return s;
+    ctx->max_ctas_per_sm = std::min(keep, ctx->max_ctas_per_sm);
+  }
+  ctx->ctas_per_sm = c.ctas_per_sm > 0 ? std::min(c.ctas_per_sm, ctx->max_ctas_per_sm) : ctx->max_ctas_per_sm;
+  ctx->grid = c.grid > 0 ? c.grid : ctx->sms * ctx->ctas_per_sm;
+  if (ctx->grid > ctx->sms * ctx->max_ctas_per_sm)
+    return fail(ctx, APK_EINVAL,
+                "grid %d exceeds the %d resident slots; CTAs beyond residency would never "
+                "observe a yield (src/yield.cu:815-822)",
+                ctx->grid, ctx->sms * ctx->max_ctas_per_sm);
+
+  int lo = 0, hi = 0;
+  APK_CU(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+  APK_CU(cudaStreamCreateWithPriority(&ctx->kstream, cudaStreamNonBlocking, lo));
+  APK_CU(cudaStreamCreateWithPriority(&ctx->cstream, cudaStreamNonBlocking, hi));
+  APK_CU(cudaStreamCreateWithPriority(&ctx->ustream, cudaStreamNonBlocking, hi));
+  APK_CU(cudaEventCreate(&ctx->ev_start));
+  APK_CU(cudaEventCreate(&ctx->ev_done));
+
+  const int E = c.max_events;
+  const int G = ctx->grid;
+  APK_CU(cudaMalloc(&ctx->d_ctrl, sizeof(Ctrl)));
+  APK_CU(cudaMalloc(&ctx->d_uctrl, sizeof(Ctrl)));
+  APK_CU(cudaHostAlloc(&ctx->h_flag, 64, cudaHostAllocMapped));
+  APK_CU(cudaHostGetDevicePointer((void**)&ctx->d_flag_mapped, ctx->h_flag, 0));
+  APK_CU(cudaHostAlloc(&ctx->h_ack, sizeof(int) * 2 * E, cudaHostAllocMapped));
+  APK_CU(cudaHostGetDevicePointer((void**)&ctx->d_ack_mapped, ctx->h_ack, 0));
+  APK_CU(cudaHostAlloc(&ctx->h_gen, sizeof(int) * (E + 2), cudaHostAllocDefault));
+  memset(ctx->h_flag, 0, 64);
+  memset(ctx->h_ack, 0, sizeof(int) * 2 * E);
+  APK_CU(cudaMalloc(&ctx->d_sched, sizeof(long long) * E));
+  APK_CU(cudaMalloc(&ctx->d_count, sizeof(unsigned long long) * E));
+  APK_CU(cudaMalloc(&ctx->d_set, sizeof(long long) * E));
+  APK_CU(cudaMalloc(&ctx->d_obs, sizeof(long long) * (size_t)E * G));
+  APK_CU(cudaMalloc(&ctx->d_claim_ns, sizeof(long long) * E));
+  APK_CU(cudaMalloc(&ctx->d_done, sizeof(unsigned long long) * E));
+  APK_CU(cudaMalloc(&ctx->d_claim, sizeof(int) * E));
+  APK_CU(cudaMalloc(&ctx->d_site, sizeof(int) * E));
+  APK_CU(cudaMalloc(&ctx->d_inflight, sizeof(int) * E));
+  APK_CU(cudaMalloc(&ctx->d_uq, sizeof(int) * E));
+  APK_CU(cudaMalloc(&ctx->d_udone, sizeof(int) * E));
+  APK_CU(cudaMalloc(&ctx->d_uexec, sizeof(int) * E));
+  // checkpoint slab: fp32 128x128 fp32 accumulators (64 KB), bf16 256x128 (128 KB)
+  const size_t slab_floats = (c.dtype == APK_F32 ? 128 * 128 : 256 * 128);
+  APK_CU(cudaMalloc(&ctx->d_slab, sizeof(float) * slab_floats * G));
+  APK_CU(cudaMalloc(&ctx->d_slab_hdr, sizeof(long long) * 4 * G));
+  APK_CU(cudaMalloc(&ctx->d_tiles, sizeof(unsigned long long) * G));
+  APK_CU(cudaMalloc(&ctx->d_utiles, sizeof(unsigned long long) * G));
+  ctx->host_set.assign(E, 0);
+  ctx->host_ack.assign(E, 0);
+  ctx->host_done.assign(E, 0);
+  return APK_OK;
+}
+
+apk_status apk_destroy(apk_ctx* ctx) {
+  if (!ctx) return APK_OK;
+  if (ctx->running) {
+    apk_stop(ctx);
+    apk_wait(ctx, 5000000000LL);
+  }
+  cudaSetDevice(ctx->cfg.device);
+  auto F = [](void* p) {
+    if (p) cudaFree(p);
+  };
+  if (ctx->ownA) F(ctx->dA);
+  if (ctx->ownB) F(ctx->dB);
+  if (ctx->ownC) F(ctx->dC);
+  if (ctx->ownAu) F(ctx->dAu);
+  if (ctx->ownBu) F(ctx->dBu);
+  F(ctx->dCu);
+  F(ctx->d_ctrl);
+  F(ctx->d_uctrl);
+  F(ctx->d_sched);
+  F(ctx->d_count);
+  F(ctx->d_set);
+  F(ctx->d_obs);
+  F(ctx->d_claim_ns);
+  F(ctx->d_done);
+  F(ctx->d_claim);
+  F(ctx->d_site);
+  F(ctx->d_inflight);
+  F(ctx->d_uq);
+  F(ctx->d_udone);
+  F(ctx->d_uexec);
+  F(ctx->d_slab);
+  F(ctx->d_slab_hdr);
+  F(ctx->d_tiles);
+  F(ctx->d_utiles);
+  F(ctx->d_exec);
+  if (ctx->h_flag) cudaFreeHost(ctx->h_flag);
+  if (ctx->h_ack) cudaFreeHost(ctx->h_ack);
+  if (ctx->h_gen) cudaFreeHost(ctx->h_gen);
+  if (ctx->kstream) cudaStreamDestroy(ctx->kstream);
+  if (ctx->cstream) cudaStreamDestroy(ctx->cstream);
+  if (ctx->ustream) cudaStreamDestroy(ctx->ustream);
+  if (ctx->ev_start) cudaEventDestroy(ctx->ev_start);
+  if (ctx->ev_done) cudaEventDestroy(ctx->ev_done);
+  delete ctx;
+  return APK_OK;
+}
+
+apk_status apk_get_info(apk_ctx* ctx, apk_device_info* info) {
+  if (!ctx || !info) return APK_EINVAL;
+  memset(info, 0, sizeof *info);
+  info->sms = ctx->sms;
+  info->grid = ctx->grid;
+  info->ctas_per_sm = ctx->ctas_per_sm;
+  info->max_ctas_per_sm = ctx->max_ctas_per_sm;
+  info->cc_major = ctx->cc_major;
+  info->cc_minor = ctx->cc_minor;
+  if (ctx->cfg.dtype == APK_F32) {
+    info->smem_per_cta = f32::smem_bytes(ctx->cfg.k_tile);
+    info->threads_per_cta = 256;
+    info->tile_m = 128;
+    info->tile_n = 128;
+    info->stages = ctx->cfg.k_tile == 32 ? 3 : 2;
+  } else {
+    info->smem_per_cta = bf16::smem_bytes();
+    info->threads_per_cta = bf16::threads();
+    info->tile_m = 256;
+    info->tile_n = 128;
+    info->stages = 4;
+  }
+  info->k_tile = ctx->cfg.k_tile;
+  snprintf(info->name, sizeof info->name, "%s", ctx->name);
+  return APK_OK;
+}
+
+apk_status apk_set_background(apk_ctx* ctx, const void* A, const void* B, void* C, int M, int N,
+                              int K, apk_mem_kind kind) {
+  if (!ctx) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "set_background while a launch runs");
+  if (M <= 0 || N <= 0 || K <= 0 || M % 128 || N % 128 || K % ctx->cfg.k_tile)
+    return fail(ctx, APK_EINVAL, "shape %dx%dx%d: M and N must be multiples of 128, K of %d", M, N,
+                K, ctx->cfg.k_tile);
+  if (ctx->cfg.dtype == APK_BF16 && M % 256)
+    return fail(ctx, APK_EINVAL, "bf16 background M must be a multiple of 256");
+  if (kind == APK_MEM_DEVICE && (!A || !B || !C))
+    return fail(ctx, APK_EINVAL, "device operands must be non-null");
+  APK_CU(cudaSetDevice(ctx->cfg.device));
+  const size_t es = esize_of(ctx->cfg.dtype);
+  apk_status s;
+  if ((s = upload(ctx, &ctx->dA, &ctx->ownA, &ctx->capA, A, es * M * K, kind)) != APK_OK) return s;
+  if ((s = upload(ctx, &ctx->dB, &ctx->ownB, &ctx->capB, B, es * (size_t)K * N, kind)) != APK_OK) return s;
+  if (kind == APK_MEM_DEVICE) {
+    if (ctx->ownC && ctx->dC) cudaFree(ctx->dC);
+    ctx->dC = C;
+    ctx->ownC = false;
+  } else {
+    if ((s = upload(ctx, &ctx->dC, &ctx->ownC, &ctx->capC, nullptr, 4ull * M * N, APK_MEM_HOST)) != APK_OK)
+      return s;
+  }
+  ctx->M = M;
+  ctx->N = N;
+  ctx->K = K;
+  APK_CU(cudaStreamSynchronize(ctx->kstream));
+  return APK_OK;
+}
+
+apk_status apk_set_urgent(apk_ctx* ctx, const void* A, const void* B, int M, int N, int K,
+                          apk_mem_kind kind) {
+  if (!ctx) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "set_urgent while a launch runs");
+  const int split = ctx->cfg.urgent_split_k;
+  const int tm = ctx->cfg.dtype == APK_F32 ? 128 : 256;
+  if (M <= 0 || N <= 0 || K <= 0 || M % tm || N % 128 || K % (ctx->cfg.k_tile * split))
+    return fail(ctx, APK_EINVAL,
+                "urgent shape %dx%dx%d: M a multiple of %d, N of 128, K of k_tile*split (%d)", M, N, K,
+                tm, ctx->cfg.k_tile * split);
+  APK_CU(cudaSetDevice(ctx->cfg.device));
+  const size_t es = esize_of(ctx->cfg.dtype);
+  size_t capAu = 0, capBu = 0;
+  apk_status s;
+  if ((s = upload(ctx, &ctx->dAu, &ctx->ownAu, &capAu, A, es * M * K, kind)) != APK_OK) return s;
+  if ((s = upload(ctx, &ctx->dBu, &ctx->ownBu, &capBu, B, es * (size_t)K * N, kind)) != APK_OK) return s;
+  if (ctx->dCu) cudaFree(ctx->dCu);
+  ctx->cu_slot = (size_t)M * N;
+  APK_CU(cudaMalloc(&ctx->dCu, sizeof(float) * ctx->cu_slot * (ctx->cfg.max_events + 1)));
+  ctx->Mu = M;
+  ctx->Nu = N;
+  ctx->Ku = K;
+  APK_CU(cudaStreamSynchronize(ctx->kstream));
+  return APK_OK;
+}
+
+apk_status apk_schedule_device_events(apk_ctx* ctx, const long long* offsets_ns, int n) {
+  if (!ctx) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "schedule while a launch runs");
+  if (n < 0 || n > ctx->cfg.max_events) return fail(ctx, APK_EINVAL, "n=%d out of [0,max_events]", n);
+  if (n > 0 && !offsets_ns) return fail(ctx, APK_EINVAL, "null schedule");
+  if (n > 0) APK_CU(cudaMemcpy(ctx->d_sched, offsets_ns, sizeof(long long) * n, cudaMemcpyHostToDevice));
+  ctx->n_sched = n;
+  if (n > 0) ctx->n_count = 0;
+  return APK_OK;
+}
+
+apk_status apk_schedule_count_events(apk_ctx* ctx, const unsigned long long* counts, int n) {
+  if (!ctx) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "schedule while a launch runs");
+  if (n < 0 || n > ctx->cfg.max_events) return fail(ctx, APK_EINVAL, "n=%d out of [0,max_events]", n);
+  if (n > 0 && ctx->cfg.set_mode != APK_SET_DEVICE)
+    return fail(ctx, APK_EINVAL, "count-triggered events need set_mode DEVICE");
+  for (int k = 0; k < n; ++k)
+    if (counts[k] == 0 || (k > 0 && counts[k] <= counts[k - 1]))
+      return fail(ctx, APK_EINVAL, "counts must be positive and strictly ascending");
+  if (n > 0)
+    APK_CU(cudaMemcpy(ctx->d_count, counts, sizeof(unsigned long long) * n, cudaMemcpyHostToDevice));
+  ctx->n_count = n;
+  if (n > 0) ctx->n_sched = 0;
+  return APK_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Fill the protocol structs for a launch of the main persistent kernel.
+void fill_protos(apk_ctx* ctx, unsigned long long num_tasks, EventProto* ev, QueueProto* q,
+                 int* flag_ptr) {
+  Ctrl* cb = ctx->d_ctrl;
+  memset(ev, 0, sizeof *ev);
+  memset(q, 0, sizeof *q);
+  ev->flag = flag_ptr;
+  ev->abort_word = &cb->abort_word;
+  ev->status = &cb->status;
+  ev->sched_ns = (ctx->cfg.set_mode == APK_SET_DEVICE && ctx->n_sched > 0) ? ctx->d_sched : nullptr;
+  ev->n_sched = ctx->cfg.set_mode == APK_SET_DEVICE ? ctx->n_sched : 0;
+  ev->max_events = ctx->cfg.max_events;
+  ev->set_ns = ctx->d_set;
+  ev->obs_ns = ctx->d_obs;
+  ev->claim = ctx->d_claim;
+  ev->claim_site = ctx->d_site;
+  ev->inflight = ctx->d_inflight;
+  ev->claim_ns = ctx->d_claim_ns;
+  ev->done_ns = ctx->d_done;
+  ev->uq_next = ctx->d_uq;
+  ev->udone_cnt = ctx->d_udone;
+  ev->ack = ctx->d_ack_mapped;
+  ev->uexec = ctx->d_uexec;
+  ev->count_trig = (ctx->cfg.set_mode == APK_SET_DEVICE && ctx->n_count > 0) ? ctx->d_count : nullptr;
+  ev->n_count = ev->count_trig ? ctx->n_count : 0;
+  ev->completed = &cb->completed;
+  q->next_task = &cb->next_task;
+  q->num_tasks = num_tasks;
+  q->exec_count = ctx->d_exec;
+  q->tiles_done = ctx->d_tiles;
+  q->start_min = &cb->start_min;
+  q->end_max = &cb->end_max;
+  q->exited = &cb->exited;
+  q->yields = &cb->yields;
+}
+
+apk_status reset_logs(apk_ctx* ctx, unsigned long long num_tasks) {
+  const int E = ctx->cfg.max_events, G = ctx->grid;
+  cudaStream_t s = ctx->kstream;
+  Ctrl init{};
+  init.start_min = ~0ull;
+  APK_CU(cudaMemcpyAsync(ctx->d_ctrl, &init, sizeof init, cudaMemcpyHostToDevice, s));
+  APK_CU(cudaMemsetAsync(ctx->d_set, 0, sizeof(long long) * E, s));
+  APK_CU(cudaMemsetAsync(ctx->d_obs, 0, sizeof(long long) * (size_t)E * G, s));
+  APK_CU(cudaMemsetAsync(ctx->d_claim_ns, 0, sizeof(long long) * E, s));
+  APK_CU(cudaMemsetAsync(ctx->d_done, 0, sizeof(unsigned long long) * E, s));
+  APK_CU(cudaMemsetAsync(ctx->d_claim, 0, sizeof(int) * E, s));
+  APK_CU(cudaMemsetAsync(ctx->d_site, 0xFF, sizeof(int) * E, s));
+  APK_CU(cudaMemsetAsync(ctx->d_inflight, 0, sizeof(int) * E, s));
+  APK_CU(cudaMemsetAsync(ctx->d_uq, 0, sizeof(int) * E, s));
+  APK_CU(cudaMemsetAsync(ctx->d_udone, 0, sizeof(int) * E, s));
+  APK_CU(cudaMemsetAsync(ctx->d_uexec, 0, sizeof(int) * E, s));
+  APK_CU(cudaMemsetAsync(ctx->d_tiles, 0, sizeof(unsigned long long) * G, s));
+  APK_CU(cudaMemsetAsync(ctx->d_slab_hdr, 0, sizeof(long long) * 4 * G, s));
+  if (ctx->dCu) APK_CU(cudaMemsetAsync(ctx->dCu, 0, sizeof(float) * ctx->cu_slot * (E + 1), s));
+  // verification launches pre-fill C with 0xFF bytes (NaN) so a tile that
+  // never runs fails loudly (src/persistent.cu:156-160)
+  if (ctx->cfg.oracle && ctx->dC) APK_CU(cudaMemsetAsync(ctx->dC, 0xFF, 4ull * ctx->M * ctx->N, s));
+  if (ctx->cfg.oracle && num_tasks != APK_TASKS_UNBOUNDED) {
+    if (ctx->exec_cap < num_tasks) {
+      if (ctx->d_exec) cudaFree(ctx->d_exec);
+      ctx->d_exec = nullptr;
+      APK_CU(cudaMalloc(&ctx->d_exec, sizeof(int) * num_tasks));
+      ctx->exec_cap = num_tasks;
+    }
+    APK_CU(cudaMemsetAsync(ctx->d_exec, 0, sizeof(int) * num_tasks, s));
+  }
+  // host-side state
+  std::atomic_thread_fence(std::memory_order_seq_cst);
+  *reinterpret_cast<volatile int*>(ctx->h_flag) = 0;
+  memset(ctx->h_ack, 0, sizeof(int) * 2 * E);
+  std::atomic_thread_fence(std::memory_order_seq_cst);
+  std::fill(ctx->host_set.begin(), ctx->host_set.end(), 0);
+  std::fill(ctx->host_ack.begin(), ctx->host_ack.end(), 0);
+  std::fill(ctx->host_done.begin(), ctx->host_done.end(), 0);
+  ctx->n_injected = 0;
+  return APK_OK;
+}
+
+apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cudaStream_t stream,
+                       bool record) {
+  if (!ctx->dA || !ctx->dB || !ctx->dC) return fail(ctx, APK_ESTATE, "no background operands set");
+  if (!ctx->dAu && poll != APK_POLL_OFF) return fail(ctx, APK_ESTATE, "no urgent operands set");
+  if (ctx->cfg.oracle && num_tasks == APK_TASKS_UNBOUNDED && poll != APK_POLL_OFF) {
+    // unbounded oracle runs still count urgent executions; per-task counts
+    // need a bound
+  }
+  apk_status s = reset_logs(ctx, num_tasks);
+  if (s != APK_OK) return s;
+  int* flag = ctx->cfg.set_mode == APK_SET_HOST_MAPPED ? ctx->d_flag_mapped : &ctx->d_ctrl->flag_dev;
+  EventProto ev;
+  QueueProto q;
+  fill_protos(ctx, num_tasks, &ev, &q, flag);
+  if (!(ctx->cfg.oracle && num_tasks != APK_TASKS_UNBOUNDED)) q.exec_count = nullptr;
+  ctx->last_tasks = num_tasks;
+  ctx->last_grid = ctx->grid;
+  cudaError_t e;
+  if (record) APK_CU(cudaEventRecord(ctx->ev_start, stream));
+  if (ctx->cfg.dtype == APK_F32) {
+    F32Params p;
+    memset(&p, 0, sizeof p);
+    const int bk = ctx->cfg.k_tile;
+    apk_status t;
+    if ((t = make_tmap(ctx, &p.tmA, ctx->dA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ctx->M, ctx->K, 32, 128,
+                       CU_TENSOR_MAP_SWIZZLE_128B)) != APK_OK)
+      return t;
+    if ((t = make_tmap(ctx, &p.tmB, ctx->dB, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ctx->K, ctx->N, 128, bk,
+                       CU_TENSOR_MAP_SWIZZLE_NONE)) != APK_OK)
+      return t;
+    if (ctx->dAu) {
+      if ((t = make_tmap(ctx, &p.tmAu, ctx->dAu, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ctx->Mu, ctx->Ku, 32, 128,
+                         CU_TENSOR_MAP_SWIZZLE_128B)) != APK_OK)
+        return t;
+      if ((t = make_tmap(ctx, &p.tmBu, ctx->dBu, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ctx->Ku, ctx->Nu, 128, bk,
+                         CU_TENSOR_MAP_SWIZZLE_NONE)) != APK_OK)
+        return t;
+    } else {
+      p.tmAu = p.tmA;
+      p.tmBu = p.tmB;
+    }
+    p.C = reinterpret_cast<float*>(ctx->dC);
+    p.ldc = ctx->N;
+    p.tiles_n = ctx->N / 128;
+    p.total_tiles = (ctx->M / 128) * (ctx->N / 128);
+    p.nk = ctx->K / bk;
+    p.Cu = ctx->dCu;
+    p.cu_stride = (long long)ctx->cu_slot;
+    p.ldcu = ctx->Nu;
+    p.utiles_n = ctx->Nu / 128;
+    p.usplit = ctx->cfg.urgent_split_k;
+    p.unk = ctx->Ku ? ctx->Ku / bk / p.usplit : 0;
+    p.uitems = (ctx->Mu / 128) * (ctx->Nu / 128) * p.usplit;
+    p.slab = ctx->d_slab;
+    p.slab_hdr = ctx->d_slab_hdr;
+    p.wait_limit_ns = ctx->cfg.wait_limit_ns;
+    p.ev = ev;
+    p.q = q;
+    e = f32::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, bk, stream);
+  } else {
+    ctx->bf16_params.assign(bf16::params_size() + 64, 0);
+    void* pp = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(ctx->bf16_params.data()) + 63) & ~uintptr_t(63));
+    std::string err;
+    apk_status t = bf16::build_params(pp, ctx->dA, ctx->dB, ctx->dC, ctx->M, ctx->N, ctx->K, ctx->dAu,
+                                      ctx->dBu, ctx->dCu, ctx->Mu, ctx->Nu, ctx->Ku,
+                                      ctx->cfg.urgent_split_k, ctx->cu_slot, ev, q,
+                                      ctx->cfg.wait_limit_ns, ctx->grid, &err);
+    if (t != APK_OK) return fail(ctx, t, "%s", err.c_str());
+    e = bf16::launch(pp, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, stream);
+  }
+  if (e != cudaSuccess) return fail(ctx, APK_ECUDA, "kernel launch failed: %s", cudaGetErrorString(e));
+  if (record) APK_CU(cudaEventRecord(ctx->ev_done, stream));
+  return APK_OK;
+}
+
+apk_status read_status(apk_ctx* ctx) {
+  Ctrl cb;
+  APK_CU(cudaMemcpy(&cb, ctx->d_ctrl, sizeof cb, cudaMemcpyDeviceToHost));
+  if (cb.status != 0)
+    return fail(ctx, APK_EDEVICE, "device reported status %d (a bounded wait ran out)", cb.status);
+  return APK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+apk_status apk_launch(apk_ctx* ctx, unsigned long long num_tasks) {
+  if (!ctx) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "a launch is already running");
+  if (num_tasks == 0) return fail(ctx, APK_EINVAL, "num_tasks must be > 0");
+  if (ctx->cfg.poll == APK_POLL_OFF && num_tasks == APK_TASKS_UNBOUNDED) {
+    // POLL_OFF kernels still stop through the abort word at tile boundaries
+  }
+  APK_CU(cudaSetDevice(ctx->cfg.device));
+  apk_status s = launch_impl(ctx, num_tasks, ctx->cfg.poll, ctx->kstream, true);
+  if (s != APK_OK) return s;
+  ctx->running = true;
+  return APK_OK;
+}
+
+apk_status apk_inject_urgent(apk_ctx* ctx, int* event, long long* host_set_ns) {
+  if (!ctx) return APK_EINVAL;
+  if (ctx->cfg.set_mode == APK_SET_DEVICE)
+    return fail(ctx, APK_EINVAL, "set_mode is DEVICE: events come from the device schedule");
+  const int gen = ctx->n_injected.load() + 1;
+  if (gen > ctx->cfg.max_events) return fail(ctx, APK_EINVAL, "event log full (%d)", ctx->cfg.max_events);
+  long long t;
+  if (ctx->cfg.set_mode == APK_SET_HOST_MAPPED) {
+    t = host_now_ns();
+    *reinterpret_cast<volatile int*>(ctx->h_flag) = gen;
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+  } else {
+    ctx->h_gen[gen] = gen;
+    t = host_now_ns();
+    APK_CU(cudaMemcpyAsync(&ctx->d_ctrl->flag_dev, &ctx->h_gen[gen], sizeof(int), cudaMemcpyHostToDevice,
+                           ctx->cstream));
+  }
+  ctx->host_set[gen - 1] = t;
+  ctx->n_injected = gen;
+  if (event) *event = gen - 1;
+  if (host_set_ns) *host_set_ns = t;
+  return APK_OK;
+}
+
+apk_status apk_wait_ack(apk_ctx* ctx, int event, int which, long long timeout_ns, long long* seen) {
+  if (!ctx || event < 0 || event >= ctx->cfg.max_events || (which != 0 && which != 1)) return APK_EINVAL;
+  volatile int* a = reinterpret_cast<volatile int*>(ctx->h_ack) + 2 * event + which;
+  const long long t0 = host_now_ns();
+  while (true) {
+    if (*a != 0) {
+      const long long t = host_now_ns();
+      if (which == 0) ctx->host_ack[event] = t;
+      else ctx->host_done[event] = t;
+      if (seen) *seen = t;
+      return APK_OK;
+    }
+    if (host_now_ns() - t0 > timeout_ns) return fail(ctx, APK_ETIMEDOUT, "ack %d of event %d not seen", which, event);
+  }
+}
+
+apk_status apk_stop(apk_ctx* ctx) {
+  if (!ctx) return APK_EINVAL;
+  static const int kStop = -1, kOne = 1;
+  ctx->h_gen[ctx->cfg.max_events + 1] = kStop;
+  if (ctx->cfg.set_mode == APK_SET_HOST_MAPPED) {
+    *reinterpret_cast<volatile int*>(ctx->h_flag) = kStop;
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+  } else {
+    APK_CU(cudaMemcpyAsync(&ctx->d_ctrl->flag_dev, &ctx->h_gen[ctx->cfg.max_events + 1], sizeof(int),
+                           cudaMemcpyHostToDevice, ctx->cstream));
+  }
+  // the abort word also stops POLL_OFF kernels at their next tile boundary
+  ctx->h_gen[0] = kOne;
+  APK_CU(cudaMemcpyAsync(&ctx->d_ctrl->abort_word, &ctx->h_gen[0], sizeof(int), cudaMemcpyHostToDevice,
+                         ctx->cstream));
+  APK_CU(cudaStreamSynchronize(ctx->cstream));
+  (void)kOne;
+  return APK_OK;
+}
+
+apk_status apk_wait(apk_ctx* ctx, long long timeout_ns) {
+  if (!ctx) return APK_EINVAL;
+  if (!ctx->running) return APK_OK;
+  const long long t0 = host_now_ns();
+  while (true) {
+    cudaError_t q = cudaEventQuery(ctx->ev_done);
+    if (q == cudaSuccess) break;
+    if (q != cudaErrorNotReady) {
+      ctx->running = false;
+      return fail(ctx, APK_ECUDA, "kernel failed: %s", cudaGetErrorString(q));
+    }
+    if (host_now_ns() - t0 > timeout_ns) return fail(ctx, APK_ETIMEDOUT, "launch still running");
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+  ctx->running = false;
+  APK_CU(cudaGetLastError());
+  return read_status(ctx);
+}
+
+apk_status apk_read_output(apk_ctx* ctx, void* C_host) {
+  if (!ctx || !C_host) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "launch still running");
+  APK_CU(cudaMemcpy(C_host, ctx->dC, 4ull * ctx->M * ctx->N, cudaMemcpyDeviceToHost));
+  return APK_OK;
+}
+
+apk_status apk_read_urgent_output(apk_ctx* ctx, int event, float* Cu_host) {
+  if (!ctx || !Cu_host || event < 0 || event > ctx->cfg.max_events || !ctx->dCu) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "launch still running");
+  APK_CU(cudaMemcpy(Cu_host, ctx->dCu + ctx->cu_slot * event, sizeof(float) * ctx->cu_slot,
+                    cudaMemcpyDeviceToHost));
+  return APK_OK;
+}
+
+apk_status apk_read_events(apk_ctx* ctx, apk_event_log* log) {
+  if (!ctx || !log) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "launch still running");
+  const int E = ctx->cfg.max_events;
+  log->n_injected = ctx->n_injected;
+  log->grid = ctx->last_grid;
+  auto D = [&](void* dst, const void* src, size_t bytes) -> apk_status {
+    if (dst) APK_CU(cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost));
+    return APK_OK;
+  };
+  apk_status s;
+  if ((s = D(log->set_ns, ctx->d_set, sizeof(long long) * E)) != APK_OK) return s;
+  if ((s = D(log->claim_ns, ctx->d_claim_ns, sizeof(long long) * E)) != APK_OK) return s;
+  if ((s = D(log->done_ns, ctx->d_done, sizeof(long long) * E)) != APK_OK) return s;
+  if ((s = D(log->claimer, ctx->d_claim, sizeof(int) * E)) != APK_OK) return s;
+  if ((s = D(log->claim_site, ctx->d_site, sizeof(int) * E)) != APK_OK) return s;
+  if ((s = D(log->inflight, ctx->d_inflight, sizeof(int) * E)) != APK_OK) return s;
+  if ((s = D(log->obs_ns, ctx->d_obs, sizeof(long long) * (size_t)E * ctx->last_grid)) != APK_OK) return s;
+  if (log->host_set_ns) memcpy(log->host_set_ns, ctx->host_set.data(), sizeof(long long) * E);
+  if (log->host_ack_ns) memcpy(log->host_ack_ns, ctx->host_ack.data(), sizeof(long long) * E);
+  if (log->host_done_ns) memcpy(log->host_done_ns, ctx->host_done.data(), sizeof(long long) * E);
+  std::vector<long long> set(E);
+  APK_CU(cudaMemcpy(set.data(), ctx->d_set, sizeof(long long) * E, cudaMemcpyDeviceToHost));
+  log->n_fired = (int)std::count_if(set.begin(), set.end(), [](long long v) { return v != 0; });
+  return APK_OK;
+}
+
+apk_status apk_read_oracle(apk_ctx* ctx, int* exec_counts, int* uexec_counts) {
+  if (!ctx) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "launch still running");
+  if (!ctx->cfg.oracle) return fail(ctx, APK_ESTATE, "context was created without oracle counters");
+  if (exec_counts) {
+    if (ctx->last_tasks == APK_TASKS_UNBOUNDED || !ctx->d_exec)
+      return fail(ctx, APK_ESTATE, "per-task counts need a bounded launch");
+    APK_CU(cudaMemcpy(exec_counts, ctx->d_exec, sizeof(int) * ctx->last_tasks, cudaMemcpyDeviceToHost));
+  }
+  if (uexec_counts)
+    APK_CU(cudaMemcpy(uexec_counts, ctx->d_uexec, sizeof(int) * ctx->cfg.max_events, cudaMemcpyDeviceToHost));
+  return APK_OK;
+}
+
+apk_status apk_read_run_stats(apk_ctx* ctx, apk_run_stats* st) {
+  if (!ctx || !st) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "launch still running");
+  Ctrl cb;
+  APK_CU(cudaMemcpy(&cb, ctx->d_ctrl, sizeof cb, cudaMemcpyDeviceToHost));
+  std::vector<unsigned long long> t(ctx->last_grid);
+  APK_CU(cudaMemcpy(t.data(), ctx->d_tiles, sizeof(unsigned long long) * ctx->last_grid, cudaMemcpyDeviceToHost));
+  memset(st, 0, sizeof *st);
+  st->start_ns = (long long)cb.start_min;
+  st->end_ns = (long long)cb.end_max;
+  for (auto v : t) st->tiles_done += v;
+  st->yields = cb.yields;
+  const double tile_flops = 2.0 * (ctx->cfg.dtype == APK_F32 ? 128.0 * 128.0 : 256.0 * 128.0) * ctx->K;
+  st->bg_flops = tile_flops * (double)st->tiles_done;
+  const double dt = (double)(st->end_ns - st->start_ns) * 1e-9;
+  st->bg_tflops = dt > 0 ? st->bg_flops / dt / 1e12 : 0.0;
+  st->exited = cb.exited;
+  st->device_status = cb.status;
+  float ms = 0.f;
+  if (cudaEventElapsedTime(&ms, ctx->ev_start, ctx->ev_done) == cudaSuccess) st->launch_ms = ms;
+  else cudaGetLastError();
+  return APK_OK;
+}
+
+apk_status apk_gemm(apk_ctx* ctx, const void* A, const void* B, void* C, int M, int N, int K,
+                    apk_mem_kind kind) {
+  if (!ctx || !A || !B || !C) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "a launch is already running");
+  APK_CU(cudaSetDevice(ctx->cfg.device));
+  if (M <= 0 || N <= 0 || K <= 0 || M % 128 || N % 128 || K % ctx->cfg.k_tile)
+    return fail(ctx, APK_EINVAL, "shape %dx%dx%d not tile-aligned", M, N, K);
+  if (ctx->cfg.dtype == APK_BF16 && M % 256) return fail(ctx, APK_EINVAL, "bf16 M must be a multiple of 256");
+  const size_t es = esize_of(ctx->cfg.dtype);
+  apk_status s;
+  if (kind == APK_MEM_HOST) {
+    // async copies in kstream order: upload, drain all tiles once, download
+    if ((s = upload(ctx, &ctx->dA, &ctx->ownA, &ctx->capA, A, es * M * K, kind)) != APK_OK) return s;
+    if ((s = upload(ctx, &ctx->dB, &ctx->ownB, &ctx->capB, B, es * (size_t)K * N, kind)) != APK_OK) return s;
+    if ((s = upload(ctx, &ctx->dC, &ctx->ownC, &ctx->capC, nullptr, 4ull * M * N, kind)) != APK_OK) return s;
+  } else {
+    if (ctx->ownA && ctx->dA) cudaFree(ctx->dA);
+    if (ctx->ownB && ctx->dB) cudaFree(ctx->dB);
+    if (ctx->ownC && ctx->dC) cudaFree(ctx->dC);
+    ctx->dA = const_cast<void*>(A);
+    ctx->dB = const_cast<void*>(B);
+    ctx->dC = C;
+    ctx->ownA = ctx->ownB = ctx->ownC = false;
+    ctx->capA = ctx->capB = ctx->capC = 0;
+  }
+  ctx->M = M;
+  ctx->N = N;
+  ctx->K = K;
+  const unsigned long long tiles =
+      (unsigned long long)(M / (ctx->cfg.dtype == APK_F32 ? 128 : 256)) * (N / 128);
+  const int poll = ctx->dAu ? (int)ctx->cfg.poll : APK_POLL_OFF;
+  if ((s = launch_impl(ctx, tiles, poll, ctx->kstream, true)) != APK_OK) return s;
+  ctx->running = true;
+  if (kind == APK_MEM_HOST)
+    APK_CU(cudaMemcpyAsync(C, ctx->dC, 4ull * M * N, cudaMemcpyDeviceToHost, ctx->kstream));
+  APK_CU(cudaStreamSynchronize(ctx->kstream));
+  ctx->running = false;
+  return read_status(ctx);
+}
+
+// ------------------------------------------------------------------ harness
+
+apk_status apk_probe_visibility(apk_ctx* ctx, int reps, long long* offsets_ns) {
+  if (!ctx || reps <= 0 || !offsets_ns) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "probe needs an idle device");
+  if (ctx->cfg.set_mode == APK_SET_DEVICE) return fail(ctx, APK_EINVAL, "no host-set path in DEVICE mode");
+  APK_CU(cudaSetDevice(ctx->cfg.device));
+  long long* d_out = nullptr;
+  APK_CU(cudaMalloc(&d_out, sizeof(long long)));
+  Ctrl init{};
+  for (int r = 0; r < reps; ++r) {
+    APK_CU(cudaMemcpy(ctx->d_ctrl, &init, sizeof init, cudaMemcpyHostToDevice));
+    *reinterpret_cast<volatile int*>(ctx->h_flag) = 0;
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+    const int* flag = ctx->cfg.set_mode == APK_SET_HOST_MAPPED ? ctx->d_flag_mapped : &ctx->d_ctrl->flag_dev;
+    spin_flag_kernel<<<1, 32, 0, ctx->kstream>>>(flag, 1, 200000000LL, d_out, &ctx->d_ctrl->status);
+    spin_until_ns(host_now_ns() + 200000);  // let the spin kernel start
+    long long t;
+    if (ctx->cfg.set_mode == APK_SET_HOST_MAPPED) {
+      t = host_now_ns();
+      *reinterpret_cast<volatile int*>(ctx->h_flag) = 1;
+      std::atomic_thread_fence(std::memory_order_seq_cst);
+    } else {
+      ctx->h_gen[1] = 1;
+      t = host_now_ns();
+      APK_CU(cudaMemcpyAsync(&ctx->d_ctrl->flag_dev, &ctx->h_gen[1], sizeof(int), cudaMemcpyHostToDevice,
+                             ctx->cstream));
+    }
+    APK_CU(cudaStreamSynchronize(ctx->kstream));
+    long long g = 0;
+    APK_CU(cudaMemcpy(&g, d_out, sizeof g, cudaMemcpyDeviceToHost));
+    offsets_ns[r] = g ? g - t : 0;
+  }
+  *reinterpret_cast<volatile int*>(ctx->h_flag) = 0;
+  cudaFree(d_out);
+  return read_status(ctx);
+}
+
+apk_status apk_selftest_wait_timeout(apk_ctx* ctx, long long limit_ns, int* device_status) {
+  if (!ctx || limit_ns <= 0 || !device_status) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "self-test needs an idle device");
+  APK_CU(cudaSetDevice(ctx->cfg.device));
+  Ctrl init{};
+  APK_CU(cudaMemcpy(ctx->d_uctrl, &init, sizeof init, cudaMemcpyHostToDevice));
+  long long* d_out = nullptr;
+  APK_CU(cudaMalloc(&d_out, sizeof(long long)));
+  spin_flag_kernel<<<1, 32, 0, ctx->kstream>>>(&ctx->d_uctrl->never_set, 1, limit_ns, d_out,
+                                               &ctx->d_uctrl->status);
+  APK_CU(cudaGetLastError());
+  APK_CU(cudaStreamSynchronize(ctx->kstream));
+  cudaFree(d_out);
+  Ctrl cb;
+  APK_CU(cudaMemcpy(&cb, ctx->d_uctrl, sizeof cb, cudaMemcpyDeviceToHost));
+  *device_status = cb.status;
+  return APK_OK;
+}
+
+static double pct(std::vector<double> v, double q) {  // nearest rank, src/yield.cu:322-325
+  if (v.empty()) return NAN;
+  std::sort(v.begin(), v.end());
+  return v[std::min((size_t)(q * v.size()), v.size() - 1)];
+}
+
+apk_status apk_run_latency(apk_ctx* ctx, const apk_latency_config* lc, apk_latency_result* out) {
+  if (!ctx || !lc || !out) return APK_EINVAL;
+  if (lc->events <= 0 || lc->events > ctx->cfg.max_events || lc->period_ns <= 0)
+    return fail(ctx, APK_EINVAL, "events must be in [1, max_events] and period > 0");
+  if (ctx->cfg.poll == APK_POLL_OFF) return fail(ctx, APK_EINVAL, "latency mode needs polling");
+  memset(out, 0, sizeof *out);
+  const int E = lc->events;
+  std::mt19937 rng(lc->seed);
+  std::uniform_real_distribution<double> u01(0.0, 1.0);
+  std::vector<long long> when(E);
+  for (int e = 0; e < E; ++e)
+    when[e] = lc->settle_ns + (long long)e * lc->period_ns + (long long)(u01(rng) * lc->period_ns);
+  apk_status s;
+  double offset = 0.0;
+  const bool host_set = ctx->cfg.set_mode != APK_SET_DEVICE;
+  if (host_set) {
+    std::vector<long long> offs(64);
+    if ((s = apk_probe_visibility(ctx, 64, offs.data())) != APK_OK) return s;
+    std::vector<double> o(offs.begin(), offs.end());
+    offset = pct(o, 0.5);
+    if ((s = apk_schedule_device_events(ctx, nullptr, 0)) != APK_OK) return s;
+  } else {
+    if ((s = apk_schedule_device_events(ctx, when.data(), E)) != APK_OK) return s;
+  }
+  out->vis_offset_ns = offset;
+  if ((s = apk_launch(ctx, APK_TASKS_UNBOUNDED)) != APK_OK) return s;
+  const long long t0 = host_now_ns();
+  if (host_set) {
+    for (int e = 0; e < E; ++e) {
+      spin_until_ns(t0 + when[e]);
+      int ev;
+      long long ts;
+      if ((s = apk_inject_urgent(ctx, &ev, &ts)) != APK_OK) break;
+      long long seen;
+      if (apk_wait_ack(ctx, ev, 0, lc->period_ns / 2, &seen) != APK_OK) continue;
+      apk_wait_ack(ctx, ev, 1, lc->period_ns / 2, &seen);
+    }
+  } else {
+    spin_until_ns(t0 + when[E - 1] + 20000000LL);
+  }
+  apk_status st_stop = apk_stop(ctx);
+  apk_status st_wait = apk_wait(ctx, 30000000000LL);
+  if (s != APK_OK) return s;
+  if (st_stop != APK_OK) return st_stop;
+  if (st_wait != APK_OK) return st_wait;
+
+  const int G = ctx->last_grid;
+  const int Ecap = ctx->cfg.max_events;
+  std::vector<long long> set(Ecap), claim(Ecap), done(Ecap), obs((size_t)Ecap * G), hs(Ecap), ha(Ecap), hd(Ecap);
+  std::vector<int> claimer(Ecap);
+  apk_event_log log{};
+  log.set_ns = set.data();
+  log.claim_ns = claim.data();
+  log.done_ns = done.data();
+  log.obs_ns = obs.data();
+  log.claimer = claimer.data();
+  log.host_set_ns = hs.data();
+  log.host_ack_ns = ha.data();
+  log.host_done_ns = hd.data();
+  if ((s = apk_read_events(ctx, &log)) != APK_OK) return s;
+  std::vector<double> lc_claim, lc_last, lc_done, rt_claim, rt_done;
+  for (int e = std::max(0, lc->warmup_events); e < E; ++e) {
+    double setg;
+    if (host_set) {
+      if (hs[e] == 0) continue;
+      setg = (double)hs[e] + offset;
+      if (ha[e]) rt_claim.push_back((ha[e] - hs[e]) / 1e3);
+      if (hd[e]) rt_done.push_back((hd[e] - hs[e]) / 1e3);
+    } else {
+      if (set[e] == 0) continue;
+      setg = (double)set[e];
+    }
+    ++out->n;
+    if (claimer[e] == 0) {
+      ++out->unclaimed;
+      continue;
+    }
+    lc_claim.push_back((claim[e] - setg) / 1e3);
+    if (done[e]) lc_done.push_back((done[e] - setg) / 1e3);
+    long long hi = 0;
+    int seen = 0;
+    for (int b = 0; b < G; ++b) {
+      const long long o = obs[(size_t)e * G + b];
+      if (!o) continue;
+      ++seen;
+      hi = std::max(hi, o);
+    }
+    if (seen < G) ++out->anomalies;
+    else lc_last.push_back((hi - setg) / 1e3);
+  }
+  out->claim_p50_us = pct(lc_claim, 0.5);
+  out->claim_p99_us = pct(lc_claim, 0.99);
+  out->last_obs_p50_us = pct(lc_last, 0.5);
+  out->last_obs_p99_us = pct(lc_last, 0.99);
+  out->done_p50_us = pct(lc_done, 0.5);
+  out->done_p99_us = pct(lc_done, 0.99);
+  out->rt_claim_p50_us = pct(rt_claim, 0.5);
+  out->rt_claim_p99_us = pct(rt_claim, 0.99);
+  out->rt_done_p50_us = pct(rt_done, 0.5);
+  out->rt_done_p99_us = pct(rt_done, 0.99);
+  apk_run_stats rs;
+  if ((s = apk_read_run_stats(ctx, &rs)) != APK_OK) return s;
+  out->bg_tflops = rs.bg_tflops;
+  return APK_OK;
+}
+
+apk_status apk_run_overhead(apk_ctx* ctx, unsigned long long num_tasks, int reps, double* ms_poll,
+                            double* ms_nopoll) {
+  if (!ctx || reps <= 0 || num_tasks == 0 || num_tasks == APK_TASKS_UNBOUNDED) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "a launch is already running");
+  APK_CU(cudaSetDevice(ctx->cfg.device));
+  const int warm = 2;
+  std::vector<double> on, off;
+  for (int r = 0; r < 2 * (reps + warm); ++r) {
+    // alternate which variant leads each pair (src/yield.cu:674-677)
+    const bool poll = ((r / 2) % 2 == 0) ? (r % 2 == 0) : (r % 2 == 1);
+    apk_status s = launch_impl(ctx, num_tasks, poll ? (int)ctx->cfg.poll : APK_POLL_OFF, ctx->kstream, true);
+    if (s != APK_OK) return s;
+    APK_CU(cudaEventSynchronize(ctx->ev_done));
+    if ((s = read_status(ctx)) != APK_OK) return s;
+    float ms = 0;
+    APK_CU(cudaEventElapsedTime(&ms, ctx->ev_start, ctx->ev_done));
+    if (r >= 2 * warm) (poll ? on : off).push_back(ms);
+  }
+  *ms_poll = pct(on, 0.5);
+  *ms_nopoll = pct(off, 0.5);
+  return APK_OK;
+}
+
+apk_status apk_run_baseline(apk_ctx* ctx, unsigned long long num_tasks, int trials, unsigned seed,
+                            double* e2e_us) {
+  if (!ctx || trials <= 0 || !e2e_us || num_tasks == 0 || num_tasks == APK_TASKS_UNBOUNDED) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "a launch is already running");
+  if (ctx->cfg.dtype != APK_F32) return fail(ctx, APK_EUNSUPPORTED, "baseline mode is fp32 only");
+  if (!ctx->dAu) return fail(ctx, APK_ESTATE, "no urgent operands set");
+  APK_CU(cudaSetDevice(ctx->cfg.device));
+  // urgent kernel: the same tile code as a non-persistent launch over the
+  // urgent GEMM's tiles on a max-priority stream (src/urgent_baseline.cu:101-112)
+  F32Params up;
+  memset(&up, 0, sizeof up);
+  const int bk = ctx->cfg.k_tile;
+  apk_status t;
+  if ((t = make_tmap(ctx, &up.tmA, ctx->dAu, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ctx->Mu, ctx->Ku, 32, 128,
+                     CU_TENSOR_MAP_SWIZZLE_128B)) != APK_OK)
+    return t;
+  if ((t = make_tmap(ctx, &up.tmB, ctx->dBu, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ctx->Ku, ctx->Nu, 128, bk,
+                     CU_TENSOR_MAP_SWIZZLE_NONE)) != APK_OK)
+    return t;
+  up.tmAu = up.tmA;
+  up.tmBu = up.tmB;
+  const int utiles = (ctx->Mu / 128) * (ctx->Nu / 128);
+  up.C = ctx->dCu + ctx->cu_slot * ctx->cfg.max_events;  // spare slot
+  up.ldc = ctx->Nu;
+  up.tiles_n = ctx->Nu / 128;
+  up.total_tiles = utiles;
+  up.nk = ctx->Ku / bk;
+  up.Cu = up.C;
+  up.ldcu = ctx->Nu;
+  up.usplit = 1;
+  up.utiles_n = up.tiles_n;
+  up.wait_limit_ns = ctx->cfg.wait_limit_ns;
+  up.slab = ctx->d_slab;
+  up.slab_hdr = ctx->d_slab_hdr;
+  Ctrl* ub = ctx->d_uctrl;
+  up.ev.flag = &ub->flag_dev;
+  up.ev.abort_word = &ub->abort_word;
+  up.ev.status = &ub->status;
+  up.ev.max_events = 0;
+  up.q.next_task = &ub->next_task;
+  up.q.num_tasks = (unsigned long long)utiles;
+  up.q.tiles_done = ctx->d_utiles;
+  up.q.start_min = &ub->start_min;
+  up.q.end_max = &ub->end_max;
+  up.q.exited = &ub->exited;
+  up.q.yields = &ub->yields;
+
+  // drain estimate, background alone (device timeline)
+  apk_status s = launch_impl(ctx, num_tasks, APK_POLL_OFF, ctx->kstream, true);
+  if (s != APK_OK) return s;
+  APK_CU(cudaEventSynchronize(ctx->ev_done));
+  float drain_ms = 0;
+  APK_CU(cudaEventElapsedTime(&drain_ms, ctx->ev_start, ctx->ev_done));
+  std::mt19937 rng(seed);
+  std::uniform_real_distribution<double> frac(0.2, 0.8);
+  Ctrl init{};
+  init.start_min = ~0ull;
+  for (int tr = 0; tr < trials; ++tr) {
+    APK_CU(cudaMemcpy(ub, &init, sizeof init, cudaMemcpyHostToDevice));
+    APK_CU(cudaDeviceSynchronize());
+    const double delay_ns = frac(rng) * drain_ms * 1e6;
+    if ((s = launch_impl(ctx, num_tasks, APK_POLL_OFF, ctx->kstream, true)) != APK_OK) return s;
+    const long long t0 = host_now_ns();
+    spin_until_ns(t0 + (long long)delay_ns);
+    const long long ta = host_now_ns();
+    cudaError_t e = f32::launch(up, utiles, APK_POLL_OFF, APK_DISC_DRAIN, false, bk, ctx->ustream);
+    if (e != cudaSuccess) return fail(ctx, APK_ECUDA, "urgent launch failed: %s", cudaGetErrorString(e));
+    APK_CU(cudaStreamSynchronize(ctx->ustream));
+    const long long td = host_now_ns();
+    APK_CU(cudaStreamSynchronize(ctx->kstream));
+    e2e_us[tr] = (td - ta) / 1e3;
+  }
+  return read_status(ctx);
+}
+
+void* apk_host_alloc(size_t bytes) {
+  void* p = nullptr;
+  if (cudaHostAlloc(&p, bytes, cudaHostAllocPortable) != cudaSuccess) return nullptr;
+  return p;
+}
+
+void apk_host_free(void* p) {
+  if (p) cudaFreeHost(p);
+}
+
+}  // extern "C"

@@ -1,0 +1,499 @@
+// fp32 CUDA-core persistent SGEMM with tile-boundary and per-stage yield.
+//
+// Replaces the reference's SIMT tile routine and its persistent drivers:
+//   tile_gemm            src/tile.cuh:62-107      (64x64 tile, scalar loads)
+//   persistent_gemm      src/persistent.cu:51-79  (fetch-add queue)
+//   persistent_yield     src/yield.cu:95-204      (boundary poll, mini-queue)
+//   persistent_midyield  src/midyield.cu:92-320   (per-stage checkpoint)
+//
+// B200 design:
+//   * 128x128 output tile, 256 threads, 8x8 register micro-tile per thread,
+//     K-tile BK (32 by default) staged by TMA into a STAGES-deep ring of
+//     shared-memory slots, each guarded by one transaction mbarrier.  A
+//     slot is loaded as a [128 rows][32 k] box with 128-byte swizzle (so
+//     rows read as float4 along k are bank-conflict free) and B as a
+//     [32 k][128 cols] box without swizzle (float4 along n).
+//   * One elected thread (tid 0) issues TMA and polls the yield flag; the
+//     poll result is made uniform for the CTA by __syncthreads_or at the
+//     stage barrier the ring needs anyway (the barrier that frees the slot
+//     about to be refilled), so per-stage polling adds one relaxed load per
+//     stage and no extra barrier (the reference paid two barriers per site,
+//     src/midyield.cu:197-219, and a 14% cost at 1 CTA/SM,
+//     results/summary/tc_summary.csv:8-10).
+//   * Yield = the reference's cooperative mini-queue (src/yield.cu:163-183):
+//     every CTA that observes a new generation pops urgent work items until
+//     the queue is empty; the first popper is the claimer.  Unlike the
+//     reference, a mid-pipeline yield does NOT abandon the background tile
+//     (src/midyield.cu:237-318): in-flight TMA stages are drained, the
+//     register accumulators are spilled to a global checkpoint slab with
+//     the K cursor, the urgent items run through the same ring, and the
+//     accumulators are restored so the tile continues at the same K stage
+//     with the same FMA order -- bitwise identical to an uninterrupted run.
+//   * Disciplines: DRAIN (always wait for in-flight stages before the slots
+//     are reused) and POISON (drain, then corrupt one staged urgent value:
+//     the detector's positive control, src/midyield.cu:146-147).  The
+//     reference's NAIVE discipline (no wait) is not built: with an mbarrier
+//     ring it would alias two transaction counts on one barrier phase, a
+//     protocol error rather than the data race it measured.
+//   * Every mbarrier wait is bounded (wait_limit_ns); a timeout sets the
+//     status word and the abort word and the CTA unwinds.
+#include "common.cuh"
+#include "proto.h"
+
+namespace apk {
+namespace f32 {
+
+constexpr int BM = 128, BN = 128, NT = 256;
+
+template <int BK>
+struct Cfg {
+  static constexpr int STAGES = (BK == 32) ? 3 : 2;
+  static constexpr int A_BYTES = BM * BK * 4;
+  static constexpr int B_BYTES = BK * BN * 4;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+};
+
+// One K-tile of the 128x128 tile: acc[i][j] += A[r_i][k] * B[k][c_j] for k
+// in increasing order.  Thread (warp w, lane l): rows r_i = (w&3)*32 +
+// (l>>3) + 4i, columns c_j = (w>>2)*64 + (l&7)*4 + {0..3, 32..35}.
+// A is read two k at a time (float2 per row) and B one k at a time (two
+// float4): 12 shared loads per 128 FFMA, 96 live registers for operands and
+// accumulators, which leaves headroom under the 128-register cap.
+template <int BK>
+__device__ __forceinline__ void compute_stage(const float* __restrict__ As,
+                                              const float* __restrict__ Bs, float (&acc)[8][8],
+                                              int arow0, int ty, int bcol) {
+#pragma unroll
+  for (int sub = 0; sub < BK / 32; ++sub) {
+    const float* Asub = As + sub * (BM * 32);
+    // not unrolled: any unroll lets the scheduler hoist loads until the
+    // 128-register cap of 2 CTAs/SM spills (unconstrained it takes 167)
+#pragma unroll 1
+    for (int kp = 0; kp < 16; ++kp) {
+      const int kc = kp >> 1, half = kp & 1;
+      float2 a[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        // row r = arow0 + 4i; (r & 7) == ty + 4*(i&1) because arow0 = 32*wm + ty
+        const int sw = kc ^ (ty + 4 * (i & 1));
+        a[i] = *reinterpret_cast<const float2*>(Asub + (arow0 + 4 * i) * 32 + (sw << 2) + 2 * half);
+      }
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        const float* brow = Bs + (sub * 32 + kp * 2 + kk) * BN + bcol;
+        const float4 b0 = *reinterpret_cast<const float4*>(brow);
+        const float4 b1 = *reinterpret_cast<const float4*>(brow + 32);
+        const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float av = kk == 0 ? a[i].x : a[i].y;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av, bv[j], acc[i][j]);
+        }
+      }
+    }
+  }
+}
+
+template <int BK>
+__device__ __forceinline__ void issue_stage(uint8_t* smem, uint64_t* full, uint32_t seq,
+                                            const CUtensorMap* tA, const CUtensorMap* tB,
+                                            int row0, int col0, int k0) {
+  using C = Cfg<BK>;
+  const int slot = seq % C::STAGES;
+  float* a = reinterpret_cast<float*>(smem + slot * C::A_BYTES);
+  float* b = reinterpret_cast<float*>(smem + C::STAGES * C::A_BYTES + slot * C::B_BYTES);
+  mbar_arrive_expect_tx(&full[slot], C::STAGE_BYTES);
+#pragma unroll
+  for (int sub = 0; sub < BK / 32; ++sub) tma_load_2d(a + sub * BM * 32, tA, k0 + sub * 32, row0, &full[slot]);
+  tma_load_2d(b, tB, col0, k0, &full[slot]);
+}
+
+template <int POLL, int DISC, bool ORACLE, int BK>
+__global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant__ F32Params p) {
+  using C = Cfg<BK>;
+  constexpr int S = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[S];
+  __shared__ unsigned long long s_task;
+  __shared__ int s_f, s_item;
+  // Bookkeeping touched only by tid 0, or needed only across a job switch,
+  // lives in shared memory: as per-thread locals it costs every thread
+  // registers under the 2-CTA/SM cap (the reference hit the same,
+  // src/yield.cu:106-110).
+  __shared__ int s_lastSeen, s_pend, s_nextEv, s_site, s_inflight;
+  __shared__ long long s_gBase;
+  __shared__ unsigned long long s_myTiles, s_bgTask;
+  __shared__ int s_bgRow0, s_bgCol0, s_bgC, s_pending;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int ty = lane >> 3;
+  const int arow0 = (warp & 3) * 32 + ty;
+  const int bcol = (warp >> 2) * 64 + (lane & 7) * 4;
+  const int cta = blockIdx.x;
+  const int grid = gridDim.x;
+
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+    s_lastSeen = 0;
+    s_pend = 0;
+    s_nextEv = 0;
+    s_gBase = 0;
+    s_myTiles = 0;
+    s_pending = 0;
+    tma_prefetch_desc(&p.tmA);
+    tma_prefetch_desc(&p.tmB);
+    tma_prefetch_desc(&p.tmAu);
+    tma_prefetch_desc(&p.tmBu);
+    atomicMin(p.q.start_min, (unsigned long long)globaltimer_ns());
+  }
+  __syncthreads();
+
+  uint32_t P = 0, Q = 0;  // issued / consumed stage sequence numbers (uniform)
+  bool bad = false;       // this thread saw a wait time out
+  float acc[8][8];
+
+  // Job state (uniform).  A job is a background tile or one urgent item;
+  // both run through the single mainloop below.
+  bool urgent = false;    // current job is an urgent item
+  bool bg_active = false; // a background tile is in progress (maybe suspended)
+  bool ckpt = false;      // background accumulators are in the slab
+  int row0 = 0, col0 = 0, kst0 = 0, nk = 0, c = 0;
+  int ev = 0, popE = 0, popF = 0;  // urgent queue range still to pop
+  bool popped = false;             // this CTA ran an item of event popE
+
+  auto setter = [&]() {  // device-set events (src/yield.cu:186-195), tid 0 of CTA 0
+    const int nextEv = s_nextEv;
+    if (cta == 0 && p.ev.sched_ns != nullptr && nextEv < p.ev.n_sched) {
+      const long long now = globaltimer_ns();
+      if (s_gBase == 0) s_gBase = now;
+      if (now >= s_gBase + p.ev.sched_ns[nextEv]) {
+        p.ev.set_ns[nextEv] = now;
+        atomicCAS(p.ev.flag, nextEv, nextEv + 1);  // never overwrites the -1 sentinel
+        s_nextEv = nextEv + 1;
+      }
+    }
+  };
+
+  auto drain = [&]() {  // wait out every issued-but-unconsumed stage
+    while (Q != P) {
+      if (!mbar_wait(&full[Q % S], (Q / S) & 1, p.wait_limit_ns)) bad = true;
+      ++Q;
+    }
+  };
+
+  auto prime = [&](int from) {  // issue stages [from, from + S-1) of the job
+    int n = nk - from;
+    n = n < S - 1 ? n : S - 1;
+    if (tid == 0) {
+      const CUtensorMap* tA = urgent ? &p.tmAu : &p.tmA;
+      const CUtensorMap* tB = urgent ? &p.tmBu : &p.tmB;
+      for (int s = 0; s < n; ++s) issue_stage<BK>(smem, full, P + s, tA, tB, row0, col0, (kst0 + from + s) * BK);
+    }
+    P += n;
+  };
+
+  // Observation of new generations at a poll site (tid 0 wrote s_f before
+  // the barrier that brought every thread here).  Returns true = exit.
+  auto observe = [&](int site) -> bool {
+    const int f = s_f;
+    const int anyBad = __syncthreads_or(bad);  // also: everyone has read s_f
+    if (anyBad || f < 0) {
+      drain();
+      if (anyBad && tid == 0) report_status(p.ev.status, DEV_WAIT_TIMEOUT_FULL, p.ev.abort_word);
+      return true;
+    }
+    if (tid == 0) {
+      const long long g = globaltimer_ns();
+      for (int e = s_lastSeen; e < f && e < p.ev.max_events; ++e) p.ev.obs_ns[(size_t)e * grid + cta] = g;
+      s_item = s_lastSeen;
+      s_lastSeen = f;
+      s_site = site;
+      s_inflight = (int)(P - Q);
+    }
+    __syncthreads();
+    popE = s_item;
+    popF = f < p.ev.max_events ? f : p.ev.max_events;
+    popped = false;
+    return false;
+  };
+
+  while (true) {
+    // ======================= choose the next job ===========================
+    if (popE < popF) {
+      // cooperative urgent mini-queue (src/yield.cu:163-183)
+      if (tid == 0) {
+        const int it = atomicAdd(&p.ev.uq_next[popE], 1);
+        if (it == 0) {
+          p.ev.claim_ns[popE] = globaltimer_ns();
+          p.ev.claim[popE] = cta + 1;
+          p.ev.claim_site[popE] = s_site;
+          p.ev.inflight[popE] = s_inflight;
+          if (p.ev.ack != nullptr) flag_store(&p.ev.ack[2 * popE], 1);
+        }
+        s_item = it;
+      }
+      __syncthreads();
+      const int it = s_item;
+      __syncthreads();
+      if (it >= p.uitems) {
+        if (popped && tid == 0) atomicMax(&p.ev.done_ns[popE], (unsigned long long)globaltimer_ns());
+        ++popE;
+        popped = false;
+        continue;
+      }
+      if (!ckpt) {
+        // checkpoint: drain in-flight stages, park the accumulators
+        drain();
+        if (bg_active) {
+          float4* s4 = reinterpret_cast<float4*>(p.slab) + (size_t)cta * 16 * NT;
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              s4[(i * 2 + h) * NT + tid] =
+                  make_float4(acc[i][4 * h], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
+          if (tid == 0) {
+            s_bgRow0 = row0;
+            s_bgCol0 = col0;
+            s_bgC = c;
+            long long* hdr = p.slab_hdr + (size_t)cta * 4;
+            hdr[0] = (long long)s_bgTask;
+            hdr[1] = c;
+            hdr[2] = popE;
+            hdr[3] = 1;
+            atomicAdd(p.q.yields, 1ull);
+          }
+        }
+        ckpt = true;
+      }
+      popped = true;
+      urgent = true;
+      ev = popE;
+      const int t = it / p.usplit, ks = it % p.usplit;
+      row0 = (t / p.utiles_n) * BM;
+      col0 = (t % p.utiles_n) * BN;
+      nk = p.unk;
+      kst0 = ks * p.unk;
+      c = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+      __syncthreads();  // the slot refilled first was read by the previous job
+      prime(0);
+    } else if (bg_active) {
+      if (ckpt) {
+        // resume the background tile from its checkpoint
+        urgent = false;
+        ckpt = false;
+        row0 = s_bgRow0;
+        col0 = s_bgCol0;
+        c = s_bgC;
+        kst0 = 0;
+        nk = p.nk;
+        const float4* s4 = reinterpret_cast<const float4*>(p.slab) + (size_t)cta * 16 * NT;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const float4 v = s4[(i * 2 + h) * NT + tid];
+            acc[i][4 * h] = v.x;
+            acc[i][4 * h + 1] = v.y;
+            acc[i][4 * h + 2] = v.z;
+            acc[i][4 * h + 3] = v.w;
+          }
+        __syncthreads();
+        prime(c);
+      }
+      // else: no item was popped; the job continues with its stages in flight
+    } else {
+      // ---------------- tile boundary: pop a background task --------------
+      // A task popped before a boundary yield is kept (s_pending) and run
+      // after the urgent work, never dropped (src/yield.cu:197-202).
+      ckpt = false;
+      int fl = 0;
+      bool yb = false;
+      if (tid == 0) {
+        if (!s_pending) s_task = atomicAdd(p.q.next_task, 1ull);
+        s_pending = 0;
+        const int ab = *reinterpret_cast<volatile int*>(p.ev.abort_word);
+        fl = s_lastSeen;
+        if (POLL == POLL_BOUNDARY) {
+          setter();
+          fl = flag_load(p.ev.flag);
+        }
+        if (ab) fl = -1;
+        s_f = fl;
+        yb = fl != s_lastSeen;
+      }
+      const int y = __syncthreads_or(yb || bad);
+      const unsigned long long task = s_task;
+      if (y) {
+        if (observe(-1)) break;
+        if (popE < popF) {
+          if (tid == 0) s_pending = 1;  // run this task after the urgent work
+          continue;                     // boundary yield: pipeline is empty
+        }
+      }
+      if (task >= p.q.num_tasks) break;
+      if (tid == 0) s_bgTask = task;
+      const int tile = (int)(task % (unsigned long long)p.total_tiles);
+      urgent = false;
+      bg_active = true;
+      row0 = (tile / p.tiles_n) * BM;
+      col0 = (tile % p.tiles_n) * BN;
+      kst0 = 0;
+      nk = p.nk;
+      c = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+      prime(0);
+    }
+
+    // ============================ mainloop =================================
+    bool yielded = false;
+    for (; c < nk; ++c) {
+      bool ys = false;
+      if (POLL == POLL_STAGE && !urgent && tid == 0) {
+        const int fs = s_pend;  // loaded one stage ago: the latency hides under compute
+        s_pend = flag_load(p.ev.flag);
+        setter();
+        s_f = fs;
+        ys = fs != s_lastSeen;
+      }
+      // frees the slot refilled below (read by every thread one stage ago)
+      const int y = __syncthreads_or(ys || bad);
+      if (y) {
+        yielded = true;
+        break;
+      }
+      if (c + S - 1 < nk) {
+        if (tid == 0)
+          issue_stage<BK>(smem, full, P, urgent ? &p.tmAu : &p.tmA, urgent ? &p.tmBu : &p.tmB, row0, col0,
+                          (kst0 + c + S - 1) * BK);
+        ++P;
+      }
+      if (!mbar_wait(&full[Q % S], (Q / S) & 1, p.wait_limit_ns)) bad = true;
+      const int slot = Q % S;
+      const float* As = reinterpret_cast<const float*>(smem + slot * C::A_BYTES);
+      const float* Bs = reinterpret_cast<const float*>(smem + S * C::A_BYTES + slot * C::B_BYTES);
+      if (DISC == DISC_POISON && urgent && c == 0) {
+        // detector control: one wrong staged value in each urgent item
+        if (tid == 0) {
+          const_cast<float*>(Bs)[0] += 1.0f;
+          fence_proxy_async_smem();
+        }
+        __syncthreads();
+      }
+      compute_stage<BK>(As, Bs, acc, arow0, ty, bcol);
+      ++Q;
+    }
+    if (yielded) {
+      if (observe(c)) break;
+      continue;  // pop urgent items (or resume this tile if none are left)
+    }
+
+    // ============================ epilogue =================================
+    if (!urgent) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float* crow = p.C + (size_t)(row0 + arow0 + 4 * i) * p.ldc + col0 + bcol;
+        *reinterpret_cast<float4*>(crow) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+        *reinterpret_cast<float4*>(crow + 32) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+      }
+      bg_active = false;
+      __syncthreads();  // the whole tile is stored before it counts as complete
+      if (tid == 0) {
+        ++s_myTiles;
+        if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[s_bgTask], 1);
+        count_trigger(p.ev);
+      }
+    } else {
+      float* Cu = p.Cu + (size_t)ev * p.cu_stride;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float* crow = Cu + (size_t)(row0 + arow0 + 4 * i) * p.ldcu + col0 + bcol;
+        if (p.usplit == 1) {
+          *reinterpret_cast<float4*>(crow) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+          *reinterpret_cast<float4*>(crow + 32) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            atomicAdd(crow + j, acc[i][j]);
+            atomicAdd(crow + 32 + j, acc[i][4 + j]);
+          }
+        }
+      }
+      __syncthreads();  // whole item written before it is counted
+      if (tid == 0) {
+        if (ORACLE) atomicAdd(&p.ev.uexec[ev], 1);
+        __threadfence();
+        const int done = atomicAdd(&p.ev.udone_cnt[ev], 1) + 1;
+        if (done == p.uitems && p.ev.ack != nullptr) flag_store(&p.ev.ack[2 * ev + 1], 1);
+      }
+      urgent = false;
+    }
+  }
+
+  drain();
+  if (tid == 0) {
+    if (bad) report_status(p.ev.status, DEV_WAIT_TIMEOUT_FULL, p.ev.abort_word);
+    p.q.tiles_done[cta] = s_myTiles;
+    atomicMax(p.q.end_max, (unsigned long long)globaltimer_ns());
+    atomicAdd(p.q.exited, 1);
+  }
+}
+
+// Host-side dispatch over the template instantiations.
+
+template <int POLL, int DISC, bool ORACLE, int BK>
+static const void* kernel_ptr() {
+  return reinterpret_cast<const void*>(&sgemm_persistent<POLL, DISC, ORACLE, BK>);
+}
+
+static const void* select_kernel(int poll, int disc, bool oracle, int bk) {
+#define APK_SEL(PL, DS, OR)                                                        \
+  if (poll == PL && disc == DS && oracle == OR) {                                 \
+    if (bk == 32) return kernel_ptr<PL, DS, OR, 32>();                           \
+    if (bk == 64) return kernel_ptr<PL, DS, OR, 64>();                           \
+  }
+  APK_SEL(POLL_OFF, DISC_DRAIN, false)
+  APK_SEL(POLL_OFF, DISC_DRAIN, true)
+  APK_SEL(POLL_BOUNDARY, DISC_DRAIN, false)
+  APK_SEL(POLL_BOUNDARY, DISC_DRAIN, true)
+  APK_SEL(POLL_BOUNDARY, DISC_POISON, false)
+  APK_SEL(POLL_STAGE, DISC_DRAIN, false)
+  APK_SEL(POLL_STAGE, DISC_DRAIN, true)
+  APK_SEL(POLL_STAGE, DISC_POISON, false)
+#undef APK_SEL
+  return nullptr;
+}
+
+int smem_bytes(int bk) { return bk == 32 ? Cfg<32>::SMEM_BYTES : Cfg<64>::SMEM_BYTES; }
+
+cudaError_t prepare(int poll, int disc, bool oracle, int bk, int* max_ctas_per_sm) {
+  const void* k = select_kernel(poll, disc, oracle, bk);
+  if (!k) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(bk));
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(max_ctas_per_sm, k, NT, smem_bytes(bk));
+}
+
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int bk,
+                   cudaStream_t stream) {
+  const void* k = select_kernel(poll, disc, oracle, bk);
+  if (!k) return cudaErrorInvalidValue;
+  void* args[] = {const_cast<F32Params*>(&prm)};
+  return cudaLaunchKernel(k, dim3(grid), dim3(NT), args, smem_bytes(bk), stream);
+}
+
+}  // namespace f32
+}  // namespace apk

@@ -1,0 +1,290 @@
+/*
+ * apk.h -- C ABI of the B200 preemptible persistent-GEMM runtime (libapk.so).
+ *
+ * The reference (AyaanFaisal21/APK) has no library: its boundary is the
+ * device-memory protocol between each binary's main() and its persistent
+ * kernel, plus the binaries' --mode switches.  Each entry point below names
+ * the reference code it replaces (paths relative to the reference root).
+ *
+ * Conventions
+ *   - Every function returns apk_status; APK_OK == 0.  No exceptions cross
+ *     the ABI.  apk_last_error() returns a message for the last failure.
+ *   - Plain pointers and sizes only.  Buffers passed with APK_MEM_HOST are
+ *     caller-owned host memory the runtime copies from/to; APK_MEM_DEVICE
+ *     buffers are caller-owned device memory used in place.
+ *   - One context per device per host thread.  apk_inject_urgent and
+ *     apk_stop may be called from a second host thread while a launch runs.
+ *   - Every device-side wait is bounded (apk_config.wait_limit_ns); a wait
+ *     that runs out is reported as APK_EDEVICE, never as a hung GPU.
+ *   - Matrices are row-major.  fp32: M, N multiples of 128, K a multiple of
+ *     k_tile.  bf16: M, N multiples of 128, K a multiple of 64.
+ */
+#ifndef APK_H_
+#define APK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define APK_ABI_VERSION 1
+#define APK_TASKS_UNBOUNDED 0xFFFFFFFFFFFFFFFFull
+
+typedef enum apk_status {
+  APK_OK = 0,
+  APK_EINVAL = 1,       /* bad argument (shape, null pointer, mode)          */
+  APK_ECUDA = 2,        /* a CUDA call failed (message in apk_last_error)    */
+  APK_ETIMEDOUT = 3,    /* apk_wait deadline passed; the kernel still runs   */
+  APK_ESTATE = 4,       /* call not valid now (e.g. launch while running)    */
+  APK_EDEVICE = 5,      /* the kernel reported an error (bounded wait ended) */
+  APK_ENOMEM = 6,
+  APK_EUNSUPPORTED = 7
+} apk_status;
+
+typedef enum apk_dtype { APK_F32 = 0, APK_BF16 = 1 } apk_dtype;
+
+/* Poll sites: src/midyield.cu:89 / src/tcyield.cu:88 (OFF, BOUNDARY, STAGE). */
+typedef enum apk_poll_mode {
+  APK_POLL_OFF = 0,
+  APK_POLL_BOUNDARY = 1,
+  APK_POLL_STAGE = 2
+} apk_poll_mode;
+
+/* Disciplines: src/midyield.cu:90 (DRAIN, POISON; NAIVE is not built). */
+typedef enum apk_discipline { APK_DISC_DRAIN = 0, APK_DISC_POISON = 2 } apk_discipline;
+
+/* Who sets the yield flag.  DEVICE: CTA 0 at scheduled globaltimer offsets
+ * (src/yield.cu:186-195, the reference's primary instrument).  HOST_MAPPED:
+ * the host stores the generation into mapped pinned memory the CTAs poll.
+ * HOST_MEMCPY: the host copies it into device memory with cudaMemcpyAsync
+ * on a control stream (src/yield.cu:851-852). */
+typedef enum apk_set_mode {
+  APK_SET_DEVICE = 0,
+  APK_SET_HOST_MAPPED = 1,
+  APK_SET_HOST_MEMCPY = 2
+} apk_set_mode;
+
+typedef enum apk_mem_kind { APK_MEM_HOST = 0, APK_MEM_DEVICE = 1 } apk_mem_kind;
+
+typedef struct apk_config {
+  int device;
+  apk_dtype dtype;
+  int ctas_per_sm;          /* 0 = as many as fit (full residency)            */
+  int grid;                 /* 0 = SMs * ctas_per_sm                          */
+  int k_tile;               /* fp32: 32 or 64; bf16: 64                       */
+  apk_poll_mode poll;
+  apk_discipline discipline;
+  apk_set_mode set_mode;
+  int max_events;           /* capacity of the event log                      */
+  int oracle;               /* 1 = count executions per task and per event    */
+  int urgent_split_k;       /* urgent items per urgent output tile            */
+  long long wait_limit_ns;  /* bound on every device-side wait                */
+} apk_config;
+
+/* Fill *cfg with the defaults (fp32, full residency, k_tile 32, stage
+ * polling, drain, host-mapped flag, 4096 events, split-K 4, 2 s waits). */
+void apk_config_default(apk_config* cfg);
+
+typedef struct apk_ctx apk_ctx;
+
+/* Replaces each binary's setup: device query, occupancy-derived grid and
+ * control-array allocation (src/yield.cu:349-400, src/persistent.cu:110-151). */
+apk_status apk_create(const apk_config* cfg, apk_ctx** out);
+apk_status apk_destroy(apk_ctx* ctx);
+const char* apk_last_error(const apk_ctx* ctx);
+
+typedef struct apk_device_info {
+  int sms;
+  int grid;                 /* CTAs of the persistent kernel                  */
+  int ctas_per_sm;          /* resident CTAs per SM actually used             */
+  int max_ctas_per_sm;      /* occupancy limit of the selected kernel         */
+  int cc_major, cc_minor;
+  int smem_per_cta;
+  int threads_per_cta;
+  int tile_m, tile_n, k_tile, stages;
+  char name[128];
+} apk_device_info;
+apk_status apk_get_info(apk_ctx* ctx, apk_device_info* info);
+
+/* Background GEMM C = A * B.  Replaces the operand set-up and upload of
+ * src/persistent.cu:132-151 and src/yield.cu:367-396.  For APK_MEM_HOST the
+ * runtime owns device copies; for APK_MEM_DEVICE it uses the caller's
+ * buffers (C must stay valid until the launch ends). */
+apk_status apk_set_background(apk_ctx* ctx, const void* A, const void* B, void* C, int M, int N,
+                              int K, apk_mem_kind kind);
+
+/* The urgent GEMM every event runs (the reference's urgent tile,
+ * src/yield.cu:163-178 and src/urgent_baseline.cu:101-112, generalised to
+ * an M x N x K GEMM split into work items).  Each event writes its own
+ * output slot. */
+apk_status apk_set_urgent(apk_ctx* ctx, const void* A, const void* B, int M, int N, int K,
+                          apk_mem_kind kind);
+
+/* Start the persistent kernel over num_tasks background tasks (task t
+ * computes tile t mod tiles, src/urgent_baseline.cu:78-83), or until
+ * apk_stop with APK_TASKS_UNBOUNDED.  Asynchronous.  Replaces the launch
+ * and zero_all lambdas of src/yield.cu:400-443. */
+apk_status apk_launch(apk_ctx* ctx, unsigned long long num_tasks);
+
+/* Device-set schedule: cumulative offsets (ns) from CTA 0's first poll at
+ * which CTA 0 bumps the generation (src/yield.cu:824-834).  Call before
+ * apk_launch; n = 0 clears it. */
+apk_status apk_schedule_device_events(apk_ctx* ctx, const long long* offsets_ns, int n);
+
+/* Count-triggered device events: event k fires when the k-th count of
+ * completed background tiles is reached (counts ascending).  The CTA that
+ * completes that tile bumps the generation, so the yield lands at a
+ * deterministic point of the drain -- e.g. "one yield after 50% of tiles
+ * complete".  Needs set_mode DEVICE; replaces any time schedule; call
+ * before apk_launch (n = 0 clears it).  No reference counterpart: the
+ * reference fires only at scheduled times (src/yield.cu:186-195). */
+apk_status apk_schedule_count_events(apk_ctx* ctx, const unsigned long long* counts, int n);
+
+/* Host-set injection (src/yield.cu:845-856): bump the generation.  Returns
+ * the event index and the host steady-clock time of the store. */
+apk_status apk_inject_urgent(apk_ctx* ctx, int* event, long long* host_set_ns);
+
+/* Spin (bounded) until the event's claim ack (which = 0) or done ack
+ * (which = 1) arrives from the device through mapped memory; returns the
+ * host steady-clock time it was seen. */
+apk_status apk_wait_ack(apk_ctx* ctx, int event, int which, long long timeout_ns,
+                        long long* host_seen_ns);
+
+/* Stop sentinel -1 (src/yield.cu:857-858). */
+apk_status apk_stop(apk_ctx* ctx);
+
+/* Wait for the launch to end (src/yield.cu:859) with a deadline:
+ * APK_ETIMEDOUT if it is still running, APK_EDEVICE if the kernel
+ * reported an error. */
+apk_status apk_wait(apk_ctx* ctx, long long timeout_ns);
+
+/* Copy the background C to host memory (src/persistent.cu:216-219). */
+apk_status apk_read_output(apk_ctx* ctx, void* C_host);
+
+/* Copy event e's urgent output (M_u x N_u fp32) to host memory. */
+apk_status apk_read_urgent_output(apk_ctx* ctx, int event, float* Cu_host);
+
+/* Per-event log (src/yield.cu:862-878).  Every pointer may be NULL; each
+ * non-NULL array holds max_events entries (obs_ns: max_events * grid). */
+typedef struct apk_event_log {
+  int n_injected;           /* host-set events injected in the last launch    */
+  int n_fired;              /* device-set events fired in the last launch     */
+  int grid;
+  long long* set_ns;        /* globaltimer at the device setter's store       */
+  long long* host_set_ns;   /* host steady clock at the host store            */
+  long long* host_ack_ns;   /* host steady clock when the claim ack was seen  */
+  long long* host_done_ns;  /* host steady clock when the done ack was seen   */
+  long long* claim_ns;      /* globaltimer of the first successful pop        */
+  long long* done_ns;       /* globaltimer of the last finished urgent item   */
+  int* claimer;             /* CTA index + 1 of the first popper (0 = none)   */
+  int* claim_site;          /* stage index of the claim; -1 = tile boundary   */
+  int* inflight;            /* TMA stages in flight at the claimer's yield    */
+  long long* obs_ns;        /* [event * grid + cta] observation time, 0=never */
+} apk_event_log;
+apk_status apk_read_events(apk_ctx* ctx, apk_event_log* log);
+
+/* Exactly-once scheduler verdict inputs (src/yield.cu:576-667).
+ * exec_counts: one int per background task id of the last bounded launch
+ * (requires cfg.oracle); uexec_counts: max_events ints. */
+apk_status apk_read_oracle(apk_ctx* ctx, int* exec_counts, int* uexec_counts);
+
+typedef struct apk_run_stats {
+  long long start_ns, end_ns;        /* first CTA start / last CTA exit       */
+  unsigned long long tiles_done;     /* completed background tiles            */
+  unsigned long long yields;         /* checkpoints (accumulator spills)      */
+  double bg_flops;                   /* tiles_done * 2 * tile_m * tile_n * K  */
+  double bg_tflops;                  /* bg_flops / (end - start)              */
+  int exited;                        /* CTAs that exited                      */
+  int device_status;                 /* 0 or the first device error code      */
+  double launch_ms;                  /* CUDA events around the launch, on the
+                                        stream that ran it                    */
+} apk_run_stats;
+apk_status apk_read_run_stats(apk_ctx* ctx, apk_run_stats* st);
+
+/* One synchronous GEMM through the persistent kernel: upload (host
+ * buffers), drain every tile once, download.  Replaces one pass of
+ * src/persistent.cu:155-172. */
+apk_status apk_gemm(apk_ctx* ctx, const void* A, const void* B, void* C, int M, int N, int K,
+                    apk_mem_kind kind);
+
+/* ---- harness modes (the reference binaries' --mode switches) ---------- */
+
+typedef struct apk_latency_config {
+  int events;               /* injections                                    */
+  long long period_ns;      /* one injection per period at a uniform offset  */
+  unsigned seed;
+  int warmup_events;        /* discarded (src/yield.cu:340,915)              */
+  long long settle_ns;      /* background time before the first injection    */
+} apk_latency_config;
+
+typedef struct apk_latency_result {
+  int n;                    /* events counted                                */
+  int anomalies;            /* events some CTA never observed                */
+  int unclaimed;
+  double claim_p50_us, claim_p99_us;        /* set -> urgent work claimed    */
+  double last_obs_p50_us, last_obs_p99_us;  /* set -> last CTA observed      */
+  double done_p50_us, done_p99_us;          /* set -> urgent work finished   */
+  double rt_claim_p50_us, rt_claim_p99_us;  /* host set -> host sees claim   */
+  double rt_done_p50_us, rt_done_p99_us;    /* host set -> host sees done    */
+  double bg_tflops;         /* background throughput during the run          */
+  double vis_offset_ns;     /* host->globaltimer offset used (host-set)      */
+} apk_latency_result;
+
+/* Latency mode (src/yield.cu:776-958): unbounded background launch,
+ * injections, stop, per-event latencies with nearest-rank percentiles.
+ * For host-set modes "set" is the host store mapped to globaltimer with the
+ * visibility calibration of src/yield.cu:782-813; rt_* need no mapping. */
+apk_status apk_run_latency(apk_ctx* ctx, const apk_latency_config* lc, apk_latency_result* out);
+
+/* Host->device flag visibility calibration (src/yield.cu:782-813):
+ * offsets (globaltimer at first device observation - host store time),
+ * reps entries.  Needs an idle device. */
+apk_status apk_probe_visibility(apk_ctx* ctx, int reps, long long* offsets_ns);
+
+/* Failure-path self-test: launches the bounded flag spin of
+ * apk_probe_visibility on a flag nothing sets, with the given limit.  The
+ * kernel must give up, report DEV_WAIT_TIMEOUT_SPIN (3) through its status
+ * word and exit; *device_status receives the code.  Returns APK_OK when the
+ * spin ended and reported, leaving the context usable.  Replaces the
+ * reference's unbounded spin_flag (src/yield.cu:208-214), which would hang
+ * on a lost store. */
+apk_status apk_selftest_wait_timeout(apk_ctx* ctx, long long limit_ns, int* device_status);
+
+/* Overhead mode (src/yield.cu:670-711): ABAB-interleaved drains of
+ * num_tasks tasks with polling as configured vs polling off, warmup pairs
+ * discarded; median ms of each and the ratio. */
+apk_status apk_run_overhead(apk_ctx* ctx, unsigned long long num_tasks, int reps, double* ms_poll,
+                            double* ms_nopoll);
+
+/* No-preemption baseline (src/urgent_baseline.cu:144-343, mode sat):
+ * background drain of num_tasks with polling off; the urgent GEMM is a
+ * separate kernel on a max-priority stream launched at U(0.2,0.8) of the
+ * drain.  Per trial: host arrival -> urgent done (host clock, us). */
+apk_status apk_run_baseline(apk_ctx* ctx, unsigned long long num_tasks, int trials, unsigned seed,
+                            double* e2e_us);
+
+/* ---- data and memory helpers ----------------------------------------- */
+
+/* The reference's generator: srand(seed), then A (nA values) and B (nB
+ * values) as (float)(rand()/(double)RAND_MAX*2-1), src/persistent.cu:132-135,
+ * restated from glibc's published TYPE_3 additive-feedback algorithm. */
+void apk_fill_uniform(unsigned seed, float* A, size_t nA, float* B, size_t nB);
+
+/* Seeded N(0,1) rounded to bf16 (RNE); counter-based, multi-threaded. */
+void apk_fill_normal_bf16(unsigned long long seed, uint16_t* out, size_t n);
+
+/* fp32 -> bf16 round-to-nearest-even. */
+void apk_round_bf16(const float* in, uint16_t* out, size_t n);
+
+/* Pinned host memory for APK_MEM_HOST buffers (fast copies). */
+void* apk_host_alloc(size_t bytes);
+void apk_host_free(void* p);
+
+int apk_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* APK_H_ */
