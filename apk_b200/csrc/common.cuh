@@ -49,6 +49,14 @@ __device__ __forceinline__ void flag_store(int* f, int v) {
   asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
 }
 
+// Acknowledge to the host through mapped pinned memory: the store is
+// followed by a system-scope fence so it is pushed out to host memory now
+// rather than whenever the write path drains.
+__device__ __forceinline__ void ack_host(int* p) {
+  flag_store(p, 1);
+  __threadfence_system();
+}
+
 __device__ __forceinline__ void store_sys_ll(long long* p, long long v) {
   asm volatile("st.relaxed.sys.global.s64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }

@@ -260,10 +260,10 @@ void apk_config_default(apk_config* c) {
   c->k_tile = 32;
   c->poll = APK_POLL_STAGE;
   c->discipline = APK_DISC_DRAIN;
-  c->set_mode = APK_SET_HOST_MAPPED;
+  c->set_mode = APK_SET_HOST_MEMCPY;
   c->max_events = 4096;
   c->oracle = 0;
-  c->urgent_split_k = 4;
+  c->urgent_split_k = 8;
   c->wait_limit_ns = 2000000000LL;
 }
 

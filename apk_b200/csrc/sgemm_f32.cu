@@ -60,10 +60,15 @@ struct Cfg {
 // A is read two k at a time (float2 per row) and B one k at a time (two
 // float4): 12 shared loads per 128 FFMA, 96 live registers for operands and
 // accumulators, which leaves headroom under the 128-register cap.
+// poll: when non-null (tid 0 of a background stage), the yield flag is
+// loaded into pend two k-pairs before the end of the stage, so the value the
+// next stage barrier publishes is a fraction of a stage old while the load
+// latency still hides under the remaining FMAs.
 template <int BK>
 __device__ __forceinline__ void compute_stage(const float* __restrict__ As,
                                               const float* __restrict__ Bs, float (&acc)[8][8],
-                                              int arow0, int ty, int bcol) {
+                                              int arow0, int ty, int bcol, const int* poll,
+                                              int& pend) {
 #pragma unroll
   for (int sub = 0; sub < BK / 32; ++sub) {
     const float* Asub = As + sub * (BM * 32);
@@ -71,6 +76,7 @@ __device__ __forceinline__ void compute_stage(const float* __restrict__ As,
     // 128-register cap of 2 CTAs/SM spills (unconstrained it takes 167)
 #pragma unroll 1
     for (int kp = 0; kp < 16; ++kp) {
+      if (poll != nullptr && sub == BK / 32 - 1 && kp == 14) pend = flag_load(poll);
       const int kc = kp >> 1, half = kp & 1;
       float2 a[8];
 #pragma unroll
@@ -123,7 +129,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
   // lives in shared memory: as per-thread locals it costs every thread
   // registers under the 2-CTA/SM cap (the reference hit the same,
   // src/yield.cu:106-110).
-  __shared__ int s_lastSeen, s_pend, s_nextEv, s_site, s_inflight;
+  __shared__ int s_lastSeen, s_nextEv, s_site, s_inflight;
   __shared__ long long s_gBase;
   __shared__ unsigned long long s_myTiles, s_bgTask;
   __shared__ int s_bgRow0, s_bgCol0, s_bgC, s_pending;
@@ -141,7 +147,6 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
     for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
     fence_mbar_init();
     s_lastSeen = 0;
-    s_pend = 0;
     s_nextEv = 0;
     s_gBase = 0;
     s_myTiles = 0;
@@ -156,6 +161,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
 
   uint32_t P = 0, Q = 0;  // issued / consumed stage sequence numbers (uniform)
   bool bad = false;       // this thread saw a wait time out
+  int pend = 0;           // tid 0: last flag value loaded inside a stage
   float acc[8][8];
 
   // Job state (uniform).  A job is a background tile or one urgent item;
@@ -234,7 +240,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
           p.ev.claim[popE] = cta + 1;
           p.ev.claim_site[popE] = s_site;
           p.ev.inflight[popE] = s_inflight;
-          if (p.ev.ack != nullptr) flag_store(&p.ev.ack[2 * popE], 1);
+          if (p.ev.ack != nullptr) ack_host(&p.ev.ack[2 * popE]);
         }
         s_item = it;
       }
@@ -363,8 +369,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
     for (; c < nk; ++c) {
       bool ys = false;
       if (POLL == POLL_STAGE && !urgent && tid == 0) {
-        const int fs = s_pend;  // loaded one stage ago: the latency hides under compute
-        s_pend = flag_load(p.ev.flag);
+        const int fs = pend;  // loaded near the end of the previous stage
         setter();
         s_f = fs;
         ys = fs != s_lastSeen;
@@ -393,7 +398,8 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
         }
         __syncthreads();
       }
-      compute_stage<BK>(As, Bs, acc, arow0, ty, bcol);
+      const int* poll = (POLL == POLL_STAGE && !urgent && tid == 0) ? p.ev.flag : nullptr;
+      compute_stage<BK>(As, Bs, acc, arow0, ty, bcol, poll, pend);
       ++Q;
     }
     if (yielded) {
@@ -437,7 +443,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
         if (ORACLE) atomicAdd(&p.ev.uexec[ev], 1);
         __threadfence();
         const int done = atomicAdd(&p.ev.udone_cnt[ev], 1) + 1;
-        if (done == p.uitems && p.ev.ack != nullptr) flag_store(&p.ev.ack[2 * ev + 1], 1);
+        if (done == p.uitems && p.ev.ack != nullptr) ack_host(&p.ev.ack[2 * ev + 1]);
       }
       urgent = false;
     }

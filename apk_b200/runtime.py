@@ -74,8 +74,8 @@ class Context:
 
     def __init__(self, device: int = 0, dtype: str = "f32", ctas_per_sm: int = 0, grid: int = 0,
                  k_tile: int = 32, poll: str = "stage", discipline: str = "drain",
-                 set_mode: str = "host_mapped", max_events: int = 4096, oracle: bool = False,
-                 urgent_split_k: int = 4, wait_limit_ns: int = 2_000_000_000):
+                 set_mode: str = "host_memcpy", max_events: int = 4096, oracle: bool = False,
+                 urgent_split_k: int = 8, wait_limit_ns: int = 2_000_000_000):
         self._lib = L.load()
         cfg = L.Config()
         self._lib.apk_config_default(ctypes.byref(cfg))

@@ -9,7 +9,8 @@ synthetic, no dataset involved.
 
 A step is one launch of the persistent kernel: it drains background tiles
 (task t computes tile t mod 1024) while `--events-per-step` urgent GEMMs are
-injected through mapped host memory, then the host stops it.  value = the
+injected by the host (flag stored with cudaMemcpyAsync on a high-priority
+control stream), then the host stops it.  value = the
 background GEMM's TFLOP/s over the timed steps (FLOPs of completed tiles /
 CUDA-event time of the launches, summed over ranks and divided by the max
 over ranks); the urgent preemption latencies of all timed events are
@@ -235,7 +236,7 @@ def run_ours(args, world, rank, local):
     dev = local
     A, B = apk_b200.fill_uniform(M, N, K, 21)
     Au, Bu = apk_b200.fill_uniform(U, U, U, 99)
-    ctx = apk_b200.Context(device=dev, poll="stage", set_mode="host_mapped",
+    ctx = apk_b200.Context(device=dev, poll="stage", set_mode="host_memcpy",
                            max_events=max(args.events_per_step, 16))
     info = ctx.info
     ctx.set_background(A, B)
@@ -359,12 +360,12 @@ def run_ours(args, world, rank, local):
         "warmup": args.warmup, "ms_per_step": tmax * 1e3 / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "configs[1]: persistent fp32 SGEMM 4096^3 background, 128x128 tiles, K-tile 32, "
-                               "full residency; urgent fp32 256^3 injected by the host (mapped flag) at a "
+                               "full residency; urgent fp32 256^3 injected by the host (flag via cudaMemcpyAsync) at a "
                                "uniform time in every 1 ms period",
                    "M": M, "N": N, "K": K, "urgent": [U, U, U], "events_per_step": args.events_per_step,
                    "period_us": args.period_us, "grid": allr[0]["info"]["grid"],
-                   "ctas_per_sm": allr[0]["info"]["ctas_per_sm"], "poll": "stage", "set": "host_mapped",
-                   "urgent_split_k": 4, "l2": "inputs larger than L2: A+B+C = 192 MB > 126 MB",
+                   "ctas_per_sm": allr[0]["info"]["ctas_per_sm"], "poll": "stage", "set": "host_memcpy",
+                   "urgent_split_k": 8, "l2": "inputs larger than L2: A+B+C = 192 MB > 126 MB",
                    "parallelism": f"{world} independent replicas (no collectives)"},
         "latency_us": {
             "events": len(L["claim"]) + unclaimed, "unclaimed": unclaimed, "anomalies": anomalies,

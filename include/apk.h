@@ -56,10 +56,13 @@ typedef enum apk_poll_mode {
 typedef enum apk_discipline { APK_DISC_DRAIN = 0, APK_DISC_POISON = 2 } apk_discipline;
 
 /* Who sets the yield flag.  DEVICE: CTA 0 at scheduled globaltimer offsets
- * (src/yield.cu:186-195, the reference's primary instrument).  HOST_MAPPED:
- * the host stores the generation into mapped pinned memory the CTAs poll.
- * HOST_MEMCPY: the host copies it into device memory with cudaMemcpyAsync
- * on a control stream (src/yield.cu:851-852). */
+ * (src/yield.cu:186-195, the reference's primary instrument).  HOST_MEMCPY
+ * (default host path): the host copies the generation into device memory
+ * with cudaMemcpyAsync on a high-priority control stream
+ * (src/yield.cu:851-852).  HOST_MAPPED: the host stores it into mapped
+ * pinned memory that every CTA polls across PCIe -- kept for measurement
+ * only: with one poll per stage per CTA it costs most of the background
+ * throughput. */
 typedef enum apk_set_mode {
   APK_SET_DEVICE = 0,
   APK_SET_HOST_MAPPED = 1,
@@ -84,7 +87,8 @@ typedef struct apk_config {
 } apk_config;
 
 /* Fill *cfg with the defaults (fp32, full residency, k_tile 32, stage
- * polling, drain, host-mapped flag, 4096 events, split-K 4, 2 s waits). */
+ * polling, drain, host-set flag through cudaMemcpyAsync, 4096
+ * events, urgent split-K 8, 2 s waits). */
 void apk_config_default(apk_config* cfg);
 
 typedef struct apk_ctx apk_ctx;

@@ -42,8 +42,8 @@ def test_config_defaults(libapk):
     c = _lib.Config()
     libapk.apk_config_default(ctypes.byref(c))
     assert (c.dtype, c.k_tile, c.poll, c.discipline, c.set_mode) == (
-        _lib.APK_F32, 32, _lib.APK_POLL_STAGE, _lib.APK_DISC_DRAIN, _lib.APK_SET_HOST_MAPPED)
-    assert c.max_events == 4096 and c.urgent_split_k == 4 and c.wait_limit_ns == 2_000_000_000
+        _lib.APK_F32, 32, _lib.APK_POLL_STAGE, _lib.APK_DISC_DRAIN, _lib.APK_SET_HOST_MEMCPY)
+    assert c.max_events == 4096 and c.urgent_split_k == 8 and c.wait_limit_ns == 2_000_000_000
 
 
 @pytest.mark.parametrize("seed,shape", [(21, (1024, 1024, 1024)), (0, (128, 256, 64)), (7, (256, 128, 512))])

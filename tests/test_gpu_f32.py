@@ -141,6 +141,8 @@ def test_poison_discipline_is_detected(libapk):
 
 
 def test_host_mapped_injection_and_acks(libapk):
+    """The mapped-memory host path (slow by design: every CTA polls across
+    PCIe) still claims and completes every event correctly."""
     A, B = oracle.gen_uniform(1024, 1024, 1024, 21)
     Au, Bu, refu = _urgent_ref()
     with _ctx(poll="stage", set_mode="host_mapped", max_events=64) as c:
@@ -239,10 +241,10 @@ def test_latency_mode_smoke(libapk):
     claimed, none missed by any CTA."""
     A, B = oracle.gen_uniform(4096, 4096, 4096, 21)
     Au, Bu, _ = _urgent_ref()
-    with _ctx(poll="stage", set_mode="host_mapped", max_events=256) as c:
+    with _ctx(poll="stage", set_mode="host_memcpy", max_events=256) as c:
         c.set_background(A, B)
         c.set_urgent(Au, Bu)
         r = c.run_latency(events=100, period_us=1000, seed=21, warmup_events=10)
-    assert r["n"] == 90 and r["unclaimed"] == 0
-    assert r["rt_claim_p50_us"] < 200
+    assert r["n"] == 90 and r["unclaimed"] == 0 and r["anomalies"] == 0
+    assert r["rt_claim_p50_us"] < 60
     assert r["bg_tflops"] > 1.0
