@@ -916,7 +916,7 @@ apk_status apk_probe_visibility(apk_ctx* ctx, int reps, long long* offsets_ns) {
     *reinterpret_cast<volatile int*>(ctx->h_flag) = 0;
     std::atomic_thread_fence(std::memory_order_seq_cst);
     const int* flag = ctx->cfg.set_mode == APK_SET_HOST_MAPPED ? ctx->d_flag_mapped : &ctx->d_ctrl->flag_dev;
-    spin_flag_kernel<<<1, 32, 0, ctx->kstream>>>(flag, 1, 200000000LL, d_out, &ctx->d_ctrl->status);
+    spin_flag_kernel<<<1, 32, 0, ctx->kstream>>>(flag, 1, 50000000LL, d_out, &ctx->d_ctrl->status);
     spin_until_ns(host_now_ns() + 200000);  // let the spin kernel start
     long long t;
     if (ctx->cfg.set_mode == APK_SET_HOST_MAPPED) {
@@ -936,7 +936,14 @@ apk_status apk_probe_visibility(apk_ctx* ctx, int reps, long long* offsets_ns) {
   }
   *reinterpret_cast<volatile int*>(ctx->h_flag) = 0;
   cudaFree(d_out);
-  return read_status(ctx);
+  // A rep whose spin gave up (the store never became visible within the
+  // bound, e.g. when a tool serialises launches) reads 0 and is skipped by
+  // callers; it is not an error of the runtime.
+  Ctrl cb;
+  APK_CU(cudaMemcpy(&cb, ctx->d_ctrl, sizeof cb, cudaMemcpyDeviceToHost));
+  if (cb.status != 0 && cb.status != DEV_WAIT_TIMEOUT_SPIN)
+    return fail(ctx, APK_EDEVICE, "device reported status %d", cb.status);
+  return APK_OK;
 }
 
 apk_status apk_selftest_wait_timeout(apk_ctx* ctx, long long limit_ns, int* device_status) {
@@ -982,18 +989,28 @@ apk_status apk_run_latency(apk_ctx* ctx, const apk_latency_config* lc, apk_laten
   if (host_set) {
     std::vector<long long> offs(64);
     if ((s = apk_probe_visibility(ctx, 64, offs.data())) != APK_OK) return s;
-    std::vector<double> o(offs.begin(), offs.end());
-    offset = pct(o, 0.5);
+    std::vector<double> o;
+    for (long long v : offs)
+      if (v != 0) o.push_back((double)v);
+    offset = o.empty() ? NAN : pct(o, 0.5);
     if ((s = apk_schedule_device_events(ctx, nullptr, 0)) != APK_OK) return s;
   } else {
     if ((s = apk_schedule_device_events(ctx, when.data(), E)) != APK_OK) return s;
   }
   out->vis_offset_ns = offset;
-  if ((s = apk_launch(ctx, APK_TASKS_UNBOUNDED)) != APK_OK) return s;
+  // Bounded launches (bg_tasks > 0) end by themselves: the host injects
+  // while the kernel runs and stops injecting once it has ended, so the run
+  // needs no host action to terminate (safe under tools that serialise
+  // launches).  Unbounded launches end with the stop sentinel.
+  const bool bounded = lc->bg_tasks > 0;
+  if ((s = apk_launch(ctx, bounded ? lc->bg_tasks : APK_TASKS_UNBOUNDED)) != APK_OK) return s;
   const long long t0 = host_now_ns();
+  auto ended = [&]() { return bounded && cudaEventQuery(ctx->ev_done) == cudaSuccess; };
   if (host_set) {
     for (int e = 0; e < E; ++e) {
-      spin_until_ns(t0 + when[e]);
+      while (host_now_ns() < t0 + when[e] && !ended()) {
+      }
+      if (ended()) break;
       int ev;
       long long ts;
       if ((s = apk_inject_urgent(ctx, &ev, &ts)) != APK_OK) break;
@@ -1002,9 +1019,11 @@ apk_status apk_run_latency(apk_ctx* ctx, const apk_latency_config* lc, apk_laten
       apk_wait_ack(ctx, ev, 1, lc->period_ns / 2, &seen);
     }
   } else {
-    spin_until_ns(t0 + when[E - 1] + 20000000LL);
+    const long long until = t0 + when[E - 1] + 20000000LL;
+    while (host_now_ns() < until && !ended()) {
+    }
   }
-  apk_status st_stop = apk_stop(ctx);
+  apk_status st_stop = bounded ? APK_OK : apk_stop(ctx);
   apk_status st_wait = apk_wait(ctx, 30000000000LL);
   if (s != APK_OK) return s;
   if (st_stop != APK_OK) return st_stop;

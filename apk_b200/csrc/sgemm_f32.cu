@@ -64,6 +64,32 @@ struct Cfg {
 // loaded into pend two k-pairs before the end of the stage, so the value the
 // next stage barrier publishes is a fraction of a stage old while the load
 // latency still hides under the remaining FMAs.
+// Two k (one k-pair kp) of one 32-deep sub-tile.
+__device__ __forceinline__ void kpair(const float* __restrict__ Asub, const float* __restrict__ Bsub,
+                                      float (&acc)[8][8], int arow0, int ty, int bcol, int kp) {
+  const int kc = kp >> 1, half = kp & 1;
+  float2 a[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    // row r = arow0 + 4i; (r & 7) == ty + 4*(i&1) because arow0 = 32*wm + ty
+    const int sw = kc ^ (ty + 4 * (i & 1));
+    a[i] = *reinterpret_cast<const float2*>(Asub + (arow0 + 4 * i) * 32 + (sw << 2) + 2 * half);
+  }
+#pragma unroll
+  for (int kk = 0; kk < 2; ++kk) {
+    const float* brow = Bsub + (kp * 2 + kk) * BN + bcol;
+    const float4 b0 = *reinterpret_cast<const float4*>(brow);
+    const float4 b1 = *reinterpret_cast<const float4*>(brow + 32);
+    const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float av = kk == 0 ? a[i].x : a[i].y;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av, bv[j], acc[i][j]);
+    }
+  }
+}
+
 template <int BK>
 __device__ __forceinline__ void compute_stage(const float* __restrict__ As,
                                               const float* __restrict__ Bs, float (&acc)[8][8],
@@ -72,33 +98,15 @@ __device__ __forceinline__ void compute_stage(const float* __restrict__ As,
 #pragma unroll
   for (int sub = 0; sub < BK / 32; ++sub) {
     const float* Asub = As + sub * (BM * 32);
+    const float* Bsub = Bs + sub * 32 * BN;
     // not unrolled: any unroll lets the scheduler hoist loads until the
     // 128-register cap of 2 CTAs/SM spills (unconstrained it takes 167)
 #pragma unroll 1
-    for (int kp = 0; kp < 16; ++kp) {
-      if (poll != nullptr && sub == BK / 32 - 1 && kp == 14) pend = flag_load(poll);
-      const int kc = kp >> 1, half = kp & 1;
-      float2 a[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        // row r = arow0 + 4i; (r & 7) == ty + 4*(i&1) because arow0 = 32*wm + ty
-        const int sw = kc ^ (ty + 4 * (i & 1));
-        a[i] = *reinterpret_cast<const float2*>(Asub + (arow0 + 4 * i) * 32 + (sw << 2) + 2 * half);
-      }
-#pragma unroll
-      for (int kk = 0; kk < 2; ++kk) {
-        const float* brow = Bs + (sub * 32 + kp * 2 + kk) * BN + bcol;
-        const float4 b0 = *reinterpret_cast<const float4*>(brow);
-        const float4 b1 = *reinterpret_cast<const float4*>(brow + 32);
-        const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float av = kk == 0 ? a[i].x : a[i].y;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av, bv[j], acc[i][j]);
-        }
-      }
-    }
+    for (int kp = 0; kp < 14; ++kp) kpair(Asub, Bsub, acc, arow0, ty, bcol, kp);
+    // the poll sits between two loops, not behind a per-iteration branch
+    if (sub == BK / 32 - 1 && poll != nullptr) pend = flag_load(poll);
+#pragma unroll 1
+    for (int kp = 14; kp < 16; ++kp) kpair(Asub, Bsub, acc, arow0, ty, bcol, kp);
   }
 }
 

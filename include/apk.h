@@ -221,6 +221,10 @@ typedef struct apk_latency_config {
   unsigned seed;
   int warmup_events;        /* discarded (src/yield.cu:340,915)              */
   long long settle_ns;      /* background time before the first injection    */
+  unsigned long long bg_tasks; /* 0: run until stopped after the last event;
+                                  else a bounded launch of that many tasks
+                                  that ends by itself (injection stops when
+                                  it ends)                                    */
 } apk_latency_config;
 
 typedef struct apk_latency_result {
