@@ -1,24 +1,520 @@
-// bf16 tcgen05 persistent GEMM -- placeholder until the tensor-core kernel
-// lands; every entry reports "unsupported" so the runtime fails loudly.
+// bf16 tensor-core persistent GEMM (tcgen05 + TMEM + TMA) with tile-boundary
+// and per-stage yield and an accumulator checkpoint in TMEM -> slab.
+//
+// Replaces the reference's wmma pipeline persistent_tc (src/tcyield.cu:91-356:
+// 128x128 tile, 3-stage cp.async, wmma fragments, 8 warps that all compute
+// and all take every checkpoint barrier) with a Blackwell design:
+//
+//   * tile 256x128 (two M=128 tcgen05.mma accumulators, N=128), K-tile 64,
+//     4-stage TMA ring (48 KB per stage: A as two [128 rows][64 k] boxes and
+//     B as two [64 k][64 n] boxes, all 128-byte swizzled; B is consumed
+//     MN-major straight from the row-major [K][N] operand, no transpose).
+//   * fp32 accumulators in TMEM, double-buffered (2 x 256 of the 512
+//     columns) so the epilogue of one job overlaps the MMAs of the next.
+//   * warp roles: 0 producer (queue pops, TMA, urgent mini-queue pops),
+//     1 MMA issuer (one thread issues tcgen05.mma / commit), 2-5 epilogue
+//     (tcgen05.ld -> global; each warp owns one 32-lane TMEM quadrant),
+//     6 control (polls the yield flag, runs the device setter).  No
+//     block-wide barrier per stage: the reference's per-stage checkpoint
+//     barrier pair at 1 CTA/SM cost 14% (results/summary/tc_summary.csv:8-10).
+//   * yield / checkpoint: the producer sees a new generation at a stage
+//     boundary c (from the control warp), pops urgent work items
+//     (src/yield.cu:163-183 mini-queue); if the background tile already has
+//     c > 0 stages in the ring it first emits a SUSPEND control slot.  The
+//     MMA warp consumes the in-flight stages in order (the "drain": TMA
+//     stages are never cancelled), then on SUSPEND commits the accumulator
+//     and the epilogue spills it with tcgen05.ld to the checkpoint slab.  The
+//     urgent items flow through the same ring into the other TMEM buffer.
+//     The background stage c is re-issued with a RESUME tag: the epilogue
+//     restores the slab into a TMEM buffer with tcgen05.st and the MMAs
+//     continue with accumulate=1 -- the same MMA sequence as an
+//     uninterrupted run, so the resumed tile is bitwise identical.
+//   * every mbarrier wait is bounded; a timeout raises a CTA abort flag and
+//     the device status word, every role unwinds, outstanding MMAs and TMA
+//     loads are waited for (bounded) and TMEM is freed before exit.
 #include <string>
+
 #include "../../include/apk.h"
+#include "common.cuh"
 #include "proto.h"
+#include "tcgen05.cuh"
 
 namespace apk {
 namespace bf16 {
-cudaError_t prepare(int, int, bool, int* max_ctas_per_sm) {
-  *max_ctas_per_sm = 0;
-  return cudaErrorNotSupported;
+
+constexpr int BM = 256, BN = 128, BK = 64, S = 4;
+constexpr int A_HALF = 128 * BK * 2;             // 16 KB: one [128][64] bf16 box
+constexpr int A_BYTES = 2 * A_HALF;              // 32 KB
+constexpr int B_CHUNK = BK * 64 * 2;             // 8 KB: one [64 k][64 n] box
+constexpr int B_BYTES = 2 * B_CHUNK;             // 16 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 48 KB
+constexpr int NT = 224;                          // 7 warps
+constexpr int SMEM_BYTES = S * STAGE_BYTES + 1024;
+constexpr int RING = 8;                          // epilogue job ring
+constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, 128, /*B MN-major*/ true);
+
+enum : int { T_BG = 1, T_URG = 2, T_SUSPEND = 3, T_STOP = 4 };
+enum : int { F_FIRST = 1, F_LAST = 2, F_RESUME = 4 };
+enum : int { E_STORE_C = 1, E_STORE_U = 2, E_SPILL = 3, E_RESTORE = 4, E_EXIT = 5 };
+
+struct StageTag {
+  int kind, flags, row0, col0, e, item;
+  unsigned long long task;
+};
+struct EpiJob {
+  int action, buf, row0, col0, e, item;
+  unsigned long long task;
+};
+
+struct __align__(16) Shared {
+  StageTag tag[S];
+  EpiJob epi[RING];
+  uint64_t full[S], empty[S];
+  uint64_t tfull[2], tempty[2], tres[2];
+  uint64_t efull[RING], eempty[RING];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;      // CTA-local: some role's bounded wait gave up
+  int gen;        // latest yield-flag value seen by the control warp (-1 stop)
+  int prod_done;  // producer finished: the control warp may exit
+  int consumed;   // stages consumed by the MMA warp (for the in-flight log)
+  int epi_cnt[RING];
+  unsigned long long tiles;
+};
+
+__device__ __forceinline__ int vload(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+__device__ __forceinline__ void vstore(int* p, int v) { *reinterpret_cast<volatile int*>(p) = v; }
+
+// Bounded mbarrier wait that also gives up when another role aborted.
+__device__ __noinline__ bool bwait(uint64_t* bar, uint32_t parity, const F32Params& p, Shared& sh) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = globaltimer_ns();
+  int n = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (++n == 64) {
+      n = 0;
+      if (vload(&sh.abort)) return false;
+      if (globaltimer_ns() - t0 > p.wait_limit_ns) {
+        vstore(&sh.abort, 1);
+        report_status(p.ev.status, DEV_WAIT_TIMEOUT_FULL, p.ev.abort_word);
+        return false;
+      }
+    }
+  }
 }
-cudaError_t launch(const void*, int, int, int, bool, cudaStream_t) { return cudaErrorNotSupported; }
-int smem_bytes() { return 0; }
-int threads() { return 0; }
-size_t params_size() { return 0; }
-apk_status build_params(void*, const void*, const void*, void*, int, int, int, const void*, const void*,
-                        float*, int, int, int, int, size_t, const EventProto&, const QueueProto&, long long,
-                        int, std::string* err) {
-  *err = "bf16 path not built";
-  return APK_EUNSUPPORTED;
+
+// Wait without the abort shortcut (used while unwinding: outstanding async
+// work must complete before smem / TMEM are released).
+__device__ __noinline__ void bwait_unwind(uint64_t* bar, uint32_t parity, long long limit) {
+  const long long t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer_ns() - t0 > limit) return;
 }
+
+template <int POLL, int DISC, bool ORACLE>
+__global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_constant__ F32Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ Shared sh;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int cta = blockIdx.x;
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sh.tfull[b], 1);
+      mbar_init(&sh.tempty[b], 4);
+      mbar_init(&sh.tres[b], 4);
+    }
+    for (int r = 0; r < RING; ++r) {
+      mbar_init(&sh.efull[r], 1);
+      mbar_init(&sh.eempty[r], 4);
+      sh.epi_cnt[r] = 0;
+    }
+    mbar_init(&sh.drain, 1);
+    fence_mbar_init();
+    sh.abort = 0;
+    sh.gen = 0;
+    sh.prod_done = 0;
+    sh.consumed = 0;
+    sh.tiles = 0;
+    tma_prefetch_desc(&p.tmA);
+    tma_prefetch_desc(&p.tmB);
+    tma_prefetch_desc(&p.tmAu);
+    tma_prefetch_desc(&p.tmBu);
+    atomicMin(p.q.start_min, (unsigned long long)globaltimer_ns());
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&sh.tmem_base, 512);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+
+  if (warp == 0 && lane == 0) {
+    // ================================ producer ================================
+    uint32_t P = 0;
+    int lastSeen = 0;
+    bool ok = true;
+    auto emit = [&](int kind, int flags, int row0, int col0, int e, int item, unsigned long long task,
+                    const CUtensorMap* tA, const CUtensorMap* tB, int k0) -> bool {
+      const int s = P % S;
+      if (!bwait(&sh.empty[s], ((P / S) & 1) ^ 1, p, sh)) return false;
+      StageTag& t = sh.tag[s];
+      t.kind = kind;
+      t.flags = flags;
+      t.row0 = row0;
+      t.col0 = col0;
+      t.e = e;
+      t.item = item;
+      t.task = task;
+      if (tA != nullptr) {
+        mbar_arrive_expect_tx(&sh.full[s], STAGE_BYTES);
+        uint8_t* st = stages + s * STAGE_BYTES;
+        tma_load_2d(st, tA, k0, row0, &sh.full[s]);
+        tma_load_2d(st + A_HALF, tA, k0, row0 + 128, &sh.full[s]);
+        tma_load_2d(st + A_BYTES, tB, col0, k0, &sh.full[s]);
+        tma_load_2d(st + A_BYTES + B_CHUNK, tB, col0 + 64, k0, &sh.full[s]);
+      } else {
+        mbar_arrive(&sh.full[s]);  // control slot: no data
+      }
+      ++P;
+      return true;
+    };
+    // Observe generation f at a poll site and pop urgent work items; a
+    // SUSPEND slot precedes the first item when the background tile has
+    // stages in the ring.  Returns items popped, or -1 when aborting.
+    auto handle = [&](int f, int site, bool partial) -> int {
+      const int fc = f < p.ev.max_events ? f : p.ev.max_events;
+      const long long g = globaltimer_ns();
+      for (int e = lastSeen; e < fc; ++e) p.ev.obs_ns[(size_t)e * gridDim.x + cta] = g;
+      const int old = lastSeen;
+      lastSeen = f;
+      int n = 0;
+      for (int e = old; e < fc; ++e) {
+        while (true) {
+          const int it = atomicAdd(&p.ev.uq_next[e], 1);
+          if (it >= p.uitems) break;
+          if (it == 0) {
+            p.ev.claim_ns[e] = globaltimer_ns();
+            p.ev.claim[e] = cta + 1;
+            p.ev.claim_site[e] = site;
+            p.ev.inflight[e] = (int)(P - (uint32_t)vload(&sh.consumed));
+            if (p.ev.ack != nullptr) ack_host(&p.ev.ack[2 * e]);
+          }
+          if (n == 0 && partial) {
+            if (!emit(T_SUSPEND, 0, 0, 0, 0, 0, 0, nullptr, nullptr, 0)) return -1;
+            atomicAdd(p.q.yields, 1ull);
+          }
+          ++n;
+          const int t = it / p.usplit, ks = it % p.usplit;
+          const int r0 = (t / p.utiles_n) * BM, c0 = (t % p.utiles_n) * BN;
+          for (int c = 0; c < p.unk; ++c)
+            if (!emit(T_URG, (c == 0 ? F_FIRST : 0) | (c == p.unk - 1 ? F_LAST : 0), r0, c0, e, it, 0, &p.tmAu,
+                      &p.tmBu, (ks * p.unk + c) * BK))
+              return -1;
+        }
+      }
+      return n;
+    };
+
+    while (ok) {
+      // ---- tile boundary: pop a background task (kept across a yield) ----
+      const unsigned long long task = atomicAdd(p.q.next_task, 1ull);
+      int f = vload(&sh.gen);
+      if (f < 0 || vload(&sh.abort)) break;
+      if (POLL != POLL_OFF && f != lastSeen)
+        if (handle(f, -1, false) < 0) {
+          ok = false;
+          break;
+        }
+      if (task >= p.q.num_tasks) break;
+      const int tile = (int)(task % (unsigned long long)p.total_tiles);
+      const int row0 = (tile / p.tiles_n) * BM, col0 = (tile % p.tiles_n) * BN;
+      bool resume = false;
+      for (int c = 0; c < p.nk && ok; ++c) {
+        if (POLL == POLL_STAGE) {
+          const int fs = vload(&sh.gen);
+          if (fs < 0) {
+            ok = false;  // stop sentinel: abandon the tile
+            break;
+          }
+          if (fs != lastSeen) {
+            const int n = handle(fs, c, c > 0);
+            if (n < 0) {
+              ok = false;
+              break;
+            }
+            if (n > 0 && c > 0) resume = true;
+          }
+        }
+        const int flags = (c == 0 ? F_FIRST : 0) | (c == p.nk - 1 ? F_LAST : 0) | (resume ? F_RESUME : 0);
+        resume = false;
+        if (!emit(T_BG, flags, row0, col0, 0, 0, task, &p.tmA, &p.tmB, c * BK)) ok = false;
+      }
+    }
+    emit(T_STOP, 0, 0, 0, 0, 0, 0, nullptr, nullptr, 0);
+    vstore(&sh.prod_done, 1);
+    // TMA loads still in flight (only when unwinding) must land before exit
+    for (uint32_t q = (uint32_t)vload(&sh.consumed); q < P; ++q)
+      bwait_unwind(&sh.full[q % S], (q / S) & 1, p.wait_limit_ns);
+  } else if (warp == 1 && lane == 0) {
+    // ================================== MMA ===================================
+    uint32_t Q = 0, X = 0, ub[2] = {0, 0}, rb[2] = {0, 0};
+    int nb = 0, cur = 0;
+    const uint32_t tbase = sh.tmem_base;
+    auto post = [&](int action, int buf, const StageTag& t) -> bool {
+      const int sl = X % RING;
+      if (!bwait(&sh.eempty[sl], ((X / RING) & 1) ^ 1, p, sh)) return false;
+      EpiJob& j = sh.epi[sl];
+      j.action = action;
+      j.buf = buf;
+      j.row0 = t.row0;
+      j.col0 = t.col0;
+      j.e = t.e;
+      j.item = t.item;
+      j.task = t.task;
+      mbar_arrive(&sh.efull[sl]);
+      ++X;
+      return true;
+    };
+    while (true) {
+      const int s = Q % S;
+      if (!bwait(&sh.full[s], (Q / S) & 1, p, sh)) break;
+      const StageTag t = sh.tag[s];
+      if (t.kind == T_STOP) {
+        post(E_EXIT, 0, t);
+        break;
+      }
+      if (t.kind == T_SUSPEND) {
+        if (!post(E_SPILL, cur, t)) break;
+        tc::commit(&sh.tfull[cur]);
+        mbar_arrive(&sh.empty[s]);
+        ++Q;
+        vstore(&sh.consumed, (int)Q);
+        continue;
+      }
+      if (t.flags & (F_FIRST | F_RESUME)) {
+        cur = nb;
+        nb ^= 1;
+        if (!bwait(&sh.tempty[cur], (ub[cur] & 1) ^ 1, p, sh)) break;
+        ++ub[cur];
+        tc::fence_after_sync();
+        if (t.flags & F_RESUME) {
+          if (!post(E_RESTORE, cur, t)) break;
+          if (!bwait(&sh.tres[cur], rb[cur] & 1, p, sh)) break;
+          ++rb[cur];
+          tc::fence_after_sync();
+        }
+      }
+      uint8_t* st = stages + s * STAGE_BYTES;
+      if (DISC == DISC_POISON && t.kind == T_URG && (t.flags & F_FIRST)) {
+        // detector control: one wrong staged B value (8.0) in each urgent item
+        reinterpret_cast<uint16_t*>(st + A_BYTES)[0] = 0x4100;
+        fence_proxy_async_smem();
+      }
+      const uint32_t a0 = smem_u32(st), b0 = smem_u32(st + A_BYTES);
+      const uint32_t d0 = tbase + (uint32_t)cur * 256;
+#pragma unroll
+      for (int kk = 0; kk < BK / 16; ++kk) {
+        const uint64_t bdesc = tc::smem_desc_sw128(b0 + kk * 2048, B_CHUNK, 1024);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint64_t adesc = tc::smem_desc_sw128(a0 + h * A_HALF + kk * 32, 16, 1024);
+          tc::mma_bf16(d0 + h * 128, adesc, bdesc, IDESC, (kk > 0 || !(t.flags & F_FIRST)) ? 1u : 0u);
+        }
+      }
+      tc::commit(&sh.empty[s]);  // frees the slot once these MMAs have read it
+      if (t.flags & F_LAST) {
+        if (!post(t.kind == T_BG ? E_STORE_C : E_STORE_U, cur, t)) break;
+        tc::commit(&sh.tfull[cur]);
+      }
+      ++Q;
+      vstore(&sh.consumed, (int)Q);
+    }
+    // no tcgen05.mma may still run when TMEM is released
+    tc::commit(&sh.drain);
+    bwait_unwind(&sh.drain, 0, p.wait_limit_ns);
+  } else if (warp >= 2 && warp <= 5) {
+    // ================================ epilogue ================================
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    uint32_t Y = 0, eb[2] = {0, 0};
+    const uint32_t tbase = sh.tmem_base;
+    float* slab = p.slab + (size_t)cta * (BM * BN);
+    while (true) {
+      const int sl = Y % RING;
+      if (!bwait(&sh.efull[sl], (Y / RING) & 1, p, sh)) break;
+      const EpiJob j = sh.epi[sl];
+      if (j.action == E_EXIT) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.eempty[sl]);
+        break;
+      }
+      const uint32_t tcol = tbase + ((uint32_t)(32 * q) << 16) + (uint32_t)j.buf * 256;
+      if (j.action == E_RESTORE) {
+#pragma unroll 1
+        for (int blk = 0; blk < 8; ++blk) {  // blk = h*4 + jj
+          const float4* s4 = reinterpret_cast<const float4*>(slab + (size_t)(blk * 4 + q) * 1024);
+          uint32_t v[32];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 x = s4[i * 32 + lane];
+            v[4 * i] = __float_as_uint(x.x);
+            v[4 * i + 1] = __float_as_uint(x.y);
+            v[4 * i + 2] = __float_as_uint(x.z);
+            v[4 * i + 3] = __float_as_uint(x.w);
+          }
+          tc::st_32x32b_x32(tcol + (blk >> 2) * 128 + (blk & 3) * 32, v);
+        }
+        tc::wait_st();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.tres[j.buf]);
+      } else {
+        if (!bwait(&sh.tfull[j.buf], eb[j.buf] & 1, p, sh)) break;
+        ++eb[j.buf];
+        tc::fence_after_sync();
+#pragma unroll 1
+        for (int blk = 0; blk < 8; ++blk) {
+          const int h = blk >> 2, jj = blk & 3;
+          uint32_t v[32];
+          tc::ld_32x32b_x32(tcol + h * 128 + jj * 32, v);
+          tc::wait_ld();
+          const int row = h * 128 + 32 * q + lane;
+          if (j.action == E_SPILL) {
+            float4* s4 = reinterpret_cast<float4*>(slab + (size_t)(blk * 4 + q) * 1024);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              s4[i * 32 + lane] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                              __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+          } else if (j.action == E_STORE_C) {
+            float4* d4 = reinterpret_cast<float4*>(p.C + (size_t)(j.row0 + row) * p.ldc + j.col0 + jj * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              d4[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                  __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+          } else {  // E_STORE_U
+            float* d = p.Cu + (size_t)j.e * p.cu_stride + (size_t)(j.row0 + row) * p.ldcu + j.col0 + jj * 32;
+            if (p.usplit == 1) {
+              float4* d4 = reinterpret_cast<float4*>(d);
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                d4[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                    __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) atomicAdd(d + i, __uint_as_float(v[i]));
+            }
+          }
+        }
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.tempty[j.buf]);
+        if (j.action != E_SPILL) {
+          // the last of the four epilogue warps to finish does the accounting
+          __threadfence();
+          __syncwarp();
+          if (lane == 0 && atomicAdd(&sh.epi_cnt[sl], 1) == 3) {
+            sh.epi_cnt[sl] = 0;
+            if (j.action == E_STORE_C) {
+              ++sh.tiles;
+              if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[j.task], 1);
+              count_trigger(p.ev);
+            } else {
+              if (ORACLE) atomicAdd(&p.ev.uexec[j.e], 1);
+              atomicMax(&p.ev.done_ns[j.e], (unsigned long long)globaltimer_ns());
+              const int done = atomicAdd(&p.ev.udone_cnt[j.e], 1) + 1;
+              if (done == p.uitems && p.ev.ack != nullptr) ack_host(&p.ev.ack[2 * j.e + 1]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.eempty[sl]);
+      ++Y;
+    }
+  } else if (warp == 6 && lane == 0) {
+    // ================================ control =================================
+    int nextEv = 0;
+    long long gBase = 0;
+    while (!vload(&sh.prod_done) && !vload(&sh.abort)) {
+      int f = POLL != POLL_OFF ? flag_load(p.ev.flag) : 0;
+      if (*reinterpret_cast<volatile int*>(p.ev.abort_word)) f = -1;
+      if (cta == 0 && p.ev.sched_ns != nullptr && nextEv < p.ev.n_sched) {
+        const long long now = globaltimer_ns();
+        if (gBase == 0) gBase = now;
+        if (now >= gBase + p.ev.sched_ns[nextEv]) {
+          p.ev.set_ns[nextEv] = now;
+          atomicCAS(p.ev.flag, nextEv, nextEv + 1);
+          ++nextEv;
+        }
+      }
+      vstore(&sh.gen, f);
+      __nanosleep(64);
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc::fence_after_sync();
+    tc::tmem_dealloc(sh.tmem_base, 512);
+  }
+  if (tid == 0) {
+    p.q.tiles_done[cta] = sh.tiles;
+    atomicMax(p.q.end_max, (unsigned long long)globaltimer_ns());
+    atomicAdd(p.q.exited, 1);
+  }
+}
+
+// ---------------------------------------------------------------------------
+
+template <int POLL, int DISC, bool ORACLE>
+static const void* kernel_ptr() {
+  return reinterpret_cast<const void*>(&gemm_bf16_persistent<POLL, DISC, ORACLE>);
+}
+
+static const void* select_kernel(int poll, int disc, bool oracle) {
+#define APK_SEL(PL, DS, OR) \
+  if (poll == PL && disc == DS && oracle == OR) return kernel_ptr<PL, DS, OR>();
+  APK_SEL(POLL_OFF, DISC_DRAIN, false)
+  APK_SEL(POLL_OFF, DISC_DRAIN, true)
+  APK_SEL(POLL_BOUNDARY, DISC_DRAIN, false)
+  APK_SEL(POLL_BOUNDARY, DISC_DRAIN, true)
+  APK_SEL(POLL_STAGE, DISC_DRAIN, false)
+  APK_SEL(POLL_STAGE, DISC_DRAIN, true)
+  APK_SEL(POLL_STAGE, DISC_POISON, false)
+#undef APK_SEL
+  return nullptr;
+}
+
+int smem_bytes() { return SMEM_BYTES; }
+int threads() { return NT; }
+
+cudaError_t prepare(int poll, int disc, bool oracle, int* max_ctas_per_sm) {
+  const void* k = select_kernel(poll, disc, oracle);
+  if (!k) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(max_ctas_per_sm, k, NT, SMEM_BYTES);
+  // each CTA allocates all 512 TMEM columns: never more than one per SM
+  if (e == cudaSuccess && *max_ctas_per_sm > 1) *max_ctas_per_sm = 1;
+  return e;
+}
+
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, cudaStream_t stream) {
+  const void* k = select_kernel(poll, disc, oracle);
+  if (!k) return cudaErrorInvalidValue;
+  void* args[] = {const_cast<F32Params*>(&prm)};
+  return cudaLaunchKernel(k, dim3(grid), dim3(NT), args, SMEM_BYTES, stream);
+}
+
 }  // namespace bf16
 }  // namespace apk

@@ -30,7 +30,7 @@ int smem_bytes(int bk);
 }  // namespace f32
 namespace bf16 {
 cudaError_t prepare(int poll, int disc, bool oracle, int* max_ctas_per_sm);
-cudaError_t launch(const void* prm, int grid, int poll, int disc, bool oracle, cudaStream_t stream);
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, cudaStream_t stream);
 int smem_bytes();
 int threads();
 }  // namespace bf16
@@ -140,9 +140,6 @@ struct apk_ctx {
   size_t exec_cap = 0;
   unsigned long long last_tasks = 0;
   int last_grid = 0;
-
-  // bf16 parameter block lives in the bf16 translation unit; opaque here
-  std::vector<unsigned char> bf16_params;
 };
 
 namespace {
@@ -235,17 +232,6 @@ apk_status prepare_kernel(apk_ctx* ctx, int poll) {
 }
 
 }  // namespace
-
-// bf16 parameter building lives beside its kernel.
-namespace apk {
-namespace bf16 {
-size_t params_size();
-apk_status build_params(void* out, const void* A, const void* B, void* C, int M, int N, int K,
-                        const void* Au, const void* Bu, float* Cu, int Mu, int Nu, int Ku,
-                        int usplit, size_t cu_stride, const EventProto& ev, const QueueProto& q,
-                        long long wait_limit_ns, int grid, std::string* err);
-}  // namespace bf16
-}  // namespace apk
 
 extern "C" {
 
@@ -620,57 +606,55 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
   ctx->last_grid = ctx->grid;
   cudaError_t e;
   if (record) APK_CU(cudaEventRecord(ctx->ev_start, stream));
-  if (ctx->cfg.dtype == APK_F32) {
-    F32Params p;
-    memset(&p, 0, sizeof p);
-    const int bk = ctx->cfg.k_tile;
+  const bool f32 = ctx->cfg.dtype == APK_F32;
+  const int bk = ctx->cfg.k_tile;
+  const int tm = f32 ? 128 : 256;  // output tile rows (fp32 128x128, bf16 256x128)
+  F32Params p;
+  memset(&p, 0, sizeof p);
+  {
+    // fp32: A as [128 rows][32 k] boxes (128B swizzle), B as [BK k][128 n]
+    // boxes (no swizzle).  bf16: A as [128 rows][64 k] and B as [64 k][64 n]
+    // boxes, both 128B swizzled (the tcgen05 canonical K- / MN-major atoms).
+    const CUtensorMapDataType dt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const int es = f32 ? 4 : 2;
+    const int a_box_k = f32 ? 32 : 64, b_box_n = f32 ? 128 : 64;
+    const CUtensorMapSwizzle bsw = f32 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B;
     apk_status t;
-    if ((t = make_tmap(ctx, &p.tmA, ctx->dA, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ctx->M, ctx->K, 32, 128,
-                       CU_TENSOR_MAP_SWIZZLE_128B)) != APK_OK)
+    if ((t = make_tmap(ctx, &p.tmA, ctx->dA, dt, es, ctx->M, ctx->K, a_box_k, 128, CU_TENSOR_MAP_SWIZZLE_128B)) !=
+        APK_OK)
       return t;
-    if ((t = make_tmap(ctx, &p.tmB, ctx->dB, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ctx->K, ctx->N, 128, bk,
-                       CU_TENSOR_MAP_SWIZZLE_NONE)) != APK_OK)
-      return t;
+    if ((t = make_tmap(ctx, &p.tmB, ctx->dB, dt, es, ctx->K, ctx->N, b_box_n, bk, bsw)) != APK_OK) return t;
     if (ctx->dAu) {
-      if ((t = make_tmap(ctx, &p.tmAu, ctx->dAu, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ctx->Mu, ctx->Ku, 32, 128,
+      if ((t = make_tmap(ctx, &p.tmAu, ctx->dAu, dt, es, ctx->Mu, ctx->Ku, a_box_k, 128,
                          CU_TENSOR_MAP_SWIZZLE_128B)) != APK_OK)
         return t;
-      if ((t = make_tmap(ctx, &p.tmBu, ctx->dBu, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ctx->Ku, ctx->Nu, 128, bk,
-                         CU_TENSOR_MAP_SWIZZLE_NONE)) != APK_OK)
-        return t;
+      if ((t = make_tmap(ctx, &p.tmBu, ctx->dBu, dt, es, ctx->Ku, ctx->Nu, b_box_n, bk, bsw)) != APK_OK) return t;
     } else {
       p.tmAu = p.tmA;
       p.tmBu = p.tmB;
     }
-    p.C = reinterpret_cast<float*>(ctx->dC);
-    p.ldc = ctx->N;
-    p.tiles_n = ctx->N / 128;
-    p.total_tiles = (ctx->M / 128) * (ctx->N / 128);
-    p.nk = ctx->K / bk;
-    p.Cu = ctx->dCu;
-    p.cu_stride = (long long)ctx->cu_slot;
-    p.ldcu = ctx->Nu;
-    p.utiles_n = ctx->Nu / 128;
-    p.usplit = ctx->cfg.urgent_split_k;
-    p.unk = ctx->Ku ? ctx->Ku / bk / p.usplit : 0;
-    p.uitems = (ctx->Mu / 128) * (ctx->Nu / 128) * p.usplit;
-    p.slab = ctx->d_slab;
-    p.slab_hdr = ctx->d_slab_hdr;
-    p.wait_limit_ns = ctx->cfg.wait_limit_ns;
-    p.ev = ev;
-    p.q = q;
-    e = f32::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, bk, stream);
-  } else {
-    ctx->bf16_params.assign(bf16::params_size() + 64, 0);
-    void* pp = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(ctx->bf16_params.data()) + 63) & ~uintptr_t(63));
-    std::string err;
-    apk_status t = bf16::build_params(pp, ctx->dA, ctx->dB, ctx->dC, ctx->M, ctx->N, ctx->K, ctx->dAu,
-                                      ctx->dBu, ctx->dCu, ctx->Mu, ctx->Nu, ctx->Ku,
-                                      ctx->cfg.urgent_split_k, ctx->cu_slot, ev, q,
-                                      ctx->cfg.wait_limit_ns, ctx->grid, &err);
-    if (t != APK_OK) return fail(ctx, t, "%s", err.c_str());
-    e = bf16::launch(pp, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, stream);
   }
+  p.C = reinterpret_cast<float*>(ctx->dC);
+  p.ldc = ctx->N;
+  p.tiles_n = ctx->N / 128;
+  p.total_tiles = (ctx->M / tm) * (ctx->N / 128);
+  p.nk = ctx->K / bk;
+  p.Cu = ctx->dCu;
+  p.cu_stride = (long long)ctx->cu_slot;
+  p.ldcu = ctx->Nu;
+  p.utiles_n = ctx->Nu / 128;
+  p.usplit = ctx->cfg.urgent_split_k;
+  p.unk = ctx->Ku ? ctx->Ku / bk / p.usplit : 0;
+  p.uitems = (ctx->Mu / tm) * (ctx->Nu / 128) * p.usplit;
+  p.slab = ctx->d_slab;
+  p.slab_hdr = ctx->d_slab_hdr;
+  p.wait_limit_ns = ctx->cfg.wait_limit_ns;
+  p.ev = ev;
+  p.q = q;
+  if (f32)
+    e = f32::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, bk, stream);
+  else
+    e = bf16::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, stream);
   if (e != cudaSuccess) return fail(ctx, APK_ECUDA, "kernel launch failed: %s", cudaGetErrorString(e));
   if (record) APK_CU(cudaEventRecord(ctx->ev_done, stream));
   return APK_OK;
