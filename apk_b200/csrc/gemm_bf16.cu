@@ -51,7 +51,12 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 48 KB
 constexpr int NT = 224;                          // 7 warps
 constexpr int SMEM_BYTES = S * STAGE_BYTES + 1024;
 constexpr int RING = 8;                          // epilogue job ring
-constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, 128, /*B MN-major*/ true);
+// The 256x128 C tile is computed transposed, D = C_tile^T (128 x 256): the
+// MMA's A operand is the [64 k][128 n] B tile (MN-major), its B operand the
+// [256 m][64 k] A tile (K-major).  One M=128, N=256 instruction per 16-deep
+// k-step reads 12 KB of shared memory per 2^19 MACs where two M=128, N=128
+// instructions (one per 128-row half) would read 16 KB.
+constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, 256, /*A MN-major*/ true, /*B MN-major*/ false);
 
 enum : int { T_BG = 1, T_URG = 2, T_SUSPEND = 3, T_STOP = 4 };
 enum : int { F_FIRST = 1, F_LAST = 2, F_RESUME = 4 };
@@ -319,16 +324,16 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         reinterpret_cast<uint16_t*>(st + A_BYTES)[0] = 0x4100;
         fence_proxy_async_smem();
       }
-      const uint32_t a0 = smem_u32(st), b0 = smem_u32(st + A_BYTES);
+      const uint32_t sa = smem_u32(st), sb = smem_u32(st + A_BYTES);
       const uint32_t d0 = tbase + (uint32_t)cur * 256;
 #pragma unroll
       for (int kk = 0; kk < BK / 16; ++kk) {
-        const uint64_t bdesc = tc::smem_desc_sw128(b0 + kk * 2048, B_CHUNK, 1024);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint64_t adesc = tc::smem_desc_sw128(a0 + h * A_HALF + kk * 32, 16, 1024);
-          tc::mma_bf16(d0 + h * 128, adesc, bdesc, IDESC, (kk > 0 || !(t.flags & F_FIRST)) ? 1u : 0u);
-        }
+        // MMA A = B tile rows kk*16.. (MN-major: 64-column chunks LBO apart,
+        // 8-row groups SBO apart); MMA B = A tile, K-major, 32 B per k-step
+        // inside the 128-byte swizzled rows, 8-row groups 1024 B apart
+        const uint64_t adesc = tc::smem_desc_sw128(sb + kk * 2048, B_CHUNK, 1024);
+        const uint64_t bdesc = tc::smem_desc_sw128(sa + kk * 32, 16, 1024);
+        tc::mma_bf16(d0, adesc, bdesc, IDESC, (kk > 0 || !(t.flags & F_FIRST)) ? 1u : 0u);
       }
       tc::commit(&sh.empty[s]);  // frees the slot once these MMAs have read it
       if (t.flags & F_LAST) {
@@ -356,10 +361,13 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         if (lane == 0) mbar_arrive(&sh.eempty[sl]);
         break;
       }
+      // TMEM holds the tile transposed: lane = C column (32q + lane of this
+      // warp's quadrant), column = C row.  Block blk covers C rows
+      // blk*32 .. blk*32+31, one register per row.
       const uint32_t tcol = tbase + ((uint32_t)(32 * q) << 16) + (uint32_t)j.buf * 256;
       if (j.action == E_RESTORE) {
 #pragma unroll 1
-        for (int blk = 0; blk < 8; ++blk) {  // blk = h*4 + jj
+        for (int blk = 0; blk < 8; ++blk) {
           const float4* s4 = reinterpret_cast<const float4*>(slab + (size_t)(blk * 4 + q) * 1024);
           uint32_t v[32];
 #pragma unroll
@@ -370,7 +378,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
             v[4 * i + 2] = __float_as_uint(x.z);
             v[4 * i + 3] = __float_as_uint(x.w);
           }
-          tc::st_32x32b_x32(tcol + (blk >> 2) * 128 + (blk & 3) * 32, v);
+          tc::st_32x32b_x32(tcol + blk * 32, v);
         }
         tc::wait_st();
         tc::fence_before_sync();
@@ -382,11 +390,9 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         tc::fence_after_sync();
 #pragma unroll 1
         for (int blk = 0; blk < 8; ++blk) {
-          const int h = blk >> 2, jj = blk & 3;
           uint32_t v[32];
-          tc::ld_32x32b_x32(tcol + h * 128 + jj * 32, v);
+          tc::ld_32x32b_x32(tcol + blk * 32, v);
           tc::wait_ld();
-          const int row = h * 128 + 32 * q + lane;
           if (j.action == E_SPILL) {
             float4* s4 = reinterpret_cast<float4*>(slab + (size_t)(blk * 4 + q) * 1024);
 #pragma unroll
@@ -394,22 +400,18 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
               s4[i * 32 + lane] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
                                               __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
           } else if (j.action == E_STORE_C) {
-            float4* d4 = reinterpret_cast<float4*>(p.C + (size_t)(j.row0 + row) * p.ldc + j.col0 + jj * 32);
+            // register i -> C row blk*32+i; the 32 lanes write 128 contiguous bytes
+            float* d = p.C + (size_t)(j.row0 + blk * 32) * p.ldc + j.col0 + 32 * q + lane;
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              d4[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                                  __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+            for (int i = 0; i < 32; ++i) d[(size_t)i * p.ldc] = __uint_as_float(v[i]);
           } else {  // E_STORE_U
-            float* d = p.Cu + (size_t)j.e * p.cu_stride + (size_t)(j.row0 + row) * p.ldcu + j.col0 + jj * 32;
+            float* d = p.Cu + (size_t)j.e * p.cu_stride + (size_t)(j.row0 + blk * 32) * p.ldcu + j.col0 + 32 * q + lane;
             if (p.usplit == 1) {
-              float4* d4 = reinterpret_cast<float4*>(d);
 #pragma unroll
-              for (int i = 0; i < 8; ++i)
-                d4[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                                    __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+              for (int i = 0; i < 32; ++i) d[(size_t)i * p.ldcu] = __uint_as_float(v[i]);
             } else {
 #pragma unroll
-              for (int i = 0; i < 32; ++i) atomicAdd(d + i, __uint_as_float(v[i]));
+              for (int i = 0; i < 32; ++i) atomicAdd(d + (size_t)i * p.ldcu, __uint_as_float(v[i]));
             }
           }
         }
@@ -491,6 +493,7 @@ static const void* select_kernel(int poll, int disc, bool oracle) {
   APK_SEL(POLL_STAGE, DISC_DRAIN, false)
   APK_SEL(POLL_STAGE, DISC_DRAIN, true)
   APK_SEL(POLL_STAGE, DISC_POISON, false)
+  APK_SEL(POLL_STAGE, DISC_POISON, true)
 #undef APK_SEL
   return nullptr;
 }

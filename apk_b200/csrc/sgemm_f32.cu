@@ -487,6 +487,7 @@ static const void* select_kernel(int poll, int disc, bool oracle, int bk) {
   APK_SEL(POLL_STAGE, DISC_DRAIN, false)
   APK_SEL(POLL_STAGE, DISC_DRAIN, true)
   APK_SEL(POLL_STAGE, DISC_POISON, false)
+  APK_SEL(POLL_STAGE, DISC_POISON, true)
 #undef APK_SEL
   return nullptr;
 }

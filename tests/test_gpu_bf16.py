@@ -1,0 +1,163 @@
+"""GPU parity tests of the bf16 tcgen05 persistent GEMM, through the C ABI.
+
+Reference: float64 over the bf16-rounded inputs (quantise-then-reference,
+src/tcyield.cu:459-483), tolerance rel = |got-ref|/max(1,|ref|) <= 1e-2;
+resumed tiles bitwise against an uninterrupted run of the same kernel
+(BASELINE configs[2]); scheduler invariants as src/yield.cu:630-663.
+"""
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+TOL = oracle.BF16_TOL
+
+
+def _ctx(**kw):
+    import apk_b200
+    kw.setdefault("urgent_split_k", 1)
+    return apk_b200.Context(dtype="bf16", **kw)
+
+
+def _normal(shape, seed):
+    import apk_b200
+    return apk_b200.fill_normal_bf16(shape, seed)
+
+
+def _check_rows(C, A, B, rows):
+    for r0, n in rows:
+        ref = oracle.gemm_f64_bf16_rows(A, B, r0, n)
+        mr, bad, nans = oracle.check(C[r0:r0 + n], ref, TOL)
+        assert nans == 0 and bad == 0, f"rows {r0}+{n}: {bad} bad, {nans} NaN, max rel {mr:.3e}"
+
+
+@pytest.mark.parametrize("shape", [(256, 128, 64), (256, 256, 320), (512, 384, 1024), (1024, 2048, 512)])
+def test_small_shapes_full_check(libapk, shape):
+    M, N, K = shape
+    A, B = _normal((M, K), 1), _normal((K, N), 2)
+    with _ctx(poll="off", oracle=True) as c:
+        C = c.gemm(A, B)
+    _check_rows(C, A, B, [(0, M)])
+
+
+def test_uniform_inputs_quantised(libapk):
+    """bf16 mode of the scaling-surface cells: uniform[-1,1] from the
+    reference generator, rounded to bf16."""
+    A16, B16 = oracle.gen_uniform_bf16(512, 512, 512, 21)
+    with _ctx(poll="stage", oracle=True) as c:
+        C = c.gemm(A16, B16)
+    _check_rows(C, A16, B16, [(0, 512)])
+
+
+def test_config2_shape_sampled_rows(libapk):
+    """8192^3, N(0,1) rounded to bf16; sampled row bands against
+    float64 (each band spans every K)."""
+    M = N = K = 8192
+    A, B = _normal((M, K), 21), _normal((K, N), 22)
+    with _ctx(poll="stage", oracle=True) as c:
+        C = c.gemm(A, B)
+    _check_rows(C, A, B, [(0, 8), (255, 2), (4096 + 128, 8), (M - 8, 8)])
+
+
+def _yield_run(poll, nev=30, gap_ns=20_000, discipline="drain"):
+    M = N = K = 4096
+    A, B = _normal((M, K), 21), _normal((K, N), 22)
+    Au, Bu = _normal((256, 256), 31), _normal((256, 256), 32)
+    with _ctx(poll="off") as c:
+        Cref = c.gemm(A, B)
+    with _ctx(poll=poll, set_mode="device", oracle=True, discipline=discipline) as c:
+        ntasks = 1024
+        c.set_background(A, B)
+        c.set_urgent(Au, Bu)
+        c.schedule_device_events((np.arange(nev, dtype=np.int64) + 1) * gap_ns)
+        c.launch(ntasks)
+        c.wait(60)
+        C = c.read_output()
+        ev = c.read_events()
+        st = c.run_stats()
+        ex, ue = c.read_oracle(ntasks)
+        fired = int(np.count_nonzero(ev["set_ns"][:nev]))
+        outs = [c.read_urgent_output(e) for e in range(fired) if ev["claimer"][e]]
+        uitems = 2 * c.cfg.urgent_split_k
+    refu = oracle.gemm_f64_bf16_rows(Au, Bu, 0, 256)
+    return dict(C=C, Cref=Cref, ev=ev, st=st, ex=ex, ue=ue, fired=fired, outs=outs, refu=refu, uitems=uitems)
+
+
+def test_stage_checkpoint_resume_is_bitwise(libapk):
+    """configs[2] property: yields at random pipeline stages, including
+    buffer-conflicting ones; accumulators spilled from TMEM and restored;
+    output bitwise equal to the uninterrupted run."""
+    r = _yield_run("stage")
+    ev = r["ev"]
+    assert r["fired"] >= 10
+    assert r["st"]["yields"] > 0
+    sites = [ev["claim_site"][e] for e in range(r["fired"]) if ev["claimer"][e]]
+    assert any(s > 0 for s in sites), "no mid-pipeline claim"
+    assert any(ev["inflight"][e] > 0 for e in range(r["fired"])), "no buffer-conflicting yield"
+    assert np.array_equal(r["C"].view(np.uint32), r["Cref"].view(np.uint32)), "resume not bitwise"
+    for Cu in r["outs"]:
+        mr, bad, nans = oracle.check(Cu, r["refu"], TOL)
+        assert bad == 0 and nans == 0
+    f = r["fired"]
+    v = oracle.exactly_once(r["ex"], r["ue"][:f], ev["claimer"][:f], ev["set_ns"][:f], r["uitems"], f)
+    assert v["pass"], v
+
+
+def test_boundary_yield_is_bitwise(libapk):
+    r = _yield_run("boundary")
+    assert np.array_equal(r["C"].view(np.uint32), r["Cref"].view(np.uint32))
+    assert all(r["ev"]["claim_site"][e] == -1 for e in range(r["fired"]) if r["ev"]["claimer"][e])
+    for Cu in r["outs"]:
+        assert oracle.check(Cu, r["refu"], TOL)[1] == 0
+
+
+def test_poison_discipline_is_detected(libapk):
+    r = _yield_run("stage", nev=8, discipline="poison")
+    assert r["outs"]
+    for Cu in r["outs"]:
+        assert oracle.check(Cu, r["refu"], TOL)[1] > 0
+    # the background output is still exact: poison only touches urgent stages
+    assert np.array_equal(r["C"].view(np.uint32), r["Cref"].view(np.uint32))
+
+
+def test_host_memcpy_injection(libapk):
+    M = N = K = 2048
+    A, B = _normal((M, K), 3), _normal((K, N), 4)
+    Au, Bu = _normal((256, 256), 5), _normal((256, 256), 6)
+    refu = oracle.gemm_f64_bf16_rows(Au, Bu, 0, 256)
+    with _ctx(poll="stage", set_mode="host_memcpy", max_events=32) as c:
+        c.set_background(A, B)
+        c.set_urgent(Au, Bu)
+        c.launch(None)
+        for _ in range(10):
+            e, _t = c.inject()
+            assert c.wait_ack(e, 1, 500_000_000) is not None
+        c.stop()
+        c.wait(30)
+        ev = c.read_events()
+        outs = [c.read_urgent_output(e) for e in range(10)]
+    assert all(ev["claimer"][:10] != 0)
+    for Cu in outs:
+        assert oracle.check(Cu, refu, TOL)[1] == 0
+
+
+def test_split_k_urgent_items(libapk):
+    """Urgent GEMM split into K slices accumulated with atomics."""
+    M = N = K = 2048
+    A, B = _normal((M, K), 7), _normal((K, N), 8)
+    Au, Bu = _normal((256, 256), 9), _normal((256, 256), 10)
+    refu = oracle.gemm_f64_bf16_rows(Au, Bu, 0, 256)
+    with _ctx(poll="stage", set_mode="device", urgent_split_k=4, oracle=True) as c:
+        c.set_background(A, B)
+        c.set_urgent(Au, Bu)
+        c.schedule_device_events(np.array([10_000, 30_000, 50_000], np.int64))
+        c.launch(512)
+        c.wait(60)
+        ev = c.read_events()
+        outs = [c.read_urgent_output(e) for e in range(3) if ev["claimer"][e]]
+        _, ue = c.read_oracle(512)
+    assert outs
+    for Cu in outs:
+        assert oracle.check(Cu, refu, TOL)[1] == 0
+    assert all(ue[e] == 8 for e in range(3) if ev["claimer"][e])
