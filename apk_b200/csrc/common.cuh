@@ -91,6 +91,21 @@ __device__ __forceinline__ void count_trigger(const EV& ev) {
     }
 }
 
+// Grouped raster of the output-tile grid: tiles are walked in groups of
+// `group` tile-rows, column-major inside a group, so the CTAs resident at
+// one time share a few A row-panels and B column-panels and the working set
+// of a wave stays in L2 (a row-major walk sweeps all of B once per tile-row).
+// The order changes nothing but which CTA computes which tile.
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int group, int& tm, int& tn) {
+  const int per_group = group * tiles_n;
+  const int g = tile / per_group;
+  const int first = g * group;
+  const int rows = (tiles_m - first) < group ? (tiles_m - first) : group;
+  const int local = tile - g * per_group;
+  tm = first + local % rows;
+  tn = local / rows;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

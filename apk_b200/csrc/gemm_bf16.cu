@@ -51,6 +51,7 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 48 KB
 constexpr int NT = 224;                          // 7 warps
 constexpr int SMEM_BYTES = S * STAGE_BYTES + 1024;
 constexpr int RING = 8;                          // epilogue job ring
+constexpr int RASTER_GROUP = 8;                  // tile-rows per raster group
 // The 256x128 C tile is computed transposed, D = C_tile^T (128 x 256): the
 // MMA's A operand is the [64 k][128 n] B tile (MN-major), its B operand the
 // [256 m][64 k] A tile (K-major).  One M=128, N=256 instruction per 16-deep
@@ -241,7 +242,9 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         }
       if (task >= p.q.num_tasks) break;
       const int tile = (int)(task % (unsigned long long)p.total_tiles);
-      const int row0 = (tile / p.tiles_n) * BM, col0 = (tile % p.tiles_n) * BN;
+      int tm, tn;
+      tile_coords(tile, p.total_tiles / p.tiles_n, p.tiles_n, RASTER_GROUP, tm, tn);
+      const int row0 = tm * BM, col0 = tn * BN;
       bool resume = false;
       for (int c = 0; c < p.nk && ok; ++c) {
         if (POLL == POLL_STAGE) {

@@ -360,8 +360,12 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
       const int tile = (int)(task % (unsigned long long)p.total_tiles);
       urgent = false;
       bg_active = true;
-      row0 = (tile / p.tiles_n) * BM;
-      col0 = (tile % p.tiles_n) * BN;
+      {
+        int tm, tn;
+        tile_coords(tile, p.total_tiles / p.tiles_n, p.tiles_n, 8, tm, tn);
+        row0 = tm * BM;
+        col0 = tn * BN;
+      }
       kst0 = 0;
       nk = p.nk;
       c = 0;
