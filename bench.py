@@ -358,14 +358,14 @@ def run_ours(args, world, rank, local):
     fp32_peak_clock = SMS_B200 * 128 * 2 * sm_mhz * 1e6 / 1e12
     per_gpu = value / world
     achieved = 2.0 * 128 * 128 * K * allr[0]["one_pass_tiles"] / (allr[0]["one_pass_ms"] / 1e3) / 1e12
+    # DRAM bytes per launch: the ncu capture's per-tile traffic (read + write)
+    # scaled to the tiles of one drain
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "sgemm_f32_4096_traffic.json")
+    tp = os.path.join(ROOT, "profiles", "sgemm_f32_persistent_4096.md")
     if os.path.exists(tp):
-        try:
-            tj = json.load(open(tp))
-            traffic = tj["dram_bytes_per_tile"] * allr[0]["one_pass_tiles"]
-        except Exception:
-            traffic = None
+        for ln in open(tp):
+            if ln.startswith("dram_bytes_per_tile:"):
+                traffic = float(ln.split(":", 1)[1]) * allr[0]["one_pass_tiles"]
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": tmax * 1e3 / args.steps, "higher_is_better": True,
