@@ -60,11 +60,7 @@ struct Cfg {
 // A is read two k at a time (float2 per row) and B one k at a time (two
 // float4): 12 shared loads per 128 FFMA, 96 live registers for operands and
 // accumulators, which leaves headroom under the 128-register cap.
-// poll: when non-null (tid 0 of a background stage), the yield flag is
-// loaded into pend two k-pairs before the end of the stage, so the value the
-// next stage barrier publishes is a fraction of a stage old while the load
-// latency still hides under the remaining FMAs.
-// Two k (one k-pair kp) of one 32-deep sub-tile.
+// kpair: two k (one k-pair kp) of one 32-deep sub-tile.
 __device__ __forceinline__ void kpair(const float* __restrict__ Asub, const float* __restrict__ Bsub,
                                       float (&acc)[8][8], int arow0, int ty, int bcol, int kp) {
   const int kc = kp >> 1, half = kp & 1;
@@ -90,6 +86,10 @@ __device__ __forceinline__ void kpair(const float* __restrict__ Asub, const floa
   }
 }
 
+// poll: when non-null (tid 0 of a background stage), the yield flag is
+// loaded into pend two k-pairs before the end of the stage, so the value the
+// next stage barrier publishes is a fraction of a stage old while the load
+// latency still hides under the remaining FMAs.
 template <int BK>
 __device__ __forceinline__ void compute_stage(const float* __restrict__ As,
                                               const float* __restrict__ Bs, float (&acc)[8][8],
@@ -516,3 +516,159 @@ cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool orac
 
 }  // namespace f32
 }  // namespace apk
+
+// ===========================================================================
+// Allocation-free entry point: apk_sgemm_f32_noalloc.
+//
+// For callers that cannot call cudaMalloc: a process whose device memory is
+// owned by a pool it does not control, code running where an allocation
+// would synchronize the device or is not allowed (a latency-critical serving
+// loop after start-up, a library called from inside another framework's
+// stream-ordered work).  The same persistent fp32 SGEMM drain runs with its
+// scratch -- the work-queue counter, exit bookkeeping and per-CTA tile
+// counters -- in the file-scope array below instead of memory from
+// cudaMalloc.  The caller passes inputs and output; nothing is allocated or
+// freed on this path.
+//
+// The array exists once per device that loads this library and lives until
+// the process exits.  Its device address is obtained with
+// cudaGetSymbolAddress at the first call on each device (with that device
+// current); that first call should therefore come before any stream capture.
+// Every call shares the array and it keeps the last call's contents: the
+// queue header is cleared on the caller's stream before each launch, so
+// calls issued in order on one stream are independent, while calls that
+// overlap on the GPU (different streams, or other devices' contexts sharing
+// nothing but this code) race on the same scratch and must not be issued.
+// ===========================================================================
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include <cudaTypedefs.h>
+
+#include "../../include/apk.h"
+
+namespace apk {
+namespace f32 {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 16384;  // stated maximum
+constexpr size_t kNoAllocHeaderBytes = 256;
+constexpr int kNoAllocMaxGrid = (int)((kNoAllocScratchBytes - kNoAllocHeaderBytes) / sizeof(unsigned long long));
+
+struct NoAllocHeader {
+  unsigned long long next_task, start_min, end_max, yields;
+  int exited, abort_word, status, flag;
+};
+static_assert(sizeof(NoAllocHeader) <= kNoAllocHeaderBytes, "header must fit");
+
+struct NoAllocDevice {
+  bool ready = false;
+  unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch
+  int sms = 0;
+  int max_ctas_per_sm = 0;
+};
+
+constexpr int kMaxDevices = 64;
+NoAllocDevice g_noalloc_dev[kMaxDevices];
+std::mutex g_noalloc_mu;
+PFN_cuTensorMapEncodeTiled_v12000 g_noalloc_encode = nullptr;
+
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+}  // namespace f32
+}  // namespace apk
+
+extern "C" apk_status apk_sgemm_f32_noalloc(const float* A, const float* B, float* C, int M, int N, int K,
+                                            int grid, void* stream) {
+  using namespace apk;
+  using namespace apk::f32;
+  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0 || M % 128 || N % 128 || K % 32) return APK_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(C)) & 15)
+    return APK_EINVAL;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return APK_ECUDA;
+  NoAllocDevice& d = g_noalloc_dev[dev];
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!d.ready) {
+      // one-time set-up on this device (it is current): the scratch array's
+      // device address, the kernel's shared-memory attribute, SM count
+      void* ptr = nullptr;
+      if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return APK_ECUDA;
+      int maxc = 0;
+      if (prepare(POLL_OFF, DISC_DRAIN, false, 32, &maxc) != cudaSuccess || maxc < 1) return APK_ECUDA;
+      int sms = 0;
+      if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return APK_ECUDA;
+      if (!g_noalloc_encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn)
+          return APK_ECUDA;
+        g_noalloc_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+      }
+      d.scratch = static_cast<unsigned char*>(ptr);
+      d.sms = sms;
+      d.max_ctas_per_sm = maxc;
+      d.ready = true;
+    }
+  }
+  const int resident = d.sms * d.max_ctas_per_sm;
+  if (grid <= 0) grid = resident;
+  if (grid > resident) return APK_EINVAL;  // CTAs beyond residency never start
+  if (grid > kNoAllocMaxGrid) {
+    fprintf(stderr,
+            "apk_sgemm_f32_noalloc: grid %d needs %zu bytes of scratch; the static array holds %zu (max grid %d)\n",
+            grid, kNoAllocHeaderBytes + (size_t)grid * sizeof(unsigned long long), kNoAllocScratchBytes,
+            kNoAllocMaxGrid);
+    return APK_EINVAL;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  F32Params p;
+  memset(&p, 0, sizeof p);
+  auto enc = [&](CUtensorMap* tm, const void* base, long long rows, long long cols, int box_cols, int box_rows,
+                 CUtensorMapSwizzle sw) {
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return g_noalloc_encode(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  };
+  if (!enc(&p.tmA, A, M, K, 32, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !enc(&p.tmB, B, K, N, 128, 32, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return APK_ECUDA;
+  p.tmAu = p.tmA;
+  p.tmBu = p.tmB;
+  p.C = C;
+  p.ldc = N;
+  p.tiles_n = N / 128;
+  p.total_tiles = (M / 128) * (N / 128);
+  p.nk = K / 32;
+  p.wait_limit_ns = 2000000000LL;
+
+  NoAllocHeader* h = reinterpret_cast<NoAllocHeader*>(d.scratch);
+  p.ev.flag = &h->flag;
+  p.ev.abort_word = &h->abort_word;
+  p.ev.status = &h->status;
+  p.q.next_task = &h->next_task;
+  p.q.num_tasks = (unsigned long long)p.total_tiles;
+  p.q.tiles_done = reinterpret_cast<unsigned long long*>(d.scratch + kNoAllocHeaderBytes);
+  p.q.start_min = &h->start_min;
+  p.q.end_max = &h->end_max;
+  p.q.exited = &h->exited;
+  p.q.yields = &h->yields;
+
+  // what must start at zero: the queue header (the tile counters are
+  // written, not accumulated); start_min starts at all-ones for atomicMin
+  if (cudaMemsetAsync(d.scratch, 0, kNoAllocHeaderBytes, s) != cudaSuccess) return APK_ECUDA;
+  if (cudaMemsetAsync(&h->start_min, 0xFF, sizeof(h->start_min), s) != cudaSuccess) return APK_ECUDA;
+  if (launch(p, grid, POLL_OFF, DISC_DRAIN, false, 32, s) != cudaSuccess) return APK_ECUDA;
+  return APK_OK;
+}

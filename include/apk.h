@@ -273,6 +273,31 @@ apk_status apk_run_overhead(apk_ctx* ctx, unsigned long long num_tasks, int reps
 apk_status apk_run_baseline(apk_ctx* ctx, unsigned long long num_tasks, int trials, unsigned seed,
                             double* e2e_us);
 
+/* ---- allocation-free entry point --------------------------------------- */
+
+/* C = A * B (fp32, row-major, device pointers, 16-byte aligned; M and N
+ * multiples of 128, K a multiple of 32) through the persistent fp32 SGEMM
+ * drain, for callers that cannot call cudaMalloc -- a process whose device
+ * memory belongs to a pool it does not control, or code that must not
+ * allocate (an allocation can synchronize the device) once it is serving.
+ * No counterpart in the reference: the reference allocates every buffer
+ * itself in each binary's main().
+ *
+ * Nothing is allocated or freed: the kernel's scratch (work-queue counter,
+ * exit bookkeeping, per-CTA tile counters) lives in a file-scope device
+ * array of 16 KB, which every GPU that loads this library holds until the
+ * process exits.  That fixes the limit: grid (0 = one CTA per resident
+ * slot, 296 on a B200) may be at most 2016 CTAs; a larger grid, a grid
+ * beyond residency, or a bad shape returns APK_EINVAL.  The first call on a
+ * device does a one-time set-up (the array's device address, the kernel's
+ * shared-memory attribute) and should come before any stream capture.  The
+ * call is asynchronous on `stream` (a cudaStream_t, NULL = the legacy
+ * default stream).  Every call shares the array: calls issued in order on
+ * one stream are independent (the queue header is cleared on that stream
+ * first), calls that overlap on the GPU race and must not be made. */
+apk_status apk_sgemm_f32_noalloc(const float* A, const float* B, float* C, int M, int N, int K, int grid,
+                                 void* stream);
+
 /* ---- data and memory helpers ----------------------------------------- */
 
 /* The reference's generator: srand(seed), then A (nA values) and B (nB
