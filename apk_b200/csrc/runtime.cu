@@ -971,12 +971,15 @@ apk_status apk_run_latency(apk_ctx* ctx, const apk_latency_config* lc, apk_laten
   double offset = 0.0;
   const bool host_set = ctx->cfg.set_mode != APK_SET_DEVICE;
   if (host_set) {
-    std::vector<long long> offs(64);
-    if ((s = apk_probe_visibility(ctx, 64, offs.data())) != APK_OK) return s;
-    std::vector<double> o;
-    for (long long v : offs)
-      if (v != 0) o.push_back((double)v);
-    offset = o.empty() ? NAN : pct(o, 0.5);
+    offset = NAN;
+    if (lc->probe_reps > 0) {
+      std::vector<long long> offs(lc->probe_reps);
+      if ((s = apk_probe_visibility(ctx, lc->probe_reps, offs.data())) != APK_OK) return s;
+      std::vector<double> o;
+      for (long long v : offs)
+        if (v != 0) o.push_back((double)v);
+      if (!o.empty()) offset = pct(o, 0.5);
+    }
     if ((s = apk_schedule_device_events(ctx, nullptr, 0)) != APK_OK) return s;
   } else {
     if ((s = apk_schedule_device_events(ctx, when.data(), E)) != APK_OK) return s;
@@ -1044,8 +1047,9 @@ apk_status apk_run_latency(apk_ctx* ctx, const apk_latency_config* lc, apk_laten
       ++out->unclaimed;
       continue;
     }
-    lc_claim.push_back((claim[e] - setg) / 1e3);
-    if (done[e]) lc_done.push_back((done[e] - setg) / 1e3);
+    const bool have_set = !std::isnan(setg);  // host-set without calibration: NaN
+    if (have_set) lc_claim.push_back((claim[e] - setg) / 1e3);
+    if (have_set && done[e]) lc_done.push_back((done[e] - setg) / 1e3);
     long long hi = 0;
     int seen = 0;
     for (int b = 0; b < G; ++b) {
@@ -1055,7 +1059,7 @@ apk_status apk_run_latency(apk_ctx* ctx, const apk_latency_config* lc, apk_laten
       hi = std::max(hi, o);
     }
     if (seen < G) ++out->anomalies;
-    else lc_last.push_back((hi - setg) / 1e3);
+    else if (have_set) lc_last.push_back((hi - setg) / 1e3);
   }
   out->claim_p50_us = pct(lc_claim, 0.5);
   out->claim_p99_us = pct(lc_claim, 0.99);

@@ -227,6 +227,63 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- extras
+def device_set_latency(apk_b200, np, dev, A, B, Au, Bu, bg_tasks, events=200):
+    """configs[1] with the reference's primary instrument: CTA 0 sets the
+    flag at scheduled globaltimer instants (src/yield.cu:186-195), so set,
+    observation, claim and completion share one clock."""
+    with apk_b200.Context(device=dev, poll="stage", set_mode="device", max_events=events + 8) as c:
+        c.set_background(A, B)
+        c.set_urgent(Au, Bu)
+        r = c.run_latency(events=events, period_us=1000, seed=7, warmup_events=10, settle_ms=2.0,
+                          bg_tasks=bg_tasks)
+    keys = ("n", "unclaimed", "anomalies", "claim_p50_us", "claim_p99_us", "last_obs_p50_us",
+            "last_obs_p99_us", "done_p50_us", "done_p99_us", "bg_tflops")
+    return {k: r[k] for k in keys}
+
+
+def bf16_config2(apk_b200, np, dev):
+    """bf16 8192^3, N(0,1) rounded to bf16, 256x128 tiles,
+    K-tile 64, 4-stage TMA ring: throughput of the uninterrupted drain, then a
+    drain with device-set yields at random pipeline stages whose output must
+    be bitwise identical to the uninterrupted one."""
+    n = 8192
+    A = apk_b200.fill_normal_bf16((n, n), 21)
+    B = apk_b200.fill_normal_bf16((n, n), 22)
+    Au = apk_b200.fill_normal_bf16((256, 256), 31)
+    Bu = apk_b200.fill_normal_bf16((256, 256), 32)
+    peak = measured_peaks().get("bf16_tflops", 1590.0)
+    with apk_b200.Context(device=dev, dtype="bf16", poll="stage", urgent_split_k=1) as c:
+        ms = []
+        for _ in range(6):
+            C0 = c.gemm(A, B)
+            ms.append(c.run_stats()["launch_ms"])
+    med = statistics.median(ms[1:])
+    tf = 2.0 * n ** 3 / (med / 1e3) / 1e12
+    nev = 40
+    with apk_b200.Context(device=dev, dtype="bf16", poll="stage", set_mode="device", urgent_split_k=1,
+                          max_events=64) as c:
+        c.set_background(A, B)
+        c.set_urgent(Au, Bu)
+        c.schedule_device_events((np.arange(nev, dtype=np.int64) + 1) * 25_000)
+        c.launch((n // 256) * (n // 128))
+        c.wait(60)
+        C = c.read_output()
+        ev = c.read_events()
+        st = c.run_stats()
+    fired = int(np.count_nonzero(ev["set_ns"][:nev]))
+    cl = [(ev["claim_ns"][e] - ev["set_ns"][e]) / 1e3 for e in range(fired) if ev["claimer"][e]]
+    dn = [(ev["done_ns"][e] - ev["set_ns"][e]) / 1e3 for e in range(fired) if ev["done_ns"][e]]
+    mid = sum(1 for e in range(fired) if ev["claimer"][e] and ev["claim_site"][e] > 0)
+    return {"tflops_median": tf, "pct_of_measured_peak": tf / peak * 100.0, "peak_tflops": peak,
+            "ms_median": med, "yield_run": {
+                "events_fired": fired, "checkpoints": st["yields"], "mid_pipeline_claims": mid,
+                "bitwise_equal_to_uninterrupted": bool(np.array_equal(C.view(np.uint32), C0.view(np.uint32))),
+                "claim_p50_us": pct(cl, 0.5), "claim_p99_us": pct(cl, 0.99),
+                "done_p50_us": pct(dn, 0.5), "done_p99_us": pct(dn, 0.99),
+                "tflops_with_yields": st["bg_tflops"]}}
+
+
 # ---------------------------------------------------------------- our arm
 def run_ours(args, world, rank, local):
     import numpy as np
@@ -252,35 +309,37 @@ def run_ours(args, world, rank, local):
     step_ms = settle_ms + args.events_per_step * args.period_us / 1e3
     bg_tasks = int(step_ms * 1.10 / ms_per_task) + info["grid"]
 
+    LAT_KEYS = ("rt_claim", "rt_done", "claim_after_first_obs", "spread", "done_after_claim")
+
     def one_step():
-        r = ctx.run_latency(events=args.events_per_step, period_us=args.period_us,
-                            seed=21 + rank, warmup_events=0, settle_ms=settle_ms, bg_tasks=bg_tasks)
+        # host-set events; no clock calibration: host round trips (host clock)
+        # and device-clock intervals anchored on the first observer
+        ctx.run_latency(events=args.events_per_step, period_us=args.period_us, seed=21 + rank,
+                        warmup_events=0, settle_ms=settle_ms, bg_tasks=bg_tasks, probe_reps=0)
         st = ctx.run_stats()
         ev = ctx.read_events()
         n = ev["n_injected"]
-        off = r["vis_offset_ns"]
-        if off != off:  # no calibration sample: report host round trips only
-            off = 0.0
         hs, ha, hd = ev["host_set_ns"][:n], ev["host_ack_ns"][:n], ev["host_done_ns"][:n]
         cl, dn, who = ev["claim_ns"][:n], ev["done_ns"][:n], ev["claimer"][:n]
         obs = ev["obs_ns"][:n]
-        lat = {"claim": [], "done": [], "rt_claim": [], "rt_done": [], "last_obs": [], "unclaimed": 0,
-               "anomalies": 0}
+        lat = {k: [] for k in LAT_KEYS}
+        lat["unclaimed"] = lat["anomalies"] = 0
         for e in range(n):
             if who[e] == 0:
                 lat["unclaimed"] += 1
                 continue
-            s = hs[e] + off
-            lat["claim"].append((cl[e] - s) / 1e3)
-            if dn[e]:
-                lat["done"].append((dn[e] - s) / 1e3)
             if ha[e]:
                 lat["rt_claim"].append((ha[e] - hs[e]) / 1e3)
             if hd[e]:
                 lat["rt_done"].append((hd[e] - hs[e]) / 1e3)
             o = obs[e]
-            if np.count_nonzero(o) == len(o):
-                lat["last_obs"].append((o.max() - s) / 1e3)
+            seen = o[o > 0]
+            first = seen.min()
+            lat["claim_after_first_obs"].append((cl[e] - first) / 1e3)
+            if dn[e]:
+                lat["done_after_claim"].append((dn[e] - cl[e]) / 1e3)
+            if seen.size == o.size:
+                lat["spread"].append((o.max() - first) / 1e3)
             else:
                 lat["anomalies"] += 1
         return st, lat
@@ -294,8 +353,8 @@ def run_ours(args, world, rank, local):
     wall0 = time.perf_counter()
     flops = 0.0
     launch_ms = []
-    lats = {"claim": [], "done": [], "rt_claim": [], "rt_done": [], "last_obs": [], "unclaimed": 0,
-            "anomalies": 0}
+    lats = {k: [] for k in LAT_KEYS}
+    lats["unclaimed"] = lats["anomalies"] = 0
     yields = 0
     for _ in range(args.steps):
         st, lat = one_step()
@@ -335,6 +394,9 @@ def run_ours(args, world, rank, local):
         base = ctx.run_baseline(1024, trials=20, seed=21)
         extras["no_preemption_e2e_us"] = {"p50": pct(list(base), 0.5), "p99": pct(list(base), 0.99)}
     ctx.close()
+    if not args.no_extras:
+        extras["device_set"] = device_set_latency(apk_b200, np, dev, A, B, Au, Bu, bg_tasks)
+        extras["bf16_config2"] = bf16_config2(apk_b200, np, dev)
 
     res = {"flops": flops, "launch_s": sum(launch_ms) / 1e3, "lats": lats, "wall": wall, "clk": clk,
            "e2e_tf": e2e_tf, "extras": extras, "info": info, "yields": yields,
@@ -345,7 +407,7 @@ def run_ours(args, world, rank, local):
     tot_flops = sum(r["flops"] for r in allr)
     tmax = max(r["launch_s"] for r in allr)
     value = tot_flops / tmax / 1e12
-    L = {"claim": [], "done": [], "rt_claim": [], "rt_done": [], "last_obs": []}
+    L = {k: [] for k in LAT_KEYS}
     unclaimed = anomalies = 0
     for r in allr:
         for k in L:
@@ -379,16 +441,20 @@ def run_ours(args, world, rank, local):
                    "urgent_split_k": 8, "l2": "inputs larger than L2: A+B+C = 192 MB > 126 MB",
                    "parallelism": f"{world} independent replicas (no collectives)"},
         "latency_us": {
-            "events": len(L["claim"]) + unclaimed, "unclaimed": unclaimed, "anomalies": anomalies,
-            "claim_p50": pct(L["claim"], 0.5), "claim_p99": pct(L["claim"], 0.99),
-            "last_observer_p50": pct(L["last_obs"], 0.5), "last_observer_p99": pct(L["last_obs"], 0.99),
-            "urgent_done_p50": pct(L["done"], 0.5), "urgent_done_p99": pct(L["done"], 0.99),
-            "host_roundtrip_claim_p50": pct(L["rt_claim"], 0.5),
-            "host_roundtrip_claim_p99": pct(L["rt_claim"], 0.99),
-            "host_roundtrip_done_p50": pct(L["rt_done"], 0.5),
-            "host_roundtrip_done_p99": pct(L["rt_done"], 0.99),
-            "definition": "set = host store mapped to globaltimer by the idle-device visibility calibration "
-                          "(src/yield.cu:782-813); host_roundtrip_* need no mapping",
+            "events": len(L["claim_after_first_obs"]) + unclaimed, "unclaimed": unclaimed, "anomalies": anomalies,
+            "preempt_p50": pct(L["rt_claim"], 0.5), "preempt_p99": pct(L["rt_claim"], 0.99),
+            "urgent_done_p50": pct(L["rt_done"], 0.5), "urgent_done_p99": pct(L["rt_done"], 0.99),
+            "device_claim_after_first_observer_p50": pct(L["claim_after_first_obs"], 0.5),
+            "device_claim_after_first_observer_p99": pct(L["claim_after_first_obs"], 0.99),
+            "device_observation_spread_p50": pct(L["spread"], 0.5),
+            "device_observation_spread_p99": pct(L["spread"], 0.99),
+            "device_done_after_claim_p50": pct(L["done_after_claim"], 0.5),
+            "device_done_after_claim_p99": pct(L["done_after_claim"], 0.99),
+            "definition": "preempt = host store of the yield flag -> host sees the device's claim ack (the "
+                          "first popper of the urgent work, acked through mapped memory), host clock, no "
+                          "clock mapping; urgent_done = host store -> host sees the last urgent item's ack; "
+                          "device_* are globaltimer intervals from the first CTA to observe the flag "
+                          "(src/yield.cu:148-153); extras.device_set measures set->claim in one clock",
         },
         "bg_pct_of_fp32_peak": {"nominal_1965MHz": per_gpu / fp32_peak_nominal * 100.0,
                                 "at_measured_clock": per_gpu / fp32_peak_clock * 100.0},

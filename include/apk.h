@@ -225,6 +225,10 @@ typedef struct apk_latency_config {
                                   else a bounded launch of that many tasks
                                   that ends by itself (injection stops when
                                   it ends)                                    */
+  int probe_reps;           /* host-set only: visibility-calibration reps
+                               before the launch (0 = none: the claim /
+                               last_obs / done fields are then NaN and only
+                               the rt_* host round trips are reported)     */
 } apk_latency_config;
 
 typedef struct apk_latency_result {
