@@ -49,7 +49,9 @@ constexpr int B_CHUNK = BK * 64 * 2;             // 8 KB: one [64 k][64 n] box
 constexpr int B_BYTES = 2 * B_CHUNK;             // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 48 KB
 constexpr int NT = 224;                          // 7 warps
-constexpr int SMEM_BYTES = S * STAGE_BYTES + 1024;
+constexpr int STAGE_OUT = 32 * 32 * 4;           // one 32x32 fp32 epilogue block
+constexpr int OUT_BYTES = 4 * 2 * STAGE_OUT;     // 4 epilogue warps x 2 ping-pong buffers
+constexpr int SMEM_BYTES = S * STAGE_BYTES + OUT_BYTES + 1024;
 constexpr int RING = 8;                          // epilogue job ring
 constexpr int RASTER_GROUP = 8;                  // tile-rows per raster group
 // The 256x128 C tile is computed transposed, D = C_tile^T (128 x 256): the
@@ -230,9 +232,14 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
       return n;
     };
 
+    // the queue is popped one task ahead: the atomic's round trip overlaps
+    // the current tile's stage issue instead of stalling the ring at every
+    // tile boundary (a popped task is kept across a yield and run after it)
+    unsigned long long next_task = atomicAdd(p.q.next_task, 1ull);
     while (ok) {
-      // ---- tile boundary: pop a background task (kept across a yield) ----
-      const unsigned long long task = atomicAdd(p.q.next_task, 1ull);
+      // ---- tile boundary: take the popped background task ----
+      const unsigned long long task = next_task;
+      if (task < p.q.num_tasks) next_task = atomicAdd(p.q.next_task, 1ull);
       int f = vload(&sh.gen);
       if (f < 0 || vload(&sh.abort)) break;
       if (POLL != POLL_OFF && f != lastSeen)
@@ -355,6 +362,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
     uint32_t Y = 0, eb[2] = {0, 0};
     const uint32_t tbase = sh.tmem_base;
     float* slab = p.slab + (size_t)cta * (BM * BN);
+    float* out_stage = reinterpret_cast<float*>(stages + S * STAGE_BYTES);
     while (true) {
       const int sl = Y % RING;
       if (!bwait(&sh.efull[sl], (Y / RING) & 1, p, sh)) break;
@@ -402,19 +410,31 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
             for (int i = 0; i < 8; ++i)
               s4[i * 32 + lane] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
                                               __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
-          } else if (j.action == E_STORE_C) {
-            // register i -> C row blk*32+i; the 32 lanes write 128 contiguous bytes
-            float* d = p.C + (size_t)(j.row0 + blk * 32) * p.ldc + j.col0 + 32 * q + lane;
+          } else {
+            // Stage the 32x32 block row-major in this warp's ping-pong buffer
+            // (register i -> row blk*32+i, lane -> column 32q+lane: one
+            // conflict-free 128-byte row per store) and hand it to the TMA
+            // engine: a tensor store for C / urgent slots, a reduce-add for
+            // split-K urgent items.
+            float* ob = out_stage + (2 * q + (blk & 1)) * (STAGE_OUT / 4);
+            if (blk >= 2) {
+              if (lane == 0) bulk_wait_read<1>();  // this buffer's previous store has read it
+              __syncwarp();
+            }
 #pragma unroll
-            for (int i = 0; i < 32; ++i) d[(size_t)i * p.ldc] = __uint_as_float(v[i]);
-          } else {  // E_STORE_U
-            float* d = p.Cu + (size_t)j.e * p.cu_stride + (size_t)(j.row0 + blk * 32) * p.ldcu + j.col0 + 32 * q + lane;
-            if (p.usplit == 1) {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) d[(size_t)i * p.ldcu] = __uint_as_float(v[i]);
-            } else {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) atomicAdd(d + (size_t)i * p.ldcu, __uint_as_float(v[i]));
+            for (int i = 0; i < 32; ++i) ob[i * 32 + lane] = __uint_as_float(v[i]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              const int x = j.col0 + 32 * q;
+              if (j.action == E_STORE_C) {
+                tma_store_2d(&p.tmC, x, j.row0 + blk * 32, ob);
+              } else {
+                const int y = j.e * (int)(p.cu_stride / p.ldcu) + j.row0 + blk * 32;
+                if (p.usplit == 1) tma_store_2d(&p.tmCu, x, y, ob);
+                else tma_reduce_add_2d(&p.tmCu, x, y, ob);
+              }
+              bulk_commit();
             }
           }
         }
@@ -422,7 +442,9 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh.tempty[j.buf]);
         if (j.action != E_SPILL) {
+          // the tile's stores are complete and visible before it is counted;
           // the last of the four epilogue warps to finish does the accounting
+          if (lane == 0) bulk_wait_all();
           __threadfence();
           __syncwarp();
           if (lane == 0 && atomicAdd(&sh.epi_cnt[sl], 1) == 3) {
@@ -444,6 +466,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
       if (lane == 0) mbar_arrive(&sh.eempty[sl]);
       ++Y;
     }
+    if (lane == 0) bulk_wait_all();  // no bulk store may still read smem at exit
   } else if (warp == 6 && lane == 0) {
     // ================================ control =================================
     int nextEv = 0;

@@ -58,6 +58,8 @@ struct F32Params {
   CUtensorMap tmB;   // background B [K][N]  (box 128 cols x BK rows, no swizzle)
   CUtensorMap tmAu;  // urgent A
   CUtensorMap tmBu;  // urgent B
+  CUtensorMap tmC;   // background C [M][N] fp32, 32x32 boxes (bf16 path epilogue stores)
+  CUtensorMap tmCu;  // urgent output slots [(max_events+1)*Mu][Nu] fp32, 32x32 boxes
   float* C;
   int ldc, tiles_n, total_tiles, nk;   // nk = K / BK
   float* Cu;                           // urgent output, one slot per event

@@ -633,6 +633,19 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
       p.tmAu = p.tmA;
       p.tmBu = p.tmB;
     }
+    // fp32 outputs as 32x32 boxes for the TMA-store epilogue (bf16 path);
+    // the urgent slots are one [(max_events+1)*Mu][Nu] array
+    if ((t = make_tmap(ctx, &p.tmC, ctx->dC, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ctx->M, ctx->N, 32, 32,
+                       CU_TENSOR_MAP_SWIZZLE_NONE)) != APK_OK)
+      return t;
+    if (ctx->dCu) {
+      if ((t = make_tmap(ctx, &p.tmCu, ctx->dCu, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4,
+                         (long long)ctx->Mu * (ctx->cfg.max_events + 1), ctx->Nu, 32, 32,
+                         CU_TENSOR_MAP_SWIZZLE_NONE)) != APK_OK)
+        return t;
+    } else {
+      p.tmCu = p.tmC;
+    }
   }
   p.C = reinterpret_cast<float*>(ctx->dC);
   p.ldc = ctx->N;
