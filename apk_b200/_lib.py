@@ -99,6 +99,13 @@ SIGNATURES = {
     "apk_selftest_wait_timeout": (c_int, [P, c_ll, ctypes.POINTER(c_int)]),
     "apk_run_overhead": (c_int, [P, c_ull, c_int, ctypes.POINTER(c_double), ctypes.POINTER(c_double)]),
     "apk_run_baseline": (c_int, [P, c_ull, c_int, c_uint, P]),
+    "apk_set_task_pool": (c_int, [P, P, c_int, c_int, P, c_int, c_int, c_int, c_int, c_int]),
+    "apk_set_tasks": (c_int, [P, P, c_int, c_ll, ctypes.POINTER(c_ull)]),
+    "apk_read_checksums": (c_int, [P, P, c_ll]),
+    "apk_read_pool_window": (c_int, [P, c_int, c_int, c_int, c_int, P]),
+    "apk_gen_tasks": (c_ll, [c_ull, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                             c_int, P]),
+    "apk_shard_tasks": (c_int, [P, c_int, c_int, c_int, P]),
     "apk_sgemm_f32_noalloc": (c_int, [P, P, P, c_int, c_int, c_int, c_int, P]),
     "apk_fill_uniform": (None, [c_uint, P, c_size_t, P, c_size_t]),
     "apk_fill_normal_bf16": (None, [c_ull, P, c_size_t]),

@@ -114,3 +114,96 @@ void apk_round_bf16(const float* in, uint16_t* out, size_t n) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// configs[4] task generator and static shard.
+
+#include <algorithm>
+#include <numeric>
+#include <queue>
+#include <random>
+
+namespace {
+
+// uniform double in [0,1) from one 64-bit draw
+inline double u01(std::mt19937_64& g) { return (double)(g() >> 11) * 0x1.0p-53; }
+
+int log_uniform_rounded(std::mt19937_64& g, int lo, int hi, int q) {
+  const double x = std::exp(std::log((double)lo) + u01(g) * (std::log((double)hi) - std::log((double)lo)));
+  int v = (int)std::floor(x / q + 0.5) * q;
+  if (v < lo) v = lo;
+  if (v > hi) v = hi;
+  return v;
+}
+
+// uniform multiple of q in [0, hi] (hi >= 0)
+int uniform_multiple(std::mt19937_64& g, int hi, int q) {
+  const int slots = hi / q + 1;
+  return (int)(g() % (unsigned long long)slots) * q;
+}
+
+}  // namespace
+
+extern "C" {
+
+long long apk_gen_tasks(unsigned long long seed, int n, int mn_lo, int mn_hi, int k_lo, int k_hi, int a_rows,
+                        int a_cols, int b_rows, int b_cols, int c_rows, int c_cols, int n_samples,
+                        apk_task* out) {
+  std::mt19937_64 g(seed);
+  const int sample_rows = 2048 * ((n_samples + 3) / 4);
+  const int c_free_rows = c_rows - sample_rows;  // rows [0, c_free_rows) are shared by non-sampled tasks
+  long long chk = 0;
+  for (int t = 0; t < n; ++t) {
+    apk_task& d = out[t];
+    d.m = log_uniform_rounded(g, mn_lo, mn_hi, 128);
+    d.n = log_uniform_rounded(g, mn_lo, mn_hi, 128);
+    d.k = log_uniform_rounded(g, k_lo, k_hi, 64);
+    const int tiles_m = (d.m + 255) / 256, tiles_n = d.n / 128;
+    d.a_row0 = (int)(g() % (unsigned long long)(a_rows - tiles_m * 256 + 1));
+    d.a_k0 = uniform_multiple(g, a_cols - d.k, 64);
+    d.b_k0 = uniform_multiple(g, b_rows - d.k, 64);
+    d.b_col0 = uniform_multiple(g, b_cols - d.n, 64);
+    if (t < n_samples) {
+      // disjoint 2048 x 2048 output windows that no other task touches
+      d.c_row0 = c_free_rows + (t / 4) * 2048;
+      d.c_col0 = (t % 4) * 2048;
+      d.flags = 1;
+    } else {
+      d.c_row0 = (int)(g() % (unsigned long long)(c_free_rows - d.m + 1));
+      d.c_col0 = uniform_multiple(g, c_cols - d.n, 64);
+      d.flags = 0;
+    }
+    d.chk_base = chk;
+    chk += (long long)tiles_m * tiles_n;
+  }
+  return chk;
+}
+
+int apk_shard_tasks(const apk_task* tasks, int n, int world, int rank, int* idx) {
+  if (world <= 1) {
+    for (int t = 0; t < n; ++t) idx[t] = t;
+    return n;
+  }
+  std::vector<int> order(n);
+  std::iota(order.begin(), order.end(), 0);
+  auto flops = [&](int t) { return 2.0 * tasks[t].m * tasks[t].n * (double)tasks[t].k; };
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return flops(a) > flops(b); });
+  // least-loaded rank first; ties to the lowest rank
+  using Load = std::pair<double, int>;
+  std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
+  for (int r = 0; r < world; ++r) heap.push({0.0, r});
+  std::vector<int> owner(n);
+  for (int t : order) {
+    Load l = heap.top();
+    heap.pop();
+    owner[t] = l.second;
+    l.first += flops(t);
+    heap.push(l);
+  }
+  int m = 0;
+  for (int t = 0; t < n; ++t)
+    if (owner[t] == rank) idx[m++] = t;
+  return m;
+}
+
+}  // extern "C"

@@ -87,6 +87,7 @@ struct __align__(16) Shared {
   int prod_done;  // producer finished: the control warp may exit
   int consumed;   // stages consumed by the MMA warp (for the in-flight log)
   int epi_cnt[RING];
+  double chk_part[RING][4];  // per-warp sum(c^2) of a task tile
   unsigned long long tiles;
 };
 
@@ -170,8 +171,11 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
     uint32_t P = 0;
     int lastSeen = 0;
     bool ok = true;
+    // One ring slot.  The tag (row0, col0 = output origin of the job; e, item,
+    // task = epilogue bookkeeping) travels with the data; the A rows from ar0
+    // and B columns from bc0 are loaded at k offsets ak / bk.
     auto emit = [&](int kind, int flags, int row0, int col0, int e, int item, unsigned long long task,
-                    const CUtensorMap* tA, const CUtensorMap* tB, int k0) -> bool {
+                    const CUtensorMap* tA, const CUtensorMap* tB, int ar0, int bc0, int ak, int bk) -> bool {
       const int s = P % S;
       if (!bwait(&sh.empty[s], ((P / S) & 1) ^ 1, p, sh)) return false;
       StageTag& t = sh.tag[s];
@@ -185,10 +189,10 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
       if (tA != nullptr) {
         mbar_arrive_expect_tx(&sh.full[s], STAGE_BYTES);
         uint8_t* st = stages + s * STAGE_BYTES;
-        tma_load_2d(st, tA, k0, row0, &sh.full[s]);
-        tma_load_2d(st + A_HALF, tA, k0, row0 + 128, &sh.full[s]);
-        tma_load_2d(st + A_BYTES, tB, col0, k0, &sh.full[s]);
-        tma_load_2d(st + A_BYTES + B_CHUNK, tB, col0 + 64, k0, &sh.full[s]);
+        tma_load_2d(st, tA, ak, ar0, &sh.full[s]);
+        tma_load_2d(st + A_HALF, tA, ak, ar0 + 128, &sh.full[s]);
+        tma_load_2d(st + A_BYTES, tB, bc0, bk, &sh.full[s]);
+        tma_load_2d(st + A_BYTES + B_CHUNK, tB, bc0 + 64, bk, &sh.full[s]);
       } else {
         mbar_arrive(&sh.full[s]);  // control slot: no data
       }
@@ -217,16 +221,18 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
             if (p.ev.ack != nullptr) ack_host(&p.ev.ack[2 * e]);
           }
           if (n == 0 && partial) {
-            if (!emit(T_SUSPEND, 0, 0, 0, 0, 0, 0, nullptr, nullptr, 0)) return -1;
+            if (!emit(T_SUSPEND, 0, 0, 0, 0, 0, 0, nullptr, nullptr, 0, 0, 0, 0)) return -1;
             atomicAdd(p.q.yields, 1ull);
           }
           ++n;
           const int t = it / p.usplit, ks = it % p.usplit;
           const int r0 = (t / p.utiles_n) * BM, c0 = (t % p.utiles_n) * BN;
-          for (int c = 0; c < p.unk; ++c)
+          for (int c = 0; c < p.unk; ++c) {
+            const int kk = (ks * p.unk + c) * BK;
             if (!emit(T_URG, (c == 0 ? F_FIRST : 0) | (c == p.unk - 1 ? F_LAST : 0), r0, c0, e, it, 0, &p.tmAu,
-                      &p.tmBu, (ks * p.unk + c) * BK))
+                      &p.tmBu, r0, c0, kk, kk))
               return -1;
+          }
         }
       }
       return n;
@@ -248,12 +254,34 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
           break;
         }
       if (task >= p.q.num_tasks) break;
-      const int tile = (int)(task % (unsigned long long)p.total_tiles);
-      int tm, tn;
-      tile_coords(tile, p.total_tiles / p.tiles_n, p.tiles_n, RASTER_GROUP, tm, tn);
-      const int row0 = tm * BM, col0 = tn * BN;
+      // job geometry: output origin (row0, col0), operand origins, K steps
+      int row0, col0, ar0, bc0, ak0, bk0, nk, mvalid;
+      unsigned long long tag_task = task;
+      if (p.task_mode) {
+        const unsigned w = p.work[task];
+        const TaskDesc td = p.tasks[w >> 12];
+        const int tm = (w >> 6) & 63, tn = w & 63;
+        row0 = td.c_row0 + tm * BM;
+        col0 = td.c_col0 + tn * BN;
+        ar0 = td.a_row0 + tm * BM;
+        bc0 = td.b_col0 + tn * BN;
+        ak0 = td.a_k0;
+        bk0 = td.b_k0;
+        nk = td.k / BK;
+        mvalid = (td.m - tm * BM) < BM ? (td.m - tm * BM) : BM;
+        tag_task = (unsigned long long)(td.chk_base + (long long)tm * ((td.n + BN - 1) / BN) + tn);
+      } else {
+        const int tile = (int)(task % (unsigned long long)p.total_tiles);
+        int tm, tn;
+        tile_coords(tile, p.total_tiles / p.tiles_n, p.tiles_n, RASTER_GROUP, tm, tn);
+        row0 = ar0 = tm * BM;
+        col0 = bc0 = tn * BN;
+        ak0 = bk0 = 0;
+        nk = p.nk;
+        mvalid = BM;
+      }
       bool resume = false;
-      for (int c = 0; c < p.nk && ok; ++c) {
+      for (int c = 0; c < nk && ok; ++c) {
         if (POLL == POLL_STAGE) {
           const int fs = vload(&sh.gen);
           if (fs < 0) {
@@ -269,12 +297,15 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
             if (n > 0 && c > 0) resume = true;
           }
         }
-        const int flags = (c == 0 ? F_FIRST : 0) | (c == p.nk - 1 ? F_LAST : 0) | (resume ? F_RESUME : 0);
+        const int flags = (c == 0 ? F_FIRST : 0) | (c == nk - 1 ? F_LAST : 0) | (resume ? F_RESUME : 0);
         resume = false;
-        if (!emit(T_BG, flags, row0, col0, 0, 0, task, &p.tmA, &p.tmB, c * BK)) ok = false;
+        // e carries the valid rows of the tile, task the oracle / checksum index
+        if (!emit(T_BG, flags, row0, col0, mvalid, 0, tag_task, &p.tmA, &p.tmB, ar0, bc0, ak0 + c * BK,
+                  bk0 + c * BK))
+          ok = false;
       }
     }
-    emit(T_STOP, 0, 0, 0, 0, 0, 0, nullptr, nullptr, 0);
+    emit(T_STOP, 0, 0, 0, 0, 0, 0, nullptr, nullptr, 0, 0, 0, 0);
     vstore(&sh.prod_done, 1);
     // TMA loads still in flight (only when unwinding) must land before exit
     for (uint32_t q = (uint32_t)vload(&sh.consumed); q < P; ++q)
@@ -399,11 +430,22 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         if (!bwait(&sh.tfull[j.buf], eb[j.buf] & 1, p, sh)) break;
         ++eb[j.buf];
         tc::fence_after_sync();
+        double csum = 0.0;  // task mode: this lane's sum(c^2), fixed order
 #pragma unroll 1
         for (int blk = 0; blk < 8; ++blk) {
+          // rows past the task's m (a 128-row task in a 256-row tile) are
+          // neither stored nor summed
+          if (j.action == E_STORE_C && blk * 32 >= j.e) break;
           uint32_t v[32];
           tc::ld_32x32b_x32(tcol + blk * 32, v);
           tc::wait_ld();
+          if (p.task_mode && j.action == E_STORE_C) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const double x = (double)__uint_as_float(v[i]);
+              csum += x * x;
+            }
+          }
           if (j.action == E_SPILL) {
             float4* s4 = reinterpret_cast<float4*>(slab + (size_t)(blk * 4 + q) * 1024);
 #pragma unroll
@@ -442,6 +484,11 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh.tempty[j.buf]);
         if (j.action != E_SPILL) {
+          if (p.task_mode && j.action == E_STORE_C) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) csum += __shfl_xor_sync(0xffffffffu, csum, o);
+            if (lane == 0) sh.chk_part[sl][q] = csum;
+          }
           // the tile's stores are complete and visible before it is counted;
           // the last of the four epilogue warps to finish does the accounting
           if (lane == 0) bulk_wait_all();
@@ -452,6 +499,9 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
             if (j.action == E_STORE_C) {
               ++sh.tiles;
               if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[j.task], 1);
+              if (p.task_mode)
+                p.chk[j.task] = ((sh.chk_part[sl][0] + sh.chk_part[sl][1]) + sh.chk_part[sl][2]) +
+                                sh.chk_part[sl][3];
               count_trigger(p.ev);
             } else {
               if (ORACLE) atomicAdd(&p.ev.uexec[j.e], 1);

@@ -52,7 +52,20 @@ struct QueueProto {
   unsigned long long* yields;      // checkpoints taken (accumulator spills)
 };
 
-// fp32 CUDA-core persistent SGEMM (tile 128x128, K-tile BK).
+// One heterogeneous background task: C window = A window *
+// B window, each a window of a shared operand pool (so the tensor maps are
+// fixed).  Layout-identical to apk_task in include/apk.h.
+struct TaskDesc {
+  int m, n, k;
+  int a_row0, a_k0;
+  int b_k0, b_col0;
+  int c_row0, c_col0;
+  int flags;
+  long long chk_base;  // checksum index of the task's tile (0,0); tile (tm,tn) at +tm*tiles_n+tn
+};
+
+// Kernel parameters (both kernels; the fp32 kernel ignores tmC/tmCu and the
+// task-mode fields).
 struct F32Params {
   CUtensorMap tmA;   // background A [M][K]  (box BK-slices of 32 x 128 rows, 128B swizzle)
   CUtensorMap tmB;   // background B [K][N]  (box 128 cols x BK rows, no swizzle)
@@ -67,6 +80,12 @@ struct F32Params {
   int ldcu, utiles_n, usplit, unk, uitems;  // unk = stages per urgent item
   float* slab;                         // [grid][16][256] float4 accumulator checkpoints
   long long* slab_hdr;                 // [grid][4]: task, stage cursor, event, valid
+  // task mode (bf16): queue entries index `work` (task << 12 | tm << 6 | tn);
+  // A/B/C maps cover the pools; each finished tile writes sum(c^2) to chk
+  const unsigned* work;
+  const TaskDesc* tasks;
+  double* chk;
+  int task_mode;
   long long wait_limit_ns;
   EventProto ev;
   QueueProto q;

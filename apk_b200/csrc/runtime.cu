@@ -140,6 +140,21 @@ struct apk_ctx {
   size_t exec_cap = 0;
   unsigned long long last_tasks = 0;
   int last_grid = 0;
+
+  // task mode: operand pools, task table, flat work list
+  bool task_mode = false;
+  void *dApool = nullptr, *dBpool = nullptr;
+  float* dCpool = nullptr;
+  bool ownApool = false, ownBpool = false;
+  int a_rows = 0, a_cols = 0, b_rows = 0, b_cols = 0, c_rows = 0, c_cols = 0;
+  TaskDesc* d_tasks = nullptr;
+  unsigned* d_work = nullptr;
+  double* d_chk = nullptr;
+  int n_tasks = 0;
+  unsigned long long n_work = 0;
+  long long n_chk = 0;
+  double task_flops = 0.0;  // sum of 2*m*n*k over installed tasks
+  unsigned long long last_exec_n = 0;  // oracle counters of the last launch
 };
 
 namespace {
@@ -381,6 +396,12 @@ apk_status apk_destroy(apk_ctx* ctx) {
   F(ctx->d_tiles);
   F(ctx->d_utiles);
   F(ctx->d_exec);
+  if (ctx->ownApool) F(ctx->dApool);
+  if (ctx->ownBpool) F(ctx->dBpool);
+  F(ctx->dCpool);
+  F(ctx->d_tasks);
+  F(ctx->d_work);
+  F(ctx->d_chk);
   if (ctx->h_flag) cudaFreeHost(ctx->h_flag);
   if (ctx->h_ack) cudaFreeHost(ctx->h_ack);
   if (ctx->h_gen) cudaFreeHost(ctx->h_gen);
@@ -447,7 +468,101 @@ apk_status apk_set_background(apk_ctx* ctx, const void* A, const void* B, void* 
   ctx->M = M;
   ctx->N = N;
   ctx->K = K;
+  ctx->task_mode = false;
   APK_CU(cudaStreamSynchronize(ctx->kstream));
+  return APK_OK;
+}
+
+apk_status apk_set_task_pool(apk_ctx* ctx, const void* A, int a_rows, int a_cols, const void* B, int b_rows,
+                             int b_cols, int c_rows, int c_cols, apk_mem_kind kind) {
+  if (!ctx || !A || !B) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "set_task_pool while a launch runs");
+  if (ctx->cfg.dtype != APK_BF16) return fail(ctx, APK_EUNSUPPORTED, "task pools need a bf16 context");
+  if (a_rows < 256 || b_rows < 64 || c_rows < 128 || a_cols % 64 || b_cols % 64 || c_cols % 64 || a_cols < 64 ||
+      b_cols < 128 || c_cols < 128)
+    return fail(ctx, APK_EINVAL, "pool dimensions out of range (columns multiples of 64)");
+  APK_CU(cudaSetDevice(ctx->cfg.device));
+  size_t capA = 0, capB = 0;
+  apk_status s;
+  if ((s = upload(ctx, &ctx->dApool, &ctx->ownApool, &capA, A, 2ull * a_rows * a_cols, kind)) != APK_OK) return s;
+  if ((s = upload(ctx, &ctx->dBpool, &ctx->ownBpool, &capB, B, 2ull * b_rows * b_cols, kind)) != APK_OK) return s;
+  if (ctx->dCpool) cudaFree(ctx->dCpool);
+  ctx->dCpool = nullptr;
+  APK_CU(cudaMalloc(&ctx->dCpool, 4ull * c_rows * c_cols));
+  APK_CU(cudaMemsetAsync(ctx->dCpool, 0, 4ull * c_rows * c_cols, ctx->kstream));
+  ctx->a_rows = a_rows;
+  ctx->a_cols = a_cols;
+  ctx->b_rows = b_rows;
+  ctx->b_cols = b_cols;
+  ctx->c_rows = c_rows;
+  ctx->c_cols = c_cols;
+  APK_CU(cudaStreamSynchronize(ctx->kstream));
+  return APK_OK;
+}
+
+apk_status apk_set_tasks(apk_ctx* ctx, const apk_task* tasks, int n, long long n_chk,
+                         unsigned long long* n_work_out) {
+  if (!ctx || !tasks || n <= 0 || n_chk <= 0) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "set_tasks while a launch runs");
+  if (!ctx->dApool) return fail(ctx, APK_ESTATE, "no task pool set");
+  // a work-list entry packs task (20 bits), tile row and tile column (6 each)
+  if ((long long)n > (1ll << 20)) return fail(ctx, APK_EINVAL, "at most 2^20 tasks per context");
+  static_assert(sizeof(apk_task) == sizeof(TaskDesc), "apk_task and TaskDesc must match");
+  std::vector<unsigned> work;
+  double flops = 0.0;
+  for (int t = 0; t < n; ++t) {
+    const apk_task& d = tasks[t];
+    const int tiles_m = (d.m + 255) / 256, tiles_n = d.n / 128;
+    if (d.m <= 0 || d.n <= 0 || d.k <= 0 || d.m % 128 || d.n % 128 || d.k % 64 || d.a_k0 % 64 || d.b_k0 % 64 ||
+        d.b_col0 % 64 || d.c_col0 % 64 || d.a_row0 < 0 || d.a_k0 < 0 || d.b_k0 < 0 || d.b_col0 < 0 ||
+        d.c_row0 < 0 || d.c_col0 < 0 || d.a_row0 + tiles_m * 256 > ctx->a_rows || d.a_k0 + d.k > ctx->a_cols ||
+        d.b_k0 + d.k > ctx->b_rows || d.b_col0 + d.n > ctx->b_cols || d.c_row0 + d.m > ctx->c_rows ||
+        d.c_col0 + d.n > ctx->c_cols || tiles_m > 63 || tiles_n > 63 || d.chk_base < 0 ||
+        d.chk_base + (long long)tiles_m * tiles_n > n_chk)
+      return fail(ctx, APK_EINVAL, "task %d does not fit the pools / checksum array", t);
+    for (int tm = 0; tm < tiles_m; ++tm)
+      for (int tn = 0; tn < tiles_n; ++tn) work.push_back(((unsigned)t << 12) | ((unsigned)tm << 6) | (unsigned)tn);
+    flops += 2.0 * d.m * d.n * (double)d.k;
+  }
+  APK_CU(cudaSetDevice(ctx->cfg.device));
+  auto F = [](void* p) {
+    if (p) cudaFree(p);
+  };
+  F(ctx->d_tasks);
+  F(ctx->d_work);
+  F(ctx->d_chk);
+  ctx->d_tasks = nullptr;
+  ctx->d_work = nullptr;
+  ctx->d_chk = nullptr;
+  APK_CU(cudaMalloc(&ctx->d_tasks, sizeof(TaskDesc) * n));
+  APK_CU(cudaMalloc(&ctx->d_work, sizeof(unsigned) * work.size()));
+  APK_CU(cudaMalloc(&ctx->d_chk, sizeof(double) * n_chk));
+  APK_CU(cudaMemcpy(ctx->d_tasks, tasks, sizeof(TaskDesc) * n, cudaMemcpyHostToDevice));
+  APK_CU(cudaMemcpy(ctx->d_work, work.data(), sizeof(unsigned) * work.size(), cudaMemcpyHostToDevice));
+  ctx->n_tasks = n;
+  ctx->n_work = work.size();
+  ctx->n_chk = n_chk;
+  ctx->task_flops = flops;
+  ctx->task_mode = true;
+  if (n_work_out) *n_work_out = ctx->n_work;
+  return APK_OK;
+}
+
+apk_status apk_read_checksums(apk_ctx* ctx, double* chk, long long n) {
+  if (!ctx || !chk || n <= 0) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "launch still running");
+  if (!ctx->d_chk || n > ctx->n_chk) return fail(ctx, APK_EINVAL, "no checksum array of that size");
+  APK_CU(cudaMemcpy(chk, ctx->d_chk, sizeof(double) * n, cudaMemcpyDeviceToHost));
+  return APK_OK;
+}
+
+apk_status apk_read_pool_window(apk_ctx* ctx, int row0, int col0, int rows, int cols, float* out) {
+  if (!ctx || !out || !ctx->dCpool || row0 < 0 || col0 < 0 || rows <= 0 || cols <= 0 ||
+      row0 + rows > ctx->c_rows || col0 + cols > ctx->c_cols)
+    return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "launch still running");
+  APK_CU(cudaMemcpy2D(out, sizeof(float) * cols, ctx->dCpool + (size_t)row0 * ctx->c_cols + col0,
+                      sizeof(float) * ctx->c_cols, sizeof(float) * cols, rows, cudaMemcpyDeviceToHost));
   return APK_OK;
 }
 
@@ -565,16 +680,22 @@ apk_status reset_logs(apk_ctx* ctx, unsigned long long num_tasks) {
   if (ctx->dCu) APK_CU(cudaMemsetAsync(ctx->dCu, 0, sizeof(float) * ctx->cu_slot * (E + 1), s));
   // verification launches pre-fill C with 0xFF bytes (NaN) so a tile that
   // never runs fails loudly (src/persistent.cu:156-160)
-  if (ctx->cfg.oracle && ctx->dC) APK_CU(cudaMemsetAsync(ctx->dC, 0xFF, 4ull * ctx->M * ctx->N, s));
+  if (ctx->cfg.oracle && ctx->dC && !ctx->task_mode)
+    APK_CU(cudaMemsetAsync(ctx->dC, 0xFF, 4ull * ctx->M * ctx->N, s));
+  if (ctx->task_mode) APK_CU(cudaMemsetAsync(ctx->d_chk, 0, sizeof(double) * ctx->n_chk, s));
+  // oracle execution counters: one per queue entry, or in task mode one per
+  // global tile (checksum index) so shards can be unioned
+  const unsigned long long n_exec = ctx->task_mode ? (unsigned long long)ctx->n_chk : num_tasks;
   if (ctx->cfg.oracle && num_tasks != APK_TASKS_UNBOUNDED) {
-    if (ctx->exec_cap < num_tasks) {
+    if (ctx->exec_cap < n_exec) {
       if (ctx->d_exec) cudaFree(ctx->d_exec);
       ctx->d_exec = nullptr;
-      APK_CU(cudaMalloc(&ctx->d_exec, sizeof(int) * num_tasks));
-      ctx->exec_cap = num_tasks;
+      APK_CU(cudaMalloc(&ctx->d_exec, sizeof(int) * n_exec));
+      ctx->exec_cap = n_exec;
     }
-    APK_CU(cudaMemsetAsync(ctx->d_exec, 0, sizeof(int) * num_tasks, s));
+    APK_CU(cudaMemsetAsync(ctx->d_exec, 0, sizeof(int) * n_exec, s));
   }
+  ctx->last_exec_n = n_exec;
   // host-side state
   std::atomic_thread_fence(std::memory_order_seq_cst);
   *reinterpret_cast<volatile int*>(ctx->h_flag) = 0;
@@ -589,12 +710,15 @@ apk_status reset_logs(apk_ctx* ctx, unsigned long long num_tasks) {
 
 apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cudaStream_t stream,
                        bool record) {
-  if (!ctx->dA || !ctx->dB || !ctx->dC) return fail(ctx, APK_ESTATE, "no background operands set");
-  if (!ctx->dAu && poll != APK_POLL_OFF) return fail(ctx, APK_ESTATE, "no urgent operands set");
-  if (ctx->cfg.oracle && num_tasks == APK_TASKS_UNBOUNDED && poll != APK_POLL_OFF) {
-    // unbounded oracle runs still count urgent executions; per-task counts
-    // need a bound
+  if (ctx->task_mode) {
+    if (!ctx->dApool || !ctx->d_work) return fail(ctx, APK_ESTATE, "no tasks installed");
+    if (num_tasks != APK_TASKS_UNBOUNDED && num_tasks > ctx->n_work)
+      return fail(ctx, APK_EINVAL, "task mode drains at most the %llu work items", ctx->n_work);
+    if (num_tasks == APK_TASKS_UNBOUNDED) return fail(ctx, APK_EINVAL, "task mode needs a bounded launch");
+  } else if (!ctx->dA || !ctx->dB || !ctx->dC) {
+    return fail(ctx, APK_ESTATE, "no background operands set");
   }
+  if (!ctx->dAu && poll != APK_POLL_OFF) return fail(ctx, APK_ESTATE, "no urgent operands set");
   apk_status s = reset_logs(ctx, num_tasks);
   if (s != APK_OK) return s;
   int* flag = ctx->cfg.set_mode == APK_SET_HOST_MAPPED ? ctx->d_flag_mapped : &ctx->d_ctrl->flag_dev;
@@ -620,10 +744,15 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
     const int a_box_k = f32 ? 32 : 64, b_box_n = f32 ? 128 : 64;
     const CUtensorMapSwizzle bsw = f32 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B;
     apk_status t;
-    if ((t = make_tmap(ctx, &p.tmA, ctx->dA, dt, es, ctx->M, ctx->K, a_box_k, 128, CU_TENSOR_MAP_SWIZZLE_128B)) !=
-        APK_OK)
+    // task mode: the maps cover the operand pools, tasks are windows of them
+    const bool tk = ctx->task_mode;
+    const void* srcA = tk ? ctx->dApool : ctx->dA;
+    const void* srcB = tk ? ctx->dBpool : ctx->dB;
+    const long long ar = tk ? ctx->a_rows : ctx->M, ac = tk ? ctx->a_cols : ctx->K;
+    const long long br = tk ? ctx->b_rows : ctx->K, bc = tk ? ctx->b_cols : ctx->N;
+    if ((t = make_tmap(ctx, &p.tmA, srcA, dt, es, ar, ac, a_box_k, 128, CU_TENSOR_MAP_SWIZZLE_128B)) != APK_OK)
       return t;
-    if ((t = make_tmap(ctx, &p.tmB, ctx->dB, dt, es, ctx->K, ctx->N, b_box_n, bk, bsw)) != APK_OK) return t;
+    if ((t = make_tmap(ctx, &p.tmB, srcB, dt, es, br, bc, b_box_n, bk, bsw)) != APK_OK) return t;
     if (ctx->dAu) {
       if ((t = make_tmap(ctx, &p.tmAu, ctx->dAu, dt, es, ctx->Mu, ctx->Ku, a_box_k, 128,
                          CU_TENSOR_MAP_SWIZZLE_128B)) != APK_OK)
@@ -635,9 +764,14 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
     }
     // fp32 outputs as 32x32 boxes for the TMA-store epilogue (bf16 path);
     // the urgent slots are one [(max_events+1)*Mu][Nu] array
-    if ((t = make_tmap(ctx, &p.tmC, ctx->dC, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ctx->M, ctx->N, 32, 32,
-                       CU_TENSOR_MAP_SWIZZLE_NONE)) != APK_OK)
+    if (tk) {
+      if ((t = make_tmap(ctx, &p.tmC, ctx->dCpool, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ctx->c_rows, ctx->c_cols, 32,
+                         32, CU_TENSOR_MAP_SWIZZLE_NONE)) != APK_OK)
+        return t;
+    } else if ((t = make_tmap(ctx, &p.tmC, ctx->dC, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ctx->M, ctx->N, 32, 32,
+                              CU_TENSOR_MAP_SWIZZLE_NONE)) != APK_OK) {
       return t;
+    }
     if (ctx->dCu) {
       if ((t = make_tmap(ctx, &p.tmCu, ctx->dCu, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4,
                          (long long)ctx->Mu * (ctx->cfg.max_events + 1), ctx->Nu, 32, 32,
@@ -647,11 +781,23 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
       p.tmCu = p.tmC;
     }
   }
-  p.C = reinterpret_cast<float*>(ctx->dC);
-  p.ldc = ctx->N;
-  p.tiles_n = ctx->N / 128;
-  p.total_tiles = (ctx->M / tm) * (ctx->N / 128);
-  p.nk = ctx->K / bk;
+  if (ctx->task_mode) {
+    p.C = ctx->dCpool;
+    p.ldc = ctx->c_cols;
+    p.tiles_n = 1;
+    p.total_tiles = 1;
+    p.nk = 1;
+    p.task_mode = 1;
+    p.work = ctx->d_work;
+    p.tasks = ctx->d_tasks;
+    p.chk = ctx->d_chk;
+  } else {
+    p.C = reinterpret_cast<float*>(ctx->dC);
+    p.ldc = ctx->N;
+    p.tiles_n = ctx->N / 128;
+    p.total_tiles = (ctx->M / tm) * (ctx->N / 128);
+    p.nk = ctx->K / bk;
+  }
   p.Cu = ctx->dCu;
   p.cu_stride = (long long)ctx->cu_slot;
   p.ldcu = ctx->Nu;
@@ -827,7 +973,8 @@ apk_status apk_read_oracle(apk_ctx* ctx, int* exec_counts, int* uexec_counts) {
   if (exec_counts) {
     if (ctx->last_tasks == APK_TASKS_UNBOUNDED || !ctx->d_exec)
       return fail(ctx, APK_ESTATE, "per-task counts need a bounded launch");
-    APK_CU(cudaMemcpy(exec_counts, ctx->d_exec, sizeof(int) * ctx->last_tasks, cudaMemcpyDeviceToHost));
+    // one counter per queue entry, or per global tile in task mode
+    APK_CU(cudaMemcpy(exec_counts, ctx->d_exec, sizeof(int) * ctx->last_exec_n, cudaMemcpyDeviceToHost));
   }
   if (uexec_counts)
     APK_CU(cudaMemcpy(uexec_counts, ctx->d_uexec, sizeof(int) * ctx->cfg.max_events, cudaMemcpyDeviceToHost));
@@ -846,8 +993,14 @@ apk_status apk_read_run_stats(apk_ctx* ctx, apk_run_stats* st) {
   st->end_ns = (long long)cb.end_max;
   for (auto v : t) st->tiles_done += v;
   st->yields = cb.yields;
-  const double tile_flops = 2.0 * (ctx->cfg.dtype == APK_F32 ? 128.0 * 128.0 : 256.0 * 128.0) * ctx->K;
-  st->bg_flops = tile_flops * (double)st->tiles_done;
+  if (ctx->task_mode) {
+    // tiles differ in size: a complete drain did every task's 2*m*n*k; a
+    // partial one is prorated by tiles
+    st->bg_flops = ctx->n_work ? ctx->task_flops * (double)st->tiles_done / (double)ctx->n_work : 0.0;
+  } else {
+    const double tile_flops = 2.0 * (ctx->cfg.dtype == APK_F32 ? 128.0 * 128.0 : 256.0 * 128.0) * ctx->K;
+    st->bg_flops = tile_flops * (double)st->tiles_done;
+  }
   const double dt = (double)(st->end_ns - st->start_ns) * 1e-9;
   st->bg_tflops = dt > 0 ? st->bg_flops / dt / 1e12 : 0.0;
   st->exited = cb.exited;

@@ -55,6 +55,35 @@ def round_bf16(x: np.ndarray) -> np.ndarray:
     return out
 
 
+# numpy mirror of apk_task (include/apk.h): 10 int32 + int64 = 48 bytes
+TASK_DTYPE = np.dtype([("m", "<i4"), ("n", "<i4"), ("k", "<i4"), ("a_row0", "<i4"), ("a_k0", "<i4"),
+                       ("b_k0", "<i4"), ("b_col0", "<i4"), ("c_row0", "<i4"), ("c_col0", "<i4"),
+                       ("flags", "<i4"), ("chk_base", "<i8")], align=True)
+assert TASK_DTYPE.itemsize == 48
+
+# configs[4] pools: windows of these operand pools (A, B bf16; C fp32)
+POOL = dict(a_rows=4096 + 256, a_cols=4096, b_rows=4096, b_cols=4096, c_rows=4096 + 4096, c_cols=8192)
+
+
+def gen_tasks(n: int, seed: int = 21, mn_lo: int = 128, mn_hi: int = 2048, k_lo: int = 256, k_hi: int = 4096,
+              n_samples: int = 8, pool: dict | None = None):
+    """configs[4] task list (log-uniform m, n in [mn_lo, mn_hi] to x128, k in
+    [k_lo, k_hi] to x64) as windows of the pools; returns (tasks, n_chk)."""
+    pool = pool or POOL
+    out = np.zeros(n, TASK_DTYPE)
+    n_chk = L.load().apk_gen_tasks(seed, n, mn_lo, mn_hi, k_lo, k_hi, pool["a_rows"], pool["a_cols"],
+                                   pool["b_rows"], pool["b_cols"], pool["c_rows"], pool["c_cols"], n_samples,
+                                   _ptr(out))
+    return out, int(n_chk)
+
+
+def shard_tasks(tasks: np.ndarray, world: int, rank: int) -> np.ndarray:
+    """Static LPT shard: this rank's task indices (ascending)."""
+    idx = np.zeros(len(tasks), np.int32)
+    m = L.load().apk_shard_tasks(_ptr(tasks), len(tasks), world, rank, _ptr(idx))
+    return idx[:m].copy()
+
+
 def pinned_empty(shape, dtype) -> np.ndarray:
     """Page-locked host array (freed when the array is garbage collected)."""
     dtype = np.dtype(dtype)
@@ -146,6 +175,30 @@ class Context:
         assert K == K2
         self._check(self._lib.apk_set_urgent(self._h, _ptr(A), _ptr(B), M, N, K, L.APK_MEM_HOST))
         self.Mu, self.Nu, self.Ku = M, N, K
+
+    # ------------------------------------------------------ task queue (cfg 4)
+    def set_task_pool(self, A_pool: np.ndarray, B_pool: np.ndarray, c_rows: int, c_cols: int):
+        self._check(self._lib.apk_set_task_pool(self._h, _ptr(A_pool), A_pool.shape[0], A_pool.shape[1],
+                                                _ptr(B_pool), B_pool.shape[0], B_pool.shape[1], c_rows, c_cols,
+                                                L.APK_MEM_HOST))
+        self.c_pool = (c_rows, c_cols)
+
+    def set_tasks(self, tasks: np.ndarray, n_chk: int) -> int:
+        tasks = np.ascontiguousarray(tasks, TASK_DTYPE)
+        nw = ctypes.c_ulonglong()
+        self._check(self._lib.apk_set_tasks(self._h, _ptr(tasks), len(tasks), n_chk, ctypes.byref(nw)))
+        self.n_chk = n_chk
+        return nw.value
+
+    def read_checksums(self) -> np.ndarray:
+        out = np.zeros(self.n_chk, np.float64)
+        self._check(self._lib.apk_read_checksums(self._h, _ptr(out), self.n_chk))
+        return out
+
+    def read_pool_window(self, row0: int, col0: int, rows: int, cols: int) -> np.ndarray:
+        out = np.empty((rows, cols), np.float32)
+        self._check(self._lib.apk_read_pool_window(self._h, row0, col0, rows, cols, _ptr(out)))
+        return out
 
     # ---------------------------------------------------------------- launch
     def schedule_device_events(self, offsets_ns):

@@ -191,6 +191,7 @@ apk_status apk_read_events(apk_ctx* ctx, apk_event_log* log);
 
 /* Exactly-once scheduler verdict inputs (src/yield.cu:576-667).
  * exec_counts: one int per background task id of the last bounded launch
+ * -- in task mode one per global tile (checksum index, n_chk ints) --
  * (requires cfg.oracle); uexec_counts: max_events ints. */
 apk_status apk_read_oracle(apk_ctx* ctx, int* exec_counts, int* uexec_counts);
 
@@ -276,6 +277,62 @@ apk_status apk_run_overhead(apk_ctx* ctx, unsigned long long num_tasks, int reps
  * drain.  Per trial: host arrival -> urgent done (host clock, us). */
 apk_status apk_run_baseline(apk_ctx* ctx, unsigned long long num_tasks, int trials, unsigned seed,
                             double* e2e_us);
+
+/* ---- heterogeneous task queue (configs[4], bf16 contexts) -------------- */
+
+/* One background GEMM task: C window = A window * B window, each a window
+ * of a shared operand pool (so 2^20 tasks need no private matrices).
+ * m, n multiples of 128 (an odd multiple of 128 rows runs half of its last
+ * 256-row tile: the A pool must hold 128 rows past such a window), k a
+ * multiple of 64; a_k0, b_k0, b_col0 and c_col0 multiples of 64 (TMA
+ * alignment), row offsets free.  chk_base: index of the task's first tile
+ * in the checksum array (tile (tm,tn) at chk_base + tm*ceil(n/128) + tn),
+ * global across shards so a shard's checksums land where an unsharded run
+ * puts them.  No reference counterpart: the reference queues identical
+ * tiles of one GEMM (src/urgent_baseline.cu:78-83). */
+typedef struct apk_task {
+  int m, n, k;
+  int a_row0, a_k0;
+  int b_k0, b_col0;
+  int c_row0, c_col0;
+  int flags;
+  long long chk_base;
+} apk_task;
+
+/* Operand pools of a bf16 context: A [a_rows][a_cols] bf16, B [b_rows][b_cols]
+ * bf16, C [c_rows][c_cols] fp32 (task outputs land in their windows). */
+apk_status apk_set_task_pool(apk_ctx* ctx, const void* A, int a_rows, int a_cols, const void* B, int b_rows,
+                             int b_cols, int c_rows, int c_cols, apk_mem_kind kind);
+
+/* Install n tasks (checked against the pools) and build the flat tile work
+ * list the persistent queue drains; n_chk = size of the checksum array.
+ * The next apk_launch(ctx, n_work) runs task mode (n_work from *n_work_out);
+ * apk_set_background switches back. */
+apk_status apk_set_tasks(apk_ctx* ctx, const apk_task* tasks, int n, long long n_chk,
+                         unsigned long long* n_work_out);
+
+/* Per-tile checksums sum(c^2) (float64, fixed summation order) of the last
+ * task-mode launch; untouched entries read 0. */
+apk_status apk_read_checksums(apk_ctx* ctx, double* chk, long long n);
+
+/* Copy a window of the C pool to host memory (rows x cols fp32). */
+apk_status apk_read_pool_window(apk_ctx* ctx, int row0, int col0, int rows, int cols, float* out);
+
+/* configs[4] generator: n tasks, m and n log-uniform in [mn_lo, mn_hi]
+ * rounded to multiples of 128, k log-uniform in [k_lo, k_hi] rounded to
+ * multiples of 64, windows placed at seeded offsets inside the pools;
+ * chk_base is the running tile count.  The first n_samples tasks get
+ * disjoint C windows in rows [c_rows - 2048*ceil(n_samples/4), c_rows) so
+ * their outputs survive the run; every other task writes rows below that.
+ * Returns the total tile count (the checksum array size). */
+long long apk_gen_tasks(unsigned long long seed, int n, int mn_lo, int mn_hi, int k_lo, int k_hi, int a_rows,
+                        int a_cols, int b_rows, int b_cols, int c_rows, int c_cols, int n_samples,
+                        apk_task* out);
+
+/* Static LPT shard of tasks over world ranks by 2*m*n*k (ties by task id):
+ * writes this rank's task indices to idx (ascending) and returns their
+ * count.  Deterministic, disjoint, and the ranks' union is every task. */
+int apk_shard_tasks(const apk_task* tasks, int n, int world, int rank, int* idx);
 
 /* ---- allocation-free entry point --------------------------------------- */
 
