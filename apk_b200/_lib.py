@@ -57,7 +57,7 @@ class RunStats(ctypes.Structure):
 
 class LatencyConfig(ctypes.Structure):
     _fields_ = [("events", c_int), ("period_ns", c_ll), ("seed", c_uint), ("warmup_events", c_int),
-                ("settle_ns", c_ll), ("bg_tasks", c_ull), ("probe_reps", c_int)]
+                ("settle_ns", c_ll), ("bg_tasks", c_ull), ("probe_reps", c_int), ("poisson", c_int)]
 
 
 class LatencyResult(ctypes.Structure):

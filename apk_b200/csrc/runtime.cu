@@ -1131,8 +1131,17 @@ apk_status apk_run_latency(apk_ctx* ctx, const apk_latency_config* lc, apk_laten
   std::mt19937 rng(lc->seed);
   std::uniform_real_distribution<double> u01(0.0, 1.0);
   std::vector<long long> when(E);
-  for (int e = 0; e < E; ++e)
-    when[e] = lc->settle_ns + (long long)e * lc->period_ns + (long long)(u01(rng) * lc->period_ns);
+  if (lc->poisson) {
+    // exponential gaps with mean period_ns (inverse-CDF of a uniform draw)
+    double t = (double)lc->settle_ns;
+    for (int e = 0; e < E; ++e) {
+      t += -std::log(1.0 - u01(rng)) * (double)lc->period_ns;
+      when[e] = (long long)t;
+    }
+  } else {
+    for (int e = 0; e < E; ++e)
+      when[e] = lc->settle_ns + (long long)e * lc->period_ns + (long long)(u01(rng) * lc->period_ns);
+  }
   apk_status s;
   double offset = 0.0;
   const bool host_set = ctx->cfg.set_mode != APK_SET_DEVICE;

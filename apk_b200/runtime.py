@@ -295,12 +295,15 @@ class Context:
 
     # ---------------------------------------------------------------- modes
     def run_latency(self, events: int, period_us: float = 1000.0, seed: int = 21, warmup_events: int = 0,
-                    settle_ms: float = 20.0, bg_tasks: int = 0, probe_reps: int = 64) -> dict:
+                    settle_ms: float = 20.0, bg_tasks: int = 0, probe_reps: int = 64,
+                    poisson: bool = False) -> dict:
         """bg_tasks = 0: unbounded launch stopped after the last event;
         bg_tasks > 0: a bounded launch that ends by itself.  probe_reps:
-        host-set visibility calibration reps (0 = host round trips only)."""
+        host-set visibility calibration reps (0 = host round trips only).
+        poisson: exponential gaps with mean period_us instead of one arrival
+        per period."""
         lc = L.LatencyConfig(events, int(period_us * 1000), seed, warmup_events, int(settle_ms * 1e6),
-                             int(bg_tasks), int(probe_reps))
+                             int(bg_tasks), int(probe_reps), int(poisson))
         r = L.LatencyResult()
         self._check(self._lib.apk_run_latency(self._h, ctypes.byref(lc), ctypes.byref(r)))
         return {f: getattr(r, f) for f, _ in L.LatencyResult._fields_}

@@ -230,6 +230,9 @@ typedef struct apk_latency_config {
                                before the launch (0 = none: the claim /
                                last_obs / done fields are then NaN and only
                                the rt_* host round trips are reported)     */
+  int poisson;              /* 0: one arrival at a uniform offset in every
+                               period; 1: Poisson arrivals with
+                               mean gap period_ns (configs[4], 2 kHz)      */
 } apk_latency_config;
 
 typedef struct apk_latency_result {
