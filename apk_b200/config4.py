@@ -84,6 +84,7 @@ def main():
         n_inj = ev["n_injected"]
         claimed = int(np.count_nonzero(ev["claimer"][:n_inj]))
         outs = [c.read_urgent_output(e) for e in range(n_inj) if ev["claimer"][e]]
+        uitems = (256 // c.info["tile_m"]) * (-(-256 // c.info["tile_n"]))
     uchk = [float((o.astype(np.float64) ** 2).sum()) for o in outs]
     urgent_consistent = all(u == uchk[0] for u in uchk) if uchk else True
     own = np.zeros(n_chk, bool)
@@ -96,7 +97,7 @@ def main():
         "exactly_once_local": bool(np.all(ex0[own] == 1) and np.all(ex0[~own] == 0) and np.all(ex1[own] == 1)),
         "checksums_bitwise": bool(np.array_equal(chk0[own].view(np.uint64), chk1[own].view(np.uint64))),
         "urgent_injected": int(n_inj), "urgent_claimed": claimed, "urgent_consistent": urgent_consistent,
-        "urgent_items_exact": bool(all(ue[e] == 2 for e in range(n_inj) if ev["claimer"][e])),
+        "urgent_items_exact": bool(all(ue[e] == uitems for e in range(n_inj) if ev["claimer"][e])),
         "yields": int(st1["yields"]),
         "rt_claim_p50_us": r["rt_claim_p50_us"], "rt_claim_p99_us": r["rt_claim_p99_us"],
         "rt_done_p50_us": r["rt_done_p50_us"],

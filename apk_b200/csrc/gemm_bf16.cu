@@ -5,12 +5,21 @@
 // 128x128 tile, 3-stage cp.async, wmma fragments, 8 warps that all compute
 // and all take every checkpoint barrier) with a Blackwell design:
 //
-//   * tile 256x128 (two M=128 tcgen05.mma accumulators, N=128), K-tile 64,
-//     4-stage TMA ring (48 KB per stage: A as two [128 rows][64 k] boxes and
-//     B as two [64 k][64 n] boxes, all 128-byte swizzled; B is consumed
+//   * output tile 256x256 ("wide" job: two M=128, N=256 tcgen05.mma
+//     accumulators, each one 128-column half of the tile), K-tile 64,
+//     3-stage TMA ring (64 KB per stage: A as two [128 rows][64 k] boxes and
+//     B as four [64 k][64 n] boxes, all 128-byte swizzled; B is consumed
 //     MN-major straight from the row-major [K][N] operand, no transpose).
-//   * fp32 accumulators in TMEM, double-buffered (2 x 256 of the 512
-//     columns) so the epilogue of one job overlaps the MMAs of the next.
+//     A 256-wide tile moves a third fewer operand bytes from L2 into shared
+//     memory per MMA than a 256x128 tile; with the ring's 192 KB unchanged
+//     that took 8192^3 from 1178 to 1455 TFLOPS on one B200, bitwise equal.
+//     A job whose tile ends 128 columns in (an output width that is an odd
+//     multiple of 128) is "narrow": one accumulator, two B boxes.
+//   * fp32 accumulators in TMEM (512 columns = two 256-column buffers).  A
+//     narrow job takes one buffer and alternates, so its epilogue overlaps
+//     the MMAs of the next narrow job; a wide job takes both, so its
+//     epilogue (tcgen05.ld -> TMA store, a few percent of a tile's MMAs)
+//     runs before the next job's first MMA.
 //   * warp roles: 0 producer (queue pops, TMA, urgent mini-queue pops),
 //     1 MMA issuer (one thread issues tcgen05.mma / commit), 2-5 epilogue
 //     (tcgen05.ld -> global; each warp owns one 32-lane TMEM quadrant),
@@ -42,27 +51,28 @@
 namespace apk {
 namespace bf16 {
 
-constexpr int BM = 256, BN = 128, BK = 64, S = 4;
+constexpr int BM = 256, BN = 256, BNH = 128, BK = 64, S = 3;
 constexpr int A_HALF = 128 * BK * 2;             // 16 KB: one [128][64] bf16 box
 constexpr int A_BYTES = 2 * A_HALF;              // 32 KB
 constexpr int B_CHUNK = BK * 64 * 2;             // 8 KB: one [64 k][64 n] box
-constexpr int B_BYTES = 2 * B_CHUNK;             // 16 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 48 KB
+constexpr int B_BYTES = 4 * B_CHUNK;             // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 64 KB (a narrow job loads 48)
 constexpr int NT = 224;                          // 7 warps
 constexpr int STAGE_OUT = 32 * 32 * 4;           // one 32x32 fp32 epilogue block
 constexpr int OUT_BYTES = 4 * 2 * STAGE_OUT;     // 4 epilogue warps x 2 ping-pong buffers
 constexpr int SMEM_BYTES = S * STAGE_BYTES + OUT_BYTES + 1024;
 constexpr int RING = 8;                          // epilogue job ring
 constexpr int RASTER_GROUP = 8;                  // tile-rows per raster group
-// The 256x128 C tile is computed transposed, D = C_tile^T (128 x 256): the
-// MMA's A operand is the [64 k][128 n] B tile (MN-major), its B operand the
-// [256 m][64 k] A tile (K-major).  One M=128, N=256 instruction per 16-deep
-// k-step reads 12 KB of shared memory per 2^19 MACs where two M=128, N=128
-// instructions (one per 128-row half) would read 16 KB.
+// Each 256x128 half of the C tile is computed transposed, D = C_half^T
+// (128 x 256): the MMA's A operand is the half's [64 k][128 n] B columns
+// (MN-major), its B operand the [256 m][64 k] A tile (K-major).  One M=128,
+// N=256 instruction per half and 16-deep k-step reads 12 KB of shared memory
+// per 2^19 MACs where two M=128, N=128 instructions (one per 128-row half)
+// would read 16 KB.
 constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, 256, /*A MN-major*/ true, /*B MN-major*/ false);
 
 enum : int { T_BG = 1, T_URG = 2, T_SUSPEND = 3, T_STOP = 4 };
-enum : int { F_FIRST = 1, F_LAST = 2, F_RESUME = 4 };
+enum : int { F_FIRST = 1, F_LAST = 2, F_RESUME = 4, F_WIDE = 8 };
 enum : int { E_STORE_C = 1, E_STORE_U = 2, E_SPILL = 3, E_RESTORE = 4, E_EXIT = 5 };
 
 struct StageTag {
@@ -70,7 +80,7 @@ struct StageTag {
   unsigned long long task;
 };
 struct EpiJob {
-  int action, buf, row0, col0, e, item;
+  int action, buf, wide, row0, col0, e, item;
   unsigned long long task;
 };
 
@@ -87,7 +97,7 @@ struct __align__(16) Shared {
   int prod_done;  // producer finished: the control warp may exit
   int consumed;   // stages consumed by the MMA warp (for the in-flight log)
   int epi_cnt[RING];
-  double chk_part[RING][4];  // per-warp sum(c^2) of a task tile
+  double chk_part[RING][2][4];  // per-warp sum(c^2) of each 256x128 half of a task tile
   unsigned long long tiles;
 };
 
@@ -173,7 +183,8 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
     bool ok = true;
     // One ring slot.  The tag (row0, col0 = output origin of the job; e, item,
     // task = epilogue bookkeeping) travels with the data; the A rows from ar0
-    // and B columns from bc0 are loaded at k offsets ak / bk.
+    // and B columns from bc0 (256 of them, 128 for a narrow job) are loaded at
+    // k offsets ak / bk.
     auto emit = [&](int kind, int flags, int row0, int col0, int e, int item, unsigned long long task,
                     const CUtensorMap* tA, const CUtensorMap* tB, int ar0, int bc0, int ak, int bk) -> bool {
       const int s = P % S;
@@ -187,12 +198,12 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
       t.item = item;
       t.task = task;
       if (tA != nullptr) {
-        mbar_arrive_expect_tx(&sh.full[s], STAGE_BYTES);
+        const int nb_chunks = (flags & F_WIDE) ? 4 : 2;
+        mbar_arrive_expect_tx(&sh.full[s], A_BYTES + nb_chunks * B_CHUNK);
         uint8_t* st = stages + s * STAGE_BYTES;
         tma_load_2d(st, tA, ak, ar0, &sh.full[s]);
         tma_load_2d(st + A_HALF, tA, ak, ar0 + 128, &sh.full[s]);
-        tma_load_2d(st + A_BYTES, tB, bc0, bk, &sh.full[s]);
-        tma_load_2d(st + A_BYTES + B_CHUNK, tB, bc0 + 64, bk, &sh.full[s]);
+        for (int b = 0; b < nb_chunks; ++b) tma_load_2d(st + A_BYTES + b * B_CHUNK, tB, bc0 + 64 * b, bk, &sh.full[s]);
       } else {
         mbar_arrive(&sh.full[s]);  // control slot: no data
       }
@@ -227,10 +238,11 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
           ++n;
           const int t = it / p.usplit, ks = it % p.usplit;
           const int r0 = (t / p.utiles_n) * BM, c0 = (t % p.utiles_n) * BN;
+          const int wide = c0 + BN <= p.ldcu ? F_WIDE : 0;
           for (int c = 0; c < p.unk; ++c) {
             const int kk = (ks * p.unk + c) * BK;
-            if (!emit(T_URG, (c == 0 ? F_FIRST : 0) | (c == p.unk - 1 ? F_LAST : 0), r0, c0, e, it, 0, &p.tmAu,
-                      &p.tmBu, r0, c0, kk, kk))
+            if (!emit(T_URG, (c == 0 ? F_FIRST : 0) | (c == p.unk - 1 ? F_LAST : 0) | wide, r0, c0, e, it, 0,
+                      &p.tmAu, &p.tmBu, r0, c0, kk, kk))
               return -1;
           }
         }
@@ -254,22 +266,26 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
           break;
         }
       if (task >= p.q.num_tasks) break;
-      // job geometry: output origin (row0, col0), operand origins, K steps
-      int row0, col0, ar0, bc0, ak0, bk0, nk, mvalid;
+      // job geometry: output origin (row0, col0), operand origins, K steps,
+      // width (wide = 256 columns, else 128)
+      int row0, col0, ar0, bc0, ak0, bk0, nk, mvalid, wide;
       unsigned long long tag_task = task;
       if (p.task_mode) {
+        // work entry: task, tile row, first 128-column block (even) of the tile
         const unsigned w = p.work[task];
         const TaskDesc td = p.tasks[w >> 12];
         const int tm = (w >> 6) & 63, tn = w & 63;
         row0 = td.c_row0 + tm * BM;
-        col0 = td.c_col0 + tn * BN;
+        col0 = td.c_col0 + tn * BNH;
         ar0 = td.a_row0 + tm * BM;
-        bc0 = td.b_col0 + tn * BN;
+        bc0 = td.b_col0 + tn * BNH;
         ak0 = td.a_k0;
         bk0 = td.b_k0;
         nk = td.k / BK;
         mvalid = (td.m - tm * BM) < BM ? (td.m - tm * BM) : BM;
-        tag_task = (unsigned long long)(td.chk_base + (long long)tm * ((td.n + BN - 1) / BN) + tn);
+        wide = (tn + 2) * BNH <= td.n ? F_WIDE : 0;
+        // checksum / oracle index of the tile's first 256x128 half
+        tag_task = (unsigned long long)(td.chk_base + (long long)tm * (td.n / BNH) + tn);
       } else {
         const int tile = (int)(task % (unsigned long long)p.total_tiles);
         int tm, tn;
@@ -279,6 +295,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         ak0 = bk0 = 0;
         nk = p.nk;
         mvalid = BM;
+        wide = col0 + BN <= p.ldc ? F_WIDE : 0;
       }
       bool resume = false;
       for (int c = 0; c < nk && ok; ++c) {
@@ -297,7 +314,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
             if (n > 0 && c > 0) resume = true;
           }
         }
-        const int flags = (c == 0 ? F_FIRST : 0) | (c == nk - 1 ? F_LAST : 0) | (resume ? F_RESUME : 0);
+        const int flags = (c == 0 ? F_FIRST : 0) | (c == nk - 1 ? F_LAST : 0) | (resume ? F_RESUME : 0) | wide;
         resume = false;
         // e carries the valid rows of the tile, task the oracle / checksum index
         if (!emit(T_BG, flags, row0, col0, mvalid, 0, tag_task, &p.tmA, &p.tmB, ar0, bc0, ak0 + c * BK,
@@ -312,15 +329,19 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
       bwait_unwind(&sh.full[q % S], (q / S) & 1, p.wait_limit_ns);
   } else if (warp == 1 && lane == 0) {
     // ================================== MMA ===================================
+    // TMEM buffer use: ub[b] counts the jobs that took buffer b (the
+    // epilogue frees it with one tempty phase per job), rb[b] the restores
+    // into it.  cur / cwide: buffer and width of the job being fed.
     uint32_t Q = 0, X = 0, ub[2] = {0, 0}, rb[2] = {0, 0};
-    int nb = 0, cur = 0;
+    int nb = 0, cur = 0, cwide = 0;
     const uint32_t tbase = sh.tmem_base;
-    auto post = [&](int action, int buf, const StageTag& t) -> bool {
+    auto post = [&](int action, int buf, int wide, const StageTag& t) -> bool {
       const int sl = X % RING;
       if (!bwait(&sh.eempty[sl], ((X / RING) & 1) ^ 1, p, sh)) return false;
       EpiJob& j = sh.epi[sl];
       j.action = action;
       j.buf = buf;
+      j.wide = wide;
       j.row0 = t.row0;
       j.col0 = t.col0;
       j.e = t.e;
@@ -335,11 +356,11 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
       if (!bwait(&sh.full[s], (Q / S) & 1, p, sh)) break;
       const StageTag t = sh.tag[s];
       if (t.kind == T_STOP) {
-        post(E_EXIT, 0, t);
+        post(E_EXIT, 0, 0, t);
         break;
       }
       if (t.kind == T_SUSPEND) {
-        if (!post(E_SPILL, cur, t)) break;
+        if (!post(E_SPILL, cur, cwide, t)) break;
         tc::commit(&sh.tfull[cur]);
         mbar_arrive(&sh.empty[s]);
         ++Q;
@@ -347,13 +368,19 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         continue;
       }
       if (t.flags & (F_FIRST | F_RESUME)) {
-        cur = nb;
-        nb ^= 1;
-        if (!bwait(&sh.tempty[cur], (ub[cur] & 1) ^ 1, p, sh)) break;
-        ++ub[cur];
+        // a narrow job takes the next buffer, a wide one both
+        cwide = (t.flags & F_WIDE) ? 1 : 0;
+        cur = cwide ? 0 : nb;
+        nb = cwide ? 0 : nb ^ 1;
+        bool ok = true;
+        for (int b = cur; b <= (cwide ? 1 : cur) && ok; ++b) {
+          ok = bwait(&sh.tempty[b], (ub[b] & 1) ^ 1, p, sh);
+          ++ub[b];
+        }
+        if (!ok) break;
         tc::fence_after_sync();
         if (t.flags & F_RESUME) {
-          if (!post(E_RESTORE, cur, t)) break;
+          if (!post(E_RESTORE, cur, cwide, t)) break;
           if (!bwait(&sh.tres[cur], rb[cur] & 1, p, sh)) break;
           ++rb[cur];
           tc::fence_after_sync();
@@ -371,14 +398,18 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
       for (int kk = 0; kk < BK / 16; ++kk) {
         // MMA A = B tile rows kk*16.. (MN-major: 64-column chunks LBO apart,
         // 8-row groups SBO apart); MMA B = A tile, K-major, 32 B per k-step
-        // inside the 128-byte swizzled rows, 8-row groups 1024 B apart
-        const uint64_t adesc = tc::smem_desc_sw128(sb + kk * 2048, B_CHUNK, 1024);
+        // inside the 128-byte swizzled rows, 8-row groups 1024 B apart.  The
+        // second half of a wide tile reads B chunks 2-3 into buffer 1.
+        const uint32_t acc = (kk > 0 || !(t.flags & F_FIRST)) ? 1u : 0u;
         const uint64_t bdesc = tc::smem_desc_sw128(sa + kk * 32, 16, 1024);
-        tc::mma_bf16(d0, adesc, bdesc, IDESC, (kk > 0 || !(t.flags & F_FIRST)) ? 1u : 0u);
+        tc::mma_bf16(d0, tc::smem_desc_sw128(sb + kk * 2048, B_CHUNK, 1024), bdesc, IDESC, acc);
+        if (cwide)
+          tc::mma_bf16(d0 + 256, tc::smem_desc_sw128(sb + 2 * B_CHUNK + kk * 2048, B_CHUNK, 1024), bdesc, IDESC,
+                       acc);
       }
       tc::commit(&sh.empty[s]);  // frees the slot once these MMAs have read it
       if (t.flags & F_LAST) {
-        if (!post(t.kind == T_BG ? E_STORE_C : E_STORE_U, cur, t)) break;
+        if (!post(t.kind == T_BG ? E_STORE_C : E_STORE_U, cur, cwide, t)) break;
         tc::commit(&sh.tfull[cur]);
       }
       ++Q;
@@ -403,14 +434,19 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         if (lane == 0) mbar_arrive(&sh.eempty[sl]);
         break;
       }
-      // TMEM holds the tile transposed: lane = C column (32q + lane of this
-      // warp's quadrant), column = C row.  Block blk covers C rows
-      // blk*32 .. blk*32+31, one register per row.
+      // TMEM holds each 256x128 half of the tile transposed: lane = C column
+      // (32q + lane of this warp's quadrant, plus 128 in the second half),
+      // column = C row.  Block (hh, blk) covers C rows blk*32 .. blk*32+31 of
+      // half hh, one register per row; a wide job's second half sits in the
+      // next 256 TMEM columns.
       const uint32_t tcol = tbase + ((uint32_t)(32 * q) << 16) + (uint32_t)j.buf * 256;
+      const int nh = j.wide ? 2 : 1;
+      auto slab_blk = [&](int hh, int blk) { return slab + (size_t)((hh * 8 + blk) * 4 + q) * 1024; };
       if (j.action == E_RESTORE) {
 #pragma unroll 1
-        for (int blk = 0; blk < 8; ++blk) {
-          const float4* s4 = reinterpret_cast<const float4*>(slab + (size_t)(blk * 4 + q) * 1024);
+        for (int bb = 0; bb < 8 * nh; ++bb) {
+          const int hh = bb >> 3, blk = bb & 7;
+          const float4* s4 = reinterpret_cast<const float4*>(slab_blk(hh, blk));
           uint32_t v[32];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
@@ -420,7 +456,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
             v[4 * i + 2] = __float_as_uint(x.z);
             v[4 * i + 3] = __float_as_uint(x.w);
           }
-          tc::st_32x32b_x32(tcol + blk * 32, v);
+          tc::st_32x32b_x32(tcol + hh * 256 + blk * 32, v);
         }
         tc::wait_st();
         tc::fence_before_sync();
@@ -430,24 +466,26 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         if (!bwait(&sh.tfull[j.buf], eb[j.buf] & 1, p, sh)) break;
         ++eb[j.buf];
         tc::fence_after_sync();
-        double csum = 0.0;  // task mode: this lane's sum(c^2), fixed order
+        double csum[2] = {0.0, 0.0};  // task mode: this lane's sum(c^2) per half, fixed order
+        int nst = 0;                  // bulk stores issued for this job (staging ping-pong)
 #pragma unroll 1
-        for (int blk = 0; blk < 8; ++blk) {
+        for (int bb = 0; bb < 8 * nh; ++bb) {
+          const int hh = bb >> 3, blk = bb & 7;
           // rows past the task's m (a 128-row task in a 256-row tile) are
           // neither stored nor summed
-          if (j.action == E_STORE_C && blk * 32 >= j.e) break;
+          if (j.action == E_STORE_C && blk * 32 >= j.e) continue;
           uint32_t v[32];
-          tc::ld_32x32b_x32(tcol + blk * 32, v);
+          tc::ld_32x32b_x32(tcol + hh * 256 + blk * 32, v);
           tc::wait_ld();
           if (p.task_mode && j.action == E_STORE_C) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               const double x = (double)__uint_as_float(v[i]);
-              csum += x * x;
+              csum[hh] += x * x;
             }
           }
           if (j.action == E_SPILL) {
-            float4* s4 = reinterpret_cast<float4*>(slab + (size_t)(blk * 4 + q) * 1024);
+            float4* s4 = reinterpret_cast<float4*>(slab_blk(hh, blk));
 #pragma unroll
             for (int i = 0; i < 8; ++i)
               s4[i * 32 + lane] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
@@ -458,8 +496,8 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
             // conflict-free 128-byte row per store) and hand it to the TMA
             // engine: a tensor store for C / urgent slots, a reduce-add for
             // split-K urgent items.
-            float* ob = out_stage + (2 * q + (blk & 1)) * (STAGE_OUT / 4);
-            if (blk >= 2) {
+            float* ob = out_stage + (2 * q + (nst & 1)) * (STAGE_OUT / 4);
+            if (nst >= 2) {
               if (lane == 0) bulk_wait_read<1>();  // this buffer's previous store has read it
               __syncwarp();
             }
@@ -468,7 +506,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              const int x = j.col0 + 32 * q;
+              const int x = j.col0 + BNH * hh + 32 * q;
               if (j.action == E_STORE_C) {
                 tma_store_2d(&p.tmC, x, j.row0 + blk * 32, ob);
               } else {
@@ -478,16 +516,23 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
               }
               bulk_commit();
             }
+            ++nst;
           }
         }
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sh.tempty[j.buf]);
+        if (lane == 0) {
+          mbar_arrive(&sh.tempty[j.buf]);
+          if (j.wide) mbar_arrive(&sh.tempty[1]);  // a wide job held both buffers (buf 0 and 1)
+        }
         if (j.action != E_SPILL) {
           if (p.task_mode && j.action == E_STORE_C) {
+            for (int hh = 0; hh < nh; ++hh) {
+              double s = csum[hh];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) csum += __shfl_xor_sync(0xffffffffu, csum, o);
-            if (lane == 0) sh.chk_part[sl][q] = csum;
+              for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+              if (lane == 0) sh.chk_part[sl][hh][q] = s;
+            }
           }
           // the tile's stores are complete and visible before it is counted;
           // the last of the four epilogue warps to finish does the accounting
@@ -497,11 +542,19 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
           if (lane == 0 && atomicAdd(&sh.epi_cnt[sl], 1) == 3) {
             sh.epi_cnt[sl] = 0;
             if (j.action == E_STORE_C) {
-              ++sh.tiles;
-              if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[j.task], 1);
-              if (p.task_mode)
-                p.chk[j.task] = ((sh.chk_part[sl][0] + sh.chk_part[sl][1]) + sh.chk_part[sl][2]) +
-                                sh.chk_part[sl][3];
+              if (p.task_mode) {
+                // task mode counts and checksums each 256x128 half
+                for (int hh = 0; hh < nh; ++hh) {
+                  ++sh.tiles;
+                  if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[j.task + hh], 1);
+                  p.chk[j.task + hh] = ((sh.chk_part[sl][hh][0] + sh.chk_part[sl][hh][1]) +
+                                        sh.chk_part[sl][hh][2]) +
+                                       sh.chk_part[sl][hh][3];
+                }
+              } else {
+                ++sh.tiles;
+                if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[j.task], 1);
+              }
               count_trigger(p.ev);
             } else {
               if (ORACLE) atomicAdd(&p.ev.uexec[j.e], 1);

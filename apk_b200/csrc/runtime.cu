@@ -152,6 +152,7 @@ struct apk_ctx {
   double* d_chk = nullptr;
   int n_tasks = 0;
   unsigned long long n_work = 0;
+  unsigned long long n_halves = 0;  // 256x128 halves of all work tiles (the kernel's task-mode tile count)
   long long n_chk = 0;
   double task_flops = 0.0;  // sum of 2*m*n*k over installed tasks
   unsigned long long last_exec_n = 0;  // oracle counters of the last launch
@@ -207,6 +208,12 @@ apk_status make_tmap(apk_ctx* ctx, CUtensorMap* tm, const void* base, CUtensorMa
 }
 
 size_t esize_of(apk_dtype d) { return d == APK_BF16 ? 2 : 4; }
+
+// Output tiles: fp32 128x128; bf16 256 rows by 256 columns, the last tile of
+// a row 128 wide when the width is an odd multiple of 128.
+int tile_rows(const apk_ctx* ctx) { return ctx->cfg.dtype == APK_F32 ? 128 : 256; }
+int tile_cols(const apk_ctx* ctx) { return ctx->cfg.dtype == APK_F32 ? 128 : 256; }
+int tiles_across(const apk_ctx* ctx, int n) { return (n + tile_cols(ctx) - 1) / tile_cols(ctx); }
 
 apk_status upload(apk_ctx* ctx, void** dst, bool* own, size_t* cap, const void* src, size_t bytes,
                   apk_mem_kind kind) {
@@ -349,8 +356,8 @@ apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
   APK_CU(cudaMalloc(&ctx->d_uq, sizeof(int) * E));
   APK_CU(cudaMalloc(&ctx->d_udone, sizeof(int) * E));
   APK_CU(cudaMalloc(&ctx->d_uexec, sizeof(int) * E));
-  // checkpoint slab: fp32 128x128 fp32 accumulators (64 KB), bf16 256x128 (128 KB)
-  const size_t slab_floats = (c.dtype == APK_F32 ? 128 * 128 : 256 * 128);
+  // checkpoint slab: fp32 128x128 fp32 accumulators (64 KB), bf16 256x256 (256 KB)
+  const size_t slab_floats = (c.dtype == APK_F32 ? 128 * 128 : 256 * 256);
   APK_CU(cudaMalloc(&ctx->d_slab, sizeof(float) * slab_floats * G));
   APK_CU(cudaMalloc(&ctx->d_slab_hdr, sizeof(long long) * 4 * G));
   APK_CU(cudaMalloc(&ctx->d_tiles, sizeof(unsigned long long) * G));
@@ -433,8 +440,8 @@ apk_status apk_get_info(apk_ctx* ctx, apk_device_info* info) {
     info->smem_per_cta = bf16::smem_bytes();
     info->threads_per_cta = bf16::threads();
     info->tile_m = 256;
-    info->tile_n = 128;
-    info->stages = 4;
+    info->tile_n = 256;
+    info->stages = 3;
   }
   info->k_tile = ctx->cfg.k_tile;
   snprintf(info->name, sizeof info->name, "%s", ctx->name);
@@ -505,11 +512,15 @@ apk_status apk_set_tasks(apk_ctx* ctx, const apk_task* tasks, int n, long long n
   if (!ctx || !tasks || n <= 0 || n_chk <= 0) return APK_EINVAL;
   if (ctx->running) return fail(ctx, APK_ESTATE, "set_tasks while a launch runs");
   if (!ctx->dApool) return fail(ctx, APK_ESTATE, "no task pool set");
-  // a work-list entry packs task (20 bits), tile row and tile column (6 each)
+  // a work-list entry packs task (20 bits), tile row and the tile's first
+  // 128-column block (6 bits each); a tile is 256x256, or 256x128 where the
+  // task's n ends 128 columns into it.  Checksums and oracle counters are
+  // kept per 256x128 half (chk_base + tile_row * n/128 + block).
   if ((long long)n > (1ll << 20)) return fail(ctx, APK_EINVAL, "at most 2^20 tasks per context");
   static_assert(sizeof(apk_task) == sizeof(TaskDesc), "apk_task and TaskDesc must match");
   std::vector<unsigned> work;
   double flops = 0.0;
+  unsigned long long halves = 0;
   for (int t = 0; t < n; ++t) {
     const apk_task& d = tasks[t];
     const int tiles_m = (d.m + 255) / 256, tiles_n = d.n / 128;
@@ -521,8 +532,9 @@ apk_status apk_set_tasks(apk_ctx* ctx, const apk_task* tasks, int n, long long n
         d.chk_base + (long long)tiles_m * tiles_n > n_chk)
       return fail(ctx, APK_EINVAL, "task %d does not fit the pools / checksum array", t);
     for (int tm = 0; tm < tiles_m; ++tm)
-      for (int tn = 0; tn < tiles_n; ++tn) work.push_back(((unsigned)t << 12) | ((unsigned)tm << 6) | (unsigned)tn);
+      for (int tn = 0; tn < tiles_n; tn += 2) work.push_back(((unsigned)t << 12) | ((unsigned)tm << 6) | (unsigned)tn);
     flops += 2.0 * d.m * d.n * (double)d.k;
+    halves += (unsigned long long)tiles_m * tiles_n;
   }
   APK_CU(cudaSetDevice(ctx->cfg.device));
   auto F = [](void* p) {
@@ -541,6 +553,7 @@ apk_status apk_set_tasks(apk_ctx* ctx, const apk_task* tasks, int n, long long n
   APK_CU(cudaMemcpy(ctx->d_work, work.data(), sizeof(unsigned) * work.size(), cudaMemcpyHostToDevice));
   ctx->n_tasks = n;
   ctx->n_work = work.size();
+  ctx->n_halves = halves;
   ctx->n_chk = n_chk;
   ctx->task_flops = flops;
   ctx->task_mode = true;
@@ -732,7 +745,7 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
   if (record) APK_CU(cudaEventRecord(ctx->ev_start, stream));
   const bool f32 = ctx->cfg.dtype == APK_F32;
   const int bk = ctx->cfg.k_tile;
-  const int tm = f32 ? 128 : 256;  // output tile rows (fp32 128x128, bf16 256x128)
+  const int tm = tile_rows(ctx);
   F32Params p;
   memset(&p, 0, sizeof p);
   {
@@ -794,17 +807,17 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
   } else {
     p.C = reinterpret_cast<float*>(ctx->dC);
     p.ldc = ctx->N;
-    p.tiles_n = ctx->N / 128;
-    p.total_tiles = (ctx->M / tm) * (ctx->N / 128);
+    p.tiles_n = tiles_across(ctx, ctx->N);
+    p.total_tiles = (ctx->M / tm) * p.tiles_n;
     p.nk = ctx->K / bk;
   }
   p.Cu = ctx->dCu;
   p.cu_stride = (long long)ctx->cu_slot;
   p.ldcu = ctx->Nu;
-  p.utiles_n = ctx->Nu / 128;
+  p.utiles_n = tiles_across(ctx, ctx->Nu);
   p.usplit = ctx->cfg.urgent_split_k;
   p.unk = ctx->Ku ? ctx->Ku / bk / p.usplit : 0;
-  p.uitems = (ctx->Mu / tm) * (ctx->Nu / 128) * p.usplit;
+  p.uitems = (ctx->Mu / tm) * p.utiles_n * p.usplit;
   p.slab = ctx->d_slab;
   p.slab_hdr = ctx->d_slab_hdr;
   p.wait_limit_ns = ctx->cfg.wait_limit_ns;
@@ -995,11 +1008,12 @@ apk_status apk_read_run_stats(apk_ctx* ctx, apk_run_stats* st) {
   st->yields = cb.yields;
   if (ctx->task_mode) {
     // tiles differ in size: a complete drain did every task's 2*m*n*k; a
-    // partial one is prorated by tiles
-    st->bg_flops = ctx->n_work ? ctx->task_flops * (double)st->tiles_done / (double)ctx->n_work : 0.0;
+    // partial one is prorated by the 256x128 halves it completed
+    st->bg_flops = ctx->n_halves ? ctx->task_flops * (double)st->tiles_done / (double)ctx->n_halves : 0.0;
   } else {
-    const double tile_flops = 2.0 * (ctx->cfg.dtype == APK_F32 ? 128.0 * 128.0 : 256.0 * 128.0) * ctx->K;
-    st->bg_flops = tile_flops * (double)st->tiles_done;
+    // the average tile (bf16 tiles at the right edge may be 128 wide)
+    const double tiles = (double)(ctx->M / tile_rows(ctx)) * tiles_across(ctx, ctx->N);
+    st->bg_flops = tiles > 0 ? 2.0 * ctx->M * ctx->N * (double)ctx->K / tiles * (double)st->tiles_done : 0.0;
   }
   const double dt = (double)(st->end_ns - st->start_ns) * 1e-9;
   st->bg_tflops = dt > 0 ? st->bg_flops / dt / 1e12 : 0.0;
@@ -1039,8 +1053,7 @@ apk_status apk_gemm(apk_ctx* ctx, const void* A, const void* B, void* C, int M, 
   ctx->M = M;
   ctx->N = N;
   ctx->K = K;
-  const unsigned long long tiles =
-      (unsigned long long)(M / (ctx->cfg.dtype == APK_F32 ? 128 : 256)) * (N / 128);
+  const unsigned long long tiles = (unsigned long long)(M / tile_rows(ctx)) * tiles_across(ctx, N);
   const int poll = ctx->dAu ? (int)ctx->cfg.poll : APK_POLL_OFF;
   if ((s = launch_impl(ctx, tiles, poll, ctx->kstream, true)) != APK_OK) return s;
   ctx->running = true;

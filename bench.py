@@ -243,10 +243,12 @@ def device_set_latency(apk_b200, np, dev, A, B, Au, Bu, bg_tasks, events=200):
 
 
 def bf16_config2(apk_b200, np, dev):
-    """bf16 8192^3, N(0,1) rounded to bf16, 256x128 tiles,
-    K-tile 64, 4-stage TMA ring: throughput of the uninterrupted drain, then a
-    drain with device-set yields at random pipeline stages whose output must
-    be bitwise identical to the uninterrupted one."""
+    """bf16 8192^3, N(0,1) rounded to bf16, K-tile 64 (the
+    reference's shape is 256x128 tiles in a 4-stage ring; this kernel runs
+    256x256 tiles in a 3-stage ring of the same 192 KB): throughput of the
+    uninterrupted drain, then a drain with device-set yields at random
+    pipeline stages whose output must be bitwise identical to the
+    uninterrupted one."""
     n = 8192
     A = apk_b200.fill_normal_bf16((n, n), 21)
     B = apk_b200.fill_normal_bf16((n, n), 22)
@@ -266,7 +268,8 @@ def bf16_config2(apk_b200, np, dev):
         c.set_background(A, B)
         c.set_urgent(Au, Bu)
         c.schedule_device_events((np.arange(nev, dtype=np.int64) + 1) * 25_000)
-        c.launch((n // 256) * (n // 128))
+        info = c.info
+        c.launch((n // info["tile_m"]) * (n // info["tile_n"]))
         c.wait(60)
         C = c.read_output()
         ev = c.read_events()

@@ -107,7 +107,9 @@ typedef struct apk_device_info {
   int cc_major, cc_minor;
   int smem_per_cta;
   int threads_per_cta;
-  int tile_m, tile_n, k_tile, stages;
+  int tile_m, tile_n, k_tile, stages; /* output tile: fp32 128x128; bf16 256x256
+                                         (the last tile of a row 128 wide when
+                                         N is an odd multiple of 128)          */
   char name[128];
 } apk_device_info;
 apk_status apk_get_info(apk_ctx* ctx, apk_device_info* info);
@@ -197,9 +199,10 @@ apk_status apk_read_oracle(apk_ctx* ctx, int* exec_counts, int* uexec_counts);
 
 typedef struct apk_run_stats {
   long long start_ns, end_ns;        /* first CTA start / last CTA exit       */
-  unsigned long long tiles_done;     /* completed background tiles            */
+  unsigned long long tiles_done;     /* completed background tiles (task mode:
+                                        256x128 halves of tiles)              */
   unsigned long long yields;         /* checkpoints (accumulator spills)      */
-  double bg_flops;                   /* tiles_done * 2 * tile_m * tile_n * K  */
+  double bg_flops;                   /* tiles_done * 2*M*N*K / tiles; task mode: prorated by 256x128 halves */
   double bg_tflops;                  /* bg_flops / (end - start)              */
   int exited;                        /* CTAs that exited                      */
   int device_status;                 /* 0 or the first device error code      */

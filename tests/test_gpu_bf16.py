@@ -79,7 +79,8 @@ def _yield_run(poll, nev=30, gap_ns=20_000, discipline="drain"):
         ex, ue = c.read_oracle(ntasks)
         fired = int(np.count_nonzero(ev["set_ns"][:nev]))
         outs = [c.read_urgent_output(e) for e in range(fired) if ev["claimer"][e]]
-        uitems = 2 * c.cfg.urgent_split_k
+        info = c.info
+        uitems = (256 // info["tile_m"]) * (-(-256 // info["tile_n"])) * c.cfg.urgent_split_k
     refu = oracle.gemm_f64_bf16_rows(Au, Bu, 0, 256)
     return dict(C=C, Cref=Cref, ev=ev, st=st, ex=ex, ue=ue, fired=fired, outs=outs, refu=refu, uitems=uitems)
 
@@ -157,7 +158,45 @@ def test_split_k_urgent_items(libapk):
         ev = c.read_events()
         outs = [c.read_urgent_output(e) for e in range(3) if ev["claimer"][e]]
         _, ue = c.read_oracle(512)
+        items = (256 // c.info["tile_m"]) * (-(-256 // c.info["tile_n"])) * 4
     assert outs
     for Cu in outs:
         assert oracle.check(Cu, refu, TOL)[1] == 0
-    assert all(ue[e] == 8 for e in range(3) if ev["claimer"][e])
+    assert all(ue[e] == items for e in range(3) if ev["claimer"][e])
+
+
+def test_narrow_edge_tiles_yield_bitwise(libapk):
+    """Widths that are odd multiples of 128 end each tile row with a 256x128
+    tile (one TMEM accumulator) after 256x256 ones (two): stage yields
+    checkpoint and resume both kinds bitwise; a 384-wide urgent GEMM runs one
+    item of each kind."""
+    M, N, K = 2048, 1152, 8192
+    A, B = _normal((M, K), 41), _normal((K, N), 42)
+    Au, Bu = _normal((256, 256), 43), _normal((256, 384), 44)
+    with _ctx(poll="off") as c:
+        Cref = c.gemm(A, B)
+    _check_rows(Cref, A, B, [(0, 4), (M - 4, 4)])
+    nev = 16
+    with _ctx(poll="stage", set_mode="device", oracle=True) as c:
+        ntasks = 3 * c.info["grid"]
+        c.set_background(A, B)
+        c.set_urgent(Au, Bu)
+        c.schedule_device_events((np.arange(nev, dtype=np.int64) + 1) * 8_000)
+        c.launch(ntasks)
+        c.wait(60)
+        C = c.read_output()
+        ev = c.read_events()
+        st = c.run_stats()
+        ex, ue = c.read_oracle(ntasks)
+        fired = int(np.count_nonzero(ev["set_ns"][:nev]))
+        outs = [c.read_urgent_output(e) for e in range(fired) if ev["claimer"][e]]
+    assert fired >= 8 and st["yields"] > 0
+    assert any(ev["claim_site"][e] > 0 for e in range(fired) if ev["claimer"][e]), "no mid-pipeline claim"
+    assert np.array_equal(C.view(np.uint32), Cref.view(np.uint32)), "resume not bitwise"
+    refu = oracle.gemm_f64_bf16_rows(Au, Bu, 0, 256)
+    assert outs
+    for Cu in outs:
+        mr, bad, nans = oracle.check(Cu, refu, TOL)
+        assert bad == 0 and nans == 0, f"urgent: {bad} bad, max rel {mr:.3e}"
+    v = oracle.exactly_once(ex, ue[:fired], ev["claimer"][:fired], ev["set_ns"][:fired], 2, fired)
+    assert v["pass"], v
