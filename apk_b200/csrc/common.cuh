@@ -173,26 +173,4 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, in
       : "memory");
 }
 
-// TMA store / reduce-add of a box from this CTA's shared memory (bulk-group
-// completion, issued by one thread; wait with bulk_wait_read before the
-// source buffer is rewritten and with bulk_wait_all before the data must be
-// visible).  Coordinates follow the loads: x innermost.
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, int x, int y, const void* src) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tm), "r"(x),
-               "r"(y), "r"(smem_u32(src))
-               : "memory");
-}
-__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* tm, int x, int y, const void* src) {
-  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
-                   tm),
-               "r"(x), "r"(y), "r"(smem_u32(src))
-               : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void bulk_wait_read() {
-  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
 }  // namespace apk

@@ -18,12 +18,13 @@
 //   * fp32 accumulators in TMEM (512 columns = two 256-column buffers).  A
 //     narrow job takes one buffer and alternates, so its epilogue overlaps
 //     the MMAs of the next narrow job; a wide job takes both, so its
-//     epilogue (tcgen05.ld -> TMA store, a few percent of a tile's MMAs)
-//     runs before the next job's first MMA.
+//     epilogue (tcgen05.ld -> global stores, a few percent of a tile's
+//     MMAs) runs before the next job's first MMA.
 //   * warp roles: 0 producer (queue pops, TMA, urgent mini-queue pops),
-//     1 MMA issuer (one thread issues tcgen05.mma / commit), 2-5 epilogue
-//     (tcgen05.ld -> global; each warp owns one 32-lane TMEM quadrant),
-//     6 control (polls the yield flag, runs the device setter).  No
+//     1 MMA issuer (one thread issues tcgen05.mma / commit), 2-9 epilogue
+//     (tcgen05.ld -> global; warp w may access TMEM lane quadrant w%4, so
+//     two warps share each quadrant and take alternate 32-row blocks),
+//     10 control (polls the yield flag, runs the device setter).  No
 //     block-wide barrier per stage: the reference's per-stage checkpoint
 //     barrier pair at 1 CTA/SM cost 14% (results/summary/tc_summary.csv:8-10).
 //   * yield / checkpoint: the producer sees a new generation at a stage
@@ -51,16 +52,29 @@
 namespace apk {
 namespace bf16 {
 
-constexpr int BM = 256, BN = 256, BNH = 128, BK = 64, S = 3;
-constexpr int A_HALF = 128 * BK * 2;             // 16 KB: one [128][64] bf16 box
-constexpr int A_BYTES = 2 * A_HALF;              // 32 KB
-constexpr int B_CHUNK = BK * 64 * 2;             // 8 KB: one [64 k][64 n] box
-constexpr int B_BYTES = 4 * B_CHUNK;             // 32 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 64 KB (a narrow job loads 48)
-constexpr int NT = 224;                          // 7 warps
-constexpr int STAGE_OUT = 32 * 32 * 4;           // one 32x32 fp32 epilogue block
-constexpr int OUT_BYTES = 4 * 2 * STAGE_OUT;     // 4 epilogue warps x 2 ping-pong buffers
-constexpr int SMEM_BYTES = S * STAGE_BYTES + OUT_BYTES + 1024;
+constexpr int BM = 256, BN = 256, BNH = 128;
+constexpr int EPI_WARPS = 8;                     // warps 2-9
+constexpr int CTRL_WARP = 2 + EPI_WARPS;         // warp 10
+constexpr int NT = 32 * (CTRL_WARP + 1);         // 11 warps
+
+// The TMA ring for a K-tile of BK (64 or 32): A as two [128 rows][BK k] boxes
+// (K-major: 128-byte swizzle for BK 64, 64-byte for BK 32, one row = one
+// swizzle span) and B as four [BK k][64 n] boxes (MN-major, 128-byte
+// swizzle).  BK 64: 3 slots of 64 KB; BK 32: 7 slots of 32 KB -- 192 or
+// 224 KB of operands in flight.
+template <int BK>
+struct Ring {
+  static constexpr int S = BK == 64 ? 3 : 7;
+  static constexpr int A_HALF = 128 * BK * 2;            // one [128][BK] bf16 box
+  static constexpr int A_BYTES = 2 * A_HALF;
+  static constexpr int B_CHUNK = BK * 64 * 2;            // one [BK k][64 n] box
+  static constexpr int B_BYTES = 4 * B_CHUNK;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // a narrow job loads A + 2 chunks
+  static constexpr int SMEM_BYTES = S * STAGE_BYTES + 1024;
+  static constexpr uint32_t A_LAYOUT = BK == 64 ? tc::LAYOUT_SW128 : tc::LAYOUT_SW64;
+  static constexpr uint32_t A_SBO = BK * 2 * 8;          // 8 rows of one swizzle span
+};
+constexpr int S_MAX = 7;
 constexpr int RING = 8;                          // epilogue job ring
 constexpr int RASTER_GROUP = 8;                  // tile-rows per raster group
 // Each 256x128 half of the C tile is computed transposed, D = C_half^T
@@ -85,9 +99,9 @@ struct EpiJob {
 };
 
 struct __align__(16) Shared {
-  StageTag tag[S];
+  StageTag tag[S_MAX];
   EpiJob epi[RING];
-  uint64_t full[S], empty[S];
+  uint64_t full[S_MAX], empty[S_MAX];
   uint64_t tfull[2], tempty[2], tres[2];
   uint64_t efull[RING], eempty[RING];
   uint64_t drain;
@@ -97,7 +111,7 @@ struct __align__(16) Shared {
   int prod_done;  // producer finished: the control warp may exit
   int consumed;   // stages consumed by the MMA warp (for the in-flight log)
   int epi_cnt[RING];
-  double chk_part[RING][2][4];  // per-warp sum(c^2) of each 256x128 half of a task tile
+  double chk_part[RING][2][EPI_WARPS];  // per-warp sum(c^2) of each 256x128 half of a task tile
   unsigned long long tiles;
 };
 
@@ -131,8 +145,11 @@ __device__ __noinline__ void bwait_unwind(uint64_t* bar, uint32_t parity, long l
     if (globaltimer_ns() - t0 > limit) return;
 }
 
-template <int POLL, int DISC, bool ORACLE>
+template <int POLL, int DISC, bool ORACLE, int BK>
 __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_constant__ F32Params p) {
+  using R = Ring<BK>;
+  constexpr int S = R::S, A_HALF = R::A_HALF, A_BYTES = R::A_BYTES, B_CHUNK = R::B_CHUNK;
+  constexpr int STAGE_BYTES = R::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ Shared sh;
@@ -147,12 +164,12 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sh.tfull[b], 1);
-      mbar_init(&sh.tempty[b], 4);
-      mbar_init(&sh.tres[b], 4);
+      mbar_init(&sh.tempty[b], EPI_WARPS);
+      mbar_init(&sh.tres[b], EPI_WARPS);
     }
     for (int r = 0; r < RING; ++r) {
       mbar_init(&sh.efull[r], 1);
-      mbar_init(&sh.eempty[r], 4);
+      mbar_init(&sh.eempty[r], EPI_WARPS);
       sh.epi_cnt[r] = 0;
     }
     mbar_init(&sh.drain, 1);
@@ -401,11 +418,11 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         // inside the 128-byte swizzled rows, 8-row groups 1024 B apart.  The
         // second half of a wide tile reads B chunks 2-3 into buffer 1.
         const uint32_t acc = (kk > 0 || !(t.flags & F_FIRST)) ? 1u : 0u;
-        const uint64_t bdesc = tc::smem_desc_sw128(sa + kk * 32, 16, 1024);
-        tc::mma_bf16(d0, tc::smem_desc_sw128(sb + kk * 2048, B_CHUNK, 1024), bdesc, IDESC, acc);
+        const uint64_t bdesc = tc::smem_desc(sa + kk * 32, 16, R::A_SBO, R::A_LAYOUT);
+        tc::mma_bf16(d0, tc::smem_desc(sb + kk * 2048, B_CHUNK, 1024, tc::LAYOUT_SW128), bdesc, IDESC, acc);
         if (cwide)
-          tc::mma_bf16(d0 + 256, tc::smem_desc_sw128(sb + 2 * B_CHUNK + kk * 2048, B_CHUNK, 1024), bdesc, IDESC,
-                       acc);
+          tc::mma_bf16(d0 + 256, tc::smem_desc(sb + 2 * B_CHUNK + kk * 2048, B_CHUNK, 1024, tc::LAYOUT_SW128),
+                       bdesc, IDESC, acc);
       }
       tc::commit(&sh.empty[s]);  // frees the slot once these MMAs have read it
       if (t.flags & F_LAST) {
@@ -418,13 +435,14 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
     // no tcgen05.mma may still run when TMEM is released
     tc::commit(&sh.drain);
     bwait_unwind(&sh.drain, 0, p.wait_limit_ns);
-  } else if (warp >= 2 && warp <= 5) {
+  } else if (warp >= 2 && warp < CTRL_WARP) {
     // ================================ epilogue ================================
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int q = warp & 3;          // TMEM lane quadrant this warp may access
+    const int g = (warp - 2) >> 2;   // which of the quadrant's two warps: 32-row blocks g, g+2, ...
+    const int ew = (warp - 2);       // epilogue warp index (checksum slot)
     uint32_t Y = 0, eb[2] = {0, 0};
     const uint32_t tbase = sh.tmem_base;
     float* slab = p.slab + (size_t)cta * (BM * BN);
-    float* out_stage = reinterpret_cast<float*>(stages + S * STAGE_BYTES);
     while (true) {
       const int sl = Y % RING;
       if (!bwait(&sh.efull[sl], (Y / RING) & 1, p, sh)) break;
@@ -436,15 +454,15 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
       }
       // TMEM holds each 256x128 half of the tile transposed: lane = C column
       // (32q + lane of this warp's quadrant, plus 128 in the second half),
-      // column = C row.  Block (hh, blk) covers C rows blk*32 .. blk*32+31 of
-      // half hh, one register per row; a wide job's second half sits in the
-      // next 256 TMEM columns.
+      // column = C row.  Block bb = (hh, blk) covers C rows blk*32 ..
+      // blk*32+31 of half hh, one register per row; a wide job's second half
+      // sits in the next 256 TMEM columns.
       const uint32_t tcol = tbase + ((uint32_t)(32 * q) << 16) + (uint32_t)j.buf * 256;
       const int nh = j.wide ? 2 : 1;
       auto slab_blk = [&](int hh, int blk) { return slab + (size_t)((hh * 8 + blk) * 4 + q) * 1024; };
       if (j.action == E_RESTORE) {
 #pragma unroll 1
-        for (int bb = 0; bb < 8 * nh; ++bb) {
+        for (int bb = g; bb < 8 * nh; bb += 2) {
           const int hh = bb >> 3, blk = bb & 7;
           const float4* s4 = reinterpret_cast<const float4*>(slab_blk(hh, blk));
           uint32_t v[32];
@@ -467,9 +485,8 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         ++eb[j.buf];
         tc::fence_after_sync();
         double csum[2] = {0.0, 0.0};  // task mode: this lane's sum(c^2) per half, fixed order
-        int nst = 0;                  // bulk stores issued for this job (staging ping-pong)
 #pragma unroll 1
-        for (int bb = 0; bb < 8 * nh; ++bb) {
+        for (int bb = g; bb < 8 * nh; bb += 2) {
           const int hh = bb >> 3, blk = bb & 7;
           // rows past the task's m (a 128-row task in a 256-row tile) are
           // neither stored nor summed
@@ -477,46 +494,37 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
           uint32_t v[32];
           tc::ld_32x32b_x32(tcol + hh * 256 + blk * 32, v);
           tc::wait_ld();
-          if (p.task_mode && j.action == E_STORE_C) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const double x = (double)__uint_as_float(v[i]);
-              csum[hh] += x * x;
-            }
-          }
           if (j.action == E_SPILL) {
             float4* s4 = reinterpret_cast<float4*>(slab_blk(hh, blk));
 #pragma unroll
             for (int i = 0; i < 8; ++i)
               s4[i * 32 + lane] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
                                               __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
-          } else {
-            // Stage the 32x32 block row-major in this warp's ping-pong buffer
-            // (register i -> row blk*32+i, lane -> column 32q+lane: one
-            // conflict-free 128-byte row per store) and hand it to the TMA
-            // engine: a tensor store for C / urgent slots, a reduce-add for
-            // split-K urgent items.
-            float* ob = out_stage + (2 * q + (nst & 1)) * (STAGE_OUT / 4);
-            if (nst >= 2) {
-              if (lane == 0) bulk_wait_read<1>();  // this buffer's previous store has read it
-              __syncwarp();
-            }
+            continue;
+          }
+          // register i -> C row blk*32+i, lane -> C column: each store
+          // instruction writes one contiguous 128-byte row segment
+          const int col = j.col0 + BNH * hh + 32 * q + lane;
+          if (j.action == E_STORE_C) {
+            float* dst = p.C + (size_t)(j.row0 + blk * 32) * p.ldc + col;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ob[i * 32 + lane] = __uint_as_float(v[i]);
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              const int x = j.col0 + BNH * hh + 32 * q;
-              if (j.action == E_STORE_C) {
-                tma_store_2d(&p.tmC, x, j.row0 + blk * 32, ob);
-              } else {
-                const int y = j.e * (int)(p.cu_stride / p.ldcu) + j.row0 + blk * 32;
-                if (p.usplit == 1) tma_store_2d(&p.tmCu, x, y, ob);
-                else tma_reduce_add_2d(&p.tmCu, x, y, ob);
+            for (int i = 0; i < 32; ++i) dst[(size_t)i * p.ldc] = __uint_as_float(v[i]);
+            if (p.task_mode) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const double x = (double)__uint_as_float(v[i]);
+                csum[hh] += x * x;
               }
-              bulk_commit();
             }
-            ++nst;
+          } else {
+            float* dst = p.Cu + (size_t)j.e * p.cu_stride + (size_t)(j.row0 + blk * 32) * p.ldcu + col;
+            if (p.usplit == 1) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) dst[(size_t)i * p.ldcu] = __uint_as_float(v[i]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) atomicAdd(dst + (size_t)i * p.ldcu, __uint_as_float(v[i]));
+            }
           }
         }
         tc::fence_before_sync();
@@ -531,25 +539,25 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
               double s = csum[hh];
 #pragma unroll
               for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-              if (lane == 0) sh.chk_part[sl][hh][q] = s;
+              if (lane == 0) sh.chk_part[sl][hh][ew] = s;
             }
           }
           // the tile's stores are complete and visible before it is counted;
-          // the last of the four epilogue warps to finish does the accounting
-          if (lane == 0) bulk_wait_all();
+          // the last of the epilogue warps to finish does the accounting
           __threadfence();
           __syncwarp();
-          if (lane == 0 && atomicAdd(&sh.epi_cnt[sl], 1) == 3) {
+          if (lane == 0 && atomicAdd(&sh.epi_cnt[sl], 1) == EPI_WARPS - 1) {
             sh.epi_cnt[sl] = 0;
             if (j.action == E_STORE_C) {
               if (p.task_mode) {
-                // task mode counts and checksums each 256x128 half
+                // task mode counts and checksums each 256x128 half; the
+                // partial sums are added in a fixed order
                 for (int hh = 0; hh < nh; ++hh) {
                   ++sh.tiles;
                   if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[j.task + hh], 1);
-                  p.chk[j.task + hh] = ((sh.chk_part[sl][hh][0] + sh.chk_part[sl][hh][1]) +
-                                        sh.chk_part[sl][hh][2]) +
-                                       sh.chk_part[sl][hh][3];
+                  double s = 0.0;
+                  for (int w = 0; w < EPI_WARPS; ++w) s += sh.chk_part[sl][hh][w];
+                  p.chk[j.task + hh] = s;
                 }
               } else {
                 ++sh.tiles;
@@ -569,8 +577,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
       if (lane == 0) mbar_arrive(&sh.eempty[sl]);
       ++Y;
     }
-    if (lane == 0) bulk_wait_all();  // no bulk store may still read smem at exit
-  } else if (warp == 6 && lane == 0) {
+  } else if (warp == CTRL_WARP && lane == 0) {
     // ================================ control =================================
     int nextEv = 0;
     long long gBase = 0;
@@ -607,14 +614,17 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
 
 // ---------------------------------------------------------------------------
 
-template <int POLL, int DISC, bool ORACLE>
+template <int POLL, int DISC, bool ORACLE, int BK>
 static const void* kernel_ptr() {
-  return reinterpret_cast<const void*>(&gemm_bf16_persistent<POLL, DISC, ORACLE>);
+  return reinterpret_cast<const void*>(&gemm_bf16_persistent<POLL, DISC, ORACLE, BK>);
 }
 
-static const void* select_kernel(int poll, int disc, bool oracle) {
-#define APK_SEL(PL, DS, OR) \
-  if (poll == PL && disc == DS && oracle == OR) return kernel_ptr<PL, DS, OR>();
+static const void* select_kernel(int poll, int disc, bool oracle, int bk) {
+#define APK_SEL(PL, DS, OR)                                     \
+  if (poll == PL && disc == DS && oracle == OR) {              \
+    if (bk == 64) return kernel_ptr<PL, DS, OR, 64>();         \
+    if (bk == 32) return kernel_ptr<PL, DS, OR, 32>();         \
+  }
   APK_SEL(POLL_OFF, DISC_DRAIN, false)
   APK_SEL(POLL_OFF, DISC_DRAIN, true)
   APK_SEL(POLL_BOUNDARY, DISC_DRAIN, false)
@@ -627,25 +637,27 @@ static const void* select_kernel(int poll, int disc, bool oracle) {
   return nullptr;
 }
 
-int smem_bytes() { return SMEM_BYTES; }
+int smem_bytes(int bk) { return bk == 32 ? Ring<32>::SMEM_BYTES : Ring<64>::SMEM_BYTES; }
+int stages(int bk) { return bk == 32 ? Ring<32>::S : Ring<64>::S; }
 int threads() { return NT; }
+size_t params_bytes() { return sizeof(F32Params); }
 
-cudaError_t prepare(int poll, int disc, bool oracle, int* max_ctas_per_sm) {
-  const void* k = select_kernel(poll, disc, oracle);
+cudaError_t prepare(int poll, int disc, bool oracle, int bk, int* max_ctas_per_sm) {
+  const void* k = select_kernel(poll, disc, oracle, bk);
   if (!k) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(bk));
   if (e != cudaSuccess) return e;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(max_ctas_per_sm, k, NT, SMEM_BYTES);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(max_ctas_per_sm, k, NT, smem_bytes(bk));
   // each CTA allocates all 512 TMEM columns: never more than one per SM
   if (e == cudaSuccess && *max_ctas_per_sm > 1) *max_ctas_per_sm = 1;
   return e;
 }
 
-cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, cudaStream_t stream) {
-  const void* k = select_kernel(poll, disc, oracle);
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int bk, cudaStream_t stream) {
+  const void* k = select_kernel(poll, disc, oracle, bk);
   if (!k) return cudaErrorInvalidValue;
   void* args[] = {const_cast<F32Params*>(&prm)};
-  return cudaLaunchKernel(k, dim3(grid), dim3(NT), args, SMEM_BYTES, stream);
+  return cudaLaunchKernel(k, dim3(grid), dim3(NT), args, smem_bytes(bk), stream);
 }
 
 }  // namespace bf16

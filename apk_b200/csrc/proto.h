@@ -64,15 +64,13 @@ struct TaskDesc {
   long long chk_base;  // checksum index of the task's tile (0,0); tile (tm,tn) at +tm*tiles_n+tn
 };
 
-// Kernel parameters (both kernels; the fp32 kernel ignores tmC/tmCu and the
-// task-mode fields).
+// Kernel parameters (both kernels; the fp32 kernel ignores the task-mode
+// fields).
 struct F32Params {
-  CUtensorMap tmA;   // background A [M][K]  (box BK-slices of 32 x 128 rows, 128B swizzle)
-  CUtensorMap tmB;   // background B [K][N]  (box 128 cols x BK rows, no swizzle)
+  CUtensorMap tmA;   // background A [M][K]  (fp32: 128 rows x 32 k boxes; bf16: 128 x BK, swizzled)
+  CUtensorMap tmB;   // background B [K][N]  (fp32: BK x 128 boxes; bf16: BK x 64, 128B swizzle)
   CUtensorMap tmAu;  // urgent A
   CUtensorMap tmBu;  // urgent B
-  CUtensorMap tmC;   // background C [M][N] fp32, 32x32 boxes (bf16 path epilogue stores)
-  CUtensorMap tmCu;  // urgent output slots [(max_events+1)*Mu][Nu] fp32, 32x32 boxes
   float* C;
   int ldc, tiles_n, total_tiles, nk;   // nk = K / BK
   float* Cu;                           // urgent output, one slot per event

@@ -27,12 +27,15 @@ cudaError_t prepare(int poll, int disc, bool oracle, int bk, int* max_ctas_per_s
 cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int bk,
                    cudaStream_t stream);
 int smem_bytes(int bk);
+size_t params_bytes();
 }  // namespace f32
 namespace bf16 {
-cudaError_t prepare(int poll, int disc, bool oracle, int* max_ctas_per_sm);
-cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, cudaStream_t stream);
-int smem_bytes();
+cudaError_t prepare(int poll, int disc, bool oracle, int bk, int* max_ctas_per_sm);
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int bk, cudaStream_t stream);
+int smem_bytes(int bk);
+int stages(int bk);
 int threads();
+size_t params_bytes();
 }  // namespace bf16
 }  // namespace apk
 
@@ -243,7 +246,7 @@ apk_status prepare_kernel(apk_ctx* ctx, int poll) {
   if (ctx->cfg.dtype == APK_F32)
     e = f32::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->cfg.k_tile, &maxc);
   else
-    e = bf16::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, &maxc);
+    e = bf16::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->cfg.k_tile, &maxc);
   if (e != cudaSuccess)
     return fail(ctx, APK_EUNSUPPORTED, "kernel variant unavailable (dtype %d poll %d disc %d oracle %d k_tile %d): %s",
                 ctx->cfg.dtype, poll, ctx->cfg.discipline, ctx->cfg.oracle, ctx->cfg.k_tile,
@@ -265,7 +268,7 @@ void apk_config_default(apk_config* c) {
   c->dtype = APK_F32;
   c->ctas_per_sm = 0;
   c->grid = 0;
-  c->k_tile = 32;
+  c->k_tile = 0;  // the dtype's default: fp32 32, bf16 64
   c->poll = APK_POLL_STAGE;
   c->discipline = APK_DISC_DRAIN;
   c->set_mode = APK_SET_HOST_MEMCPY;
@@ -283,15 +286,23 @@ apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
   apk_ctx* ctx = new apk_ctx();
   ctx->cfg = *cfg;
   apk_config& c = ctx->cfg;
+  // every translation unit must agree on the kernel parameter block (objects
+  // compiled against different copies of proto.h would read garbage pointers)
+  if (f32::params_bytes() != sizeof(F32Params) || bf16::params_bytes() != sizeof(F32Params)) {
+    fail(ctx, APK_EUNSUPPORTED, "kernel parameter layout mismatch (f32 %zu, bf16 %zu, runtime %zu bytes): rebuild",
+         f32::params_bytes(), bf16::params_bytes(), sizeof(F32Params));
+    *out = ctx;
+    return APK_EUNSUPPORTED;
+  }
   if (c.max_events < 1) c.max_events = 1;
   if (c.urgent_split_k < 1) c.urgent_split_k = 1;
   if (c.wait_limit_ns <= 0) c.wait_limit_ns = 2000000000LL;
-  if (c.dtype == APK_F32 && c.k_tile != 32 && c.k_tile != 64) {
-    fail(ctx, APK_EINVAL, "fp32 k_tile must be 32 or 64");
+  if (c.k_tile == 0) c.k_tile = c.dtype == APK_BF16 ? 64 : 32;
+  if (c.k_tile != 32 && c.k_tile != 64) {
+    fail(ctx, APK_EINVAL, "k_tile must be 32 or 64");
     *out = ctx;
     return APK_EINVAL;
   }
-  if (c.dtype == APK_BF16) c.k_tile = 64;
   if (c.discipline == APK_DISC_POISON && c.poll == APK_POLL_OFF) {
     fail(ctx, APK_EINVAL, "the poison discipline needs a poll mode");
     *out = ctx;
@@ -437,11 +448,11 @@ apk_status apk_get_info(apk_ctx* ctx, apk_device_info* info) {
     info->tile_n = 128;
     info->stages = ctx->cfg.k_tile == 32 ? 3 : 2;
   } else {
-    info->smem_per_cta = bf16::smem_bytes();
+    info->smem_per_cta = bf16::smem_bytes(ctx->cfg.k_tile);
     info->threads_per_cta = bf16::threads();
     info->tile_m = 256;
     info->tile_n = 256;
-    info->stages = 3;
+    info->stages = bf16::stages(ctx->cfg.k_tile);
   }
   info->k_tile = ctx->cfg.k_tile;
   snprintf(info->name, sizeof info->name, "%s", ctx->name);
@@ -750,11 +761,13 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
   memset(&p, 0, sizeof p);
   {
     // fp32: A as [128 rows][32 k] boxes (128B swizzle), B as [BK k][128 n]
-    // boxes (no swizzle).  bf16: A as [128 rows][64 k] and B as [64 k][64 n]
-    // boxes, both 128B swizzled (the tcgen05 canonical K- / MN-major atoms).
+    // boxes (no swizzle).  bf16: A as [128 rows][BK k] boxes, one swizzle
+    // span per row (128B for BK 64, 64B for BK 32), and B as [BK k][64 n]
+    // boxes, 128B swizzled (the tcgen05 canonical K- / MN-major atoms).
     const CUtensorMapDataType dt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     const int es = f32 ? 4 : 2;
-    const int a_box_k = f32 ? 32 : 64, b_box_n = f32 ? 128 : 64;
+    const int a_box_k = f32 ? 32 : bk, b_box_n = f32 ? 128 : 64;
+    const CUtensorMapSwizzle asw = (f32 || bk == 64) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     const CUtensorMapSwizzle bsw = f32 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B;
     apk_status t;
     // task mode: the maps cover the operand pools, tasks are windows of them
@@ -763,35 +776,15 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
     const void* srcB = tk ? ctx->dBpool : ctx->dB;
     const long long ar = tk ? ctx->a_rows : ctx->M, ac = tk ? ctx->a_cols : ctx->K;
     const long long br = tk ? ctx->b_rows : ctx->K, bc = tk ? ctx->b_cols : ctx->N;
-    if ((t = make_tmap(ctx, &p.tmA, srcA, dt, es, ar, ac, a_box_k, 128, CU_TENSOR_MAP_SWIZZLE_128B)) != APK_OK)
-      return t;
+    if ((t = make_tmap(ctx, &p.tmA, srcA, dt, es, ar, ac, a_box_k, 128, asw)) != APK_OK) return t;
     if ((t = make_tmap(ctx, &p.tmB, srcB, dt, es, br, bc, b_box_n, bk, bsw)) != APK_OK) return t;
     if (ctx->dAu) {
-      if ((t = make_tmap(ctx, &p.tmAu, ctx->dAu, dt, es, ctx->Mu, ctx->Ku, a_box_k, 128,
-                         CU_TENSOR_MAP_SWIZZLE_128B)) != APK_OK)
+      if ((t = make_tmap(ctx, &p.tmAu, ctx->dAu, dt, es, ctx->Mu, ctx->Ku, a_box_k, 128, asw)) != APK_OK)
         return t;
       if ((t = make_tmap(ctx, &p.tmBu, ctx->dBu, dt, es, ctx->Ku, ctx->Nu, b_box_n, bk, bsw)) != APK_OK) return t;
     } else {
       p.tmAu = p.tmA;
       p.tmBu = p.tmB;
-    }
-    // fp32 outputs as 32x32 boxes for the TMA-store epilogue (bf16 path);
-    // the urgent slots are one [(max_events+1)*Mu][Nu] array
-    if (tk) {
-      if ((t = make_tmap(ctx, &p.tmC, ctx->dCpool, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ctx->c_rows, ctx->c_cols, 32,
-                         32, CU_TENSOR_MAP_SWIZZLE_NONE)) != APK_OK)
-        return t;
-    } else if ((t = make_tmap(ctx, &p.tmC, ctx->dC, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ctx->M, ctx->N, 32, 32,
-                              CU_TENSOR_MAP_SWIZZLE_NONE)) != APK_OK) {
-      return t;
-    }
-    if (ctx->dCu) {
-      if ((t = make_tmap(ctx, &p.tmCu, ctx->dCu, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4,
-                         (long long)ctx->Mu * (ctx->cfg.max_events + 1), ctx->Nu, 32, 32,
-                         CU_TENSOR_MAP_SWIZZLE_NONE)) != APK_OK)
-        return t;
-    } else {
-      p.tmCu = p.tmC;
     }
   }
   if (ctx->task_mode) {
@@ -826,7 +819,7 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
   if (f32)
     e = f32::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, bk, stream);
   else
-    e = bf16::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, stream);
+    e = bf16::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, bk, stream);
   if (e != cudaSuccess) return fail(ctx, APK_ECUDA, "kernel launch failed: %s", cudaGetErrorString(e));
   if (record) APK_CU(cudaEventRecord(ctx->ev_done, stream));
   return APK_OK;

@@ -497,6 +497,7 @@ static const void* select_kernel(int poll, int disc, bool oracle, int bk) {
 }
 
 int smem_bytes(int bk) { return bk == 32 ? Cfg<32>::SMEM_BYTES : Cfg<64>::SMEM_BYTES; }
+size_t params_bytes() { return sizeof(F32Params); }
 
 cudaError_t prepare(int poll, int disc, bool oracle, int bk, int* max_ctas_per_sm) {
   const void* k = select_kernel(poll, disc, oracle, bk);

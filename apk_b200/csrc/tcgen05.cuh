@@ -33,14 +33,16 @@ __device__ __forceinline__ void fence_after_sync() {
 // ---- descriptors -------------------------------------------------------------
 // Shared-memory matrix descriptor: start address, leading- and stride-
 // dimension byte offsets (all >> 4), descriptor version 1 (bits 46-47), and
-// the layout type in bits 61-63 (2 = 128-byte swizzle).
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+// the layout type in bits 61-63 (2 = 128-byte swizzle, 4 = 64-byte swizzle).
+constexpr uint32_t LAYOUT_SW128 = 2, LAYOUT_SW64 = 4;
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
   d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
+  d |= (uint64_t)layout << 61;
   return d;
 }
 

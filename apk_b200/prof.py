@@ -1,0 +1,55 @@
+"""One bounded drain of the persistent kernel, repeated, for profilers.
+
+    python -m apk_b200.prof f32  [--n 4096] [--poll stage] [--reps 2]
+    python -m apk_b200.prof bf16 [--n 6144] [--poll stage] [--reps 3]
+
+Each repetition drains every tile of an n^3 background GEMM once (fp32:
+uniform[-1,1] operands from the reference generator, seed 21; bf16: N(0,1)
+rounded to bf16, seeds 21/22) with an urgent operand set installed but no
+event fired, and prints the launch time.  Under ncu, skip the first launch
+(`-s 1`) so the captured one runs with warm tensor maps and caches; the
+launches are bounded, so a serialised capture cannot leave a kernel waiting
+for a host flag.
+"""
+from __future__ import annotations
+
+import argparse
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("dtype", choices=("f32", "bf16"))
+    ap.add_argument("--n", type=int, default=0)
+    ap.add_argument("--poll", default="stage", choices=("off", "boundary", "stage"))
+    ap.add_argument("--reps", type=int, default=0)
+    args = ap.parse_args()
+
+    import apk_b200
+
+    bf16 = args.dtype == "bf16"
+    n = args.n or (6144 if bf16 else 4096)
+    reps = args.reps or (3 if bf16 else 2)
+    if bf16:
+        A = apk_b200.fill_normal_bf16((n, n), 21)
+        B = apk_b200.fill_normal_bf16((n, n), 22)
+        Au = apk_b200.fill_normal_bf16((256, 256), 31)
+        Bu = apk_b200.fill_normal_bf16((256, 256), 32)
+    else:
+        A, B = apk_b200.fill_uniform(n, n, n, 21)
+        Au, Bu = apk_b200.fill_uniform(256, 256, 256, 99)
+    with apk_b200.Context(dtype=args.dtype, poll=args.poll, urgent_split_k=1) as c:
+        c.set_background(A, B)
+        c.set_urgent(Au, Bu)
+        info = c.info
+        tiles = (n // info["tile_m"]) * (-(-n // info["tile_n"]))
+        for _ in range(reps):
+            c.launch(tiles)
+            c.wait(60)
+            st = c.run_stats()
+            print("%s %d^3 poll=%s: %.3f ms, %.1f TFLOP/s, %d tiles" % (
+                args.dtype, n, args.poll, st["launch_ms"], 2.0 * n ** 3 / st["launch_ms"] / 1e9,
+                st["tiles_done"]), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -102,7 +102,7 @@ class Context:
     """One preemptible persistent-GEMM runtime on one device."""
 
     def __init__(self, device: int = 0, dtype: str = "f32", ctas_per_sm: int = 0, grid: int = 0,
-                 k_tile: int = 32, poll: str = "stage", discipline: str = "drain",
+                 k_tile: int = 0, poll: str = "stage", discipline: str = "drain",
                  set_mode: str = "host_memcpy", max_events: int = 4096, oracle: bool = False,
                  urgent_split_k: int = 8, wait_limit_ns: int = 2_000_000_000):
         self._lib = L.load()

@@ -17,7 +17,7 @@
  *   - Every device-side wait is bounded (apk_config.wait_limit_ns); a wait
  *     that runs out is reported as APK_EDEVICE, never as a hung GPU.
  *   - Matrices are row-major.  fp32: M, N multiples of 128, K a multiple of
- *     k_tile.  bf16: M, N multiples of 128, K a multiple of 64.
+ *     k_tile.  bf16: M a multiple of 256, N of 128, K of k_tile.
  */
 #ifndef APK_H_
 #define APK_H_
@@ -76,7 +76,8 @@ typedef struct apk_config {
   apk_dtype dtype;
   int ctas_per_sm;          /* 0 = as many as fit (full residency)            */
   int grid;                 /* 0 = SMs * ctas_per_sm                          */
-  int k_tile;               /* fp32: 32 or 64; bf16: 64                       */
+  int k_tile;               /* 32 or 64; 0 = the dtype's default (fp32 32,
+                               bf16 64)                                       */
   apk_poll_mode poll;
   apk_discipline discipline;
   apk_set_mode set_mode;
@@ -86,7 +87,7 @@ typedef struct apk_config {
   long long wait_limit_ns;  /* bound on every device-side wait                */
 } apk_config;
 
-/* Fill *cfg with the defaults (fp32, full residency, k_tile 32, stage
+/* Fill *cfg with the defaults (fp32, full residency, default k_tile, stage
  * polling, drain, host-set flag through cudaMemcpyAsync, 4096
  * events, urgent split-K 8, 2 s waits). */
 void apk_config_default(apk_config* cfg);

@@ -42,7 +42,7 @@ def test_config_defaults(libapk):
     c = _lib.Config()
     libapk.apk_config_default(ctypes.byref(c))
     assert (c.dtype, c.k_tile, c.poll, c.discipline, c.set_mode) == (
-        _lib.APK_F32, 32, _lib.APK_POLL_STAGE, _lib.APK_DISC_DRAIN, _lib.APK_SET_HOST_MEMCPY)
+        _lib.APK_F32, 0, _lib.APK_POLL_STAGE, _lib.APK_DISC_DRAIN, _lib.APK_SET_HOST_MEMCPY)
     assert c.max_events == 4096 and c.urgent_split_k == 8 and c.wait_limit_ns == 2_000_000_000
 
 

@@ -200,3 +200,46 @@ def test_narrow_edge_tiles_yield_bitwise(libapk):
         assert bad == 0 and nans == 0, f"urgent: {bad} bad, max rel {mr:.3e}"
     v = oracle.exactly_once(ex, ue[:fired], ev["claimer"][:fired], ev["set_ns"][:fired], 2, fired)
     assert v["pass"], v
+
+
+@pytest.mark.parametrize("shape", [(256, 128, 32), (512, 384, 1056), (1024, 2048, 512)])
+def test_k_tile_32_full_check(libapk, shape):
+    """K-tile 32: [128][32] A boxes in the 64-byte-swizzled K-major layout,
+    a 7-slot ring."""
+    M, N, K = shape
+    A, B = _normal((M, K), 11), _normal((K, N), 12)
+    with _ctx(poll="off", oracle=True, k_tile=32) as c:
+        assert c.info["k_tile"] == 32 and c.info["stages"] == 7
+        C = c.gemm(A, B)
+    _check_rows(C, A, B, [(0, M)])
+
+
+def test_k_tile_32_stage_yield_bitwise(libapk):
+    M = N = K = 4096
+    A, B = _normal((M, K), 13), _normal((K, N), 14)
+    Au, Bu = _normal((256, 256), 15), _normal((256, 256), 16)
+    with _ctx(poll="off", k_tile=32) as c:
+        Cref = c.gemm(A, B)
+    _check_rows(Cref, A, B, [(0, 4), (M - 4, 4)])
+    nev = 20
+    with _ctx(poll="stage", set_mode="device", oracle=True, k_tile=32) as c:
+        ntasks = 1024
+        c.set_background(A, B)
+        c.set_urgent(Au, Bu)
+        c.schedule_device_events((np.arange(nev, dtype=np.int64) + 1) * 15_000)
+        c.launch(ntasks)
+        c.wait(60)
+        C = c.read_output()
+        ev = c.read_events()
+        st = c.run_stats()
+        ex, ue = c.read_oracle(ntasks)
+        fired = int(np.count_nonzero(ev["set_ns"][:nev]))
+        outs = [c.read_urgent_output(e) for e in range(fired) if ev["claimer"][e]]
+    assert fired >= 10 and st["yields"] > 0
+    assert np.array_equal(C.view(np.uint32), Cref.view(np.uint32)), "resume not bitwise"
+    refu = oracle.gemm_f64_bf16_rows(Au, Bu, 0, 256)
+    for Cu in outs:
+        mr, bad, nans = oracle.check(Cu, refu, TOL)
+        assert bad == 0 and nans == 0
+    v = oracle.exactly_once(ex, ue[:fired], ev["claimer"][:fired], ev["set_ns"][:fired], 1, fired)
+    assert v["pass"], v
