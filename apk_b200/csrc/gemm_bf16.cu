@@ -647,6 +647,8 @@ cudaError_t prepare(int poll, int disc, bool oracle, int bk, int* max_ctas_per_s
   if (!k) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(bk));
   if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return e;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(max_ctas_per_sm, k, NT, smem_bytes(bk));
   // each CTA allocates all 512 TMEM columns: never more than one per SM
   if (e == cudaSuccess && *max_ctas_per_sm > 1) *max_ctas_per_sm = 1;
