@@ -99,6 +99,7 @@ SIGNATURES = {
     "apk_selftest_wait_timeout": (c_int, [P, c_ll, ctypes.POINTER(c_int)]),
     "apk_run_overhead": (c_int, [P, c_ull, c_int, ctypes.POINTER(c_double), ctypes.POINTER(c_double)]),
     "apk_run_baseline": (c_int, [P, c_ull, c_int, c_uint, P]),
+    "apk_run_reserved": (c_int, [P, c_ull, c_int, c_int, c_uint, P, ctypes.POINTER(c_double)]),
     "apk_set_task_pool": (c_int, [P, P, c_int, c_int, P, c_int, c_int, c_int, c_int, c_int]),
     "apk_set_tasks": (c_int, [P, P, c_int, c_ll, ctypes.POINTER(c_ull)]),
     "apk_read_checksums": (c_int, [P, P, c_ll]),

@@ -1281,9 +1281,11 @@ apk_status apk_run_overhead(apk_ctx* ctx, unsigned long long num_tasks, int reps
   return APK_OK;
 }
 
-apk_status apk_run_baseline(apk_ctx* ctx, unsigned long long num_tasks, int trials, unsigned seed,
-                            double* e2e_us) {
+apk_status apk_run_reserved(apk_ctx* ctx, unsigned long long num_tasks, int reserve, int trials, unsigned seed,
+                            double* e2e_us, double* bg_tflops) {
   if (!ctx || trials <= 0 || !e2e_us || num_tasks == 0 || num_tasks == APK_TASKS_UNBOUNDED) return APK_EINVAL;
+  if (reserve < 0 || reserve >= ctx->grid)
+    return fail(ctx, APK_EINVAL, "reserve %d must leave at least one of the %d background CTAs", reserve, ctx->grid);
   if (ctx->running) return fail(ctx, APK_ESTATE, "a launch is already running");
   if (ctx->cfg.dtype != APK_F32) return fail(ctx, APK_EUNSUPPORTED, "baseline mode is fp32 only");
   if (!ctx->dAu) return fail(ctx, APK_ESTATE, "no urgent operands set");
@@ -1328,12 +1330,23 @@ apk_status apk_run_baseline(apk_ctx* ctx, unsigned long long num_tasks, int tria
   up.q.exited = &ub->exited;
   up.q.yields = &ub->yields;
 
+  // the background holds grid - reserve resident slots; the rest stay free
+  // for the urgent launch (restored on every return path)
+  struct GridGuard {
+    apk_ctx* c;
+    int keep;
+    ~GridGuard() { c->grid = keep; }
+  } guard{ctx, ctx->grid};
+  ctx->grid -= reserve;
+
   // drain estimate, background alone (device timeline)
   apk_status s = launch_impl(ctx, num_tasks, APK_POLL_OFF, ctx->kstream, true);
   if (s != APK_OK) return s;
   APK_CU(cudaEventSynchronize(ctx->ev_done));
   float drain_ms = 0;
   APK_CU(cudaEventElapsedTime(&drain_ms, ctx->ev_start, ctx->ev_done));
+  if (bg_tflops)
+    *bg_tflops = drain_ms > 0 ? 2.0 * 128.0 * 128.0 * ctx->K * (double)num_tasks / (drain_ms * 1e-3) / 1e12 : 0.0;
   std::mt19937 rng(seed);
   std::uniform_real_distribution<double> frac(0.2, 0.8);
   Ctrl init{};
@@ -1354,6 +1367,11 @@ apk_status apk_run_baseline(apk_ctx* ctx, unsigned long long num_tasks, int tria
     e2e_us[tr] = (td - ta) / 1e3;
   }
   return read_status(ctx);
+}
+
+apk_status apk_run_baseline(apk_ctx* ctx, unsigned long long num_tasks, int trials, unsigned seed,
+                            double* e2e_us) {
+  return apk_run_reserved(ctx, num_tasks, 0, trials, seed, e2e_us, nullptr);
 }
 
 void* apk_host_alloc(size_t bytes) {

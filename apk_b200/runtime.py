@@ -323,3 +323,12 @@ class Context:
         out = np.zeros(trials, np.float64)
         self._check(self._lib.apk_run_baseline(self._h, num_tasks, trials, seed, _ptr(out)))
         return out
+
+    def run_reserved(self, num_tasks: int, reserve: int, trials: int, seed: int = 21):
+        """Reserved-capacity arm: (e2e_us per trial, background TFLOP/s with
+        `reserve` resident slots held out)."""
+        out = np.zeros(trials, np.float64)
+        tf = ctypes.c_double()
+        self._check(self._lib.apk_run_reserved(self._h, num_tasks, reserve, trials, seed, _ptr(out),
+                                               ctypes.byref(tf)))
+        return out, tf.value

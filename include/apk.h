@@ -285,6 +285,16 @@ apk_status apk_run_overhead(apk_ctx* ctx, unsigned long long num_tasks, int reps
 apk_status apk_run_baseline(apk_ctx* ctx, unsigned long long num_tasks, int trials, unsigned seed,
                             double* e2e_us);
 
+/* Reserved-capacity arm (src/urgent_baseline.cu:152-175, --reserve R, and
+ * the reserved side of scripts/pareto.sh): as apk_run_baseline, but the
+ * background runs on grid - reserve CTAs, so `reserve` resident slots stay
+ * free and the urgent kernel (one CTA per 128x128 urgent tile) starts in them
+ * at once instead of waiting for the drain.  reserve = 0 is the baseline.
+ * e2e_us: trials doubles, host arrival -> urgent done; *bg_tflops (may be
+ * NULL): the background's rate with the slots held out. */
+apk_status apk_run_reserved(apk_ctx* ctx, unsigned long long num_tasks, int reserve, int trials, unsigned seed,
+                            double* e2e_us, double* bg_tflops);
+
 /* ---- heterogeneous task queue (configs[4], bf16 contexts) -------------- */
 
 /* One background GEMM task: C window = A window * B window, each a window

@@ -248,3 +248,24 @@ def test_latency_mode_smoke(libapk):
     assert r["n"] == 90 and r["unclaimed"] == 0 and r["anomalies"] == 0
     assert r["rt_claim_p50_us"] < 60
     assert r["bg_tflops"] > 1.0
+
+
+def test_reserved_capacity_arm(libapk):
+    """Reserved-capacity arm (src/urgent_baseline.cu:152-175): with R free
+    resident slots the urgent kernel starts at once instead of waiting for
+    the drain (R = 0, the no-preemption baseline); holding slots out costs
+    background throughput roughly in proportion."""
+    A, B = oracle.gen_uniform(4096, 4096, 4096, 21)
+    Au, Bu, _ = _urgent_ref()
+    with _ctx(poll="off", urgent_split_k=1) as c:
+        c.set_background(A, B)
+        c.set_urgent(Au, Bu)
+        grid = c.info["grid"]
+        e0, tf0 = c.run_reserved(4096, 0, 8, seed=3)
+        e4, tf4 = c.run_reserved(4096, 4, 8, seed=3)
+        assert c.info["grid"] == grid  # the reduced grid is restored
+        with pytest.raises(Exception):
+            c.run_reserved(4096, grid, 2)
+    assert np.all(e0 > 0) and np.all(e4 > 0)
+    assert np.median(e4) * 5 < np.median(e0), (np.median(e4), np.median(e0))
+    assert 0 < tf4 <= tf0 * 1.02 and tf4 > tf0 * 0.9
