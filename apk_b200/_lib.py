@@ -70,6 +70,18 @@ class LatencyResult(ctypes.Structure):
                 ("bg_tflops", c_double), ("vis_offset_ns", c_double)]
 
 
+class VisibilityConfig(ctypes.Structure):
+    _fields_ = [("events", c_int), ("gap_min_ns", c_ll), ("gap_max_ns", c_ll), ("seed", c_uint),
+                ("warmup_events", c_int), ("work_iters", c_int), ("loaded", c_int), ("traffic_bytes", c_ll)]
+
+
+class VisibilityResult(ctypes.Structure):
+    _fields_ = [("n", c_int), ("unset", c_int), ("anomalies", c_int), ("cadence_ns", c_double),
+                ("dmin_p50_us", c_double), ("d50_p50_us", c_double), ("d95_p50_us", c_double),
+                ("dmax_p50_us", c_double), ("dmax_p99_us", c_double), ("hbm_gbs", c_double),
+                ("device_status", c_int)]
+
+
 P = c_void_p
 # name -> (restype, argtypes); every symbol include/apk.h declares
 SIGNATURES = {
@@ -96,6 +108,7 @@ SIGNATURES = {
     "apk_gemm": (c_int, [P, P, P, P, c_int, c_int, c_int, c_int]),
     "apk_run_latency": (c_int, [P, ctypes.POINTER(LatencyConfig), ctypes.POINTER(LatencyResult)]),
     "apk_probe_visibility": (c_int, [P, c_int, P]),
+    "apk_run_visibility": (c_int, [P, ctypes.POINTER(VisibilityConfig), ctypes.POINTER(VisibilityResult), P, P]),
     "apk_selftest_wait_timeout": (c_int, [P, c_ll, ctypes.POINTER(c_int)]),
     "apk_run_overhead": (c_int, [P, c_ull, c_int, ctypes.POINTER(c_double), ctypes.POINTER(c_double)]),
     "apk_run_baseline": (c_int, [P, c_ull, c_int, c_uint, P]),

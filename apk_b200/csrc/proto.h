@@ -89,4 +89,24 @@ struct F32Params {
   QueueProto q;
 };
 
+// Visibility microbenchmark parameters (the flag-notification probe of
+// src/yield.cu:227-293, decoupled from tile work).
+struct VisParams {
+  int* flag;                  // generation word; CTA 0 raises it on schedule, -1 ends the run
+  const long long* sched_ns;  // cumulative event offsets from CTA 0's start
+  int n_events;
+  long long* set_ns;          // [n_events] globaltimer of each raise
+  long long* obs_ns;          // [n_events][grid] first observation per CTA
+  long long* iters;           // [grid] polling iterations per CTA
+  long long* t_begin;         // [grid] globaltimer at CTA start / end
+  long long* t_end;
+  int work_iters;             // dependent FMA chain per iteration (known cadence)
+  const float4* traffic;      // loaded variant: streamed operand, far larger than L2
+  unsigned long long traffic_n4;
+  float* sink;                // [grid * threads] keeps the work live
+  long long tail_ns;          // CTA 0 stores -1 this long after the last event
+  long long limit_ns;         // every CTA leaves after this long, whatever the flag says
+  int* status;                // DEV_WAIT_TIMEOUT_SPIN if a CTA hit limit_ns
+};
+
 }  // namespace apk

@@ -29,6 +29,11 @@ cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool orac
 int smem_bytes(int bk);
 size_t params_bytes();
 }  // namespace f32
+namespace vis {
+cudaError_t launch(const VisParams& prm, int grid, int smem_bytes, bool loaded, cudaStream_t stream);
+int threads();
+int loads_per_iter();
+}  // namespace vis
 namespace bf16 {
 cudaError_t prepare(int poll, int disc, bool oracle, int bk, int* max_ctas_per_sm);
 cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int bk, cudaStream_t stream);
@@ -1372,6 +1377,150 @@ apk_status apk_run_reserved(apk_ctx* ctx, unsigned long long num_tasks, int rese
 apk_status apk_run_baseline(apk_ctx* ctx, unsigned long long num_tasks, int trials, unsigned seed,
                             double* e2e_us) {
   return apk_run_reserved(ctx, num_tasks, 0, trials, seed, e2e_us, nullptr);
+}
+
+apk_status apk_run_visibility(apk_ctx* ctx, const apk_visibility_config* vc, apk_visibility_result* out,
+                              long long* set_out, long long* obs_out) {
+  if (!ctx || !vc || !out) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "a launch is already running");
+  if (vc->events <= 0 || vc->gap_min_ns <= 0 || vc->gap_max_ns < vc->gap_min_ns || vc->work_iters < 0 ||
+      vc->warmup_events < 0 || vc->traffic_bytes < 0)
+    return fail(ctx, APK_EINVAL, "visibility: events > 0, 0 < gap_min <= gap_max, work_iters >= 0");
+  APK_CU(cudaSetDevice(ctx->cfg.device));
+  memset(out, 0, sizeof *out);
+  const int E = vc->events, G = ctx->grid, NT = vis::threads();
+  const unsigned long long stride = (unsigned long long)G * NT;
+  unsigned long long n4 = (unsigned long long)(vc->traffic_bytes ? vc->traffic_bytes : (1ll << 30)) / 16;
+  const unsigned long long min_n4 = 2ull * vis::loads_per_iter() * stride;
+  if (n4 < min_n4) n4 = min_n4;
+  // the studied kernel's shared memory per CTA keeps the residency the same
+  const int smem = std::max(4 * NT, ctx->cfg.dtype == APK_F32 ? f32::smem_bytes(ctx->cfg.k_tile)
+                                                               : bf16::smem_bytes(ctx->cfg.k_tile));
+  std::mt19937 rng(vc->seed);
+  std::uniform_real_distribution<double> gap((double)vc->gap_min_ns, (double)vc->gap_max_ns);
+  std::vector<long long> sched(E);
+  long long acc = 0;
+  for (int e = 0; e < E; ++e) sched[e] = (acc += (long long)gap(rng));
+
+  struct Bufs {
+    void* p[10] = {};
+    ~Bufs() {
+      for (void* q : p)
+        if (q) cudaFree(q);
+    }
+  } b;
+  int *d_flag, *d_status;
+  long long *d_sched, *d_set, *d_obs, *d_iters, *d_t0, *d_t1;
+  float* d_sink;
+  float4* d_traffic = nullptr;
+  APK_CU(cudaMalloc(&d_flag, sizeof(int)));
+  b.p[0] = d_flag;
+  APK_CU(cudaMalloc(&d_status, sizeof(int)));
+  b.p[1] = d_status;
+  APK_CU(cudaMalloc(&d_sched, sizeof(long long) * E));
+  b.p[2] = d_sched;
+  APK_CU(cudaMalloc(&d_set, sizeof(long long) * E));
+  b.p[3] = d_set;
+  APK_CU(cudaMalloc(&d_obs, sizeof(long long) * (size_t)E * G));
+  b.p[4] = d_obs;
+  APK_CU(cudaMalloc(&d_iters, sizeof(long long) * G));
+  b.p[5] = d_iters;
+  APK_CU(cudaMalloc(&d_t0, sizeof(long long) * G));
+  b.p[6] = d_t0;
+  APK_CU(cudaMalloc(&d_t1, sizeof(long long) * G));
+  b.p[7] = d_t1;
+  APK_CU(cudaMalloc(&d_sink, sizeof(float) * stride));
+  b.p[8] = d_sink;
+  if (vc->loaded) {
+    APK_CU(cudaMalloc(&d_traffic, 16 * n4));
+    b.p[9] = d_traffic;
+    APK_CU(cudaMemset(d_traffic, 0, 16 * n4));
+  }
+  APK_CU(cudaMemset(d_flag, 0, sizeof(int)));
+  APK_CU(cudaMemset(d_status, 0, sizeof(int)));
+  APK_CU(cudaMemset(d_set, 0, sizeof(long long) * E));
+  APK_CU(cudaMemset(d_obs, 0, sizeof(long long) * (size_t)E * G));
+  APK_CU(cudaMemcpy(d_sched, sched.data(), sizeof(long long) * E, cudaMemcpyHostToDevice));
+  APK_CU(cudaDeviceSynchronize());
+
+  VisParams p;
+  memset(&p, 0, sizeof p);
+  p.flag = d_flag;
+  p.sched_ns = d_sched;
+  p.n_events = E;
+  p.set_ns = d_set;
+  p.obs_ns = d_obs;
+  p.iters = d_iters;
+  p.t_begin = d_t0;
+  p.t_end = d_t1;
+  p.work_iters = vc->work_iters;
+  p.traffic = d_traffic;
+  p.traffic_n4 = n4;
+  p.sink = d_sink;
+  p.tail_ns = 2000000;  // 2 ms after the last raise, as src/yield.cu:262-264
+  p.limit_ns = sched[E - 1] + p.tail_ns + 2000000000LL;
+  p.status = d_status;
+  cudaError_t e = vis::launch(p, G, smem, vc->loaded != 0, ctx->kstream);
+  if (e != cudaSuccess) return fail(ctx, APK_ECUDA, "visibility launch failed: %s", cudaGetErrorString(e));
+  APK_CU(cudaStreamSynchronize(ctx->kstream));
+
+  std::vector<long long> set(E), obs((size_t)E * G), iters(G), t0(G), t1(G);
+  int status = 0;
+  APK_CU(cudaMemcpy(set.data(), d_set, sizeof(long long) * E, cudaMemcpyDeviceToHost));
+  APK_CU(cudaMemcpy(obs.data(), d_obs, sizeof(long long) * (size_t)E * G, cudaMemcpyDeviceToHost));
+  APK_CU(cudaMemcpy(iters.data(), d_iters, sizeof(long long) * G, cudaMemcpyDeviceToHost));
+  APK_CU(cudaMemcpy(t0.data(), d_t0, sizeof(long long) * G, cudaMemcpyDeviceToHost));
+  APK_CU(cudaMemcpy(t1.data(), d_t1, sizeof(long long) * G, cudaMemcpyDeviceToHost));
+  APK_CU(cudaMemcpy(&status, d_status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (set_out) memcpy(set_out, set.data(), sizeof(long long) * E);
+  if (obs_out) memcpy(obs_out, obs.data(), sizeof(long long) * (size_t)E * G);
+
+  std::vector<double> dmin, d50, d95, dmax, cad;
+  for (int e2 = 0; e2 < E; ++e2) {
+    if (set[e2] == 0) {
+      ++out->unset;
+      continue;
+    }
+    std::vector<double> d;
+    bool complete = true;
+    for (int c = 1; c < G; ++c) {  // CTA 0 raised the flag itself
+      const long long o = obs[(size_t)e2 * G + c];
+      if (o == 0) {
+        complete = false;
+        break;
+      }
+      d.push_back((o - set[e2]) / 1e3);
+    }
+    if (!complete || d.empty()) {
+      ++out->anomalies;
+      continue;
+    }
+    if (e2 < vc->warmup_events) continue;
+    std::sort(d.begin(), d.end());
+    dmin.push_back(d.front());
+    d50.push_back(pct(d, 0.5));
+    d95.push_back(pct(d, 0.95));
+    dmax.push_back(d.back());
+  }
+  long long tmin = t0[0], tmax = t1[0], total_iters = 0;
+  for (int c = 0; c < G; ++c) {
+    if (iters[c] > 0) cad.push_back((double)(t1[c] - t0[c]) / (double)iters[c]);
+    tmin = std::min(tmin, t0[c]);
+    tmax = std::max(tmax, t1[c]);
+    total_iters += iters[c];
+  }
+  out->n = (int)dmax.size();
+  out->cadence_ns = cad.empty() ? 0.0 : pct(cad, 0.5);
+  out->dmin_p50_us = pct(dmin, 0.5);
+  out->d50_p50_us = pct(d50, 0.5);
+  out->d95_p50_us = pct(d95, 0.5);
+  out->dmax_p50_us = pct(dmax, 0.5);
+  out->dmax_p99_us = pct(dmax, 0.99);
+  if (vc->loaded && tmax > tmin)
+    out->hbm_gbs = (double)total_iters * NT * vis::loads_per_iter() * 16.0 / (double)(tmax - tmin);
+  out->device_status = status;
+  if (status != 0) return fail(ctx, APK_EDEVICE, "visibility probe: a CTA reached its time limit (status %d)", status);
+  return APK_OK;
 }
 
 void* apk_host_alloc(size_t bytes) {

@@ -313,6 +313,21 @@ class Context:
         self._check(self._lib.apk_probe_visibility(self._h, reps, _ptr(out)))
         return out
 
+    def run_visibility(self, events: int = 1000, gap_us=(150.0, 400.0), seed: int = 21, warmup_events: int = 100,
+                       work_iters: int = 0, loaded: bool = False, traffic_bytes: int = 0, raw: bool = False):
+        """Flag-visibility microbenchmark (no tile work).  Returns the summary
+        dict; with raw=True also (set_ns, obs_ns[events][grid]) for OBS1."""
+        vc = L.VisibilityConfig(events, int(gap_us[0] * 1000), int(gap_us[1] * 1000), seed, warmup_events,
+                                work_iters, int(loaded), int(traffic_bytes))
+        r = L.VisibilityResult()
+        grid = self.info["grid"]
+        set_ns = np.zeros(events, np.int64)
+        obs_ns = np.zeros((events, grid), np.int64)
+        self._check(self._lib.apk_run_visibility(self._h, ctypes.byref(vc), ctypes.byref(r), _ptr(set_ns),
+                                                 _ptr(obs_ns)))
+        res = {f: getattr(r, f) for f, _ in L.VisibilityResult._fields_}
+        return (res, set_ns, obs_ns) if raw else res
+
     def run_overhead(self, num_tasks: int, reps: int = 5):
         a = ctypes.c_double()
         b = ctypes.c_double()

@@ -263,6 +263,41 @@ apk_status apk_run_latency(apk_ctx* ctx, const apk_latency_config* lc, apk_laten
  * reps entries.  Needs an idle device. */
 apk_status apk_probe_visibility(apk_ctx* ctx, int reps, long long* offsets_ns);
 
+/* Flag-visibility microbenchmark (src/yield.cu:227-293 and its driver,
+ * src/yield.cu:466-564): no tile work; every CTA of this context's grid (with
+ * the studied kernel's shared memory, so the residency is the same) runs a
+ * work_iters-long dependent FMA chain per iteration, optionally streams
+ * loads from a traffic_bytes buffer far larger than L2 (loaded = 1: HBM
+ * busy), and thread 0 polls the flag; CTA 0 raises it at uniform-random gaps
+ * in [gap_min_ns, gap_max_ns] and ends the run itself.  Delays are
+ * observation - raise on the device clock, over CTAs 1..grid-1 (CTA 0 sees
+ * its own store). */
+typedef struct apk_visibility_config {
+  int events;
+  long long gap_min_ns, gap_max_ns;
+  unsigned seed;
+  int warmup_events;          /* first events left out of the statistics  */
+  int work_iters;             /* FMA chain per polling iteration          */
+  int loaded;                 /* 1 = stream HBM traffic while polling     */
+  long long traffic_bytes;    /* loaded buffer; 0 = 1 GiB                 */
+} apk_visibility_config;
+
+typedef struct apk_visibility_result {
+  int n;                      /* events in the statistics                 */
+  int unset, anomalies;       /* never raised / not seen by every CTA     */
+  double cadence_ns;          /* median CTA's time per polling iteration  */
+  /* per event: min / median / p95 / max delay across CTAs; then p50 over
+   * events (and p99 of the max) */
+  double dmin_p50_us, d50_p50_us, d95_p50_us, dmax_p50_us, dmax_p99_us;
+  double hbm_gbs;             /* loaded: bytes streamed / run time        */
+  int device_status;          /* DEV_WAIT_TIMEOUT_SPIN if a CTA hit its limit */
+} apk_visibility_result;
+
+/* set_ns (events) and obs_ns (events x grid) may be NULL; when given they
+ * receive the raw matrix (0 = not observed), e.g. for an OBS1 dump. */
+apk_status apk_run_visibility(apk_ctx* ctx, const apk_visibility_config* cfg, apk_visibility_result* out,
+                              long long* set_ns, long long* obs_ns);
+
 /* Failure-path self-test: launches the bounded flag spin of
  * apk_probe_visibility on a flag nothing sets, with the given limit.  The
  * kernel must give up, report DEV_WAIT_TIMEOUT_SPIN (3) through its status

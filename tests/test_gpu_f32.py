@@ -269,3 +269,23 @@ def test_reserved_capacity_arm(libapk):
     assert np.all(e0 > 0) and np.all(e4 > 0)
     assert np.median(e4) * 5 < np.median(e0), (np.median(e4), np.median(e0))
     assert 0 < tf4 <= tf0 * 1.02 and tf4 > tf0 * 0.9
+
+
+@pytest.mark.parametrize("loaded", [False, True])
+def test_visibility_probe(libapk, loaded):
+    """Flag-visibility microbenchmark (src/yield.cu:227-293): every raise
+    seen by every CTA, the run ends by itself, the C++ summary matches the
+    OBS1 analysis of the same matrix, the loaded variant keeps HBM busy."""
+    from apk_b200 import obs
+    with _ctx(poll="stage", set_mode="device") as c:
+        res, s, o = c.run_visibility(events=200, warmup_events=20, loaded=loaded, raw=True)
+        grid = c.info["grid"]
+    assert res["device_status"] == 0 and res["unset"] == 0 and res["anomalies"] == 0
+    assert res["n"] == 180 and res["cadence_ns"] > 0
+    assert o.shape == (200, grid)
+    a = obs.analyze(s, o, warmup=20)
+    for k in ("dmin_p50_us", "d50_p50_us", "d95_p50_us", "dmax_p50_us", "dmax_p99_us"):
+        assert abs(a[k] - res[k]) < 1e-9, k
+    assert res["dmax_p99_us"] < 1000.0
+    if loaded:
+        assert res["hbm_gbs"] > 1000.0
