@@ -24,6 +24,7 @@ APK_POLL_OFF, APK_POLL_BOUNDARY, APK_POLL_STAGE = 0, 1, 2
 APK_DISC_DRAIN, APK_DISC_POISON = 0, 2
 APK_SET_DEVICE, APK_SET_HOST_MAPPED, APK_SET_HOST_MEMCPY = 0, 1, 2
 APK_MEM_HOST, APK_MEM_DEVICE = 0, 1
+APK_SCHED_QUEUE, APK_SCHED_CLC = 0, 1
 APK_TASKS_UNBOUNDED = 0xFFFFFFFFFFFFFFFF
 
 
@@ -31,7 +32,7 @@ class Config(ctypes.Structure):
     _fields_ = [("device", c_int), ("dtype", c_int), ("ctas_per_sm", c_int), ("grid", c_int),
                 ("k_tile", c_int), ("poll", c_int), ("discipline", c_int), ("set_mode", c_int),
                 ("max_events", c_int), ("oracle", c_int), ("urgent_split_k", c_int),
-                ("wait_limit_ns", c_ll)]
+                ("wait_limit_ns", c_ll), ("scheduler", c_int)]
 
 
 class DeviceInfo(ctypes.Structure):

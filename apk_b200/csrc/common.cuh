@@ -173,4 +173,60 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, in
       : "memory");
 }
 
+// ---- cluster launch control (sm_100) ---------------------------------------
+// Ask the hardware to cancel one not-yet-launched CTA of this grid; the
+// 16-byte answer lands in *resp and completes 16 transaction bytes on bar
+// (the caller arms bar with expect_tx first).  One-CTA clusters: no
+// multicast form.
+__device__ __forceinline__ void clc_try_cancel(void* resp, uint64_t* bar) {
+  asm volatile("clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];" ::"r"(
+                   smem_u32(resp)),
+               "r"(smem_u32(bar))
+               : "memory");
+}
+// Decode an answer: true and the cancelled CTA's x index, or false (nothing
+// left to take, or the hardware kept the CTA for its own scheduling).
+__device__ __forceinline__ bool clc_query(const void* resp, unsigned* ctaid_x) {
+  unsigned valid = 0, x = 0;
+  asm volatile(
+      "{ .reg .pred p; .reg .b128 r;\n\t"
+      "ld.shared.b128 r, [%2];\n\t"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t"
+      "@p clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, r;\n\t"
+      "}"
+      : "=r"(valid), "=r"(x)
+      : "r"(smem_u32(resp))
+      : "memory");
+  // the next request writes resp through the async proxy
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  *ctaid_x = x;
+  return valid != 0;
+}
+
+// Claim a free bit of a resident-slot bitmap (nslots bits); -1 if none came
+// free within limit_ns.  At most nslots CTAs of one kernel are resident, and a
+// CTA returns its bit before it exits, so a starting CTA finds one.
+__device__ __forceinline__ int slot_claim(unsigned* bits, int nslots, long long limit_ns) {
+  const int W = (nslots + 31) / 32;
+  const long long t0 = globaltimer_ns();
+  while (true) {
+    for (int w = 0; w < W; ++w) {
+      const int valid = nslots - 32 * w < 32 ? nslots - 32 * w : 32;
+      const unsigned full = valid == 32 ? ~0u : ((1u << valid) - 1u);
+      unsigned cur = *reinterpret_cast<volatile unsigned*>(&bits[w]);
+      while ((cur & full) != full) {
+        const int b = __ffs(~cur) - 1;
+        const unsigned old = atomicOr(&bits[w], 1u << b);
+        if (!(old & (1u << b))) return 32 * w + b;
+        cur = old;
+      }
+    }
+    if (globaltimer_ns() - t0 > limit_ns) return -1;
+  }
+}
+__device__ __forceinline__ void slot_release(unsigned* bits, int slot) {
+  atomicAnd(&bits[slot >> 5], ~(1u << (slot & 31)));
+}
+
 }  // namespace apk

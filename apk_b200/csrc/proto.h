@@ -50,6 +50,12 @@ struct QueueProto {
   unsigned long long* end_max;     // atomicMax of CTA exit globaltimer
   int* exited;
   unsigned long long* yields;      // checkpoints taken (accumulator spills)
+  // cluster launch control scheduler: one CTA per task; per-CTA logs,
+  // counters and checkpoint slabs are indexed by a resident slot taken from
+  // this bitmap at CTA start and returned at exit (CTAs come and go)
+  unsigned* slot_bits;             // [(nslots + 31) / 32]
+  int nslots;                      // resident CTAs (sms * ctas_per_sm)
+  long long* setter_state;         // [2] device setter's next event and time base across slot-0 holders
 };
 
 // One heterogeneous background task: C window = A window *

@@ -23,8 +23,8 @@
 
 namespace apk {
 namespace f32 {
-cudaError_t prepare(int poll, int disc, bool oracle, int bk, int* max_ctas_per_sm);
-cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int bk,
+cudaError_t prepare(int poll, int disc, bool oracle, int bk, int sched, int* max_ctas_per_sm);
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int bk, int sched,
                    cudaStream_t stream);
 int smem_bytes(int bk);
 size_t params_bytes();
@@ -142,6 +142,8 @@ struct apk_ctx {
   // checkpoint slab, per-CTA counters
   float* d_slab = nullptr;
   long long* d_slab_hdr = nullptr;
+  unsigned* d_slot_bits = nullptr;    // CLC resident-slot bitmap
+  long long* d_setter_state = nullptr;  // CLC: device setter state across slot-0 holders
   unsigned long long* d_tiles = nullptr;
   unsigned long long* d_utiles = nullptr;
   int* d_exec = nullptr;
@@ -249,7 +251,7 @@ apk_status prepare_kernel(apk_ctx* ctx, int poll) {
   int maxc = 0;
   cudaError_t e;
   if (ctx->cfg.dtype == APK_F32)
-    e = f32::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->cfg.k_tile, &maxc);
+    e = f32::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->cfg.k_tile, ctx->cfg.scheduler, &maxc);
   else
     e = bf16::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->cfg.k_tile, &maxc);
   if (e != cudaSuccess)
@@ -312,6 +314,16 @@ apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
     fail(ctx, APK_EINVAL, "the poison discipline needs a poll mode");
     *out = ctx;
     return APK_EINVAL;
+  }
+  if (c.scheduler != APK_SCHED_QUEUE && c.scheduler != APK_SCHED_CLC) {
+    fail(ctx, APK_EINVAL, "unknown scheduler %d", (int)c.scheduler);
+    *out = ctx;
+    return APK_EINVAL;
+  }
+  if (c.scheduler == APK_SCHED_CLC && (c.dtype != APK_F32 || c.discipline != APK_DISC_DRAIN)) {
+    fail(ctx, APK_EUNSUPPORTED, "the cluster-launch-control scheduler is built for fp32 with the drain discipline");
+    *out = ctx;
+    return APK_EUNSUPPORTED;
   }
   *out = ctx;
   APK_CU(cudaSetDevice(c.device));
@@ -376,6 +388,8 @@ apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
   const size_t slab_floats = (c.dtype == APK_F32 ? 128 * 128 : 256 * 256);
   APK_CU(cudaMalloc(&ctx->d_slab, sizeof(float) * slab_floats * G));
   APK_CU(cudaMalloc(&ctx->d_slab_hdr, sizeof(long long) * 4 * G));
+  APK_CU(cudaMalloc(&ctx->d_slot_bits, sizeof(unsigned) * ((G + 31) / 32)));
+  APK_CU(cudaMalloc(&ctx->d_setter_state, sizeof(long long) * 2));
   APK_CU(cudaMalloc(&ctx->d_tiles, sizeof(unsigned long long) * G));
   APK_CU(cudaMalloc(&ctx->d_utiles, sizeof(unsigned long long) * G));
   ctx->host_set.assign(E, 0);
@@ -416,6 +430,8 @@ apk_status apk_destroy(apk_ctx* ctx) {
   F(ctx->d_uexec);
   F(ctx->d_slab);
   F(ctx->d_slab_hdr);
+  F(ctx->d_slot_bits);
+  F(ctx->d_setter_state);
   F(ctx->d_tiles);
   F(ctx->d_utiles);
   F(ctx->d_exec);
@@ -748,12 +764,22 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
     return fail(ctx, APK_ESTATE, "no background operands set");
   }
   if (!ctx->dAu && poll != APK_POLL_OFF) return fail(ctx, APK_ESTATE, "no urgent operands set");
+  const bool clc = ctx->cfg.scheduler == APK_SCHED_CLC;
+  if (clc && (num_tasks == APK_TASKS_UNBOUNDED || num_tasks > 0x7fffffffull))
+    return fail(ctx, APK_EINVAL, "the CLC scheduler launches one CTA per task: a bounded launch of < 2^31 tasks");
   apk_status s = reset_logs(ctx, num_tasks);
   if (s != APK_OK) return s;
   int* flag = ctx->cfg.set_mode == APK_SET_HOST_MAPPED ? ctx->d_flag_mapped : &ctx->d_ctrl->flag_dev;
   EventProto ev;
   QueueProto q;
   fill_protos(ctx, num_tasks, &ev, &q, flag);
+  if (clc) {
+    APK_CU(cudaMemsetAsync(ctx->d_slot_bits, 0, sizeof(unsigned) * ((ctx->grid + 31) / 32), stream));
+    APK_CU(cudaMemsetAsync(ctx->d_setter_state, 0, sizeof(long long) * 2, stream));
+    q.slot_bits = ctx->d_slot_bits;
+    q.setter_state = ctx->d_setter_state;
+  }
+  q.nslots = ctx->grid;
   if (!(ctx->cfg.oracle && num_tasks != APK_TASKS_UNBOUNDED)) q.exec_count = nullptr;
   ctx->last_tasks = num_tasks;
   ctx->last_grid = ctx->grid;
@@ -822,7 +848,8 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
   p.ev = ev;
   p.q = q;
   if (f32)
-    e = f32::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, bk, stream);
+    e = f32::launch(p, ctx->cfg.scheduler == APK_SCHED_CLC ? (int)num_tasks : ctx->grid, poll,
+                    ctx->cfg.discipline, ctx->cfg.oracle != 0, bk, ctx->cfg.scheduler, stream);
   else
     e = bf16::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, bk, stream);
   if (e != cudaSuccess) return fail(ctx, APK_ECUDA, "kernel launch failed: %s", cudaGetErrorString(e));
@@ -1291,6 +1318,9 @@ apk_status apk_run_reserved(apk_ctx* ctx, unsigned long long num_tasks, int rese
   if (!ctx || trials <= 0 || !e2e_us || num_tasks == 0 || num_tasks == APK_TASKS_UNBOUNDED) return APK_EINVAL;
   if (reserve < 0 || reserve >= ctx->grid)
     return fail(ctx, APK_EINVAL, "reserve %d must leave at least one of the %d background CTAs", reserve, ctx->grid);
+  // a CLC grid occupies every slot the hardware gives it: nothing to hold out
+  if (ctx->cfg.scheduler == APK_SCHED_CLC && reserve != 0)
+    return fail(ctx, APK_EINVAL, "with the CLC scheduler the urgent kernel takes SMs the hardware frees; reserve must be 0");
   if (ctx->running) return fail(ctx, APK_ESTATE, "a launch is already running");
   if (ctx->cfg.dtype != APK_F32) return fail(ctx, APK_EUNSUPPORTED, "baseline mode is fp32 only");
   if (!ctx->dAu) return fail(ctx, APK_ESTATE, "no urgent operands set");
@@ -1364,7 +1394,7 @@ apk_status apk_run_reserved(apk_ctx* ctx, unsigned long long num_tasks, int rese
     const long long t0 = host_now_ns();
     spin_until_ns(t0 + (long long)delay_ns);
     const long long ta = host_now_ns();
-    cudaError_t e = f32::launch(up, utiles, APK_POLL_OFF, APK_DISC_DRAIN, false, bk, ctx->ustream);
+    cudaError_t e = f32::launch(up, utiles, APK_POLL_OFF, APK_DISC_DRAIN, false, bk, APK_SCHED_QUEUE, ctx->ustream);
     if (e != cudaSuccess) return fail(ctx, APK_ECUDA, "urgent launch failed: %s", cudaGetErrorString(e));
     APK_CU(cudaStreamSynchronize(ctx->ustream));
     const long long td = host_now_ns();

@@ -128,7 +128,16 @@ __device__ __forceinline__ void issue_stage(uint8_t* smem, uint64_t* full, uint3
   tma_load_2d(b, tB, col0, k0, &full[slot]);
 }
 
-template <int POLL, int DISC, bool ORACLE, int BK>
+// Work distribution: SCHED_QUEUE = persistent grid of resident CTAs popping
+// a global fetch-add counter (src/persistent.cu:51-79); SCHED_CLC = one CTA
+// per task, each running CTA taking not-yet-launched CTAs' tasks with
+// cluster launch control.  Under CLC the hardware may decline a request
+// (e.g. while a higher-priority stream's kernel waits for an SM); the CTA
+// then exits and frees its SM, and the grid's remaining CTAs launch later.
+enum Sched : int { SCHED_QUEUE = 0, SCHED_CLC = 1 };
+constexpr unsigned long long NO_TASK = ~0ull;
+
+template <int POLL, int DISC, bool ORACLE, int BK, int SCHED>
 __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant__ F32Params p) {
   using C = Cfg<BK>;
   constexpr int S = C::STAGES;
@@ -137,6 +146,13 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
   __shared__ __align__(8) uint64_t full[S];
   __shared__ unsigned long long s_task;
   __shared__ int s_f, s_item;
+  // CLC: the answer buffer and barrier of the one request kept in flight,
+  // the task it will yield, and this CTA's resident slot
+  __shared__ __align__(16) uint4 s_clcResp;
+  __shared__ __align__(8) uint64_t s_clcBar;
+  __shared__ unsigned long long s_clcNext;
+  __shared__ int s_clcInFlight, s_slot;
+  __shared__ uint32_t s_clcPhase;
   // Bookkeeping touched only by tid 0, or needed only across a job switch,
   // lives in shared memory: as per-thread locals it costs every thread
   // registers under the 2-CTA/SM cap (the reference hit the same,
@@ -151,18 +167,35 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
   const int ty = lane >> 3;
   const int arow0 = (warp & 3) * 32 + ty;
   const int bcol = (warp >> 2) * 64 + (lane & 7) * 4;
-  const int cta = blockIdx.x;
-  const int grid = gridDim.x;
+  // (defined here, before the set-up block: ptxas keeps the 2-CTA/SM queue
+  // variants spill-free with this order and not with the definitions below it)
+  const int cta_q = blockIdx.x;
+  const int grid = SCHED == SCHED_CLC ? p.q.nslots : (int)gridDim.x;
 
   if (tid == 0) {
 #pragma unroll
     for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
+    if constexpr (SCHED == SCHED_CLC) mbar_init(&s_clcBar, 1);
     fence_mbar_init();
     s_lastSeen = 0;
     s_nextEv = 0;
     s_gBase = 0;
     s_myTiles = 0;
     s_pending = 0;
+    if constexpr (SCHED == SCHED_CLC) {
+      s_slot = slot_claim(p.q.slot_bits, p.q.nslots, p.wait_limit_ns);
+      s_clcNext = blockIdx.x;
+      s_clcInFlight = 0;
+      s_clcPhase = 0;
+      // a CTA launched mid-run takes the generations raised before it as
+      // seen: their urgent work was popped by the CTAs that observed them
+      const int f0 = flag_load(p.ev.flag);
+      s_lastSeen = f0 > 0 ? f0 : 0;
+      if (s_slot == 0 && p.q.setter_state != nullptr) {
+        s_nextEv = (int)p.q.setter_state[0];
+        s_gBase = p.q.setter_state[1];
+      }
+    }
     tma_prefetch_desc(&p.tmA);
     tma_prefetch_desc(&p.tmB);
     tma_prefetch_desc(&p.tmAu);
@@ -170,6 +203,43 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
     atomicMin(p.q.start_min, (unsigned long long)globaltimer_ns());
   }
   __syncthreads();
+  // per-CTA logs, counters and the checkpoint slab are indexed by cta(): the
+  // block index, or the resident slot under CLC -- re-read where it is used
+  // (rare paths) rather than held in a register under the 128-register cap
+  auto cta = [&]() -> int {
+    if constexpr (SCHED == SCHED_CLC) return *reinterpret_cast<volatile int*>(&s_slot);
+    else return cta_q;
+  };
+  if constexpr (SCHED == SCHED_CLC) {
+    if (s_slot < 0) {  // no slot came free (cannot happen while residency holds)
+      if (tid == 0) report_status(p.ev.status, DEV_BAD_CONFIG, p.ev.abort_word);
+      return;
+    }
+  }
+
+  // CLC: hand out the task prefetched one request earlier and put the next
+  // request in flight, so its latency hides under the coming tile (tid 0)
+  auto clc_take = [&]() -> unsigned long long {
+    if (s_clcInFlight) {
+      s_clcInFlight = 0;
+      if (!mbar_wait(&s_clcBar, s_clcPhase, p.wait_limit_ns)) {
+        report_status(p.ev.status, DEV_WAIT_TIMEOUT_SPIN, p.ev.abort_word);
+        s_clcNext = NO_TASK;
+      } else {
+        unsigned x = 0;
+        s_clcNext = clc_query(&s_clcResp, &x) ? (unsigned long long)x : NO_TASK;
+      }
+      s_clcPhase ^= 1u;
+    }
+    const unsigned long long t = s_clcNext;
+    s_clcNext = NO_TASK;
+    if (t != NO_TASK) {
+      mbar_arrive_expect_tx(&s_clcBar, 16);
+      clc_try_cancel(&s_clcResp, &s_clcBar);
+      s_clcInFlight = 1;
+    }
+    return t;
+  };
 
   uint32_t P = 0, Q = 0;  // issued / consumed stage sequence numbers (uniform)
   bool bad = false;       // this thread saw a wait time out
@@ -187,7 +257,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
 
   auto setter = [&]() {  // device-set events (src/yield.cu:186-195), tid 0 of CTA 0
     const int nextEv = s_nextEv;
-    if (cta == 0 && p.ev.sched_ns != nullptr && nextEv < p.ev.n_sched) {
+    if (cta() == 0 && p.ev.sched_ns != nullptr && nextEv < p.ev.n_sched) {
       const long long now = globaltimer_ns();
       if (s_gBase == 0) s_gBase = now;
       if (now >= s_gBase + p.ev.sched_ns[nextEv]) {
@@ -228,7 +298,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
     }
     if (tid == 0) {
       const long long g = globaltimer_ns();
-      for (int e = s_lastSeen; e < f && e < p.ev.max_events; ++e) p.ev.obs_ns[(size_t)e * grid + cta] = g;
+      for (int e = s_lastSeen; e < f && e < p.ev.max_events; ++e) p.ev.obs_ns[(size_t)e * grid + cta()] = g;
       s_item = s_lastSeen;
       s_lastSeen = f;
       s_site = site;
@@ -249,7 +319,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
         const int it = atomicAdd(&p.ev.uq_next[popE], 1);
         if (it == 0) {
           p.ev.claim_ns[popE] = globaltimer_ns();
-          p.ev.claim[popE] = cta + 1;
+          p.ev.claim[popE] = cta() + 1;
           p.ev.claim_site[popE] = s_site;
           p.ev.inflight[popE] = s_inflight;
           if (p.ev.ack != nullptr) ack_host(&p.ev.ack[2 * popE]);
@@ -269,7 +339,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
         // checkpoint: drain in-flight stages, park the accumulators
         drain();
         if (bg_active) {
-          float4* s4 = reinterpret_cast<float4*>(p.slab) + (size_t)cta * 16 * NT;
+          float4* s4 = reinterpret_cast<float4*>(p.slab) + (size_t)cta() * 16 * NT;
 #pragma unroll
           for (int i = 0; i < 8; ++i)
 #pragma unroll
@@ -280,7 +350,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
             s_bgRow0 = row0;
             s_bgCol0 = col0;
             s_bgC = c;
-            long long* hdr = p.slab_hdr + (size_t)cta * 4;
+            long long* hdr = p.slab_hdr + (size_t)cta() * 4;
             hdr[0] = (long long)s_bgTask;
             hdr[1] = c;
             hdr[2] = popE;
@@ -315,7 +385,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
         c = s_bgC;
         kst0 = 0;
         nk = p.nk;
-        const float4* s4 = reinterpret_cast<const float4*>(p.slab) + (size_t)cta * 16 * NT;
+        const float4* s4 = reinterpret_cast<const float4*>(p.slab) + (size_t)cta() * 16 * NT;
 #pragma unroll
         for (int i = 0; i < 8; ++i)
 #pragma unroll
@@ -338,7 +408,10 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
       int fl = 0;
       bool yb = false;
       if (tid == 0) {
-        if (!s_pending) s_task = atomicAdd(p.q.next_task, 1ull);
+        if (!s_pending) {
+          if constexpr (SCHED == SCHED_CLC) s_task = clc_take();
+          else s_task = atomicAdd(p.q.next_task, 1ull);
+        }
         s_pending = 0;
         const int ab = *reinterpret_cast<volatile int*>(p.ev.abort_word);
         fl = s_lastSeen;
@@ -468,34 +541,55 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
   drain();
   if (tid == 0) {
     if (bad) report_status(p.ev.status, DEV_WAIT_TIMEOUT_FULL, p.ev.abort_word);
-    p.q.tiles_done[cta] = s_myTiles;
+    if constexpr (SCHED == SCHED_CLC) {
+      // a request still in flight (a stopped or aborted run) must land before
+      // shared memory goes away; a task it took is dropped with the run
+      if (s_clcInFlight) mbar_wait(&s_clcBar, s_clcPhase, p.wait_limit_ns);
+      if (cta() == 0 && p.q.setter_state != nullptr) {
+        p.q.setter_state[0] = s_nextEv;
+        p.q.setter_state[1] = s_gBase;
+      }
+      atomicAdd(&p.q.tiles_done[cta()], s_myTiles);
+    } else {
+      p.q.tiles_done[cta()] = s_myTiles;
+    }
     atomicMax(p.q.end_max, (unsigned long long)globaltimer_ns());
     atomicAdd(p.q.exited, 1);
+    if constexpr (SCHED == SCHED_CLC) {
+      __threadfence();
+      slot_release(p.q.slot_bits, cta());  // last: the slot's logs are written
+    }
   }
 }
 
 // Host-side dispatch over the template instantiations.
 
-template <int POLL, int DISC, bool ORACLE, int BK>
+template <int POLL, int DISC, bool ORACLE, int BK, int SCHED>
 static const void* kernel_ptr() {
-  return reinterpret_cast<const void*>(&sgemm_persistent<POLL, DISC, ORACLE, BK>);
+  return reinterpret_cast<const void*>(&sgemm_persistent<POLL, DISC, ORACLE, BK, SCHED>);
 }
 
-static const void* select_kernel(int poll, int disc, bool oracle, int bk) {
-#define APK_SEL(PL, DS, OR)                                                        \
-  if (poll == PL && disc == DS && oracle == OR) {                                 \
-    if (bk == 32) return kernel_ptr<PL, DS, OR, 32>();                           \
-    if (bk == 64) return kernel_ptr<PL, DS, OR, 64>();                           \
+static const void* select_kernel(int poll, int disc, bool oracle, int bk, int sched) {
+#define APK_SEL(PL, DS, OR, SC)                                                    \
+  if (poll == PL && disc == DS && oracle == OR && sched == SC) {                  \
+    if (bk == 32) return kernel_ptr<PL, DS, OR, 32, SC>();                       \
+    if (bk == 64) return kernel_ptr<PL, DS, OR, 64, SC>();                       \
   }
-  APK_SEL(POLL_OFF, DISC_DRAIN, false)
-  APK_SEL(POLL_OFF, DISC_DRAIN, true)
-  APK_SEL(POLL_BOUNDARY, DISC_DRAIN, false)
-  APK_SEL(POLL_BOUNDARY, DISC_DRAIN, true)
-  APK_SEL(POLL_BOUNDARY, DISC_POISON, false)
-  APK_SEL(POLL_STAGE, DISC_DRAIN, false)
-  APK_SEL(POLL_STAGE, DISC_DRAIN, true)
-  APK_SEL(POLL_STAGE, DISC_POISON, false)
-  APK_SEL(POLL_STAGE, DISC_POISON, true)
+  APK_SEL(POLL_OFF, DISC_DRAIN, false, SCHED_QUEUE)
+  APK_SEL(POLL_OFF, DISC_DRAIN, true, SCHED_QUEUE)
+  APK_SEL(POLL_BOUNDARY, DISC_DRAIN, false, SCHED_QUEUE)
+  APK_SEL(POLL_BOUNDARY, DISC_DRAIN, true, SCHED_QUEUE)
+  APK_SEL(POLL_BOUNDARY, DISC_POISON, false, SCHED_QUEUE)
+  APK_SEL(POLL_STAGE, DISC_DRAIN, false, SCHED_QUEUE)
+  APK_SEL(POLL_STAGE, DISC_DRAIN, true, SCHED_QUEUE)
+  APK_SEL(POLL_STAGE, DISC_POISON, false, SCHED_QUEUE)
+  APK_SEL(POLL_STAGE, DISC_POISON, true, SCHED_QUEUE)
+  APK_SEL(POLL_OFF, DISC_DRAIN, false, SCHED_CLC)
+  APK_SEL(POLL_OFF, DISC_DRAIN, true, SCHED_CLC)
+  APK_SEL(POLL_BOUNDARY, DISC_DRAIN, false, SCHED_CLC)
+  APK_SEL(POLL_BOUNDARY, DISC_DRAIN, true, SCHED_CLC)
+  APK_SEL(POLL_STAGE, DISC_DRAIN, false, SCHED_CLC)
+  APK_SEL(POLL_STAGE, DISC_DRAIN, true, SCHED_CLC)
 #undef APK_SEL
   return nullptr;
 }
@@ -503,8 +597,8 @@ static const void* select_kernel(int poll, int disc, bool oracle, int bk) {
 int smem_bytes(int bk) { return bk == 32 ? Cfg<32>::SMEM_BYTES : Cfg<64>::SMEM_BYTES; }
 size_t params_bytes() { return sizeof(F32Params); }
 
-cudaError_t prepare(int poll, int disc, bool oracle, int bk, int* max_ctas_per_sm) {
-  const void* k = select_kernel(poll, disc, oracle, bk);
+cudaError_t prepare(int poll, int disc, bool oracle, int bk, int sched, int* max_ctas_per_sm) {
+  const void* k = select_kernel(poll, disc, oracle, bk, sched);
   if (!k) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(bk));
   if (e != cudaSuccess) return e;
@@ -514,9 +608,9 @@ cudaError_t prepare(int poll, int disc, bool oracle, int bk, int* max_ctas_per_s
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(max_ctas_per_sm, k, NT, smem_bytes(bk));
 }
 
-cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int bk,
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int bk, int sched,
                    cudaStream_t stream) {
-  const void* k = select_kernel(poll, disc, oracle, bk);
+  const void* k = select_kernel(poll, disc, oracle, bk, sched);
   if (!k) return cudaErrorInvalidValue;
   void* args[] = {const_cast<F32Params*>(&prm)};
   return cudaLaunchKernel(k, dim3(grid), dim3(NT), args, smem_bytes(bk), stream);
@@ -607,7 +701,7 @@ extern "C" apk_status apk_sgemm_f32_noalloc(const float* A, const float* B, floa
       void* ptr = nullptr;
       if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return APK_ECUDA;
       int maxc = 0;
-      if (prepare(POLL_OFF, DISC_DRAIN, false, 32, &maxc) != cudaSuccess || maxc < 1) return APK_ECUDA;
+      if (prepare(POLL_OFF, DISC_DRAIN, false, 32, SCHED_QUEUE, &maxc) != cudaSuccess || maxc < 1) return APK_ECUDA;
       int sms = 0;
       if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return APK_ECUDA;
       if (!g_noalloc_encode) {
@@ -677,6 +771,6 @@ extern "C" apk_status apk_sgemm_f32_noalloc(const float* A, const float* B, floa
   // written, not accumulated); start_min starts at all-ones for atomicMin
   if (cudaMemsetAsync(d.scratch, 0, kNoAllocHeaderBytes, s) != cudaSuccess) return APK_ECUDA;
   if (cudaMemsetAsync(&h->start_min, 0xFF, sizeof(h->start_min), s) != cudaSuccess) return APK_ECUDA;
-  if (launch(p, grid, POLL_OFF, DISC_DRAIN, false, 32, s) != cudaSuccess) return APK_ECUDA;
+  if (launch(p, grid, POLL_OFF, DISC_DRAIN, false, 32, SCHED_QUEUE, s) != cudaSuccess) return APK_ECUDA;
   return APK_OK;
 }

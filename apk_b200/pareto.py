@@ -12,6 +12,11 @@ outputs, K = 256), uniform[-1,1] from the reference generator.
   urgent job is a separate kernel of U CTAs on a max-priority stream
   launched at U(0.2, 0.8) of the drain.  y: host arrival -> urgent done
   (host clock); x: the background's TFLOP/s with R slots held out.
+* Priority arm (cluster launch control): the background grid is one CTA
+  per task, scheduled by CLC work stealing with nothing held out; the urgent
+  kernel is launched on the max-priority stream as in the reserved arm.
+  While it waits the hardware declines the background's requests, CTAs exit
+  at their next tile boundary and it takes their SMs.
 * Cooperative arm: the full grid polls every stage; the host stores the
   yield flag once per 1 ms at a uniform offset and the urgent tiles are
   popped by the CTAs that observe it (split-K 1: U items).  y: host store ->
@@ -60,6 +65,14 @@ def main():
                        "e2e_p50_us": _pct(e2e, 0.5), "e2e_p99_us": _pct(e2e, 0.99), "trials": len(e2e)}
                 rows.append(row)
                 print(json.dumps(row), flush=True)
+        with apk_b200.Context(poll="off", urgent_split_k=1, scheduler="clc") as c:
+            c.set_background(A, B)
+            c.set_urgent(Au, Bu)
+            e2e, tf = c.run_reserved(args.bg_tasks, 0, args.trials, seed=21)
+            row = {"arm": "clc_priority", "urgent_tiles": u, "reserve": 0, "bg_tflops": tf,
+                   "e2e_p50_us": _pct(e2e, 0.5), "e2e_p99_us": _pct(e2e, 0.99), "trials": len(e2e)}
+            rows.append(row)
+            print(json.dumps(row), flush=True)
         with apk_b200.Context(poll="stage", set_mode="host_memcpy", urgent_split_k=1,
                               max_events=args.events + 8) as c:
             c.set_background(A, B)

@@ -20,6 +20,7 @@ _DISC = {"drain": L.APK_DISC_DRAIN, "poison": L.APK_DISC_POISON}
 _SET = {"device": L.APK_SET_DEVICE, "host_mapped": L.APK_SET_HOST_MAPPED,
         "host_memcpy": L.APK_SET_HOST_MEMCPY}
 _DTYPE = {"f32": L.APK_F32, "bf16": L.APK_BF16}
+_SCHED = {"queue": L.APK_SCHED_QUEUE, "clc": L.APK_SCHED_CLC}
 
 
 class ApkError(RuntimeError):
@@ -104,7 +105,7 @@ class Context:
     def __init__(self, device: int = 0, dtype: str = "f32", ctas_per_sm: int = 0, grid: int = 0,
                  k_tile: int = 0, poll: str = "stage", discipline: str = "drain",
                  set_mode: str = "host_memcpy", max_events: int = 4096, oracle: bool = False,
-                 urgent_split_k: int = 8, wait_limit_ns: int = 2_000_000_000):
+                 urgent_split_k: int = 8, wait_limit_ns: int = 2_000_000_000, scheduler: str = "queue"):
         self._lib = L.load()
         cfg = L.Config()
         self._lib.apk_config_default(ctypes.byref(cfg))
@@ -112,6 +113,7 @@ class Context:
         cfg.k_tile, cfg.poll, cfg.discipline = k_tile, _POLL[poll], _DISC[discipline]
         cfg.set_mode, cfg.max_events, cfg.oracle = _SET[set_mode], max_events, int(oracle)
         cfg.urgent_split_k, cfg.wait_limit_ns = urgent_split_k, int(wait_limit_ns)
+        cfg.scheduler = _SCHED[scheduler]
         self.cfg = cfg
         self.dtype = dtype
         h = ctypes.c_void_p()

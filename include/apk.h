@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define APK_ABI_VERSION 1
+#define APK_ABI_VERSION 2
 #define APK_TASKS_UNBOUNDED 0xFFFFFFFFFFFFFFFFull
 
 typedef enum apk_status {
@@ -71,6 +71,15 @@ typedef enum apk_set_mode {
 
 typedef enum apk_mem_kind { APK_MEM_HOST = 0, APK_MEM_DEVICE = 1 } apk_mem_kind;
 
+/* How background tasks reach CTAs.  QUEUE: a persistent grid of resident
+ * CTAs popping a global fetch-add counter (src/persistent.cu:51-79).  CLC
+ * (fp32, drain discipline, bounded launches only): one CTA per task, running
+ * CTAs take not-yet-launched CTAs' tasks through Blackwell cluster launch
+ * control; when the hardware declines (a higher-priority stream's kernel is
+ * waiting) CTAs exit and free their SMs, and the rest of the grid launches
+ * later.  The cooperative yield works the same under both. */
+typedef enum apk_scheduler { APK_SCHED_QUEUE = 0, APK_SCHED_CLC = 1 } apk_scheduler;
+
 typedef struct apk_config {
   int device;
   apk_dtype dtype;
@@ -85,6 +94,7 @@ typedef struct apk_config {
   int oracle;               /* 1 = count executions per task and per event    */
   int urgent_split_k;       /* urgent items per urgent output tile            */
   long long wait_limit_ns;  /* bound on every device-side wait                */
+  apk_scheduler scheduler;  /* (ABI 2) background work distribution           */
 } apk_config;
 
 /* Fill *cfg with the defaults (fp32, full residency, default k_tile, stage

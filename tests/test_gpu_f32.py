@@ -289,3 +289,68 @@ def test_visibility_probe(libapk, loaded):
     assert res["dmax_p99_us"] < 1000.0
     if loaded:
         assert res["hbm_gbs"] > 1000.0
+
+
+def test_clc_scheduler_drain_exactly_once(libapk):
+    """Cluster-launch-control scheduler: one CTA per task, running CTAs take
+    the pending ones; every task exactly once, output within tolerance."""
+    A, B = oracle.gen_uniform(1024, 1024, 1024, 21)
+    ref = oracle.gemm_f64(A, B)
+    with _ctx(poll="off", oracle=True, scheduler="clc") as c:
+        C = c.gemm(A, B)
+        st = c.run_stats()
+        c.set_background(A, B)
+        c.set_urgent(*oracle.gen_uniform(U_M, U_N, U_K, 99))
+        c.launch(3 * 64)
+        c.wait(30)
+        ex, _ = c.read_oracle(3 * 64)
+    _check(C, ref, 1024)
+    assert st["tiles_done"] == 64 and st["device_status"] == 0
+    assert np.all(ex == 1)
+
+
+def test_clc_stage_yields_bitwise(libapk):
+    """CLC scheduler with per-stage device-set yields: checkpoint/resume is
+    bitwise and every task and urgent item runs exactly once."""
+    A, B = oracle.gen_uniform(4096, 4096, 4096, 21)
+    Au, Bu, refu = _urgent_ref()
+    with _ctx(poll="off") as c:
+        Cref = c.gemm(A, B)
+    nev = 20
+    with _ctx(poll="stage", set_mode="device", oracle=True, scheduler="clc") as c:
+        ntasks = 2048
+        c.set_background(A, B)
+        c.set_urgent(Au, Bu)
+        c.schedule_device_events((np.arange(nev, dtype=np.int64) + 1) * 150_000)
+        c.launch(ntasks)
+        c.wait(60)
+        C = c.read_output()
+        ev = c.read_events()
+        st = c.run_stats()
+        ex, ue = c.read_oracle(ntasks)
+        fired = int(np.count_nonzero(ev["set_ns"][:nev]))
+        outs = [c.read_urgent_output(e) for e in range(fired) if ev["claimer"][e]]
+        uitems = 4 * c.cfg.urgent_split_k
+    assert fired >= 10 and st["yields"] > 0 and st["device_status"] == 0
+    assert np.array_equal(C.view(np.uint32), Cref.view(np.uint32)), "resume not bitwise"
+    for Cu in outs:
+        _check(Cu, refu, U_K)
+    v = oracle.exactly_once(ex, ue[:fired], ev["claimer"][:fired], ev["set_ns"][:fired], uitems, fired)
+    assert v["pass"], v
+
+
+def test_clc_yields_sms_to_a_higher_priority_kernel(libapk):
+    """With the queue scheduler the urgent kernel on the high-priority stream
+    waits for the whole drain; under CLC the hardware declines requests while
+    it waits, CTAs exit at tile boundaries and it starts within a few tiles."""
+    A, B = oracle.gen_uniform(4096, 4096, 4096, 21)
+    Au, Bu, _ = _urgent_ref()
+    med = {}
+    for sched in ("queue", "clc"):
+        with _ctx(poll="off", urgent_split_k=1, scheduler=sched) as c:
+            c.set_background(A, B)
+            c.set_urgent(Au, Bu)
+            e2e, tf = c.run_reserved(8192, 0, 8, seed=3)
+            med[sched] = float(np.median(e2e))
+            assert tf > 10
+    assert med["clc"] * 5 < med["queue"], med
