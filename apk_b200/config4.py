@@ -35,6 +35,8 @@ def main():
     ap.add_argument("--tasks", type=int, default=1 << 20)
     ap.add_argument("--seed", type=int, default=21)
     ap.add_argument("--rate-hz", type=float, default=2000.0)
+    ap.add_argument("--narrow-k", type=int, default=0,
+                    help="tasks with k below this run as 256x128 tiles (APK_TASK_NARROW)")
     args = ap.parse_args()
 
     import numpy as np
@@ -50,6 +52,8 @@ def main():
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
 
     tasks, n_chk = gen_tasks(args.tasks, args.seed)
+    if args.narrow_k > 0:
+        tasks["flags"] |= np.where(tasks["k"] < args.narrow_k, 2, 0).astype(tasks["flags"].dtype)
     mine = shard_tasks(tasks, world, rank)
     my_tasks = tasks[mine]
     my_flops = float((2.0 * my_tasks["m"].astype(np.float64) * my_tasks["n"] * my_tasks["k"]).sum())

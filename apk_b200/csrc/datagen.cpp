@@ -167,7 +167,7 @@ long long apk_gen_tasks(unsigned long long seed, int n, int mn_lo, int mn_hi, in
       // disjoint 2048 x 2048 output windows that no other task touches
       d.c_row0 = c_free_rows + (t / 4) * 2048;
       d.c_col0 = (t % 4) * 2048;
-      d.flags = 1;
+      d.flags = APK_TASK_SAMPLED;
     } else {
       d.c_row0 = (int)(g() % (unsigned long long)(c_free_rows - d.m + 1));
       d.c_col0 = uniform_multiple(g, c_cols - d.n, 64);

@@ -84,9 +84,13 @@ constexpr int RASTER_GROUP = 8;                  // tile-rows per raster group
 // per 2^19 MACs where two M=128, N=128 instructions (one per 128-row half)
 // would read 16 KB.
 constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, 256, /*A MN-major*/ true, /*B MN-major*/ false);
+// A task tile with only 128 valid rows (m an odd multiple of 128) multiplies
+// just those: N = 128, one A box per stage (9.5% of configs[4]'s MMA work
+// went to rows no one stores).
+constexpr uint32_t IDESC_HALF = tc::idesc_bf16_f32(128, 128, true, false);
 
 enum : int { T_BG = 1, T_URG = 2, T_SUSPEND = 3, T_STOP = 4 };
-enum : int { F_FIRST = 1, F_LAST = 2, F_RESUME = 4, F_WIDE = 8 };
+enum : int { F_FIRST = 1, F_LAST = 2, F_RESUME = 4, F_WIDE = 8, F_HALF = 16 };
 enum : int { E_STORE_C = 1, E_STORE_U = 2, E_SPILL = 3, E_RESTORE = 4, E_EXIT = 5 };
 
 struct StageTag {
@@ -216,10 +220,11 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
       t.task = task;
       if (tA != nullptr) {
         const int nb_chunks = (flags & F_WIDE) ? 4 : 2;
-        mbar_arrive_expect_tx(&sh.full[s], A_BYTES + nb_chunks * B_CHUNK);
+        const bool half = (flags & F_HALF) != 0;
+        mbar_arrive_expect_tx(&sh.full[s], (half ? A_HALF : A_BYTES) + nb_chunks * B_CHUNK);
         uint8_t* st = stages + s * STAGE_BYTES;
         tma_load_2d(st, tA, ak, ar0, &sh.full[s]);
-        tma_load_2d(st + A_HALF, tA, ak, ar0 + 128, &sh.full[s]);
+        if (!half) tma_load_2d(st + A_HALF, tA, ak, ar0 + 128, &sh.full[s]);
         for (int b = 0; b < nb_chunks; ++b) tma_load_2d(st + A_BYTES + b * B_CHUNK, tB, bc0 + 64 * b, bk, &sh.full[s]);
       } else {
         mbar_arrive(&sh.full[s]);  // control slot: no data
@@ -300,7 +305,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         bk0 = td.b_k0;
         nk = td.k / BK;
         mvalid = (td.m - tm * BM) < BM ? (td.m - tm * BM) : BM;
-        wide = (tn + 2) * BNH <= td.n ? F_WIDE : 0;
+        wide = !(td.flags & APK_TASK_NARROW) && (tn + 2) * BNH <= td.n ? F_WIDE : 0;
         // checksum / oracle index of the tile's first 256x128 half
         tag_task = (unsigned long long)(td.chk_base + (long long)tm * (td.n / BNH) + tn);
       } else {
@@ -331,7 +336,8 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
             if (n > 0 && c > 0) resume = true;
           }
         }
-        const int flags = (c == 0 ? F_FIRST : 0) | (c == nk - 1 ? F_LAST : 0) | (resume ? F_RESUME : 0) | wide;
+        const int flags = (c == 0 ? F_FIRST : 0) | (c == nk - 1 ? F_LAST : 0) | (resume ? F_RESUME : 0) | wide |
+                          (mvalid <= BNH ? F_HALF : 0);
         resume = false;
         // e carries the valid rows of the tile, task the oracle / checksum index
         if (!emit(T_BG, flags, row0, col0, mvalid, 0, tag_task, &p.tmA, &p.tmB, ar0, bc0, ak0 + c * BK,
@@ -419,10 +425,11 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         // second half of a wide tile reads B chunks 2-3 into buffer 1.
         const uint32_t acc = (kk > 0 || !(t.flags & F_FIRST)) ? 1u : 0u;
         const uint64_t bdesc = tc::smem_desc(sa + kk * 32, 16, R::A_SBO, R::A_LAYOUT);
-        tc::mma_bf16(d0, tc::smem_desc(sb + kk * 2048, B_CHUNK, 1024, tc::LAYOUT_SW128), bdesc, IDESC, acc);
+        const uint32_t idesc = (t.flags & F_HALF) ? IDESC_HALF : IDESC;
+        tc::mma_bf16(d0, tc::smem_desc(sb + kk * 2048, B_CHUNK, 1024, tc::LAYOUT_SW128), bdesc, idesc, acc);
         if (cwide)
           tc::mma_bf16(d0 + 256, tc::smem_desc(sb + 2 * B_CHUNK + kk * 2048, B_CHUNK, 1024, tc::LAYOUT_SW128),
-                       bdesc, IDESC, acc);
+                       bdesc, idesc, acc);
       }
       tc::commit(&sh.empty[s]);  // frees the slot once these MMAs have read it
       if (t.flags & F_LAST) {

@@ -563,8 +563,10 @@ apk_status apk_set_tasks(apk_ctx* ctx, const apk_task* tasks, int n, long long n
         d.c_col0 + d.n > ctx->c_cols || tiles_m > 63 || tiles_n > 63 || d.chk_base < 0 ||
         d.chk_base + (long long)tiles_m * tiles_n > n_chk)
       return fail(ctx, APK_EINVAL, "task %d does not fit the pools / checksum array", t);
+    const int step = (d.flags & APK_TASK_NARROW) ? 1 : 2;
     for (int tm = 0; tm < tiles_m; ++tm)
-      for (int tn = 0; tn < tiles_n; tn += 2) work.push_back(((unsigned)t << 12) | ((unsigned)tm << 6) | (unsigned)tn);
+      for (int tn = 0; tn < tiles_n; tn += step)
+        work.push_back(((unsigned)t << 12) | ((unsigned)tm << 6) | (unsigned)tn);
     flops += 2.0 * d.m * d.n * (double)d.k;
     halves += (unsigned long long)tiles_m * tiles_n;
   }

@@ -357,9 +357,16 @@ typedef struct apk_task {
   int a_row0, a_k0;
   int b_k0, b_col0;
   int c_row0, c_col0;
-  int flags;
+  int flags;                /* APK_TASK_* bits                                 */
   long long chk_base;
 } apk_task;
+/* task flags: SAMPLED marks a task whose output window no other task touches
+ * (set by apk_gen_tasks for spot checks); NARROW runs the task as 256x128
+ * tiles, each holding one of the two TMEM accumulator buffers so its
+ * epilogue overlaps the next tile's MMAs, instead of 256x256 tiles that hold
+ * both (better for short-k tasks, whose epilogue is a larger share). */
+#define APK_TASK_SAMPLED 1
+#define APK_TASK_NARROW 2
 
 /* Operand pools of a bf16 context: A [a_rows][a_cols] bf16, B [b_rows][b_cols]
  * bf16, C [c_rows][c_cols] fp32 (task outputs land in their windows). */
