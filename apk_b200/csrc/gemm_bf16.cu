@@ -491,7 +491,10 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         if (!bwait(&sh.tfull[j.buf], eb[j.buf] & 1, p, sh)) break;
         ++eb[j.buf];
         tc::fence_after_sync();
-        double csum[2] = {0.0, 0.0};  // task mode: this lane's sum(c^2) per half, fixed order
+        // task mode: this lane's sum(c^2) per half in a fixed order; fp32 per
+        // lane (256 terms, ~1e-6 relative) keeps the double conversions off
+        // the path that frees TMEM, the lanes and warps add up in double
+        float csum[2] = {0.0f, 0.0f};
 #pragma unroll 1
         for (int bb = g; bb < 8 * nh; bb += 2) {
           const int hh = bb >> 3, blk = bb & 7;
@@ -519,8 +522,8 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
             if (p.task_mode) {
 #pragma unroll
               for (int i = 0; i < 32; ++i) {
-                const double x = (double)__uint_as_float(v[i]);
-                csum[hh] += x * x;
+                const float x = __uint_as_float(v[i]);
+                csum[hh] = fmaf(x, x, csum[hh]);
               }
             }
           } else {
@@ -543,7 +546,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         if (j.action != E_SPILL) {
           if (p.task_mode && j.action == E_STORE_C) {
             for (int hh = 0; hh < nh; ++hh) {
-              double s = csum[hh];
+              double s = (double)csum[hh];
 #pragma unroll
               for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
               if (lane == 0) sh.chk_part[sl][hh][ew] = s;
