@@ -173,6 +173,23 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, in
       : "memory");
 }
 
+// ---- streamed operands ------------------------------------------------------
+// Wait (bounded) until both readiness words are nonzero; the copies they
+// announce were written by a copy engine, so order this thread's later
+// async-proxy (TMA) reads after the acquire.  False on timeout.
+__device__ __forceinline__ bool wait_ready2(const int* a, const int* b, long long limit_ns) {
+  const long long t0 = globaltimer_ns();
+  while (true) {
+    int va, vb;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(va) : "l"(a) : "memory");
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(vb) : "l"(b) : "memory");
+    if (va != 0 && vb != 0) break;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
+
 // ---- cluster launch control (sm_100) ---------------------------------------
 // Ask the hardware to cancel one not-yet-launched CTA of this grid; the
 // 16-byte answer lands in *resp and completes 16 transaction bytes on bar

@@ -318,6 +318,19 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         nk = p.nk;
         mvalid = BM;
         wide = col0 + BN <= p.ldc ? F_WIDE : 0;
+        // streamed operands: the A row panel and the B column panel(s) of
+        // the tile must have landed before its first TMA load
+        if (p.st.a_ready != nullptr) {
+          const int* ar = &p.st.a_ready[tm / p.st.panel_tm];
+          const int u = col0 / BNH;
+          if (!wait_ready2(ar, &p.st.b_ready[u / p.st.b_units], p.wait_limit_ns) ||
+              (wide && !wait_ready2(ar, &p.st.b_ready[(u + 1) / p.st.b_units], p.wait_limit_ns))) {
+            vstore(&sh.abort, 1);
+            report_status(p.ev.status, DEV_WAIT_TIMEOUT_SPIN, p.ev.abort_word);
+            ok = false;
+            break;
+          }
+        }
       }
       bool resume = false;
       for (int c = 0; c < nk && ok; ++c) {
@@ -572,6 +585,12 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
               } else {
                 ++sh.tiles;
                 if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[j.task], 1);
+                if (p.st.done != nullptr) {  // every warp fenced its stores above
+                  const int tiles_m = p.total_tiles / p.tiles_n, pn = (j.row0 / BM) / p.st.panel_tm;
+                  const int rows =
+                      tiles_m - pn * p.st.panel_tm < p.st.panel_tm ? tiles_m - pn * p.st.panel_tm : p.st.panel_tm;
+                  if (atomicAdd(&p.st.done[pn], 1u) + 1u == (unsigned)(rows * p.tiles_n)) ack_host(&p.st.ack[pn]);
+                }
               }
               count_trigger(p.ev);
             } else {

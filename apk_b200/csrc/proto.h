@@ -58,6 +58,20 @@ struct QueueProto {
   long long* setter_state;         // [2] device setter's next event and time base across slot-0 holders
 };
 
+// Streamed operands (apk_gemm from host memory): A arrives in row panels of
+// panel_tm tile rows and B in 128-column panels while the kernel runs; a
+// tile starts once its A row panel and B column panel are flagged, and each
+// finished C row panel is acknowledged to the host for its copy back.
+struct StreamProto {
+  const int* a_ready;   // [n_panels] set by the copy stream after A panel p (nullptr = resident)
+  const int* b_ready;   // [N / (128 * b_units)] after B column panel j
+  int b_units;          // 128-column units per B column panel
+  int panel_tm;         // tile rows per panel
+  int n_panels;
+  unsigned* done;       // [n_panels] finished tiles per C row panel
+  int* ack;             // mapped host memory [n_panels]: panel p complete
+};
+
 // One heterogeneous background task: C window = A window *
 // B window, each a window of a shared operand pool (so the tensor maps are
 // fixed).  Layout-identical to apk_task in include/apk.h.
@@ -93,6 +107,7 @@ struct F32Params {
   long long wait_limit_ns;
   EventProto ev;
   QueueProto q;
+  StreamProto st;
 };
 
 // Visibility microbenchmark parameters (the flag-notification probe of

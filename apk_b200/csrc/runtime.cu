@@ -103,6 +103,19 @@ struct apk_ctx {
   int cc_major = 0, cc_minor = 0;
   char name[128] = {0};
   cudaStream_t kstream = nullptr, cstream = nullptr, ustream = nullptr;
+  // streamed apk_gemm (host operands): copy-in and copy-back streams, the
+  // readiness words the kernel waits on, per-panel tile counters, mapped
+  // per-panel completion acks and a pinned 1 the readiness writes copy from
+  cudaStream_t h2dstream = nullptr, d2hstream = nullptr;
+  cudaEvent_t ev_reset = nullptr;
+  int* d_ready = nullptr;
+  unsigned* d_pdone = nullptr;
+  int* h_pack = nullptr;
+  int* d_pack_mapped = nullptr;
+  int* h_one = nullptr;
+  int stream_cap = 0;       // capacity of d_ready (panels + column panels)
+  int pack_cap = 0;         // capacity of d_pdone / h_pack
+  StreamProto st_cfg{};     // copied into the launch's parameters (zeros = resident operands)
   cudaEvent_t ev_start = nullptr, ev_done = nullptr;
   bool running = false;
 
@@ -447,6 +460,13 @@ apk_status apk_destroy(apk_ctx* ctx) {
   if (ctx->kstream) cudaStreamDestroy(ctx->kstream);
   if (ctx->cstream) cudaStreamDestroy(ctx->cstream);
   if (ctx->ustream) cudaStreamDestroy(ctx->ustream);
+  if (ctx->h2dstream) cudaStreamDestroy(ctx->h2dstream);
+  if (ctx->d2hstream) cudaStreamDestroy(ctx->d2hstream);
+  if (ctx->ev_reset) cudaEventDestroy(ctx->ev_reset);
+  F(ctx->d_ready);
+  F(ctx->d_pdone);
+  if (ctx->h_pack) cudaFreeHost(ctx->h_pack);
+  if (ctx->h_one) cudaFreeHost(ctx->h_one);
   if (ctx->ev_start) cudaEventDestroy(ctx->ev_start);
   if (ctx->ev_done) cudaEventDestroy(ctx->ev_done);
   delete ctx;
@@ -849,6 +869,7 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
   p.wait_limit_ns = ctx->cfg.wait_limit_ns;
   p.ev = ev;
   p.q = q;
+  p.st = ctx->st_cfg;
   if (f32)
     e = f32::launch(p, ctx->cfg.scheduler == APK_SCHED_CLC ? (int)num_tasks : ctx->grid, poll,
                     ctx->cfg.discipline, ctx->cfg.oracle != 0, bk, ctx->cfg.scheduler, stream);
@@ -865,6 +886,111 @@ apk_status read_status(apk_ctx* ctx) {
   if (cb.status != 0)
     return fail(ctx, APK_EDEVICE, "device reported status %d (a bounded wait ran out)", cb.status);
   return APK_OK;
+}
+
+// apk_gemm from host memory with the transfers overlapped: on a copy stream
+// A panel 0, then B in 512-column panels, then the other A row panels (one
+// raster group of 8 tile rows each), each followed by a 4-byte readiness
+// write (copy engine, no SM); the kernel, launched at once, starts a tile
+// when its A and B panels are flagged; every finished C row panel is
+// acknowledged through mapped memory and copied back on a second stream
+// while the rest still computes.
+apk_status gemm_streamed(apk_ctx* ctx, const char* A, const char* B, float* C) {
+  const int M = ctx->M, N = ctx->N, K = ctx->K;
+  const size_t es = esize_of(ctx->cfg.dtype);
+  const int TM = tile_rows(ctx), tiles_m = M / TM;
+  const int panel_tm = 8, np = (tiles_m + panel_tm - 1) / panel_tm;
+  const int b_units = N % 512 == 0 ? 4 : 1;  // 128-column units per B panel
+  const int nb = N / (128 * b_units);
+  if (!ctx->h2dstream) {
+    APK_CU(cudaStreamCreateWithFlags(&ctx->h2dstream, cudaStreamNonBlocking));
+    APK_CU(cudaStreamCreateWithFlags(&ctx->d2hstream, cudaStreamNonBlocking));
+    APK_CU(cudaEventCreateWithFlags(&ctx->ev_reset, cudaEventDisableTiming));
+    APK_CU(cudaHostAlloc(&ctx->h_one, sizeof(int), cudaHostAllocPortable));
+    *ctx->h_one = 1;
+  }
+  if (ctx->stream_cap < np + nb) {
+    if (ctx->d_ready) cudaFree(ctx->d_ready);
+    ctx->d_ready = nullptr;
+    APK_CU(cudaMalloc(&ctx->d_ready, sizeof(int) * (np + nb)));
+    ctx->stream_cap = np + nb;
+  }
+  if (ctx->pack_cap < np) {
+    if (ctx->d_pdone) cudaFree(ctx->d_pdone);
+    if (ctx->h_pack) cudaFreeHost(ctx->h_pack);
+    ctx->d_pdone = nullptr;
+    ctx->h_pack = nullptr;
+    APK_CU(cudaMalloc(&ctx->d_pdone, sizeof(unsigned) * np));
+    APK_CU(cudaHostAlloc(&ctx->h_pack, sizeof(int) * np, cudaHostAllocMapped | cudaHostAllocPortable));
+    APK_CU(cudaHostGetDevicePointer(reinterpret_cast<void**>(&ctx->d_pack_mapped), ctx->h_pack, 0));
+    ctx->pack_cap = np;
+  }
+  volatile int* ack = ctx->h_pack;
+  for (int i = 0; i < np; ++i) ack[i] = 0;
+  std::atomic_thread_fence(std::memory_order_seq_cst);
+  cudaStream_t hs = ctx->h2dstream, ds = ctx->d2hstream;
+  APK_CU(cudaMemsetAsync(ctx->d_ready, 0, sizeof(int) * (np + nb), hs));
+  APK_CU(cudaMemsetAsync(ctx->d_pdone, 0, sizeof(unsigned) * np, hs));
+  APK_CU(cudaEventRecord(ctx->ev_reset, hs));
+  char* dA = static_cast<char*>(ctx->dA);
+  char* dB = static_cast<char*>(ctx->dB);
+  auto copy_a = [&](int pn) -> apk_status {
+    const size_t r0 = (size_t)pn * panel_tm * TM;
+    const size_t rows = std::min((size_t)M - r0, (size_t)panel_tm * TM);
+    APK_CU(cudaMemcpyAsync(dA + r0 * K * es, A + r0 * K * es, rows * K * es, cudaMemcpyHostToDevice, hs));
+    APK_CU(cudaMemcpyAsync(ctx->d_ready + pn, ctx->h_one, sizeof(int), cudaMemcpyHostToDevice, hs));
+    return APK_OK;
+  };
+  apk_status s;
+  if ((s = copy_a(0)) != APK_OK) return s;
+  const size_t bw = (size_t)128 * b_units * es;  // bytes per B panel row
+  for (int j = 0; j < nb; ++j) {
+    APK_CU(cudaMemcpy2DAsync(dB + j * bw, (size_t)N * es, B + j * bw, (size_t)N * es, bw, K, cudaMemcpyHostToDevice,
+                             hs));
+    APK_CU(cudaMemcpyAsync(ctx->d_ready + np + j, ctx->h_one, sizeof(int), cudaMemcpyHostToDevice, hs));
+  }
+  for (int pn = 1; pn < np; ++pn)
+    if ((s = copy_a(pn)) != APK_OK) return s;
+
+  StreamProto st{};
+  st.a_ready = ctx->d_ready;
+  st.b_ready = ctx->d_ready + np;
+  st.b_units = b_units;
+  st.panel_tm = panel_tm;
+  st.n_panels = np;
+  st.done = ctx->d_pdone;
+  st.ack = ctx->d_pack_mapped;
+  ctx->st_cfg = st;
+  APK_CU(cudaStreamWaitEvent(ctx->kstream, ctx->ev_reset, 0));
+  const unsigned long long tiles = (unsigned long long)tiles_m * tiles_across(ctx, N);
+  const int poll = ctx->dAu ? (int)ctx->cfg.poll : APK_POLL_OFF;
+  s = launch_impl(ctx, tiles, poll, ctx->kstream, true);
+  ctx->st_cfg = StreamProto{};
+  if (s != APK_OK) return s;
+  ctx->running = true;
+  // copy each C row panel back once the device has finished it; if the
+  // kernel ends without acknowledging a panel (an aborted run) stop waiting
+  apk_status out = APK_OK;
+  for (int pn = 0; pn < np && out == APK_OK; ++pn) {
+    while (ack[pn] == 0) {
+      if (cudaEventQuery(ctx->ev_done) == cudaSuccess) {
+        std::atomic_thread_fence(std::memory_order_seq_cst);
+        if (ack[pn] == 0) out = fail(ctx, APK_EDEVICE, "kernel ended without finishing C panel %d", pn);
+        break;
+      }
+    }
+    if (out != APK_OK) break;
+    const size_t r0 = (size_t)pn * panel_tm * TM;
+    const size_t rows = std::min((size_t)M - r0, (size_t)panel_tm * TM);
+    APK_CU(cudaMemcpyAsync(C + r0 * N, static_cast<float*>(ctx->dC) + r0 * N, rows * N * sizeof(float),
+                           cudaMemcpyDeviceToHost, ds));
+  }
+  APK_CU(cudaStreamSynchronize(ds));
+  APK_CU(cudaStreamSynchronize(hs));
+  APK_CU(cudaStreamSynchronize(ctx->kstream));
+  ctx->running = false;
+  const apk_status st2 = read_status(ctx);
+  return out != APK_OK ? out : st2;
 }
 
 }  // namespace
@@ -1063,10 +1189,14 @@ apk_status apk_gemm(apk_ctx* ctx, const void* A, const void* B, void* C, int M, 
   const size_t es = esize_of(ctx->cfg.dtype);
   apk_status s;
   if (kind == APK_MEM_HOST) {
-    // async copies in kstream order: upload, drain all tiles once, download
-    if ((s = upload(ctx, &ctx->dA, &ctx->ownA, &ctx->capA, A, es * M * K, kind)) != APK_OK) return s;
-    if ((s = upload(ctx, &ctx->dB, &ctx->ownB, &ctx->capB, B, es * (size_t)K * N, kind)) != APK_OK) return s;
+    // device buffers only: the operands stream in while the kernel runs
+    if ((s = upload(ctx, &ctx->dA, &ctx->ownA, &ctx->capA, nullptr, es * M * K, kind)) != APK_OK) return s;
+    if ((s = upload(ctx, &ctx->dB, &ctx->ownB, &ctx->capB, nullptr, es * (size_t)K * N, kind)) != APK_OK) return s;
     if ((s = upload(ctx, &ctx->dC, &ctx->ownC, &ctx->capC, nullptr, 4ull * M * N, kind)) != APK_OK) return s;
+    ctx->M = M;
+    ctx->N = N;
+    ctx->K = K;
+    return gemm_streamed(ctx, static_cast<const char*>(A), static_cast<const char*>(B), static_cast<float*>(C));
   } else {
     if (ctx->ownA && ctx->dA) cudaFree(ctx->dA);
     if (ctx->ownB && ctx->dB) cudaFree(ctx->dB);
@@ -1084,8 +1214,6 @@ apk_status apk_gemm(apk_ctx* ctx, const void* A, const void* B, void* C, int M, 
   const int poll = ctx->dAu ? (int)ctx->cfg.poll : APK_POLL_OFF;
   if ((s = launch_impl(ctx, tiles, poll, ctx->kstream, true)) != APK_OK) return s;
   ctx->running = true;
-  if (kind == APK_MEM_HOST)
-    APK_CU(cudaMemcpyAsync(C, ctx->dC, 4ull * M * N, cudaMemcpyDeviceToHost, ctx->kstream));
   APK_CU(cudaStreamSynchronize(ctx->kstream));
   ctx->running = false;
   return read_status(ctx);

@@ -450,6 +450,14 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
       for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+      // streamed operands: the tile's A row panel and B column panel must
+      // have landed before its first TMA load
+      if (p.st.a_ready != nullptr && tid == 0 &&
+          !wait_ready2(&p.st.a_ready[(row0 / BM) / p.st.panel_tm], &p.st.b_ready[(col0 / BN) / p.st.b_units],
+                       p.wait_limit_ns)) {
+        bad = true;
+        report_status(p.ev.status, DEV_WAIT_TIMEOUT_SPIN, p.ev.abort_word);
+      }
       prime(0);
     }
 
@@ -505,11 +513,17 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
         *reinterpret_cast<float4*>(crow + 32) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
       }
       bg_active = false;
+      if (p.st.done != nullptr) __threadfence();  // the panel's copy back reads these stores
       __syncthreads();  // the whole tile is stored before it counts as complete
       if (tid == 0) {
         ++s_myTiles;
         if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[s_bgTask], 1);
         count_trigger(p.ev);
+        if (p.st.done != nullptr) {
+          const int tiles_m = p.total_tiles / p.tiles_n, pn = (row0 / BM) / p.st.panel_tm;
+          const int rows = tiles_m - pn * p.st.panel_tm < p.st.panel_tm ? tiles_m - pn * p.st.panel_tm : p.st.panel_tm;
+          if (atomicAdd(&p.st.done[pn], 1u) + 1u == (unsigned)(rows * p.tiles_n)) ack_host(&p.st.ack[pn]);
+        }
       }
     } else {
       float* Cu = p.Cu + (size_t)ev * p.cu_stride;

@@ -331,8 +331,12 @@ def run_ours(args, world, rank, local):
         ctx.gemm(hA, hB, hC)
         e2e_t.append(time.perf_counter() - t)
     e2e_tf = 2.0 * M * N * K / statistics.median(e2e_t) / 1e12
-    # single-pass kernel time for the roofline (one 4096^3 drain, device-resident)
-    ctx.gemm(hA, hB, hC)
+    # single-pass kernel time for the roofline: one 4096^3 drain with the
+    # operands already resident (apk_gemm from host memory streams them in
+    # while the kernel runs, so its launch time includes the transfers)
+    ctx.set_background(A, B)
+    ctx.launch((M // info["tile_m"]) * (N // info["tile_n"]))
+    ctx.wait(60)
     one_pass = ctx.run_stats()
 
     extras = {}
@@ -416,7 +420,8 @@ def run_ours(args, world, rank, local):
                      "kernel": "apk::f32::sgemm_persistent<POLL_STAGE,...,32>, one 4096^3 drain"},
         "e2e": {"value": sum(r["e2e_tf"] for r in allr), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": 2 * M * K * 4, "d2h_bytes_per_step": M * N * 4,
-                "path": "apk_gemm with pinned host A, B -> C (H2D + drain + D2H)"},
+                "path": "apk_gemm with pinned host A, B -> C: A row panels and B column panels stream in "
+                        "while the persistent kernel runs, C row panels stream back as they finish"},
         "gpu_launches": args.steps,
         "clocks": clk,
         "gpu": gpu_identity(local),
