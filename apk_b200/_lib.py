@@ -53,7 +53,9 @@ class EventLog(ctypes.Structure):
 class RunStats(ctypes.Structure):
     _fields_ = [("start_ns", c_ll), ("end_ns", c_ll), ("tiles_done", c_ull), ("yields", c_ull),
                 ("bg_flops", c_double), ("bg_tflops", c_double), ("exited", c_int),
-                ("device_status", c_int), ("launch_ms", c_double)]
+                ("device_status", c_int), ("launch_ms", c_double),
+                ("ckpt_spill_bytes", c_ull), ("ckpt_restore_bytes", c_ull),
+                ("ckpt_spill_ns", c_ll), ("ckpt_restore_ns", c_ll)]
 
 
 class LatencyConfig(ctypes.Structure):

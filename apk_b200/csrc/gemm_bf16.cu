@@ -481,6 +481,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
       const int nh = j.wide ? 2 : 1;
       auto slab_blk = [&](int hh, int blk) { return slab + (size_t)((hh * 8 + blk) * 4 + q) * 1024; };
       if (j.action == E_RESTORE) {
+        const long long r0 = globaltimer_ns();
 #pragma unroll 1
         for (int bb = g; bb < 8 * nh; bb += 2) {
           const int hh = bb >> 3, blk = bb & 7;
@@ -499,11 +500,19 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         tc::wait_st();
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sh.tres[j.buf]);
+        if (lane == 0) {
+          mbar_arrive(&sh.tres[j.buf]);
+          if (p.q.ckpt != nullptr) {
+            // this warp moved 4 * nh blocks of 32 x 32 floats from the slab
+            atomicAdd(&p.q.ckpt[2], (unsigned long long)(globaltimer_ns() - r0));
+            atomicAdd(&p.q.ckpt[3], (unsigned long long)nh * 4 * 4096);
+          }
+        }
       } else {
         if (!bwait(&sh.tfull[j.buf], eb[j.buf] & 1, p, sh)) break;
         ++eb[j.buf];
         tc::fence_after_sync();
+        const long long s0 = globaltimer_ns();
         // task mode: this lane's sum(c^2) per half in a fixed order; fp32 per
         // lane (256 terms, ~1e-6 relative) keeps the double conversions off
         // the path that frees TMEM, the lanes and warps add up in double
@@ -555,6 +564,12 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         if (lane == 0) {
           mbar_arrive(&sh.tempty[j.buf]);
           if (j.wide) mbar_arrive(&sh.tempty[1]);  // a wide job held both buffers (buf 0 and 1)
+          if (j.action == E_SPILL && p.q.ckpt != nullptr) {
+            // TMEM free again: this warp's 4 * nh blocks are read and their
+            // slab stores issued
+            atomicAdd(&p.q.ckpt[0], (unsigned long long)(globaltimer_ns() - s0));
+            atomicAdd(&p.q.ckpt[1], (unsigned long long)nh * 4 * 4096);
+          }
         }
         if (j.action != E_SPILL) {
           if (p.task_mode && j.action == E_STORE_C) {
@@ -669,6 +684,7 @@ static const void* select_kernel(int poll, int disc, bool oracle, int bk) {
 int smem_bytes(int bk) { return bk == 32 ? Ring<32>::SMEM_BYTES : Ring<64>::SMEM_BYTES; }
 int stages(int bk) { return bk == 32 ? Ring<32>::S : Ring<64>::S; }
 int threads() { return NT; }
+int epi_warps() { return EPI_WARPS; }
 size_t params_bytes() { return sizeof(F32Params); }
 
 cudaError_t prepare(int poll, int disc, bool oracle, int bk, int* max_ctas_per_sm) {

@@ -56,6 +56,10 @@ struct QueueProto {
   unsigned* slot_bits;             // [(nslots + 31) / 32]
   int nslots;                      // resident CTAs (sms * ctas_per_sm)
   long long* setter_state;         // [2] device setter's next event and time base across slot-0 holders
+  // checkpoint accounting (bf16): [0] spill ns, [1] spill bytes, [2] restore
+  // ns, [3] restore bytes, each summed over the epilogue warps; a warp's time
+  // runs from its first accumulator read to its last write (nullptr = off)
+  unsigned long long* ckpt;
 };
 
 // Streamed operands (apk_gemm from host memory): A arrives in row panels of

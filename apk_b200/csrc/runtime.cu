@@ -40,6 +40,7 @@ cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool orac
 int smem_bytes(int bk);
 int stages(int bk);
 int threads();
+int epi_warps();
 size_t params_bytes();
 }  // namespace bf16
 }  // namespace apk
@@ -66,6 +67,7 @@ struct Ctrl {
   unsigned long long end_max;
   unsigned long long yields;
   unsigned long long completed;  // completed background tiles (count triggers)
+  unsigned long long ckpt[4];    // checkpoint spill ns, bytes, restore ns, bytes
   int exited;
   int abort_word;
   int status;
@@ -724,6 +726,7 @@ void fill_protos(apk_ctx* ctx, unsigned long long num_tasks, EventProto* ev, Que
   q->end_max = &cb->end_max;
   q->exited = &cb->exited;
   q->yields = &cb->yields;
+  q->ckpt = cb->ckpt;
 }
 
 apk_status reset_logs(apk_ctx* ctx, unsigned long long num_tasks) {
@@ -1159,6 +1162,14 @@ apk_status apk_read_run_stats(apk_ctx* ctx, apk_run_stats* st) {
   st->end_ns = (long long)cb.end_max;
   for (auto v : t) st->tiles_done += v;
   st->yields = cb.yields;
+  if (ctx->cfg.dtype == APK_BF16) {
+    // the epilogue warps of a CTA split a checkpoint evenly and run side by
+    // side: their summed time / warps is the CTA's wall time
+    st->ckpt_spill_bytes = cb.ckpt[1];
+    st->ckpt_restore_bytes = cb.ckpt[3];
+    st->ckpt_spill_ns = (long long)(cb.ckpt[0] / (unsigned long long)bf16::epi_warps());
+    st->ckpt_restore_ns = (long long)(cb.ckpt[2] / (unsigned long long)bf16::epi_warps());
+  }
   if (ctx->task_mode) {
     // tiles differ in size: a complete drain did every task's 2*m*n*k; a
     // partial one is prorated by the 256x128 halves it completed

@@ -230,7 +230,20 @@ def bf16_config2(apk_b200, np, dev):
                 "bitwise_equal_to_uninterrupted": bool(np.array_equal(C.view(np.uint32), C0.view(np.uint32))),
                 "claim_p50_us": pct(cl, 0.5), "claim_p99_us": pct(cl, 0.99),
                 "done_p50_us": pct(dn, 0.5), "done_p99_us": pct(dn, 0.99),
-                "tflops_with_yields": st["bg_tflops"]}}
+                "tflops_with_yields": st["bg_tflops"], "checkpoint": ckpt_stats(st)}}
+
+
+def ckpt_stats(st):
+    """Checkpoint traffic of a bf16 yield run: bytes moved between TMEM and
+    the slab, mean CTA wall time per checkpoint and the CTA's GB/s."""
+    y = max(int(st["yields"]), 1)
+    out = {}
+    for k in ("spill", "restore"):
+        b, ns = int(st[f"ckpt_{k}_bytes"]), int(st[f"ckpt_{k}_ns"])
+        out[f"{k}_bytes"] = b
+        out[f"{k}_us_mean"] = ns / y / 1e3
+        out[f"{k}_gbs_per_cta"] = b / ns if ns > 0 else None
+    return out
 
 
 # ---------------------------------------------------------------- our arm

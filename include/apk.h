@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define APK_ABI_VERSION 2
+#define APK_ABI_VERSION 3
 #define APK_TASKS_UNBOUNDED 0xFFFFFFFFFFFFFFFFull
 
 typedef enum apk_status {
@@ -219,6 +219,13 @@ typedef struct apk_run_stats {
   int device_status;                 /* 0 or the first device error code      */
   double launch_ms;                  /* CUDA events around the launch, on the
                                         stream that ran it                    */
+  /* bf16 checkpoint traffic of the launch (0 for fp32): bytes spilled from
+   * TMEM to the slab and restored from it, and the CTA wall time of those
+   * spills / restores summed over checkpoints (spill: first tcgen05.ld to
+   * TMEM free with the slab stores issued; restore: first slab load to
+   * tcgen05.st complete).  bytes / ns = a CTA's checkpoint GB/s. */
+  unsigned long long ckpt_spill_bytes, ckpt_restore_bytes;
+  long long ckpt_spill_ns, ckpt_restore_ns;
 } apk_run_stats;
 apk_status apk_read_run_stats(apk_ctx* ctx, apk_run_stats* st);
 

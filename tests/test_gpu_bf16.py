@@ -97,6 +97,12 @@ def test_stage_checkpoint_resume_is_bitwise(libapk):
     assert any(s > 0 for s in sites), "no mid-pipeline claim"
     assert any(ev["inflight"][e] > 0 for e in range(r["fired"])), "no buffer-conflicting yield"
     assert np.array_equal(r["C"].view(np.uint32), r["Cref"].view(np.uint32)), "resume not bitwise"
+    # every checkpoint spills one wide 256x256 fp32 accumulator and the
+    # drain restores each of them
+    st = r["st"]
+    assert st["ckpt_spill_bytes"] == st["yields"] * 256 * 256 * 4
+    assert st["ckpt_restore_bytes"] == st["ckpt_spill_bytes"]
+    assert st["ckpt_spill_ns"] > 0 and st["ckpt_restore_ns"] > 0
     for Cu in r["outs"]:
         mr, bad, nans = oracle.check(Cu, r["refu"], TOL)
         assert bad == 0 and nans == 0
