@@ -311,7 +311,10 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
       } else {
         const int tile = (int)(task % (unsigned long long)p.total_tiles);
         int tm, tn;
-        tile_coords(tile, p.total_tiles / p.tiles_n, p.tiles_n, RASTER_GROUP, tm, tn);
+        if (p.st.order != nullptr)
+          stream_tile(p.st, tile, p.tiles_n, tm, tn);
+        else
+          tile_coords(tile, p.total_tiles / p.tiles_n, p.tiles_n, RASTER_GROUP, tm, tn);
         row0 = ar0 = tm * BM;
         col0 = bc0 = tn * BN;
         ak0 = bk0 = 0;
@@ -600,12 +603,8 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
               } else {
                 ++sh.tiles;
                 if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[j.task], 1);
-                if (p.st.done != nullptr) {  // every warp fenced its stores above
-                  const int tiles_m = p.total_tiles / p.tiles_n, pn = (j.row0 / BM) / p.st.panel_tm;
-                  const int rows =
-                      tiles_m - pn * p.st.panel_tm < p.st.panel_tm ? tiles_m - pn * p.st.panel_tm : p.st.panel_tm;
-                  if (atomicAdd(&p.st.done[pn], 1u) + 1u == (unsigned)(rows * p.tiles_n)) ack_host(&p.st.ack[pn]);
-                }
+                if (p.st.done != nullptr)  // every warp fenced its stores above
+                  stream_tile_done(p.st, p.total_tiles / p.tiles_n, p.tiles_n, j.row0 / BM, j.col0 / BN);
               }
               count_trigger(p.ev);
             } else {

@@ -63,18 +63,45 @@ struct QueueProto {
 };
 
 // Streamed operands (apk_gemm from host memory): A arrives in row panels of
-// panel_tm tile rows and B in 128-column panels while the kernel runs; a
-// tile starts once its A row panel and B column panel are flagged, and each
-// finished C row panel is acknowledged to the host for its copy back.
+// panel_tm tile rows and B in column panels of b_units 128-column units
+// while the kernel runs, interleaved so that the count of computable tiles
+// grows with the bytes copied; the kernel visits tiles in the order they
+// become computable (order[]), starts one once its A row panel and B column
+// panel(s) are flagged, and acknowledges each finished C block (a row panel
+// by cb_tn tile columns) to the host for its copy back.
 struct StreamProto {
-  const int* a_ready;   // [n_panels] set by the copy stream after A panel p (nullptr = resident)
-  const int* b_ready;   // [N / (128 * b_units)] after B column panel j
-  int b_units;          // 128-column units per B column panel
-  int panel_tm;         // tile rows per panel
+  const int* a_ready;     // [n_panels] set by the copy stream after A panel p (nullptr = resident)
+  const int* b_ready;     // [N / (128 * b_units)] after B column panel j
+  int b_units;            // 128-column units per B column panel
+  int panel_tm;           // tile rows per A row panel and per C block
   int n_panels;
-  unsigned* done;       // [n_panels] finished tiles per C row panel
-  int* ack;             // mapped host memory [n_panels]: panel p complete
+  int cb_tn;              // tile columns per C block
+  int n_cb;               // C blocks across
+  const unsigned* order;  // [tiles] visit order as tm * tiles_n + tn (nullptr = grouped raster)
+  unsigned* done;         // [n_panels * n_cb] finished tiles per C block
+  int* ack;               // mapped host memory [n_panels * n_cb]: C block complete
 };
+
+// Count a finished background tile of a streamed run; the last tile of a C
+// block acknowledges the block to the host.  The tile's stores are fenced.
+__device__ __forceinline__ void stream_tile_done(const StreamProto& st, int tiles_m, int tiles_n, int tm, int tn) {
+  const int pn = tm / st.panel_tm, cb = tn / st.cb_tn;
+  const int rows = tiles_m - pn * st.panel_tm < st.panel_tm ? tiles_m - pn * st.panel_tm : st.panel_tm;
+  const int cols = tiles_n - cb * st.cb_tn < st.cb_tn ? tiles_n - cb * st.cb_tn : st.cb_tn;
+  const int b = pn * st.n_cb + cb;
+  if (atomicAdd(&st.done[b], 1u) + 1u == (unsigned)(rows * cols)) {
+    // mapped host memory: the store is pushed out by a system-scope fence
+    *reinterpret_cast<volatile int*>(&st.ack[b]) = 1;
+    __threadfence_system();
+  }
+}
+
+// Tile coordinates of a streamed run's tile-visit slot.
+__device__ __forceinline__ void stream_tile(const StreamProto& st, int tile, int tiles_n, int& tm, int& tn) {
+  const int o = (int)st.order[tile];
+  tm = o / tiles_n;
+  tn = o - tm * tiles_n;
+}
 
 // One heterogeneous background task: C window = A window *
 // B window, each a window of a shared operand pool (so the tensor maps are

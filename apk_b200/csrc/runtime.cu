@@ -115,8 +115,11 @@ struct apk_ctx {
   int* h_pack = nullptr;
   int* d_pack_mapped = nullptr;
   int* h_one = nullptr;
+  unsigned* d_order = nullptr;  // tile visit order of a streamed run
+  unsigned* h_order = nullptr;
   int stream_cap = 0;       // capacity of d_ready (panels + column panels)
-  int pack_cap = 0;         // capacity of d_pdone / h_pack
+  int pack_cap = 0;         // capacity of d_pdone / h_pack (C blocks)
+  int order_cap = 0;        // capacity of d_order / h_order (tiles)
   StreamProto st_cfg{};     // copied into the launch's parameters (zeros = resident operands)
   cudaEvent_t ev_start = nullptr, ev_done = nullptr;
   bool running = false;
@@ -467,7 +470,9 @@ apk_status apk_destroy(apk_ctx* ctx) {
   if (ctx->ev_reset) cudaEventDestroy(ctx->ev_reset);
   F(ctx->d_ready);
   F(ctx->d_pdone);
+  F(ctx->d_order);
   if (ctx->h_pack) cudaFreeHost(ctx->h_pack);
+  if (ctx->h_order) cudaFreeHost(ctx->h_order);
   if (ctx->h_one) cudaFreeHost(ctx->h_one);
   if (ctx->ev_start) cudaEventDestroy(ctx->ev_start);
   if (ctx->ev_done) cudaEventDestroy(ctx->ev_done);
@@ -891,20 +896,81 @@ apk_status read_status(apk_ctx* ctx) {
   return APK_OK;
 }
 
+// Copy schedule of a streamed apk_gemm.  A moves in row panels of panel_tm
+// tile rows, B in column panels of b_units 128-column units.  After A panel
+// 0, each next copy is the next A row panel or the next B column panel,
+// whichever makes more tiles computable per byte copied; tiles are visited
+// in the order they become computable (column-major within each step's new
+// tiles).  The kernel pops tiles in that order and waits for each tile's
+// panels, so no CTA waits behind a tile whose operands come later.
+struct StreamPlan {
+  std::vector<int> copies;       // >= 0: A row panel; < 0: B column panel -(j + 1)
+  std::vector<unsigned> order;   // tile visit order, tm * tiles_n + tn
+};
+
+StreamPlan plan_stream(int tiles_m, int tiles_n, int panel_tm, int np, int nb, int tn_units, int n_units,
+                       int b_units, double a_bytes_per_tile_row, double b_bytes_per_unit) {
+  // the last B column panel tile column tn needs
+  auto last_bpanel = [&](int tn) {
+    const int last_unit = std::min(n_units, (tn + 1) * tn_units) - 1;
+    return last_unit / b_units;
+  };
+  // tile columns computable once B panels 0 .. b-1 are in (monotone in b)
+  std::vector<int> cols_ready(nb + 1, 0);
+  for (int b = 0, tn = 0; b <= nb; ++b) {
+    while (tn < tiles_n && last_bpanel(tn) < b) ++tn;
+    cols_ready[b] = tn;
+  }
+  auto rows_ready = [&](int a) { return std::min(tiles_m, a * panel_tm); };
+  StreamPlan pl;
+  pl.order.reserve((size_t)tiles_m * tiles_n);
+  int a = 0, b = 0;
+  while (a < np || b < nb) {
+    bool take_a;
+    if (a == 0 || b == nb) {
+      take_a = true;
+    } else if (a == np) {
+      take_a = false;
+    } else {
+      // new computable tiles per byte of each candidate copy
+      const int ra = rows_ready(a), rn = rows_ready(a + 1) - ra;
+      const int ca = cols_ready[b], cn = cols_ready[b + 1] - ca;
+      const int units = std::min(n_units, (b + 1) * b_units) - b * b_units;
+      const double ga = (double)rn * ca / (a_bytes_per_tile_row * rn);
+      const double gb = (double)ra * cn / (b_bytes_per_unit * units);
+      take_a = ga >= gb;
+    }
+    if (take_a) {
+      const int r0 = rows_ready(a), r1 = rows_ready(a + 1);
+      for (int tn = 0; tn < cols_ready[b]; ++tn)
+        for (int tm = r0; tm < r1; ++tm) pl.order.push_back((unsigned)(tm * tiles_n + tn));
+      pl.copies.push_back(a++);
+    } else {
+      for (int tn = cols_ready[b]; tn < cols_ready[b + 1]; ++tn)
+        for (int tm = 0; tm < rows_ready(a); ++tm) pl.order.push_back((unsigned)(tm * tiles_n + tn));
+      pl.copies.push_back(-(b++) - 1);
+    }
+  }
+  return pl;
+}
+
 // apk_gemm from host memory with the transfers overlapped: on a copy stream
-// A panel 0, then B in 512-column panels, then the other A row panels (one
-// raster group of 8 tile rows each), each followed by a 4-byte readiness
-// write (copy engine, no SM); the kernel, launched at once, starts a tile
-// when its A and B panels are flagged; every finished C row panel is
-// acknowledged through mapped memory and copied back on a second stream
-// while the rest still computes.
+// the tile-visit order, then A row panels and B column panels in the order
+// plan_stream picks, each followed by a 4-byte readiness write (copy engine,
+// no SM); the kernel, launched at once, visits tiles in that order and
+// starts a tile when its A and B panels are flagged; every finished C block
+// (row panel x cb_tn tile columns) is acknowledged through mapped memory and
+// copied back on a second stream while the rest still computes.
 apk_status gemm_streamed(apk_ctx* ctx, const char* A, const char* B, float* C) {
   const int M = ctx->M, N = ctx->N, K = ctx->K;
   const size_t es = esize_of(ctx->cfg.dtype);
   const int TM = tile_rows(ctx), tiles_m = M / TM;
+  const int TN = tile_cols(ctx), tiles_n = tiles_across(ctx, N), tn_units = TN / 128, n_units = N / 128;
   const int panel_tm = 8, np = (tiles_m + panel_tm - 1) / panel_tm;
   const int b_units = N % 512 == 0 ? 4 : 1;  // 128-column units per B panel
-  const int nb = N / (128 * b_units);
+  const int nb = n_units / b_units;
+  const int cb_tn = std::max(1, b_units / tn_units), n_cb = (tiles_n + cb_tn - 1) / cb_tn;
+  const int nblk = np * n_cb, ntiles = tiles_m * tiles_n;
   if (!ctx->h2dstream) {
     APK_CU(cudaStreamCreateWithFlags(&ctx->h2dstream, cudaStreamNonBlocking));
     APK_CU(cudaStreamCreateWithFlags(&ctx->d2hstream, cudaStreamNonBlocking));
@@ -918,42 +984,55 @@ apk_status gemm_streamed(apk_ctx* ctx, const char* A, const char* B, float* C) {
     APK_CU(cudaMalloc(&ctx->d_ready, sizeof(int) * (np + nb)));
     ctx->stream_cap = np + nb;
   }
-  if (ctx->pack_cap < np) {
+  if (ctx->pack_cap < nblk) {
     if (ctx->d_pdone) cudaFree(ctx->d_pdone);
     if (ctx->h_pack) cudaFreeHost(ctx->h_pack);
     ctx->d_pdone = nullptr;
     ctx->h_pack = nullptr;
-    APK_CU(cudaMalloc(&ctx->d_pdone, sizeof(unsigned) * np));
-    APK_CU(cudaHostAlloc(&ctx->h_pack, sizeof(int) * np, cudaHostAllocMapped | cudaHostAllocPortable));
+    APK_CU(cudaMalloc(&ctx->d_pdone, sizeof(unsigned) * nblk));
+    APK_CU(cudaHostAlloc(&ctx->h_pack, sizeof(int) * nblk, cudaHostAllocMapped | cudaHostAllocPortable));
     APK_CU(cudaHostGetDevicePointer(reinterpret_cast<void**>(&ctx->d_pack_mapped), ctx->h_pack, 0));
-    ctx->pack_cap = np;
+    ctx->pack_cap = nblk;
   }
+  if (ctx->order_cap < ntiles) {
+    if (ctx->d_order) cudaFree(ctx->d_order);
+    if (ctx->h_order) cudaFreeHost(ctx->h_order);
+    ctx->d_order = nullptr;
+    ctx->h_order = nullptr;
+    APK_CU(cudaMalloc(&ctx->d_order, sizeof(unsigned) * ntiles));
+    APK_CU(cudaHostAlloc(&ctx->h_order, sizeof(unsigned) * ntiles, cudaHostAllocPortable));
+    ctx->order_cap = ntiles;
+  }
+  const StreamPlan plan = plan_stream(tiles_m, tiles_n, panel_tm, np, nb, tn_units, n_units, b_units,
+                                      (double)TM * K * es, (double)128 * K * es);
+  if ((int)plan.order.size() != ntiles)
+    return fail(ctx, APK_EINVAL, "stream plan covers %d of %d tiles", (int)plan.order.size(), ntiles);
+  // the previous call's copies have completed (its streams were synchronised)
+  memcpy(ctx->h_order, plan.order.data(), sizeof(unsigned) * ntiles);
   volatile int* ack = ctx->h_pack;
-  for (int i = 0; i < np; ++i) ack[i] = 0;
+  for (int i = 0; i < nblk; ++i) ack[i] = 0;
   std::atomic_thread_fence(std::memory_order_seq_cst);
   cudaStream_t hs = ctx->h2dstream, ds = ctx->d2hstream;
   APK_CU(cudaMemsetAsync(ctx->d_ready, 0, sizeof(int) * (np + nb), hs));
-  APK_CU(cudaMemsetAsync(ctx->d_pdone, 0, sizeof(unsigned) * np, hs));
+  APK_CU(cudaMemsetAsync(ctx->d_pdone, 0, sizeof(unsigned) * nblk, hs));
+  APK_CU(cudaMemcpyAsync(ctx->d_order, ctx->h_order, sizeof(unsigned) * ntiles, cudaMemcpyHostToDevice, hs));
   APK_CU(cudaEventRecord(ctx->ev_reset, hs));
   char* dA = static_cast<char*>(ctx->dA);
   char* dB = static_cast<char*>(ctx->dB);
-  auto copy_a = [&](int pn) -> apk_status {
-    const size_t r0 = (size_t)pn * panel_tm * TM;
-    const size_t rows = std::min((size_t)M - r0, (size_t)panel_tm * TM);
-    APK_CU(cudaMemcpyAsync(dA + r0 * K * es, A + r0 * K * es, rows * K * es, cudaMemcpyHostToDevice, hs));
-    APK_CU(cudaMemcpyAsync(ctx->d_ready + pn, ctx->h_one, sizeof(int), cudaMemcpyHostToDevice, hs));
-    return APK_OK;
-  };
-  apk_status s;
-  if ((s = copy_a(0)) != APK_OK) return s;
   const size_t bw = (size_t)128 * b_units * es;  // bytes per B panel row
-  for (int j = 0; j < nb; ++j) {
-    APK_CU(cudaMemcpy2DAsync(dB + j * bw, (size_t)N * es, B + j * bw, (size_t)N * es, bw, K, cudaMemcpyHostToDevice,
-                             hs));
-    APK_CU(cudaMemcpyAsync(ctx->d_ready + np + j, ctx->h_one, sizeof(int), cudaMemcpyHostToDevice, hs));
+  for (const int c : plan.copies) {
+    if (c >= 0) {
+      const size_t r0 = (size_t)c * panel_tm * TM;
+      const size_t rows = std::min((size_t)M - r0, (size_t)panel_tm * TM);
+      APK_CU(cudaMemcpyAsync(dA + r0 * K * es, A + r0 * K * es, rows * K * es, cudaMemcpyHostToDevice, hs));
+      APK_CU(cudaMemcpyAsync(ctx->d_ready + c, ctx->h_one, sizeof(int), cudaMemcpyHostToDevice, hs));
+    } else {
+      const int j = -c - 1;
+      APK_CU(cudaMemcpy2DAsync(dB + j * bw, (size_t)N * es, B + j * bw, (size_t)N * es, bw, K,
+                               cudaMemcpyHostToDevice, hs));
+      APK_CU(cudaMemcpyAsync(ctx->d_ready + np + j, ctx->h_one, sizeof(int), cudaMemcpyHostToDevice, hs));
+    }
   }
-  for (int pn = 1; pn < np; ++pn)
-    if ((s = copy_a(pn)) != APK_OK) return s;
 
   StreamProto st{};
   st.a_ready = ctx->d_ready;
@@ -961,32 +1040,51 @@ apk_status gemm_streamed(apk_ctx* ctx, const char* A, const char* B, float* C) {
   st.b_units = b_units;
   st.panel_tm = panel_tm;
   st.n_panels = np;
+  st.cb_tn = cb_tn;
+  st.n_cb = n_cb;
+  st.order = ctx->d_order;
   st.done = ctx->d_pdone;
   st.ack = ctx->d_pack_mapped;
   ctx->st_cfg = st;
   APK_CU(cudaStreamWaitEvent(ctx->kstream, ctx->ev_reset, 0));
-  const unsigned long long tiles = (unsigned long long)tiles_m * tiles_across(ctx, N);
   const int poll = ctx->dAu ? (int)ctx->cfg.poll : APK_POLL_OFF;
-  s = launch_impl(ctx, tiles, poll, ctx->kstream, true);
+  apk_status s = launch_impl(ctx, (unsigned long long)ntiles, poll, ctx->kstream, true);
   ctx->st_cfg = StreamProto{};
   if (s != APK_OK) return s;
   ctx->running = true;
-  // copy each C row panel back once the device has finished it; if the
-  // kernel ends without acknowledging a panel (an aborted run) stop waiting
+  // copy each C block back once the device has acknowledged it, in the
+  // order they finish; if the kernel ends with a block unacknowledged (an
+  // aborted run) stop waiting
   apk_status out = APK_OK;
-  for (int pn = 0; pn < np && out == APK_OK; ++pn) {
-    while (ack[pn] == 0) {
-      if (cudaEventQuery(ctx->ev_done) == cudaSuccess) {
+  std::vector<char> sent(nblk, 0);
+  float* dC = static_cast<float*>(ctx->dC);
+  int left = nblk;
+  bool ended = false;
+  while (left > 0 && out == APK_OK) {
+    bool any = false;
+    for (int blk = 0; blk < nblk; ++blk) {
+      if (sent[blk] || ack[blk] == 0) continue;
+      const int pn = blk / n_cb, cb = blk % n_cb;
+      const size_t r0 = (size_t)pn * panel_tm * TM;
+      const size_t rows = std::min((size_t)M - r0, (size_t)panel_tm * TM);
+      const size_t c0 = (size_t)cb * cb_tn * TN;
+      const size_t cols = std::min((size_t)N - c0, (size_t)cb_tn * TN);
+      APK_CU(cudaMemcpy2DAsync(C + r0 * N + c0, (size_t)N * sizeof(float), dC + r0 * N + c0,
+                               (size_t)N * sizeof(float), cols * sizeof(float), rows, cudaMemcpyDeviceToHost, ds));
+      sent[blk] = 1;
+      --left;
+      any = true;
+    }
+    if (!any) {
+      if (ended) {
+        for (int blk = 0; blk < nblk && out == APK_OK; ++blk)
+          if (!sent[blk]) out = fail(ctx, APK_EDEVICE, "kernel ended without finishing C block %d", blk);
+      } else if (cudaEventQuery(ctx->ev_done) == cudaSuccess) {
+        // one more scan sees every ack the finished kernel wrote
         std::atomic_thread_fence(std::memory_order_seq_cst);
-        if (ack[pn] == 0) out = fail(ctx, APK_EDEVICE, "kernel ended without finishing C panel %d", pn);
-        break;
+        ended = true;
       }
     }
-    if (out != APK_OK) break;
-    const size_t r0 = (size_t)pn * panel_tm * TM;
-    const size_t rows = std::min((size_t)M - r0, (size_t)panel_tm * TM);
-    APK_CU(cudaMemcpyAsync(C + r0 * N, static_cast<float*>(ctx->dC) + r0 * N, rows * N * sizeof(float),
-                           cudaMemcpyDeviceToHost, ds));
   }
   APK_CU(cudaStreamSynchronize(ds));
   APK_CU(cudaStreamSynchronize(hs));

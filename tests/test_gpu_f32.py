@@ -51,6 +51,20 @@ def test_verify_1024_no_yield(libapk):
     _check(C, ref, 1024)
 
 
+@pytest.mark.parametrize("shape", [(384, 640, 96), (1152, 1536, 256), (128, 128, 32)])
+def test_streamed_gemm_ragged_shapes(libapk, shape):
+    """apk_gemm from host memory: the copy plan interleaves A row panels and
+    B column panels, the kernel visits tiles in the order they become
+    computable and C blocks come back as they finish.  Shapes with a partial
+    row panel, B panels of one 128-column unit (N % 512 != 0) and a single
+    tile."""
+    M, N, K = shape
+    A, B = oracle.gen_uniform(M, N, K, 5)
+    with _ctx(poll="stage", oracle=True) as c:
+        C = c.gemm(A, B)
+    _check(C, oracle.gemm_f64(A, B), K)
+
+
 def test_cfg0_yield_at_50_percent_boundary(libapk):
     """1024^3 fp32, one yield at a tile boundary after 50% of the
     64 tiles complete; C within tolerance and bitwise equal to the no-yield
