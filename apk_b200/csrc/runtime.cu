@@ -27,6 +27,8 @@ cudaError_t prepare(int poll, int disc, bool oracle, int bk, int sched, int* max
 cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int bk, int sched,
                    cudaStream_t stream);
 int smem_bytes(int bk);
+int stages(int bk);
+int threads();
 size_t params_bytes();
 }  // namespace f32
 namespace vis {
@@ -491,10 +493,10 @@ apk_status apk_get_info(apk_ctx* ctx, apk_device_info* info) {
   info->cc_minor = ctx->cc_minor;
   if (ctx->cfg.dtype == APK_F32) {
     info->smem_per_cta = f32::smem_bytes(ctx->cfg.k_tile);
-    info->threads_per_cta = 256;
+    info->threads_per_cta = f32::threads();
     info->tile_m = 128;
     info->tile_n = 128;
-    info->stages = ctx->cfg.k_tile == 32 ? 3 : 2;
+    info->stages = f32::stages(ctx->cfg.k_tile);
   } else {
     info->smem_per_cta = bf16::smem_bytes(ctx->cfg.k_tile);
     info->threads_per_cta = bf16::threads();

@@ -7,8 +7,11 @@
 //   persistent_midyield  src/midyield.cu:92-320   (per-stage checkpoint)
 //
 // B200 design:
-//   * 128x128 output tile, 256 threads, 8x8 register micro-tile per thread,
-//     K-tile BK (32 by default) staged by TMA into a STAGES-deep ring of
+//   * 128x128 output tile, 128 threads, 8x16 register micro-tile per thread
+//     computed with packed fp32 FMAs (fma.rn.f32x2: two round-to-nearest
+//     FMAs per instruction, so half the issue slots of scalar FFMA for the
+//     same sums), 2 CTAs per SM, K-tile BK (32 by default) staged by TMA
+//     into a STAGES-deep ring of
 //     shared-memory slots, each guarded by one transaction mbarrier.  A
 //     slot is loaded as a [128 rows][32 k] box with 128-byte swizzle (so
 //     rows read as float4 along k are bank-conflict free) and B as a
@@ -43,7 +46,7 @@
 namespace apk {
 namespace f32 {
 
-constexpr int BM = 128, BN = 128, NT = 256;
+constexpr int BM = 128, BN = 128, NT = 128;
 
 template <int BK>
 struct Cfg {
@@ -55,33 +58,48 @@ struct Cfg {
 };
 
 // One K-tile of the 128x128 tile: acc[i][j] += A[r_i][k] * B[k][c_j] for k
-// in increasing order.  Thread (warp w, lane l): rows r_i = (w&3)*32 +
-// (l>>3) + 4i, columns c_j = (w>>2)*64 + (l&7)*4 + {0..3, 32..35}.
-// A is read two k at a time (float2 per row) and B one k at a time (two
-// float4): 12 shared loads per 128 FFMA, 96 live registers for operands and
-// accumulators, which leaves headroom under the 128-register cap.
+// in increasing order.  Thread (warp w, lane l): rows r_i = 32w + (l>>3) +
+// 4i (i < 8), columns c_j = (l&7)*4 + 32(j/4) + j%4 (j < 16); a warp owns 32
+// full-width rows.  A is read two k at a time (float2 per row) and B one k
+// at a time (four float4, each row segment one 128-byte wavefront).  The
+// FMAs are packed in pairs of adjacent columns with __ffma2_rn: each lane of
+// the pair is the same round-to-nearest FMA as fmaf, so every sum and its k
+// order is exactly that of scalar FMAs, while 64 instructions per k carry
+// 128 FMAs -- half the issue slots, which is what lets 8 warps per SM keep
+// the FP32 pipe fed (the 8x8 scalar tiling at 16 warps per SM was
+// issue-bound at ~60% of the pipe).
 // kpair: two k (one k-pair kp) of one 32-deep sub-tile.
 __device__ __forceinline__ void kpair(const float* __restrict__ Asub, const float* __restrict__ Bsub,
-                                      float (&acc)[8][8], int arow0, int ty, int bcol, int kp) {
+                                      float (&acc)[8][16], int arow0, int ty, int bcol, int kp) {
   const int kc = kp >> 1, half = kp & 1;
   float2 a[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    // row r = arow0 + 4i; (r & 7) == ty + 4*(i&1) because arow0 = 32*wm + ty
+    // row r = arow0 + 4i; (r & 7) == ty + 4*(i&1) because arow0 = 32*w + ty
     const int sw = kc ^ (ty + 4 * (i & 1));
     a[i] = *reinterpret_cast<const float2*>(Asub + (arow0 + 4 * i) * 32 + (sw << 2) + 2 * half);
   }
 #pragma unroll
   for (int kk = 0; kk < 2; ++kk) {
     const float* brow = Bsub + (kp * 2 + kk) * BN + bcol;
-    const float4 b0 = *reinterpret_cast<const float4*>(brow);
-    const float4 b1 = *reinterpret_cast<const float4*>(brow + 32);
-    const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    float4 b[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) b[q] = *reinterpret_cast<const float4*>(brow + 32 * q);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float av = kk == 0 ? a[i].x : a[i].y;
+      const float2 ad = make_float2(av, av);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av, bv[j], acc[i][j]);
+      for (int q = 0; q < 4; ++q) {
+        float2 c0 = make_float2(acc[i][4 * q], acc[i][4 * q + 1]);
+        float2 c1 = make_float2(acc[i][4 * q + 2], acc[i][4 * q + 3]);
+        c0 = __ffma2_rn(ad, make_float2(b[q].x, b[q].y), c0);
+        c1 = __ffma2_rn(ad, make_float2(b[q].z, b[q].w), c1);
+        acc[i][4 * q] = c0.x;
+        acc[i][4 * q + 1] = c0.y;
+        acc[i][4 * q + 2] = c1.x;
+        acc[i][4 * q + 3] = c1.y;
+      }
     }
   }
 }
@@ -92,19 +110,20 @@ __device__ __forceinline__ void kpair(const float* __restrict__ Asub, const floa
 // latency still hides under the remaining FMAs.
 template <int BK>
 __device__ __forceinline__ void compute_stage(const float* __restrict__ As,
-                                              const float* __restrict__ Bs, float (&acc)[8][8],
-                                              int arow0, int ty, int bcol, const int* poll,
-                                              int& pend) {
+                                              const float* __restrict__ Bs, float (&acc)[8][16],
+                                              int arow0, int ty, int bcol, bool poll,
+                                              const int* flag, int& pend) {
 #pragma unroll
   for (int sub = 0; sub < BK / 32; ++sub) {
     const float* Asub = As + sub * (BM * 32);
     const float* Bsub = Bs + sub * 32 * BN;
-    // not unrolled: any unroll lets the scheduler hoist loads until the
-    // 128-register cap of 2 CTAs/SM spills (unconstrained it takes 167)
+    // not unrolled: unrolled by two the loop ran faster in a mainloop probe
+    // (56.4 against 52.1 TFLOP/s, operands resident in shared memory) but
+    // with this kernel's control state it exceeds 255 registers and spills
 #pragma unroll 1
     for (int kp = 0; kp < 14; ++kp) kpair(Asub, Bsub, acc, arow0, ty, bcol, kp);
     // the poll sits between two loops, not behind a per-iteration branch
-    if (sub == BK / 32 - 1 && poll != nullptr) pend = flag_load(poll);
+    if (sub == BK / 32 - 1 && poll) pend = flag_load(flag);
     // keeps the two loops apart when there is no poll (POLL_OFF), so that
     // variant is the polling code minus the load, not a re-fused loop whose
     // speed measured 39.7 or 42.1 TFLOP/s depending on the B200 it ran on
@@ -165,12 +184,8 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int ty = lane >> 3;
-  const int arow0 = (warp & 3) * 32 + ty;
-  const int bcol = (warp >> 2) * 64 + (lane & 7) * 4;
-  // (defined here, before the set-up block: ptxas keeps the 2-CTA/SM queue
-  // variants spill-free with this order and not with the definitions below it)
-  const int cta_q = blockIdx.x;
-  const int grid = SCHED == SCHED_CLC ? p.q.nslots : (int)gridDim.x;
+  const int arow0 = warp * 32 + ty;
+  const int bcol = (lane & 7) * 4;
 
   if (tid == 0) {
 #pragma unroll
@@ -182,6 +197,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
     s_gBase = 0;
     s_myTiles = 0;
     s_pending = 0;
+    s_slot = (int)blockIdx.x;
     if constexpr (SCHED == SCHED_CLC) {
       s_slot = slot_claim(p.q.slot_bits, p.q.nslots, p.wait_limit_ns);
       s_clcNext = blockIdx.x;
@@ -204,11 +220,14 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
   }
   __syncthreads();
   // per-CTA logs, counters and the checkpoint slab are indexed by cta(): the
-  // block index, or the resident slot under CLC -- re-read where it is used
-  // (rare paths) rather than held in a register under the 128-register cap
-  auto cta = [&]() -> int {
-    if constexpr (SCHED == SCHED_CLC) return *reinterpret_cast<volatile int*>(&s_slot);
-    else return cta_q;
+  // block index, or the resident slot under CLC, kept in shared memory and
+  // re-read where it is used (rare paths).  Read from the special register
+  // instead, the polling queue variants compiled to ~20 more registers
+  // (252 of 255) and ran 10% slower (41 against 45 TFLOP/s).
+  auto cta = [&]() -> int { return *reinterpret_cast<volatile int*>(&s_slot); };
+  auto grid = [&]() -> int {
+    if constexpr (SCHED == SCHED_CLC) return p.q.nslots;
+    else return (int)gridDim.x;
   };
   if constexpr (SCHED == SCHED_CLC) {
     if (s_slot < 0) {  // no slot came free (cannot happen while residency holds)
@@ -244,7 +263,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
   uint32_t P = 0, Q = 0;  // issued / consumed stage sequence numbers (uniform)
   bool bad = false;       // this thread saw a wait time out
   int pend = 0;           // tid 0: last flag value loaded inside a stage
-  float acc[8][8];
+  float acc[8][16];
 
   // Job state (uniform).  A job is a background tile or one urgent item;
   // both run through the single mainloop below.
@@ -298,7 +317,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
     }
     if (tid == 0) {
       const long long g = globaltimer_ns();
-      for (int e = s_lastSeen; e < f && e < p.ev.max_events; ++e) p.ev.obs_ns[(size_t)e * grid + cta()] = g;
+      for (int e = s_lastSeen; e < f && e < p.ev.max_events; ++e) p.ev.obs_ns[(size_t)e * grid() + cta()] = g;
       s_item = s_lastSeen;
       s_lastSeen = f;
       s_site = site;
@@ -339,13 +358,13 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
         // checkpoint: drain in-flight stages, park the accumulators
         drain();
         if (bg_active) {
-          float4* s4 = reinterpret_cast<float4*>(p.slab) + (size_t)cta() * 16 * NT;
+          float4* s4 = reinterpret_cast<float4*>(p.slab) + (size_t)cta() * 32 * NT;
 #pragma unroll
           for (int i = 0; i < 8; ++i)
 #pragma unroll
-            for (int h = 0; h < 2; ++h)
-              s4[(i * 2 + h) * NT + tid] =
-                  make_float4(acc[i][4 * h], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
+            for (int q = 0; q < 4; ++q)
+              s4[(i * 4 + q) * NT + tid] =
+                  make_float4(acc[i][4 * q], acc[i][4 * q + 1], acc[i][4 * q + 2], acc[i][4 * q + 3]);
           if (tid == 0) {
             s_bgRow0 = row0;
             s_bgCol0 = col0;
@@ -372,7 +391,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+        for (int j = 0; j < 16; ++j) acc[i][j] = 0.f;
       __syncthreads();  // the slot refilled first was read by the previous job
       prime(0);
     } else if (bg_active) {
@@ -385,16 +404,16 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
         c = s_bgC;
         kst0 = 0;
         nk = p.nk;
-        const float4* s4 = reinterpret_cast<const float4*>(p.slab) + (size_t)cta() * 16 * NT;
+        const float4* s4 = reinterpret_cast<const float4*>(p.slab) + (size_t)cta() * 32 * NT;
 #pragma unroll
         for (int i = 0; i < 8; ++i)
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const float4 v = s4[(i * 2 + h) * NT + tid];
-            acc[i][4 * h] = v.x;
-            acc[i][4 * h + 1] = v.y;
-            acc[i][4 * h + 2] = v.z;
-            acc[i][4 * h + 3] = v.w;
+          for (int q = 0; q < 4; ++q) {
+            const float4 v = s4[(i * 4 + q) * NT + tid];
+            acc[i][4 * q] = v.x;
+            acc[i][4 * q + 1] = v.y;
+            acc[i][4 * q + 2] = v.z;
+            acc[i][4 * q + 3] = v.w;
           }
         __syncthreads();
         prime(c);
@@ -439,7 +458,10 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
       bg_active = true;
       {
         int tm, tn;
-        tile_coords(tile, p.total_tiles / p.tiles_n, p.tiles_n, 8, tm, tn);
+        if (p.st.order != nullptr)
+          stream_tile(p.st, tile, p.tiles_n, tm, tn);
+        else
+          tile_coords(tile, p.total_tiles / p.tiles_n, p.tiles_n, 8, tm, tn);
         row0 = tm * BM;
         col0 = tn * BN;
       }
@@ -449,7 +471,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+        for (int j = 0; j < 16; ++j) acc[i][j] = 0.f;
       // streamed operands: the tile's A row panel and B column panel must
       // have landed before its first TMA load
       if (p.st.a_ready != nullptr && tid == 0 &&
@@ -495,8 +517,8 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
         }
         __syncthreads();
       }
-      const int* poll = (POLL == POLL_STAGE && !urgent && tid == 0) ? p.ev.flag : nullptr;
-      compute_stage<BK>(As, Bs, acc, arow0, ty, bcol, poll, pend);
+      compute_stage<BK>(As, Bs, acc, arow0, ty, bcol, POLL == POLL_STAGE && !urgent && tid == 0, p.ev.flag,
+                        pend);
       ++Q;
     }
     if (yielded) {
@@ -509,21 +531,20 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         float* crow = p.C + (size_t)(row0 + arow0 + 4 * i) * p.ldc + col0 + bcol;
-        *reinterpret_cast<float4*>(crow) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-        *reinterpret_cast<float4*>(crow + 32) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<float4*>(crow + 32 * q) =
+              make_float4(acc[i][4 * q], acc[i][4 * q + 1], acc[i][4 * q + 2], acc[i][4 * q + 3]);
       }
       bg_active = false;
-      if (p.st.done != nullptr) __threadfence();  // the panel's copy back reads these stores
+      if (p.st.done != nullptr) __threadfence();  // the block's copy back reads these stores
       __syncthreads();  // the whole tile is stored before it counts as complete
       if (tid == 0) {
         ++s_myTiles;
         if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[s_bgTask], 1);
         count_trigger(p.ev);
-        if (p.st.done != nullptr) {
-          const int tiles_m = p.total_tiles / p.tiles_n, pn = (row0 / BM) / p.st.panel_tm;
-          const int rows = tiles_m - pn * p.st.panel_tm < p.st.panel_tm ? tiles_m - pn * p.st.panel_tm : p.st.panel_tm;
-          if (atomicAdd(&p.st.done[pn], 1u) + 1u == (unsigned)(rows * p.tiles_n)) ack_host(&p.st.ack[pn]);
-        }
+        if (p.st.done != nullptr)
+          stream_tile_done(p.st, p.total_tiles / p.tiles_n, p.tiles_n, row0 / BM, col0 / BN);
       }
     } else {
       float* Cu = p.Cu + (size_t)ev * p.cu_stride;
@@ -531,14 +552,13 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
       for (int i = 0; i < 8; ++i) {
         float* crow = Cu + (size_t)(row0 + arow0 + 4 * i) * p.ldcu + col0 + bcol;
         if (p.usplit == 1) {
-          *reinterpret_cast<float4*>(crow) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-          *reinterpret_cast<float4*>(crow + 32) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<float4*>(crow + 32 * q) =
+                make_float4(acc[i][4 * q], acc[i][4 * q + 1], acc[i][4 * q + 2], acc[i][4 * q + 3]);
         } else {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            atomicAdd(crow + j, acc[i][j]);
-            atomicAdd(crow + 32 + j, acc[i][4 + j]);
-          }
+          for (int j = 0; j < 16; ++j) atomicAdd(crow + 32 * (j >> 2) + (j & 3), acc[i][j]);
         }
       }
       __syncthreads();  // whole item written before it is counted
@@ -609,6 +629,8 @@ static const void* select_kernel(int poll, int disc, bool oracle, int bk, int sc
 }
 
 int smem_bytes(int bk) { return bk == 32 ? Cfg<32>::SMEM_BYTES : Cfg<64>::SMEM_BYTES; }
+int stages(int bk) { return bk == 32 ? Cfg<32>::STAGES : Cfg<64>::STAGES; }
+int threads() { return NT; }
 size_t params_bytes() { return sizeof(F32Params); }
 
 cudaError_t prepare(int poll, int disc, bool oracle, int bk, int sched, int* max_ctas_per_sm) {
