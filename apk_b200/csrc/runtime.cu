@@ -31,6 +31,14 @@ int stages(int bk);
 int threads();
 size_t params_bytes();
 }  // namespace f32
+namespace f32ws {
+cudaError_t prepare(int poll, int disc, bool oracle, int* ok);
+cudaError_t launch(const F32Params& prm, int workers, int poll, int disc, bool oracle, cudaStream_t stream);
+int smem_bytes();
+int threads();
+int workers_per_cta();
+size_t params_bytes();
+}  // namespace f32ws
 namespace vis {
 cudaError_t launch(const VisParams& prm, int grid, int smem_bytes, bool loaded, cudaStream_t stream);
 int threads();
@@ -104,6 +112,11 @@ struct apk_ctx {
   apk_config cfg{};
   std::string err;
   int sms = 0, grid = 0, ctas_per_sm = 0, max_ctas_per_sm = 0;
+  // fp32: the warp-specialized kernel (two workers per 384-thread CTA) can
+  // run every poll variant this context launches; sync_only holds the
+  // block-synchronous kernel for experiments that compare grids slot by slot
+  bool ws_ok = false;
+  bool sync_only = false;
   int cc_major = 0, cc_minor = 0;
   char name[128] = {0};
   cudaStream_t kstream = nullptr, cstream = nullptr, ustream = nullptr;
@@ -280,7 +293,23 @@ apk_status prepare_kernel(apk_ctx* ctx, int poll) {
                 cudaGetErrorString(e));
   if (maxc < 1) return fail(ctx, APK_EUNSUPPORTED, "kernel does not fit on an SM");
   ctx->max_ctas_per_sm = maxc;
+  if (ctx->cfg.dtype == APK_F32 && ctx->cfg.scheduler == APK_SCHED_QUEUE && ctx->cfg.k_tile == 32) {
+    int ok = 0;
+    e = f32ws::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, &ok);
+    if (e != cudaSuccess) ok = 0;
+    ctx->ws_ok = ctx->ws_ok && ok;
+  }
   return APK_OK;
+}
+
+// The fp32 launch runs the warp-specialized kernel (one 384-thread CTA per
+// SM, two 128x128 workers) at full residency of the default schedule: queue
+// scheduler, K-tile 32, exactly two workers per SM.  Other grids (reserved
+// slots, one CTA per SM), K-tile 64 and cluster launch control run the
+// block-synchronous kernel.
+bool use_ws(const apk_ctx* ctx) {
+  return ctx->cfg.dtype == APK_F32 && ctx->ws_ok && !ctx->sync_only && ctx->cfg.scheduler == APK_SCHED_QUEUE &&
+         ctx->cfg.k_tile == 32 && ctx->grid == ctx->sms * f32ws::workers_per_cta();
 }
 
 }  // namespace
@@ -315,7 +344,8 @@ apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
   apk_config& c = ctx->cfg;
   // every translation unit must agree on the kernel parameter block (objects
   // compiled against different copies of proto.h would read garbage pointers)
-  if (f32::params_bytes() != sizeof(F32Params) || bf16::params_bytes() != sizeof(F32Params)) {
+  if (f32::params_bytes() != sizeof(F32Params) || bf16::params_bytes() != sizeof(F32Params) ||
+      f32ws::params_bytes() != sizeof(F32Params)) {
     fail(ctx, APK_EUNSUPPORTED, "kernel parameter layout mismatch (f32 %zu, bf16 %zu, runtime %zu bytes): rebuild",
          f32::params_bytes(), bf16::params_bytes(), sizeof(F32Params));
     *out = ctx;
@@ -356,6 +386,7 @@ apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
   if (prop.major != 10)
     return fail(ctx, APK_EUNSUPPORTED, "device %s is sm_%d%d; this build targets sm_100a", prop.name,
                 prop.major, prop.minor);
+  ctx->ws_ok = c.dtype == APK_F32;  // cleared by any variant the warp-specialized kernel lacks
   apk_status s = prepare_kernel(ctx, kernel_poll(ctx));
   if (s != APK_OK) return s;
   // the POLL_OFF variant is used by the overhead and baseline modes
@@ -491,7 +522,14 @@ apk_status apk_get_info(apk_ctx* ctx, apk_device_info* info) {
   info->max_ctas_per_sm = ctx->max_ctas_per_sm;
   info->cc_major = ctx->cc_major;
   info->cc_minor = ctx->cc_minor;
-  if (ctx->cfg.dtype == APK_F32) {
+  if (ctx->cfg.dtype == APK_F32 && use_ws(ctx)) {
+    // grid and ctas_per_sm count workers (two per CTA)
+    info->smem_per_cta = f32ws::smem_bytes();
+    info->threads_per_cta = f32ws::threads();
+    info->tile_m = 128;
+    info->tile_n = 128;
+    info->stages = f32::stages(ctx->cfg.k_tile);
+  } else if (ctx->cfg.dtype == APK_F32) {
     info->smem_per_cta = f32::smem_bytes(ctx->cfg.k_tile);
     info->threads_per_cta = f32::threads();
     info->tile_m = 128;
@@ -880,7 +918,9 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
   p.ev = ev;
   p.q = q;
   p.st = ctx->st_cfg;
-  if (f32)
+  if (f32 && use_ws(ctx))
+    e = f32ws::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, stream);
+  else if (f32)
     e = f32::launch(p, ctx->cfg.scheduler == APK_SCHED_CLC ? (int)num_tasks : ctx->grid, poll,
                     ctx->cfg.discipline, ctx->cfg.oracle != 0, bk, ctx->cfg.scheduler, stream);
   else
@@ -1554,8 +1594,28 @@ apk_status apk_run_overhead(apk_ctx* ctx, unsigned long long num_tasks, int reps
   return APK_OK;
 }
 
+namespace {
+apk_status run_reserved_impl(apk_ctx* ctx, unsigned long long num_tasks, int reserve, int trials, unsigned seed,
+                             double* e2e_us, double* bg_tflops, bool slot_grid);
+}
+
 apk_status apk_run_reserved(apk_ctx* ctx, unsigned long long num_tasks, int reserve, int trials, unsigned seed,
                             double* e2e_us, double* bg_tflops) {
+  return run_reserved_impl(ctx, num_tasks, reserve, trials, seed, e2e_us, bg_tflops, true);
+}
+
+apk_status apk_run_baseline(apk_ctx* ctx, unsigned long long num_tasks, int trials, unsigned seed,
+                            double* e2e_us) {
+  // the no-preemption baseline runs the context's own background kernel
+  return run_reserved_impl(ctx, num_tasks, 0, trials, seed, e2e_us, nullptr, false);
+}
+
+namespace {
+// slot_grid: run the block-synchronous kernel for every reserve (0
+// included), whose resident CTA slots (two per SM) can be held out one at a
+// time; the warp-specialized kernel's workers come two per SM-filling CTA.
+apk_status run_reserved_impl(apk_ctx* ctx, unsigned long long num_tasks, int reserve, int trials, unsigned seed,
+                             double* e2e_us, double* bg_tflops, bool slot_grid) {
   if (!ctx || trials <= 0 || !e2e_us || num_tasks == 0 || num_tasks == APK_TASKS_UNBOUNDED) return APK_EINVAL;
   if (reserve < 0 || reserve >= ctx->grid)
     return fail(ctx, APK_EINVAL, "reserve %d must leave at least one of the %d background CTAs", reserve, ctx->grid);
@@ -1611,8 +1671,12 @@ apk_status apk_run_reserved(apk_ctx* ctx, unsigned long long num_tasks, int rese
   struct GridGuard {
     apk_ctx* c;
     int keep;
-    ~GridGuard() { c->grid = keep; }
+    ~GridGuard() {
+      c->grid = keep;
+      c->sync_only = false;
+    }
   } guard{ctx, ctx->grid};
+  ctx->sync_only = slot_grid;
   ctx->grid -= reserve;
 
   // drain estimate, background alone (device timeline)
@@ -1645,10 +1709,7 @@ apk_status apk_run_reserved(apk_ctx* ctx, unsigned long long num_tasks, int rese
   return read_status(ctx);
 }
 
-apk_status apk_run_baseline(apk_ctx* ctx, unsigned long long num_tasks, int trials, unsigned seed,
-                            double* e2e_us) {
-  return apk_run_reserved(ctx, num_tasks, 0, trials, seed, e2e_us, nullptr);
-}
+}  // namespace
 
 apk_status apk_run_visibility(apk_ctx* ctx, const apk_visibility_config* vc, apk_visibility_result* out,
                               long long* set_out, long long* obs_out) {
