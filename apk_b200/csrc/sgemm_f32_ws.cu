@@ -370,6 +370,13 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
         if (task < p.q.num_tasks) next_task = atomicAdd(p.q.next_task, 1ull);
         if (!finish_tile()) break;  // the previous tile's stages are all consumed
         int f = vload(&sh.gen);
+        if (POLL != POLL_OFF) {
+          // at a boundary also read the flag itself: the control warp's copy
+          // lags a store by up to a load's latency, and a bounded drain's
+          // last tiles must not end unaware of a yield raised just before
+          const int fg = flag_load(p.ev.flag);
+          f = (fg < 0 || f < 0) ? -1 : max(f, fg);
+        }
         if (f < 0 || vload(&sh.abort)) break;
         if (POLL != POLL_OFF && f != lastSeen && handle(f, -1) == -1) break;
         if (task >= p.q.num_tasks) break;
@@ -431,7 +438,8 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
     const int ty = lane >> 3, arow0 = w * 32 + ty, bcol = (lane & 7) * 4;
     float4* slab = reinterpret_cast<float4*>(p.slab) + (size_t)worker * 32 * 128;
     float acc[8][16];
-    int cur = 0;  // K stages of the background tile accumulated by this warp
+    int cur = 0;           // K stages of the background tile accumulated by this warp
+    bool bg_regs = false;  // acc holds the background tile (not an urgent item's)
     uint32_t Q = 0;
     while (true) {
       const int s = Q % S;
@@ -439,13 +447,18 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
       const Tag t = gs.tag[s];
       if (t.kind == T_STOP) break;
       if (t.kind == T_SUSPEND) {
-        // checkpoint: this thread's 128 accumulators and the warp's cursor
+        // checkpoint: this thread's 128 accumulators and the warp's cursor.
+        // A second yield before the tile resumed finds an urgent item's
+        // values in acc: the slab already holds the tile, keep it.
+        if (bg_regs) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+          for (int i = 0; i < 8; ++i)
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            slab[(i * 4 + q) * 128 + gtid] =
-                make_float4(acc[i][4 * q], acc[i][4 * q + 1], acc[i][4 * q + 2], acc[i][4 * q + 3]);
+            for (int q = 0; q < 4; ++q)
+              slab[(i * 4 + q) * 128 + gtid] =
+                  make_float4(acc[i][4 * q], acc[i][4 * q + 1], acc[i][4 * q + 2], acc[i][4 * q + 3]);
+          bg_regs = false;
+        }
         __syncwarp();
         if (lane == 0) {
           vstore(&gs.cur[w], cur);
@@ -471,8 +484,10 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
               acc[i][4 * q + 2] = v.z;
               acc[i][4 * q + 3] = v.w;
             }
+          bg_regs = true;
         } else if (t.flags & F_FIRST) {
           cur = 0;
+          bg_regs = true;
 #pragma unroll
           for (int i = 0; i < 8; ++i)
 #pragma unroll

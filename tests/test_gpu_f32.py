@@ -134,6 +134,43 @@ def test_stage_checkpoint_resume_is_bitwise(libapk):
     assert v["pass"], v
 
 
+def test_back_to_back_yields_bitwise(libapk):
+    """Yields 4 us apart: a second yield often lands while the first one's
+    urgent items run, before the background tile has resumed.  The tile must
+    still resume from its own checkpoint (not from an urgent item's
+    accumulators): C bitwise equal to an uninterrupted run."""
+    M = N = K = 2048
+    A, B = oracle.gen_uniform(M, N, K, 21)
+    Au, Bu, refu = _urgent_ref()
+    with _ctx(poll="off") as c:
+        c.set_background(A, B)
+        c.launch(c.info["grid"] * 3)
+        c.wait(60)
+        C0 = c.read_output()
+    nev = 30
+    offs = 20_000 + np.arange(nev, dtype=np.int64) * 4_000
+    with _ctx(poll="stage", set_mode="device", oracle=True, max_events=64) as c:
+        ntasks = c.info["grid"] * 3
+        c.set_background(A, B)
+        c.set_urgent(Au, Bu)
+        c.schedule_device_events(offs)
+        c.launch(ntasks)
+        c.wait(120)
+        C = c.read_output()
+        ev = c.read_events()
+        ex, ue = c.read_oracle(ntasks)
+        st = c.run_stats()
+        outs = [c.read_urgent_output(e) for e in range(nev) if ev["claimer"][e]]
+        uitems = (U_M // 128) * (U_N // 128) * c.cfg.urgent_split_k
+    fired = int(np.count_nonzero(ev["set_ns"][:nev]))
+    assert fired == nev and st["yields"] > 0
+    assert np.array_equal(C.view(np.uint32), C0.view(np.uint32)), "resume not bitwise"
+    for Cu in outs:
+        _check(Cu, refu, U_K)
+    v = oracle.exactly_once(ex, ue[:fired], ev["claimer"][:fired], ev["set_ns"][:fired], uitems, fired)
+    assert v["pass"], v
+
+
 def test_poison_discipline_is_detected(libapk):
     """Positive control (src/midyield.cu:146-147): a corrupted staged urgent
     value must make every claimed event's urgent output fail the check."""
