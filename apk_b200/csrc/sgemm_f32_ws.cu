@@ -444,9 +444,12 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
     while (true) {
       const int s = Q % S;
       if (!bwait(&gs.full[s], (Q / S) & 1, p, sh)) break;
-      const Tag t = gs.tag[s];
-      if (t.kind == T_STOP) break;
-      if (t.kind == T_SUSPEND) {
+      // only the fields the stage needs live in registers across the
+      // mainloop; the epilogue re-reads the rest from the slot, which is not
+      // released before it is done
+      const int kind = vload(&gs.tag[s].kind), flags = vload(&gs.tag[s].flags), tc = vload(&gs.tag[s].c);
+      if (kind == T_STOP) break;
+      if (kind == T_SUSPEND) {
         // checkpoint: this thread's 128 accumulators and the warp's cursor.
         // A second yield before the tile resumed finds an urgent item's
         // values in acc: the slab already holds the tile, keep it.
@@ -469,8 +472,8 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
         continue;
       }
       bool compute = true;
-      if (t.kind == T_BG) {
-        if (t.flags & F_RESUME) {
+      if (kind == T_BG) {
+        if (flags & F_RESUME) {
           // the checkpointed accumulators; cur is this warp's own cursor,
           // kept across the urgent items (a re-issue from stage 0 also
           // carries F_FIRST, which must not reset it)
@@ -485,7 +488,7 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
               acc[i][4 * q + 3] = v.w;
             }
           bg_regs = true;
-        } else if (t.flags & F_FIRST) {
+        } else if (flags & F_FIRST) {
           cur = 0;
           bg_regs = true;
 #pragma unroll
@@ -494,8 +497,8 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
             for (int j = 0; j < 16; ++j) acc[i][j] = 0.f;
         }
         // already accumulated before a checkpoint, or queued behind a yield
-        compute = t.c == cur && !vload(&gs.skip);
-      } else if (t.flags & F_FIRST) {
+        compute = tc == cur && !vload(&gs.skip);
+      } else if (flags & F_FIRST) {
 #pragma unroll
         for (int i = 0; i < 8; ++i)
 #pragma unroll
@@ -506,7 +509,7 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
         const float* Bs = reinterpret_cast<const float*>(ring + S * A_BYTES + s * B_BYTES);
 #pragma unroll 2
         for (int kp = 0; kp < 16; ++kp) kpair(As, Bs, acc, arow0, ty, bcol, kp);
-        if (DISC == DISC_POISON && t.kind == T_URG && (t.flags & F_FIRST) && bcol == 0) {
+        if (DISC == DISC_POISON && kind == T_URG && (flags & F_FIRST) && bcol == 0) {
           // detector control: the item's first staged B value B[k0][c0] read
           // as B + 1 (src/midyield.cu:146-147), applied in registers
 #pragma unroll
@@ -515,25 +518,27 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
             acc[i][0] += As[r * 32 + (((0 ^ (r & 7))) << 2)];
           }
         }
-        if (t.kind == T_BG) cur = t.c + 1;
+        if (kind == T_BG) cur = tc + 1;
       }
-      const bool done_tile = (t.flags & F_LAST) && (t.kind == T_URG || (compute && cur == p.nk));
+      const bool done_tile = (flags & F_LAST) && (kind == T_URG || (compute && cur == p.nk));
       if (done_tile) {
+        const Tag& t = gs.tag[s];
+        const int row0 = vload(&t.row0), col0 = vload(&t.col0), e = vload(&t.e);
         // ---- epilogue: this warp's 32 rows of the tile ----
-        if (t.kind == T_BG) {
+        if (kind == T_BG) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            float* crow = p.C + (size_t)(t.row0 + arow0 + 4 * i) * p.ldc + t.col0 + bcol;
+            float* crow = p.C + (size_t)(row0 + arow0 + 4 * i) * p.ldc + col0 + bcol;
 #pragma unroll
             for (int q = 0; q < 4; ++q)
               *reinterpret_cast<float4*>(crow + 32 * q) =
                   make_float4(acc[i][4 * q], acc[i][4 * q + 1], acc[i][4 * q + 2], acc[i][4 * q + 3]);
           }
         } else {
-          float* Cu = p.Cu + (size_t)t.e * p.cu_stride;
+          float* Cu = p.Cu + (size_t)e * p.cu_stride;
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            float* crow = Cu + (size_t)(t.row0 + arow0 + 4 * i) * p.ldcu + t.col0 + bcol;
+            float* crow = Cu + (size_t)(row0 + arow0 + 4 * i) * p.ldcu + col0 + bcol;
             if (p.usplit == 1) {
 #pragma unroll
               for (int q = 0; q < 4; ++q)
@@ -552,20 +557,20 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
         // behind a yield stores it after the resume, in another slot.  An
         // urgent item (never skipped) counts on its slot, which is not
         // refilled before all four warps have released it.
-        int* cnt = t.kind == T_BG ? &gs.bg_cnt : &gs.cnt[s];
+        int* cnt = kind == T_BG ? &gs.bg_cnt : &gs.cnt[s];
         if (lane == 0 && atomicAdd(cnt, 1) == 3) {
           *cnt = 0;
-          if (t.kind == T_BG) {
+          if (kind == T_BG) {
             ++gs.tiles;
             if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[t.task], 1);
             count_trigger(p.ev);
             if (p.st.done != nullptr)
-              stream_tile_done(p.st, p.total_tiles / p.tiles_n, p.tiles_n, t.row0 / BM, t.col0 / BN);
+              stream_tile_done(p.st, p.total_tiles / p.tiles_n, p.tiles_n, row0 / BM, col0 / BN);
           } else {
-            if (ORACLE) atomicAdd(&p.ev.uexec[t.e], 1);
-            atomicMax(&p.ev.done_ns[t.e], (unsigned long long)globaltimer_ns());
-            const int done = atomicAdd(&p.ev.udone_cnt[t.e], 1) + 1;
-            if (done == p.uitems && p.ev.ack != nullptr) ack_host(&p.ev.ack[2 * t.e + 1]);
+            if (ORACLE) atomicAdd(&p.ev.uexec[e], 1);
+            atomicMax(&p.ev.done_ns[e], (unsigned long long)globaltimer_ns());
+            const int done = atomicAdd(&p.ev.udone_cnt[e], 1) + 1;
+            if (done == p.uitems && p.ev.ack != nullptr) ack_host(&p.ev.ack[2 * e + 1]);
           }
         }
       }
