@@ -308,7 +308,8 @@ apk_status prepare_kernel(apk_ctx* ctx, int poll) {
 // slots, one CTA per SM), K-tile 64 and cluster launch control run the
 // block-synchronous kernel.
 bool use_ws(const apk_ctx* ctx) {
-  return ctx->cfg.dtype == APK_F32 && ctx->ws_ok && !ctx->sync_only && ctx->cfg.scheduler == APK_SCHED_QUEUE &&
+  return ctx->cfg.dtype == APK_F32 && ctx->ws_ok && !ctx->sync_only && ctx->cfg.f32_kernel != APK_F32_BLOCK_SYNC &&
+         ctx->cfg.scheduler == APK_SCHED_QUEUE &&
          ctx->cfg.k_tile == 32 && ctx->grid == ctx->sms * f32ws::workers_per_cta();
 }
 
@@ -398,6 +399,10 @@ apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
   }
   ctx->ctas_per_sm = c.ctas_per_sm > 0 ? std::min(c.ctas_per_sm, ctx->max_ctas_per_sm) : ctx->max_ctas_per_sm;
   ctx->grid = c.grid > 0 ? c.grid : ctx->sms * ctx->ctas_per_sm;
+  if (c.dtype == APK_F32 && c.f32_kernel == APK_F32_WARP_SPECIALIZED && !use_ws(ctx))
+    return fail(ctx, APK_EUNSUPPORTED,
+                "the warp-specialized fp32 kernel needs the queue scheduler, K-tile 32 and two workers per SM "
+                "(grid %d, %d SMs)", ctx->grid, ctx->sms);
   if (ctx->grid > ctx->sms * ctx->max_ctas_per_sm)
     return fail(ctx, APK_EINVAL,
                 "grid %d exceeds the %d resident slots; CTAs beyond residency would never "

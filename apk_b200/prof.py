@@ -1,6 +1,6 @@
 """One bounded drain of the persistent kernel, repeated, for profilers.
 
-    python -m apk_b200.prof f32  [--n 4096] [--poll stage] [--reps 2]
+    python -m apk_b200.prof f32  [--n 4096] [--poll stage] [--reps 2] [--kernel auto|ws|sync]
     python -m apk_b200.prof bf16 [--n 6144] [--poll stage] [--reps 3]
 
 Each repetition drains every tile of an n^3 background GEMM once (fp32:
@@ -22,6 +22,8 @@ def main():
     ap.add_argument("--n", type=int, default=0)
     ap.add_argument("--poll", default="stage", choices=("off", "boundary", "stage"))
     ap.add_argument("--reps", type=int, default=0)
+    ap.add_argument("--kernel", default="auto", choices=("auto", "ws", "sync"),
+                    help="fp32: warp-specialized or block-synchronous kernel")
     args = ap.parse_args()
 
     import apk_b200
@@ -37,7 +39,7 @@ def main():
     else:
         A, B = apk_b200.fill_uniform(n, n, n, 21)
         Au, Bu = apk_b200.fill_uniform(256, 256, 256, 99)
-    with apk_b200.Context(dtype=args.dtype, poll=args.poll, urgent_split_k=1) as c:
+    with apk_b200.Context(dtype=args.dtype, poll=args.poll, urgent_split_k=1, f32_kernel=args.kernel) as c:
         c.set_background(A, B)
         c.set_urgent(Au, Bu)
         info = c.info

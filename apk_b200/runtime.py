@@ -21,6 +21,7 @@ _SET = {"device": L.APK_SET_DEVICE, "host_mapped": L.APK_SET_HOST_MAPPED,
         "host_memcpy": L.APK_SET_HOST_MEMCPY}
 _DTYPE = {"f32": L.APK_F32, "bf16": L.APK_BF16}
 _SCHED = {"queue": L.APK_SCHED_QUEUE, "clc": L.APK_SCHED_CLC}
+_F32K = {"auto": 0, "ws": 1, "sync": 2}
 
 
 class ApkError(RuntimeError):
@@ -105,7 +106,8 @@ class Context:
     def __init__(self, device: int = 0, dtype: str = "f32", ctas_per_sm: int = 0, grid: int = 0,
                  k_tile: int = 0, poll: str = "stage", discipline: str = "drain",
                  set_mode: str = "host_memcpy", max_events: int = 4096, oracle: bool = False,
-                 urgent_split_k: int = 8, wait_limit_ns: int = 2_000_000_000, scheduler: str = "queue"):
+                 urgent_split_k: int = 8, wait_limit_ns: int = 2_000_000_000, scheduler: str = "queue",
+                 f32_kernel: str = "auto"):
         self._lib = L.load()
         cfg = L.Config()
         self._lib.apk_config_default(ctypes.byref(cfg))
@@ -114,6 +116,7 @@ class Context:
         cfg.set_mode, cfg.max_events, cfg.oracle = _SET[set_mode], max_events, int(oracle)
         cfg.urgent_split_k, cfg.wait_limit_ns = urgent_split_k, int(wait_limit_ns)
         cfg.scheduler = _SCHED[scheduler]
+        cfg.f32_kernel = _F32K[f32_kernel]
         self.cfg = cfg
         self.dtype = dtype
         h = ctypes.c_void_p()

@@ -398,7 +398,7 @@ def run_ours(args, world, rank, local):
     # DRAM bytes per launch: the ncu capture's per-tile traffic (read + write)
     # scaled to the average tiles of a timed launch
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "sgemm_f32_persistent_4096.md")
+    tp = os.path.join(ROOT, "profiles", "sgemm_f32_ws_4096.md")
     if os.path.exists(tp):
         for ln in open(tp):
             if ln.startswith("dram_bytes_per_tile:"):

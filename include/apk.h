@@ -80,6 +80,21 @@ typedef enum apk_mem_kind { APK_MEM_HOST = 0, APK_MEM_DEVICE = 1 } apk_mem_kind;
  * later.  The cooperative yield works the same under both. */
 typedef enum apk_scheduler { APK_SCHED_QUEUE = 0, APK_SCHED_CLC = 1 } apk_scheduler;
 
+/* fp32 kernel.  WARP_SPECIALIZED: one 384-thread CTA per SM runs two
+ * 128x128 workers (compute warps fed by a TMA producer warp per worker, a
+ * control warp for the flag); it serves the queue scheduler at K-tile 32
+ * with exactly two workers per SM.  BLOCK_SYNC: 128-thread CTAs, one block
+ * barrier per stage; it serves every configuration (CLC, K-tile 64, one CTA
+ * per SM, reduced grids).  AUTO picks WARP_SPECIALIZED where it applies.
+ * Both compute every C element with the same FMA sequence: bitwise-equal
+ * outputs.  In the warp-specialized kernel a "CTA" of the grid, the event
+ * log, tile counters and checkpoint slabs is a worker. */
+typedef enum apk_f32_kernel {
+  APK_F32_AUTO = 0,
+  APK_F32_WARP_SPECIALIZED = 1,
+  APK_F32_BLOCK_SYNC = 2
+} apk_f32_kernel;
+
 typedef struct apk_config {
   int device;
   apk_dtype dtype;
@@ -95,6 +110,7 @@ typedef struct apk_config {
   int urgent_split_k;       /* urgent items per urgent output tile            */
   long long wait_limit_ns;  /* bound on every device-side wait                */
   apk_scheduler scheduler;  /* (ABI 2) background work distribution           */
+  apk_f32_kernel f32_kernel;/* (ABI 3) fp32 kernel choice                       */
 } apk_config;
 
 /* Fill *cfg with the defaults (fp32, full residency, default k_tile, stage

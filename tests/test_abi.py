@@ -44,6 +44,7 @@ def test_config_defaults(libapk):
     assert (c.dtype, c.k_tile, c.poll, c.discipline, c.set_mode) == (
         _lib.APK_F32, 0, _lib.APK_POLL_STAGE, _lib.APK_DISC_DRAIN, _lib.APK_SET_HOST_MEMCPY)
     assert c.max_events == 4096 and c.urgent_split_k == 8 and c.wait_limit_ns == 2_000_000_000
+    assert c.scheduler == _lib.APK_SCHED_QUEUE and c.f32_kernel == 0  # queue, fp32 kernel auto
 
 
 @pytest.mark.parametrize("seed,shape", [(21, (1024, 1024, 1024)), (0, (128, 256, 64)), (7, (256, 128, 512))])

@@ -65,6 +65,20 @@ def test_streamed_gemm_ragged_shapes(libapk, shape):
     _check(C, oracle.gemm_f64(A, B), K)
 
 
+def test_fp32_kernels_bitwise_equal(libapk):
+    """The warp-specialized and the block-synchronous fp32 kernels run the
+    same FMA sequence per element: bitwise-equal C, both within tolerance."""
+    A, B = oracle.gen_uniform(1024, 1536, 768, 23)
+    out = {}
+    for k in ("ws", "sync"):
+        with _ctx(poll="stage", f32_kernel=k) as c:
+            out[k] = c.gemm(A, B)
+            if k == "ws":
+                assert c.info["threads_per_cta"] == 384
+    assert np.array_equal(out["ws"].view(np.uint32), out["sync"].view(np.uint32))
+    _check(out["ws"], oracle.gemm_f64(A, B), 768)
+
+
 def test_cfg0_yield_at_50_percent_boundary(libapk):
     """1024^3 fp32, one yield at a tile boundary after 50% of the
     64 tiles complete; C within tolerance and bitwise equal to the no-yield
