@@ -62,7 +62,8 @@ def _infeasible_reason(dtype, cps, kt, info):
         elif kt == 64:
             why = "each CTA's two 64 KB stages take 129 KB of the 227 KB of shared memory"
         else:
-            why = "each 256-thread CTA holds 128 registers per thread, 32K of the SM's 64K"
+            why = ("each 128-thread CTA holds ~232 registers per thread (29.7K of the SM's 64K) and 97 KB "
+                   "of shared memory")
         return f"{cps} CTAs/SM: at most {info['max_ctas_per_sm']} fit ({why})"
     return None
 
@@ -111,6 +112,8 @@ def run_cell(apk_b200, dtype, cps, kt, shape, events, warmup, seed, operands):
         yields = c.run_stats()["yields"]
     cell.update({
         "grid": info["grid"], "tile": [info["tile_m"], info["tile_n"]], "stages": info["stages"],
+        "kernel": ("warp-specialized (2 workers per 384-thread CTA)" if info["threads_per_cta"] == 384 else
+                   f"{info['threads_per_cta']}-thread CTAs"),
         "urgent_split_k": split,
         "tflops_poll_off": flops / (ms_off / 1e3) / 1e12,
         "tflops_poll_stage": flops / (ms_poll / 1e3) / 1e12,
