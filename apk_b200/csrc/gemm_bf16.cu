@@ -520,22 +520,28 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         // lane (256 terms, ~1e-6 relative) keeps the double conversions off
         // the path that frees TMEM, the lanes and warps add up in double
         float csum[2] = {0.0f, 0.0f};
-#pragma unroll 1
-        for (int bb = g; bb < 8 * nh; bb += 2) {
+        // This warp's blocks bb = g, g+2, ... (< 8 * nh); rows past the task's
+        // m (a 128-row task in a 256-row tile) are neither stored nor summed.
+        // Software-pipelined: the next block's tcgen05.ld is issued before
+        // the current block's stores, and TMEM is released as soon as the
+        // last block is in registers, before its stores.
+        const int lim = 8 * nh;
+        auto valid = [&](int bb) { return !(j.action == E_STORE_C && (bb & 7) * 32 >= j.e); };
+        auto next = [&](int bb) {
+          bb += 2;
+          while (bb < lim && !valid(bb)) bb += 2;
+          return bb;
+        };
+        auto tload = [&](int bb, uint32_t(&v)[32]) { tc::ld_32x32b_x32(tcol + (bb >> 3) * 256 + (bb & 7) * 32, v); };
+        auto consume = [&](int bb, const uint32_t(&v)[32]) {
           const int hh = bb >> 3, blk = bb & 7;
-          // rows past the task's m (a 128-row task in a 256-row tile) are
-          // neither stored nor summed
-          if (j.action == E_STORE_C && blk * 32 >= j.e) continue;
-          uint32_t v[32];
-          tc::ld_32x32b_x32(tcol + hh * 256 + blk * 32, v);
-          tc::wait_ld();
           if (j.action == E_SPILL) {
             float4* s4 = reinterpret_cast<float4*>(slab_blk(hh, blk));
 #pragma unroll
             for (int i = 0; i < 8; ++i)
               s4[i * 32 + lane] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
                                               __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
-            continue;
+            return;
           }
           // register i -> C row blk*32+i, lane -> C column: each store
           // instruction writes one contiguous 128-byte row segment
@@ -545,11 +551,14 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
 #pragma unroll
             for (int i = 0; i < 32; ++i) dst[(size_t)i * p.ldc] = __uint_as_float(v[i]);
             if (p.task_mode) {
+              // one running sum per half, blocks in order, rows in order
+              float cs = hh == 0 ? csum[0] : csum[1];
 #pragma unroll
               for (int i = 0; i < 32; ++i) {
                 const float x = __uint_as_float(v[i]);
-                csum[hh] = fmaf(x, x, csum[hh]);
+                cs = fmaf(x, x, cs);
               }
+              if (hh == 0) csum[0] = cs; else csum[1] = cs;
             }
           } else {
             float* dst = p.Cu + (size_t)j.e * p.cu_stride + (size_t)(j.row0 + blk * 32) * p.ldcu + col;
@@ -561,19 +570,39 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
               for (int i = 0; i < 32; ++i) atomicAdd(dst + (size_t)i * p.ldcu, __uint_as_float(v[i]));
             }
           }
-        }
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&sh.tempty[j.buf]);
-          if (j.wide) mbar_arrive(&sh.tempty[1]);  // a wide job held both buffers (buf 0 and 1)
-          if (j.action == E_SPILL && p.q.ckpt != nullptr) {
-            // TMEM free again: this warp's 4 * nh blocks are read and their
-            // slab stores issued
-            atomicAdd(&p.q.ckpt[0], (unsigned long long)(globaltimer_ns() - s0));
-            atomicAdd(&p.q.ckpt[1], (unsigned long long)nh * 4 * 4096);
+        };
+        bool released = false;
+        auto release = [&]() {  // every tcgen05.ld of this warp has completed
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&sh.tempty[j.buf]);
+            if (j.wide) mbar_arrive(&sh.tempty[1]);  // a wide job held both buffers (buf 0 and 1)
+            if (j.action == E_SPILL && p.q.ckpt != nullptr) {
+              // TMEM free again: this warp's 4 * nh blocks are in registers
+              atomicAdd(&p.q.ckpt[0], (unsigned long long)(globaltimer_ns() - s0));
+              atomicAdd(&p.q.ckpt[1], (unsigned long long)nh * 4 * 4096);
+            }
           }
+          released = true;
+        };
+        uint32_t va[32], vb[32];
+        int cur = valid(g) ? g : next(g);
+        if (cur < lim) tload(cur, va);
+        while (cur < lim) {
+          tc::wait_ld();
+          int nxt = next(cur);
+          if (nxt < lim) tload(nxt, vb); else release();
+          consume(cur, va);
+          cur = nxt;
+          if (cur >= lim) break;
+          tc::wait_ld();
+          nxt = next(cur);
+          if (nxt < lim) tload(nxt, va); else release();
+          consume(cur, vb);
+          cur = nxt;
         }
+        if (!released) release();  // no block of this warp had valid rows
         if (j.action != E_SPILL) {
           if (p.task_mode && j.action == E_STORE_C) {
             for (int hh = 0; hh < nh; ++hh) {
