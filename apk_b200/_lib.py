@@ -32,7 +32,8 @@ class Config(ctypes.Structure):
     _fields_ = [("device", c_int), ("dtype", c_int), ("ctas_per_sm", c_int), ("grid", c_int),
                 ("k_tile", c_int), ("poll", c_int), ("discipline", c_int), ("set_mode", c_int),
                 ("max_events", c_int), ("oracle", c_int), ("urgent_split_k", c_int),
-                ("wait_limit_ns", c_ll), ("scheduler", c_int), ("f32_kernel", c_int)]
+                ("wait_limit_ns", c_ll), ("scheduler", c_int), ("f32_kernel", c_int),
+                ("bf16_kernel", c_int)]
 
 
 class DeviceInfo(ctypes.Structure):

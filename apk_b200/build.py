@@ -23,7 +23,8 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libapk.so")
 
-SOURCES = ["sgemm_f32.cu", "sgemm_f32_ws.cu", "gemm_bf16.cu", "visibility.cu", "runtime.cu", "datagen.cpp"]
+SOURCES = ["sgemm_f32.cu", "sgemm_f32_ws.cu", "gemm_bf16.cu", "gemm_bf16_pair.cu", "visibility.cu", "runtime.cu",
+           "datagen.cpp"]
 HEADERS = ["common.cuh", "proto.h", "tcgen05.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

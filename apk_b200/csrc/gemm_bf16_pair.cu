@@ -1,0 +1,781 @@
+// bf16 tensor-core persistent GEMM on CTA pairs (tcgen05.mma.cta_group::2):
+// the default bf16 kernel for a plain background GEMM whose N is a multiple
+// of 256 (the configs[2] shape).  Same job protocol, yields, checkpoints and
+// outputs as gemm_bf16.cu (which keeps task mode, 128-wide edges, K-tile 32
+// and every other shape); replaces the same reference code
+// (src/tcyield.cu:91-356).
+//
+// B200 design:
+//   * A cluster of two CTAs on two SMs computes a 256 x 512 output tile:
+//     two accumulators D_h (C columns [c0 + 256h, +256)), each one M=256,
+//     N=256 cta_group::2 MMA per 16-deep k-step.  CTA r stages A rows
+//     [r0 + 128r, +128) and the B columns [c0 + 256h + 128r, +128) of each
+//     half, and holds in its TMEM the accumulator lanes of its own C
+//     columns.  Per MMA each SM reads 8 KB of shared memory for 2^19 MACs
+//     (the one-CTA kernel: 12 KB), and the pair shares one A row panel:
+//     the ring moves 48 KB per CTA and stage instead of 64 KB.
+//   * The leader (cluster rank 0) decides everything: its producer pops the
+//     queue, polls, pops urgent items, issues its own TMA loads and forwards
+//     each slot's tag to the peer's producer through distributed shared
+//     memory; the peer issues the loads of its halves.  Both CTAs' loads
+//     complete on the leader's full barrier (cta_group::2 TMA).  The
+//     leader's MMA warp issues the pair MMAs, commits to the barriers of both
+//     CTAs and posts every epilogue job to both CTAs' job rings.  Each CTA's
+//     8 epilogue warps drain, store, spill and restore their own TMEM; the
+//     TMEM-free, restore-done and job-slot-free barriers live in the leader
+//     and count 16 arrivals (8 local, 8 remote).  The last of the 16 warps
+//     to finish a tile does its accounting.
+//   * Yield / checkpoint / resume exactly as in the one-CTA kernel: SUSPEND
+//     slot, both CTAs spill their accumulator lanes to their own slabs,
+//     urgent items run through the same ring, RESUME restores and the MMAs
+//     continue with the same sequence -- bitwise identical to an
+//     uninterrupted run.
+//   * No TMA multicast: each CTA loads its own operands.  Every wait is
+//     bounded; every role of both CTAs reaches the final cluster barriers,
+//     where the pair waits for outstanding MMAs and loads before TMEM is
+//     released (cta_group::2 dealloc by both CTAs) and the CTAs exit.
+#include <string>
+
+#include "../../include/apk.h"
+#include "common.cuh"
+#include "proto.h"
+#include "tcgen05.cuh"
+
+namespace apk {
+namespace bf16pair {
+
+constexpr int BM = 256, BN = 512, BK = 64, S = 4;
+constexpr int EPI_WARPS = 8;
+constexpr int CTRL_WARP = 2 + EPI_WARPS;
+constexpr int NT = 32 * (CTRL_WARP + 1);
+constexpr int A_BYTES = 128 * BK * 2;         // this CTA's 128 A rows
+constexpr int B_CHUNK = BK * 64 * 2;          // one [64 k][64 n] box
+constexpr int STAGE_BYTES = A_BYTES + 4 * B_CHUNK;
+constexpr int SMEM_BYTES = S * STAGE_BYTES + 1024;
+constexpr int RING = 8;
+// Peer tag ring.  The leader stores stage P's tag in entry P % T after its
+// wait for stage P-1's slot, i.e. after the MMAs of stage P-1-S completed;
+// those needed the peer's loads of every data stage up to P-1-S, which the
+// peer issues only after reading their tags in order -- so with T > S + 1
+// the peer has read entry P % T's previous tag (P - T) without an explicit
+// acknowledgment (a SUSPEND slot is always followed by urgent data stages).
+// A release-ordered acknowledgment from the peer cost ~1400 cycles a stage
+// and starved the ring.
+constexpr int T = 4 * S;
+constexpr int RASTER_GROUP = 8;
+// D = C_cols^T: MMA A = the B columns (MN-major), MMA B = the A rows (K-major)
+constexpr uint32_t IDESC = tc::idesc_bf16_f32(256, 256, true, false);
+
+enum : int { T_BG = 1, T_URG = 2, T_SUSPEND = 3, T_STOP = 4 };
+enum : int { F_FIRST = 1, F_LAST = 2, F_RESUME = 4, F_WIDE = 8 };
+enum : int { E_STORE_C = 1, E_STORE_U = 2, E_SPILL = 3, E_RESTORE = 4, E_EXIT = 5 };
+
+struct StageTag {
+  int kind, flags, row0, col0, e, item, k, pad;
+  unsigned long long task;
+};
+struct EpiJob {
+  int action, buf, wide, row0, col0, e, item, pad;
+  unsigned long long task;
+};
+
+struct __align__(16) Shared {
+  StageTag tag[S];   // the leader's MMA reads the slot's tag here
+  uint4 ptag[T];     // the peer's copy {kind | flags << 8, row0, col0, k}, stored by the leader
+  EpiJob epi[RING];
+  uint64_t full[S], empty[S], tagfull[T];
+  uint64_t tfull[2], tempty[2], tres[2];
+  uint64_t efull[RING], eempty[RING];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  int gen;
+  int prod_done;
+  int consumed;
+  int epi_cnt[RING];
+  unsigned long long tiles;
+};
+
+__device__ __forceinline__ int vload(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+__device__ __forceinline__ void vstore(int* p, int v) { *reinterpret_cast<volatile int*>(p) = v; }
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of this CTA's variable in CTA `rank`'s shared memory
+__device__ __forceinline__ uint32_t mapa(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_u64(uint32_t addr, unsigned long long v) {
+  asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(addr), "l"(v) : "memory");
+}
+// 16-byte store into the peer's shared memory that completes 16 transaction
+// bytes on the peer's barrier: the leader does not wait for it
+__device__ __forceinline__ void st_async_v4(uint32_t addr, uint4 v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ unsigned atom_add_cluster(uint32_t addr, unsigned v) {
+  unsigned old;
+  asm volatile("atom.shared::cluster.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(addr), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void atom_add_cluster_u64(uint32_t addr, unsigned long long v) {
+  asm volatile("red.shared::cluster.add.u64 [%0], %1;" ::"r"(addr), "l"(v) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMA load into this CTA's shared memory completing on a barrier of either
+// CTA of the pair
+__device__ __forceinline__ void tma_load_pair(void* dst, const CUtensorMap* tm, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(tm), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(acc)
+      : "memory");
+}
+// one arrival on the barrier (either CTA) once this thread's pair MMAs completed
+__device__ __forceinline__ void commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+// Bounded wait on a barrier of this CTA (remote arrivals: cluster-scope
+// acquire); also gives up when another role of this CTA aborted.
+__device__ __forceinline__ bool bwait(uint64_t* bar, uint32_t parity, const F32Params& p, Shared& sh) {
+  if (try_wait_cluster(bar, parity)) return true;
+  const long long t0 = globaltimer_ns();
+  int n = 0;
+  while (true) {
+    if (try_wait_cluster(bar, parity)) return true;
+    if (++n == 64) {
+      n = 0;
+      if (vload(&sh.abort)) return false;
+      if (globaltimer_ns() - t0 > p.wait_limit_ns) {
+        vstore(&sh.abort, 1);
+        report_status(p.ev.status, DEV_WAIT_TIMEOUT_FULL, p.ev.abort_word);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void bwait_unwind(uint64_t* bar, uint32_t parity, long long limit) {
+  const long long t0 = globaltimer_ns();
+  while (!try_wait_cluster(bar, parity))
+    if (globaltimer_ns() - t0 > limit) return;
+}
+
+template <int POLL, int DISC, bool ORACLE>
+__global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ F32Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ Shared sh;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int cta = blockIdx.x;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+    }
+    for (int t = 0; t < T; ++t) mbar_init(&sh.tagfull[t], 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sh.tfull[b], 1);
+      mbar_init(&sh.tempty[b], 2 * EPI_WARPS);
+      mbar_init(&sh.tres[b], 2 * EPI_WARPS);
+    }
+    for (int r = 0; r < RING; ++r) {
+      mbar_init(&sh.efull[r], 1);
+      mbar_init(&sh.eempty[r], 2 * EPI_WARPS);
+      sh.epi_cnt[r] = 0;
+    }
+    mbar_init(&sh.drain, 1);
+    fence_mbar_init();
+    sh.abort = 0;
+    sh.gen = 0;
+    sh.prod_done = 0;
+    sh.consumed = 0;
+    sh.tiles = 0;
+    tma_prefetch_desc(&p.tmA);
+    tma_prefetch_desc(&p.tmB);
+    tma_prefetch_desc(&p.tmAu);
+    tma_prefetch_desc(&p.tmBu);
+    atomicMin(p.q.start_min, (unsigned long long)globaltimer_ns());
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
+                     smem_u32(&sh.tmem_base))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  __syncwarp();
+  cluster_sync();  // both CTAs' barriers initialised before any remote access
+  tc::fence_after_sync();
+
+  if (warp == 0 && lane == 0 && leader) {
+    // ============================ leader producer ============================
+    uint32_t P = 0;
+    int lastSeen = 0;
+    bool ok = true;
+    auto emit = [&](int kind, int flags, int row0, int col0, int e, int item, unsigned long long task,
+                    const CUtensorMap* tA, const CUtensorMap* tB, int k) -> bool {
+      // first the peer's copy of the tag, into its tag ring: the peer then
+      // issues its loads the moment its slot frees, in step with the
+      // leader's own
+      const int ti = P % T;
+      st_async_v4(mapa(&sh.ptag[ti], 1), make_uint4((uint32_t)kind | ((uint32_t)flags << 8), (uint32_t)row0,
+                                                    (uint32_t)col0, (uint32_t)k),
+                  mapa(&sh.tagfull[ti], 1));
+      const int s = P % S;
+      if (!bwait(&sh.empty[s], ((P / S) & 1) ^ 1, p, sh)) return false;
+      StageTag& t = sh.tag[s];
+      t.kind = kind;
+      t.flags = flags;
+      t.row0 = row0;
+      t.col0 = col0;
+      t.e = e;
+      t.item = item;
+      t.k = k;
+      t.task = task;
+      if (tA != nullptr) {
+        const int nb = (flags & F_WIDE) ? 4 : 2;
+        mbar_arrive_expect_tx(&sh.full[s], 2 * (A_BYTES + nb * B_CHUNK));
+        uint8_t* st = stages + s * STAGE_BYTES;
+        const uint32_t fb = mapa(&sh.full[s], 0);
+        tma_load_pair(st, tA, k, row0, fb);
+        for (int b = 0; b < nb; ++b)
+          tma_load_pair(st + A_BYTES + b * B_CHUNK, tB, col0 + 256 * (b >> 1) + 64 * (b & 1), k, fb);
+      } else {
+        mbar_arrive(&sh.full[s]);  // control slot: no data
+      }
+      ++P;
+      return true;
+    };
+    // Observe generation f at a poll site and pop urgent work items (as in
+    // the one-CTA kernel); the observation is logged for both CTAs.
+    auto handle = [&](int f, int site, bool partial) -> int {
+      const int fc = f < p.ev.max_events ? f : p.ev.max_events;
+      const long long g = globaltimer_ns();
+      for (int e = lastSeen; e < fc; ++e) {
+        p.ev.obs_ns[(size_t)e * gridDim.x + cta] = g;
+        p.ev.obs_ns[(size_t)e * gridDim.x + cta + 1] = g;
+      }
+      const int old = lastSeen;
+      lastSeen = f;
+      int n = 0;
+      for (int e = old; e < fc; ++e) {
+        while (true) {
+          const int it = atomicAdd(&p.ev.uq_next[e], 1);
+          if (it >= p.uitems) break;
+          if (it == 0) {
+            p.ev.claim_ns[e] = globaltimer_ns();
+            p.ev.claim[e] = cta + 1;
+            p.ev.claim_site[e] = site;
+            p.ev.inflight[e] = (int)(P - (uint32_t)vload(&sh.consumed));
+            if (p.ev.ack != nullptr) ack_host(&p.ev.ack[2 * e]);
+          }
+          if (n == 0 && partial) {
+            if (!emit(T_SUSPEND, 0, 0, 0, 0, 0, 0, nullptr, nullptr, 0)) return -1;
+            atomicAdd(p.q.yields, 1ull);
+          }
+          ++n;
+          const int t = it / p.usplit, ks = it % p.usplit;
+          const int r0 = (t / p.utiles_n) * BM, c0 = (t % p.utiles_n) * BN;
+          const int wide = c0 + BN <= p.ldcu ? F_WIDE : 0;
+          for (int c = 0; c < p.unk; ++c) {
+            const int kk = (ks * p.unk + c) * BK;
+            if (!emit(T_URG, (c == 0 ? F_FIRST : 0) | (c == p.unk - 1 ? F_LAST : 0) | wide, r0, c0, e, it, 0,
+                      &p.tmAu, &p.tmBu, kk))
+              return -1;
+          }
+        }
+      }
+      return n;
+    };
+
+    unsigned long long next_task = atomicAdd(p.q.next_task, 1ull);
+    while (ok) {
+      const unsigned long long task = next_task;
+      if (task < p.q.num_tasks) next_task = atomicAdd(p.q.next_task, 1ull);
+      int f = vload(&sh.gen);
+      if (f < 0 || vload(&sh.abort)) break;
+      if (POLL != POLL_OFF && f != lastSeen)
+        if (handle(f, -1, false) < 0) {
+          ok = false;
+          break;
+        }
+      if (task >= p.q.num_tasks) break;
+      const int tile = (int)(task % (unsigned long long)p.total_tiles);
+      int tm, tn;
+      if (p.st.order != nullptr)
+        stream_tile(p.st, tile, p.tiles_n, tm, tn);
+      else
+        tile_coords(tile, p.total_tiles / p.tiles_n, p.tiles_n, RASTER_GROUP, tm, tn);
+      const int row0 = tm * BM, col0 = tn * BN;
+      const int wide = col0 + BN <= p.ldc ? F_WIDE : 0;
+      if (p.st.a_ready != nullptr) {
+        // every 128-column B unit of the tile must have landed
+        const int* ar = &p.st.a_ready[tm / p.st.panel_tm];
+        const int u0 = col0 / 128, un = (wide ? 4 : 2);
+        bool rdy = true;
+        for (int u = u0; u < u0 + un && rdy; u += p.st.b_units)
+          rdy = wait_ready2(ar, &p.st.b_ready[u / p.st.b_units], p.wait_limit_ns);
+        if (rdy) rdy = wait_ready2(ar, &p.st.b_ready[(u0 + un - 1) / p.st.b_units], p.wait_limit_ns);
+        if (!rdy) {
+          vstore(&sh.abort, 1);
+          report_status(p.ev.status, DEV_WAIT_TIMEOUT_SPIN, p.ev.abort_word);
+          ok = false;
+          break;
+        }
+      }
+      bool resume = false;
+      for (int c = 0; c < p.nk && ok; ++c) {
+        if (POLL == POLL_STAGE) {
+          const int fs = vload(&sh.gen);
+          if (fs < 0) {
+            ok = false;
+            break;
+          }
+          if (fs != lastSeen) {
+            const int n = handle(fs, c, c > 0);
+            if (n < 0) {
+              ok = false;
+              break;
+            }
+            if (n > 0 && c > 0) resume = true;
+          }
+        }
+        const int flags = (c == 0 ? F_FIRST : 0) | (c == p.nk - 1 ? F_LAST : 0) | (resume ? F_RESUME : 0) | wide;
+        resume = false;
+        if (!emit(T_BG, flags, row0, col0, 0, 0, task, &p.tmA, &p.tmB, c * BK)) ok = false;
+      }
+    }
+    emit(T_STOP, 0, 0, 0, 0, 0, 0, nullptr, nullptr, 0);
+    vstore(&sh.prod_done, 1);
+    // loads still in flight (only when unwinding) land before teardown
+    for (uint32_t q = (uint32_t)vload(&sh.consumed); q < P; ++q)
+      bwait_unwind(&sh.full[q % S], (q / S) & 1, p.wait_limit_ns);
+  } else if (warp == 0 && lane == 0) {
+    // ============================= peer producer =============================
+    // Follows the leader's tags; loads a slot's halves once the pair MMAs
+    // that read the slot's previous use have completed (its empty barrier,
+    // committed by the leader's MMA warp).
+    uint32_t P = 0;
+    const uint32_t rowoff = 128;
+    while (true) {
+      const int ti = P % T, s = P % S;
+      // this entry's phase: our arrival plus the leader's 16-byte store
+      mbar_arrive_expect_tx(&sh.tagfull[ti], 16);
+      if (!bwait(&sh.tagfull[ti], (P / T) & 1, p, sh)) break;
+      const uint4 w = sh.ptag[ti];
+      StageTag t;
+      t.kind = (int)(w.x & 0xFF);
+      t.flags = (int)(w.x >> 8);
+      t.row0 = (int)w.y;
+      t.col0 = (int)w.z;
+      t.k = (int)w.w;
+      if (t.kind == T_STOP) break;
+      if (t.kind == T_BG || t.kind == T_URG) {
+        if (!bwait(&sh.empty[s], ((P / S) & 1) ^ 1, p, sh)) break;
+        const CUtensorMap* tA = t.kind == T_BG ? &p.tmA : &p.tmAu;
+        const CUtensorMap* tB = t.kind == T_BG ? &p.tmB : &p.tmBu;
+        if (t.kind == T_BG && (t.flags & F_FIRST) && p.st.a_ready != nullptr) {
+          // the leader saw the panels land; order this CTA's loads after it
+          const int u0 = t.col0 / 128;
+          if (!wait_ready2(&p.st.a_ready[(t.row0 / BM) / p.st.panel_tm],
+                           &p.st.b_ready[(u0 + ((t.flags & F_WIDE) ? 3 : 1)) / p.st.b_units], p.wait_limit_ns))
+            break;
+        }
+        const int nb = (t.flags & F_WIDE) ? 4 : 2;
+        uint8_t* st = stages + s * STAGE_BYTES;
+        const uint32_t fb = mapa(&sh.full[s], 0);
+        tma_load_pair(st, tA, t.k, t.row0 + rowoff, fb);
+        for (int b = 0; b < nb; ++b)
+          tma_load_pair(st + A_BYTES + b * B_CHUNK, tB, t.col0 + 256 * (b >> 1) + 128 + 64 * (b & 1), t.k, fb);
+      }
+      ++P;
+    }
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ================================== MMA ===================================
+    uint32_t Q = 0, X = 0, ub[2] = {0, 0}, rb[2] = {0, 0};
+    int nb = 0, cur = 0, cwide = 0;
+    const uint32_t tbase = sh.tmem_base;
+    auto post = [&](int action, int buf, int wide, const StageTag& t) -> bool {
+      const int sl = X % RING;
+      if (!bwait(&sh.eempty[sl], ((X / RING) & 1) ^ 1, p, sh)) return false;
+      EpiJob& j = sh.epi[sl];
+      j.action = action;
+      j.buf = buf;
+      j.wide = wide;
+      j.row0 = t.row0;
+      j.col0 = t.col0;
+      j.e = t.e;
+      j.item = t.item;
+      j.task = t.task;
+      const uint32_t pj = mapa(&j, 1);
+      st_cluster_u32(pj + offsetof(EpiJob, action), (uint32_t)action);
+      st_cluster_u32(pj + offsetof(EpiJob, buf), (uint32_t)buf);
+      st_cluster_u32(pj + offsetof(EpiJob, wide), (uint32_t)wide);
+      st_cluster_u32(pj + offsetof(EpiJob, row0), (uint32_t)t.row0);
+      st_cluster_u32(pj + offsetof(EpiJob, col0), (uint32_t)t.col0);
+      st_cluster_u32(pj + offsetof(EpiJob, e), (uint32_t)t.e);
+      st_cluster_u32(pj + offsetof(EpiJob, item), (uint32_t)t.item);
+      st_cluster_u64(pj + offsetof(EpiJob, task), t.task);
+      mbar_arrive(&sh.efull[sl]);
+      arrive_cluster(mapa(&sh.efull[sl], 1));
+      ++X;
+      return true;
+    };
+    while (true) {
+      const int s = Q % S;
+      if (!bwait(&sh.full[s], (Q / S) & 1, p, sh)) break;
+      const StageTag t = sh.tag[s];
+      if (t.kind == T_STOP) {
+        post(E_EXIT, 0, 0, t);
+        break;
+      }
+      if (t.kind == T_SUSPEND) {
+        if (!post(E_SPILL, cur, cwide, t)) break;
+        commit_pair(mapa(&sh.tfull[cur], 0));
+        commit_pair(mapa(&sh.tfull[cur], 1));
+        mbar_arrive(&sh.empty[s]);
+        arrive_cluster(mapa(&sh.empty[s], 1));  // every use of a slot completes a phase in both CTAs
+        ++Q;
+        vstore(&sh.consumed, (int)Q);
+        continue;
+      }
+      if (t.flags & (F_FIRST | F_RESUME)) {
+        cwide = (t.flags & F_WIDE) ? 1 : 0;
+        cur = cwide ? 0 : nb;
+        nb = cwide ? 0 : nb ^ 1;
+        bool ok = true;
+        for (int b = cur; b <= (cwide ? 1 : cur) && ok; ++b) {
+          ok = bwait(&sh.tempty[b], (ub[b] & 1) ^ 1, p, sh);
+          ++ub[b];
+        }
+        if (!ok) break;
+        tc::fence_after_sync();
+        if (t.flags & F_RESUME) {
+          if (!post(E_RESTORE, cur, cwide, t)) break;
+          if (!bwait(&sh.tres[cur], rb[cur] & 1, p, sh)) break;
+          ++rb[cur];
+          tc::fence_after_sync();
+        }
+      }
+      uint8_t* st = stages + s * STAGE_BYTES;
+      if (DISC == DISC_POISON && t.kind == T_URG && (t.flags & F_FIRST)) {
+        // detector control: one wrong staged B value (8.0) in each urgent item
+        reinterpret_cast<uint16_t*>(st + A_BYTES)[0] = 0x4100;
+        fence_proxy_async_smem();
+      }
+      const uint32_t sa = smem_u32(st), sb = smem_u32(st + A_BYTES);
+      const uint32_t d0 = tbase + (uint32_t)cur * 256;
+#pragma unroll
+      for (int kk = 0; kk < BK / 16; ++kk) {
+        const uint32_t acc = (kk > 0 || !(t.flags & F_FIRST)) ? 1u : 0u;
+        const uint64_t bdesc = tc::smem_desc(sa + kk * 32, 16, 1024, tc::LAYOUT_SW128);
+        mma_pair(d0, tc::smem_desc(sb + kk * 2048, B_CHUNK, 1024, tc::LAYOUT_SW128), bdesc, acc);
+        if (cwide)
+          mma_pair(d0 + 256, tc::smem_desc(sb + 2 * B_CHUNK + kk * 2048, B_CHUNK, 1024, tc::LAYOUT_SW128), bdesc,
+                   acc);
+      }
+      commit_pair(mapa(&sh.empty[s], 0));  // frees the slot (both CTAs' halves) once read
+      commit_pair(mapa(&sh.empty[s], 1));
+      if (t.flags & F_LAST) {
+        if (!post(t.kind == T_BG ? E_STORE_C : E_STORE_U, cur, cwide, t)) break;
+        commit_pair(mapa(&sh.tfull[cur], 0));
+        commit_pair(mapa(&sh.tfull[cur], 1));
+      }
+      ++Q;
+      vstore(&sh.consumed, (int)Q);
+    }
+    commit_pair(mapa(&sh.drain, 0));
+    bwait_unwind(&sh.drain, 0, p.wait_limit_ns);
+  } else if (warp >= 2 && warp < CTRL_WARP) {
+    // =============================== epilogue ================================
+    const int q = warp & 3;
+    const int g = (warp - 2) >> 2;
+    uint32_t Y = 0, eb[2] = {0, 0};
+    const uint32_t tbase = sh.tmem_base;
+    float* slab = p.slab + (size_t)cta * (256 * 256);
+    // the leader's barriers and counters (this CTA's own when it leads)
+    const uint32_t L_tempty0 = mapa(&sh.tempty[0], 0), L_tempty1 = mapa(&sh.tempty[1], 0);
+    while (true) {
+      const int sl = Y % RING;
+      if (!bwait(&sh.efull[sl], (Y / RING) & 1, p, sh)) break;
+      const EpiJob j = sh.epi[sl];
+      const uint32_t L_eempty = mapa(&sh.eempty[sl], 0);
+      if (j.action == E_EXIT) {
+        __syncwarp();
+        if (lane == 0) arrive_cluster(L_eempty);
+        break;
+      }
+      // TMEM lane = this CTA's C column 128*rank + 32q + lane of each 256-wide
+      // half, column = C row
+      const uint32_t tcol = tbase + ((uint32_t)(32 * q) << 16) + (uint32_t)j.buf * 256;
+      const int nh = j.wide ? 2 : 1;
+      auto slab_blk = [&](int hh, int blk) { return slab + (size_t)((hh * 8 + blk) * 4 + q) * 1024; };
+      if (j.action == E_RESTORE) {
+        const long long r0 = globaltimer_ns();
+#pragma unroll 1
+        for (int bb = g; bb < 8 * nh; bb += 2) {
+          const int hh = bb >> 3, blk = bb & 7;
+          const float4* s4 = reinterpret_cast<const float4*>(slab_blk(hh, blk));
+          uint32_t v[32];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 x = s4[i * 32 + lane];
+            v[4 * i] = __float_as_uint(x.x);
+            v[4 * i + 1] = __float_as_uint(x.y);
+            v[4 * i + 2] = __float_as_uint(x.z);
+            v[4 * i + 3] = __float_as_uint(x.w);
+          }
+          tc::st_32x32b_x32(tcol + hh * 256 + blk * 32, v);
+        }
+        tc::wait_st();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) {
+          arrive_cluster(mapa(&sh.tres[j.buf], 0));
+          if (p.q.ckpt != nullptr) {
+            atomicAdd(&p.q.ckpt[2], (unsigned long long)(globaltimer_ns() - r0));
+            atomicAdd(&p.q.ckpt[3], (unsigned long long)nh * 4 * 4096);
+          }
+        }
+      } else {
+        if (!bwait(&sh.tfull[j.buf], eb[j.buf] & 1, p, sh)) break;
+        ++eb[j.buf];
+        tc::fence_after_sync();
+        const long long s0 = globaltimer_ns();
+        const int lim = 8 * nh;
+        auto tload = [&](int bb, uint32_t(&v)[32]) { tc::ld_32x32b_x32(tcol + (bb >> 3) * 256 + (bb & 7) * 32, v); };
+        auto consume = [&](int bb, const uint32_t(&v)[32]) {
+          const int hh = bb >> 3, blk = bb & 7;
+          if (j.action == E_SPILL) {
+            float4* s4 = reinterpret_cast<float4*>(slab_blk(hh, blk));
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              s4[i * 32 + lane] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                              __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+            return;
+          }
+          const int col = j.col0 + 256 * hh + 128 * (int)rank + 32 * q + lane;
+          if (j.action == E_STORE_C) {
+            float* dst = p.C + (size_t)(j.row0 + blk * 32) * p.ldc + col;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) dst[(size_t)i * p.ldc] = __uint_as_float(v[i]);
+          } else {
+            float* dst = p.Cu + (size_t)j.e * p.cu_stride + (size_t)(j.row0 + blk * 32) * p.ldcu + col;
+            if (p.usplit == 1) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) dst[(size_t)i * p.ldcu] = __uint_as_float(v[i]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) atomicAdd(dst + (size_t)i * p.ldcu, __uint_as_float(v[i]));
+            }
+          }
+        };
+        auto release = [&]() {
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) {
+            arrive_cluster(j.buf == 0 ? L_tempty0 : L_tempty1);
+            if (j.wide) arrive_cluster(L_tempty1);
+            if (j.action == E_SPILL && p.q.ckpt != nullptr) {
+              atomicAdd(&p.q.ckpt[0], (unsigned long long)(globaltimer_ns() - s0));
+              atomicAdd(&p.q.ckpt[1], (unsigned long long)nh * 4 * 4096);
+            }
+          }
+        };
+        uint32_t va[32], vb[32];
+        int cur = g;
+        tload(cur, va);
+        while (cur < lim) {
+          tc::wait_ld();
+          int nxt = cur + 2;
+          if (nxt < lim) tload(nxt, vb); else release();
+          consume(cur, va);
+          cur = nxt;
+          if (cur >= lim) break;
+          tc::wait_ld();
+          nxt = cur + 2;
+          if (nxt < lim) tload(nxt, va); else release();
+          consume(cur, vb);
+          cur = nxt;
+        }
+        if (j.action != E_SPILL) {
+          // the job's stores are visible before it is counted; the last of
+          // the pair's 16 epilogue warps does the accounting
+          __threadfence();
+          __syncwarp();
+          if (lane == 0 && atom_add_cluster(mapa(&sh.epi_cnt[sl], 0), 1u) == 2 * EPI_WARPS - 1) {
+            st_cluster_u32(mapa(&sh.epi_cnt[sl], 0), 0u);
+            if (j.action == E_STORE_C) {
+              atom_add_cluster_u64(mapa(&sh.tiles, 0), 1ull);
+              if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[j.task], 1);
+              if (p.st.done != nullptr)
+                stream_tile_done(p.st, p.total_tiles / p.tiles_n, p.tiles_n, j.row0 / BM, j.col0 / BN);
+              count_trigger(p.ev);
+            } else {
+              if (ORACLE) atomicAdd(&p.ev.uexec[j.e], 1);
+              atomicMax(&p.ev.done_ns[j.e], (unsigned long long)globaltimer_ns());
+              const int done = atomicAdd(&p.ev.udone_cnt[j.e], 1) + 1;
+              if (done == p.uitems && p.ev.ack != nullptr) ack_host(&p.ev.ack[2 * j.e + 1]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) arrive_cluster(L_eempty);
+      ++Y;
+    }
+  } else if (warp == CTRL_WARP && lane == 0 && leader) {
+    // ================================ control =================================
+    int nextEv = 0;
+    long long gBase = 0;
+    while (!vload(&sh.prod_done) && !vload(&sh.abort)) {
+      int f = POLL != POLL_OFF ? flag_load(p.ev.flag) : 0;
+      if (*reinterpret_cast<volatile int*>(p.ev.abort_word)) f = -1;
+      if (cta == 0 && p.ev.sched_ns != nullptr && nextEv < p.ev.n_sched) {
+        const long long now = globaltimer_ns();
+        if (gBase == 0) gBase = now;
+        if (now >= gBase + p.ev.sched_ns[nextEv]) {
+          p.ev.set_ns[nextEv] = now;
+          atomicCAS(p.ev.flag, nextEv, nextEv + 1);
+          ++nextEv;
+        }
+      }
+      vstore(&sh.gen, f);
+      __nanosleep(64);
+    }
+  }
+
+  // Teardown: every role of both CTAs is done (MMAs drained by the leader,
+  // loads landed); the pair meets, releases TMEM together, and meets again
+  // so that no remote access reaches a CTA that has exited.
+  tc::fence_before_sync();
+  __syncthreads();
+  __syncwarp();
+  cluster_sync();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, 512;" ::"r"(sh.tmem_base) : "memory");
+  }
+  __syncthreads();
+  __syncwarp();
+  cluster_sync();
+  if (tid == 0) {
+    p.q.tiles_done[cta] = leader ? sh.tiles : 0ull;
+    atomicMax(p.q.end_max, (unsigned long long)globaltimer_ns());
+    atomicAdd(p.q.exited, 1);
+  }
+}
+
+// ---------------------------------------------------------------------------
+
+template <int POLL, int DISC, bool ORACLE>
+static const void* kernel_ptr() {
+  return reinterpret_cast<const void*>(&gemm_bf16_pair<POLL, DISC, ORACLE>);
+}
+
+static const void* select_kernel(int poll, int disc, bool oracle) {
+#define APK_SEL(PL, DS, OR) \
+  if (poll == PL && disc == DS && oracle == OR) return kernel_ptr<PL, DS, OR>();
+  APK_SEL(POLL_OFF, DISC_DRAIN, false)
+  APK_SEL(POLL_OFF, DISC_DRAIN, true)
+  APK_SEL(POLL_BOUNDARY, DISC_DRAIN, false)
+  APK_SEL(POLL_BOUNDARY, DISC_DRAIN, true)
+  APK_SEL(POLL_STAGE, DISC_DRAIN, false)
+  APK_SEL(POLL_STAGE, DISC_DRAIN, true)
+  APK_SEL(POLL_STAGE, DISC_POISON, false)
+  APK_SEL(POLL_STAGE, DISC_POISON, true)
+#undef APK_SEL
+  return nullptr;
+}
+
+int smem_bytes() { return SMEM_BYTES; }
+int stages() { return S; }
+int threads() { return NT; }
+int epi_warps() { return EPI_WARPS; }
+size_t params_bytes() { return sizeof(F32Params); }
+
+// *pairs = clusters of two that can be resident at once (0: the kernel does
+// not run here).
+cudaError_t prepare(int poll, int disc, bool oracle, int sms, int* pairs) {
+  *pairs = 0;
+  const void* k = select_kernel(poll, disc, oracle);
+  if (!k) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(sms - (sms & 1));
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaOccupancyMaxActiveClusters(pairs, k, &cfg);
+}
+
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, cudaStream_t stream) {
+  const void* k = select_kernel(poll, disc, oracle);
+  if (!k || grid % 2) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = stream;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  void* args[] = {const_cast<F32Params*>(&prm)};
+  return cudaLaunchKernelExC(&cfg, k, args);
+}
+
+}  // namespace bf16pair
+}  // namespace apk

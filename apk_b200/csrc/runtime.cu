@@ -31,6 +31,15 @@ int stages(int bk);
 int threads();
 size_t params_bytes();
 }  // namespace f32
+namespace bf16pair {
+cudaError_t prepare(int poll, int disc, bool oracle, int sms, int* pairs);
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, cudaStream_t stream);
+int smem_bytes();
+int stages();
+int threads();
+int epi_warps();
+size_t params_bytes();
+}  // namespace bf16pair
 namespace f32ws {
 cudaError_t prepare(int poll, int disc, bool oracle, int* ok);
 cudaError_t launch(const F32Params& prm, int workers, int poll, int disc, bool oracle, cudaStream_t stream);
@@ -117,6 +126,9 @@ struct apk_ctx {
   // block-synchronous kernel for experiments that compare grids slot by slot
   bool ws_ok = false;
   bool sync_only = false;
+  // bf16: the CTA-pair kernel can run every poll variant this context
+  // launches with every SM in a pair
+  bool pair_ok = false;
   int cc_major = 0, cc_minor = 0;
   char name[128] = {0};
   cudaStream_t kstream = nullptr, cstream = nullptr, ustream = nullptr;
@@ -254,8 +266,9 @@ size_t esize_of(apk_dtype d) { return d == APK_BF16 ? 2 : 4; }
 
 // Output tiles: fp32 128x128; bf16 256 rows by 256 columns, the last tile of
 // a row 128 wide when the width is an odd multiple of 128.
+bool use_pair(const apk_ctx* ctx);
 int tile_rows(const apk_ctx* ctx) { return ctx->cfg.dtype == APK_F32 ? 128 : 256; }
-int tile_cols(const apk_ctx* ctx) { return ctx->cfg.dtype == APK_F32 ? 128 : 256; }
+int tile_cols(const apk_ctx* ctx) { return ctx->cfg.dtype == APK_F32 ? 128 : use_pair(ctx) ? 512 : 256; }
 int tiles_across(const apk_ctx* ctx, int n) { return (n + tile_cols(ctx) - 1) / tile_cols(ctx); }
 
 apk_status upload(apk_ctx* ctx, void** dst, bool* own, size_t* cap, const void* src, size_t bytes,
@@ -299,7 +312,22 @@ apk_status prepare_kernel(apk_ctx* ctx, int poll) {
     if (e != cudaSuccess) ok = 0;
     ctx->ws_ok = ctx->ws_ok && ok;
   }
+  if (ctx->cfg.dtype == APK_BF16 && ctx->cfg.k_tile == 64) {
+    int pairs = 0;
+    e = bf16pair::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->sms, &pairs);
+    if (e != cudaSuccess) pairs = 0;
+    ctx->pair_ok = ctx->pair_ok && ctx->sms % 2 == 0 && 2 * pairs >= ctx->sms;
+  }
   return APK_OK;
+}
+
+// The bf16 launch runs the CTA-pair kernel for a plain background GEMM
+// (no task list) whose N and urgent N are multiples of 256, K-tile 64, one
+// CTA per SM over every SM; the one-CTA kernel runs everything else.
+bool use_pair(const apk_ctx* ctx) {
+  return ctx->cfg.dtype == APK_BF16 && ctx->pair_ok && ctx->cfg.bf16_kernel != APK_BF16_SINGLE &&
+         !ctx->task_mode && ctx->cfg.k_tile == 64 && ctx->grid == ctx->sms && ctx->N % 256 == 0 &&
+         ctx->Nu % 256 == 0;
 }
 
 // The fp32 launch runs the warp-specialized kernel (one 384-thread CTA per
@@ -346,7 +374,7 @@ apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
   // every translation unit must agree on the kernel parameter block (objects
   // compiled against different copies of proto.h would read garbage pointers)
   if (f32::params_bytes() != sizeof(F32Params) || bf16::params_bytes() != sizeof(F32Params) ||
-      f32ws::params_bytes() != sizeof(F32Params)) {
+      f32ws::params_bytes() != sizeof(F32Params) || bf16pair::params_bytes() != sizeof(F32Params)) {
     fail(ctx, APK_EUNSUPPORTED, "kernel parameter layout mismatch (f32 %zu, bf16 %zu, runtime %zu bytes): rebuild",
          f32::params_bytes(), bf16::params_bytes(), sizeof(F32Params));
     *out = ctx;
@@ -388,6 +416,7 @@ apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
     return fail(ctx, APK_EUNSUPPORTED, "device %s is sm_%d%d; this build targets sm_100a", prop.name,
                 prop.major, prop.minor);
   ctx->ws_ok = c.dtype == APK_F32;  // cleared by any variant the warp-specialized kernel lacks
+  ctx->pair_ok = c.dtype == APK_BF16;  // likewise for the CTA-pair kernel
   apk_status s = prepare_kernel(ctx, kernel_poll(ctx));
   if (s != APK_OK) return s;
   // the POLL_OFF variant is used by the overhead and baseline modes
@@ -399,6 +428,10 @@ apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
   }
   ctx->ctas_per_sm = c.ctas_per_sm > 0 ? std::min(c.ctas_per_sm, ctx->max_ctas_per_sm) : ctx->max_ctas_per_sm;
   ctx->grid = c.grid > 0 ? c.grid : ctx->sms * ctx->ctas_per_sm;
+  if (c.dtype == APK_BF16 && c.bf16_kernel == APK_BF16_PAIR && !use_pair(ctx))
+    return fail(ctx, APK_EUNSUPPORTED,
+                "the CTA-pair bf16 kernel needs K-tile 64, one CTA on each of an even number of SMs and "
+                "every SM in a co-resident pair (grid %d, %d SMs)", ctx->grid, ctx->sms);
   if (c.dtype == APK_F32 && c.f32_kernel == APK_F32_WARP_SPECIALIZED && !use_ws(ctx))
     return fail(ctx, APK_EUNSUPPORTED,
                 "the warp-specialized fp32 kernel needs the queue scheduler, K-tile 32 and two workers per SM "
@@ -540,6 +573,12 @@ apk_status apk_get_info(apk_ctx* ctx, apk_device_info* info) {
     info->tile_m = 128;
     info->tile_n = 128;
     info->stages = f32::stages(ctx->cfg.k_tile);
+  } else if (use_pair(ctx)) {
+    info->smem_per_cta = bf16pair::smem_bytes();
+    info->threads_per_cta = bf16pair::threads();
+    info->tile_m = 256;
+    info->tile_n = 512;  // one tile per CTA pair
+    info->stages = bf16pair::stages();
   } else {
     info->smem_per_cta = bf16::smem_bytes(ctx->cfg.k_tile);
     info->threads_per_cta = bf16::threads();
@@ -928,6 +967,8 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
   else if (f32)
     e = f32::launch(p, ctx->cfg.scheduler == APK_SCHED_CLC ? (int)num_tasks : ctx->grid, poll,
                     ctx->cfg.discipline, ctx->cfg.oracle != 0, bk, ctx->cfg.scheduler, stream);
+  else if (use_pair(ctx))
+    e = bf16pair::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, stream);
   else
     e = bf16::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, bk, stream);
   if (e != cudaSuccess) return fail(ctx, APK_ECUDA, "kernel launch failed: %s", cudaGetErrorString(e));
@@ -1312,8 +1353,11 @@ apk_status apk_read_run_stats(apk_ctx* ctx, apk_run_stats* st) {
     // side: their summed time / warps is the CTA's wall time
     st->ckpt_spill_bytes = cb.ckpt[1];
     st->ckpt_restore_bytes = cb.ckpt[3];
-    st->ckpt_spill_ns = (long long)(cb.ckpt[0] / (unsigned long long)bf16::epi_warps());
-    st->ckpt_restore_ns = (long long)(cb.ckpt[2] / (unsigned long long)bf16::epi_warps());
+    // (the pair kernel: 16 warps over two CTAs spill side by side; bytes
+    // cover the pair)
+    const unsigned long long w = use_pair(ctx) ? 2ull * bf16pair::epi_warps() : (unsigned long long)bf16::epi_warps();
+    st->ckpt_spill_ns = (long long)(cb.ckpt[0] / w);
+    st->ckpt_restore_ns = (long long)(cb.ckpt[2] / w);
   }
   if (ctx->task_mode) {
     // tiles differ in size: a complete drain did every task's 2*m*n*k; a

@@ -22,6 +22,7 @@ _SET = {"device": L.APK_SET_DEVICE, "host_mapped": L.APK_SET_HOST_MAPPED,
 _DTYPE = {"f32": L.APK_F32, "bf16": L.APK_BF16}
 _SCHED = {"queue": L.APK_SCHED_QUEUE, "clc": L.APK_SCHED_CLC}
 _F32K = {"auto": 0, "ws": 1, "sync": 2}
+_BF16K = {"auto": 0, "pair": 1, "single": 2}
 
 
 class ApkError(RuntimeError):
@@ -107,7 +108,7 @@ class Context:
                  k_tile: int = 0, poll: str = "stage", discipline: str = "drain",
                  set_mode: str = "host_memcpy", max_events: int = 4096, oracle: bool = False,
                  urgent_split_k: int = 8, wait_limit_ns: int = 2_000_000_000, scheduler: str = "queue",
-                 f32_kernel: str = "auto"):
+                 f32_kernel: str = "auto", bf16_kernel: str = "auto"):
         self._lib = L.load()
         cfg = L.Config()
         self._lib.apk_config_default(ctypes.byref(cfg))
@@ -117,6 +118,7 @@ class Context:
         cfg.urgent_split_k, cfg.wait_limit_ns = urgent_split_k, int(wait_limit_ns)
         cfg.scheduler = _SCHED[scheduler]
         cfg.f32_kernel = _F32K[f32_kernel]
+        cfg.bf16_kernel = _BF16K[bf16_kernel]
         self.cfg = cfg
         self.dtype = dtype
         h = ctypes.c_void_p()

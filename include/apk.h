@@ -95,6 +95,18 @@ typedef enum apk_f32_kernel {
   APK_F32_BLOCK_SYNC = 2
 } apk_f32_kernel;
 
+/* bf16 kernel.  PAIR: clusters of two CTAs compute 256x512 output tiles
+ * with cta_group::2 MMAs (each CTA stages half the operands and holds half
+ * the accumulators); it serves a plain background GEMM (no task list) with
+ * N and the urgent N multiples of 256, K-tile 64, one CTA per SM.  SINGLE:
+ * one CTA per 256x256 tile; serves every shape, task mode and K-tile 32.
+ * AUTO picks PAIR where it applies.  info.tile_n reports 512 for PAIR. */
+typedef enum apk_bf16_kernel {
+  APK_BF16_AUTO = 0,
+  APK_BF16_PAIR = 1,
+  APK_BF16_SINGLE = 2
+} apk_bf16_kernel;
+
 typedef struct apk_config {
   int device;
   apk_dtype dtype;
@@ -111,6 +123,7 @@ typedef struct apk_config {
   long long wait_limit_ns;  /* bound on every device-side wait                */
   apk_scheduler scheduler;  /* (ABI 2) background work distribution           */
   apk_f32_kernel f32_kernel;/* (ABI 3) fp32 kernel choice                       */
+  apk_bf16_kernel bf16_kernel;/* (ABI 3) bf16 kernel choice                     */
 } apk_config;
 
 /* Fill *cfg with the defaults (fp32, full residency, default k_tile, stage

@@ -32,6 +32,23 @@ def _check_rows(C, A, B, rows):
         assert nans == 0 and bad == 0, f"rows {r0}+{n}: {bad} bad, {nans} NaN, max rel {mr:.3e}"
 
 
+@pytest.mark.parametrize("shape", [(256, 512, 64), (512, 768, 256), (1024, 2048, 512)])
+def test_pair_kernel_bitwise_equal_to_single(libapk, shape):
+    """The CTA-pair kernel (256x512 tiles over two SMs, cta_group::2 MMAs)
+    and the one-CTA kernel issue the same MMA sequence per accumulator: C
+    bitwise equal, and within tolerance of float64 over the rounded inputs.
+    N = 768 ends each tile row with a 256-wide pair tile (one accumulator)."""
+    M, N, K = shape
+    A, B = _normal((M, K), 21), _normal((K, N), 22)
+    out = {}
+    for k in ("pair", "single"):
+        with _ctx(poll="stage", oracle=True, bf16_kernel=k) as c:
+            out[k] = c.gemm(A, B)
+            assert c.info["tile_n"] == (512 if k == "pair" else 256)
+    assert np.array_equal(out["pair"].view(np.uint32), out["single"].view(np.uint32))
+    _check_rows(out["pair"], A, B, [(0, min(M, 32)), (M - 32, 32)])
+
+
 @pytest.mark.parametrize("shape", [(256, 128, 64), (256, 256, 320), (512, 384, 1024), (1024, 2048, 512)])
 def test_small_shapes_full_check(libapk, shape):
     M, N, K = shape
@@ -82,7 +99,8 @@ def _yield_run(poll, nev=30, gap_ns=20_000, discipline="drain"):
         info = c.info
         uitems = (256 // info["tile_m"]) * (-(-256 // info["tile_n"])) * c.cfg.urgent_split_k
     refu = oracle.gemm_f64_bf16_rows(Au, Bu, 0, 256)
-    return dict(C=C, Cref=Cref, ev=ev, st=st, ex=ex, ue=ue, fired=fired, outs=outs, refu=refu, uitems=uitems)
+    return dict(C=C, Cref=Cref, ev=ev, st=st, ex=ex, ue=ue, fired=fired, outs=outs, refu=refu, uitems=uitems,
+                tile_n=info["tile_n"])
 
 
 def test_stage_checkpoint_resume_is_bitwise(libapk):
@@ -97,10 +115,11 @@ def test_stage_checkpoint_resume_is_bitwise(libapk):
     assert any(s > 0 for s in sites), "no mid-pipeline claim"
     assert any(ev["inflight"][e] > 0 for e in range(r["fired"])), "no buffer-conflicting yield"
     assert np.array_equal(r["C"].view(np.uint32), r["Cref"].view(np.uint32)), "resume not bitwise"
-    # every checkpoint spills one wide 256x256 fp32 accumulator and the
-    # drain restores each of them
+    # every checkpoint spills one wide 256x256 fp32 accumulator per CTA
+    # (two CTAs for a 256x512 pair tile) and the drain restores each of them
     st = r["st"]
-    assert st["ckpt_spill_bytes"] == st["yields"] * 256 * 256 * 4
+    ctas = r["tile_n"] // 256
+    assert st["ckpt_spill_bytes"] == st["yields"] * 256 * 256 * 4 * ctas
     assert st["ckpt_restore_bytes"] == st["ckpt_spill_bytes"]
     assert st["ckpt_spill_ns"] > 0 and st["ckpt_restore_ns"] > 0
     for Cu in r["outs"]:
