@@ -1,7 +1,7 @@
 """One bounded drain of the persistent kernel, repeated, for profilers.
 
     python -m apk_b200.prof f32  [--n 4096] [--poll stage] [--reps 2] [--kernel auto|ws|sync]
-    python -m apk_b200.prof bf16 [--n 6144] [--poll stage] [--reps 3]
+    python -m apk_b200.prof bf16 [--n 6144] [--poll stage] [--reps 3] [--bf16-kernel auto|pair|single]
 
 Each repetition drains every tile of an n^3 background GEMM once (fp32:
 uniform[-1,1] operands from the reference generator, seed 21; bf16: N(0,1)
@@ -24,6 +24,8 @@ def main():
     ap.add_argument("--reps", type=int, default=0)
     ap.add_argument("--kernel", default="auto", choices=("auto", "ws", "sync"),
                     help="fp32: warp-specialized or block-synchronous kernel")
+    ap.add_argument("--bf16-kernel", default="auto", choices=("auto", "pair", "single"),
+                    help="bf16: CTA-pair or one-CTA kernel")
     args = ap.parse_args()
 
     import apk_b200
@@ -39,7 +41,8 @@ def main():
     else:
         A, B = apk_b200.fill_uniform(n, n, n, 21)
         Au, Bu = apk_b200.fill_uniform(256, 256, 256, 99)
-    with apk_b200.Context(dtype=args.dtype, poll=args.poll, urgent_split_k=1, f32_kernel=args.kernel) as c:
+    with apk_b200.Context(dtype=args.dtype, poll=args.poll, urgent_split_k=1, f32_kernel=args.kernel,
+                          bf16_kernel=args.bf16_kernel) as c:
         c.set_background(A, B)
         c.set_urgent(Au, Bu)
         info = c.info
