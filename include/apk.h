@@ -147,9 +147,12 @@ typedef struct apk_device_info {
   int cc_major, cc_minor;
   int smem_per_cta;
   int threads_per_cta;
-  int tile_m, tile_n, k_tile, stages; /* output tile: fp32 128x128; bf16 256x256
-                                         (the last tile of a row 128 wide when
-                                         N is an odd multiple of 128)          */
+  int tile_m, tile_n, k_tile, stages; /* output tile (the unit of the queue and
+                                         of the grid's per-CTA accounting):
+                                         fp32 128x128; bf16 256x256 (the last
+                                         tile of a row 128 wide when N is an
+                                         odd multiple of 128), or 256x512 per
+                                         CTA pair with the CTA-pair kernel    */
   char name[128];
 } apk_device_info;
 apk_status apk_get_info(apk_ctx* ctx, apk_device_info* info);
