@@ -141,7 +141,8 @@ const char* apk_last_error(const apk_ctx* ctx);
 
 typedef struct apk_device_info {
   int sms;
-  int grid;                 /* CTAs of the persistent kernel                  */
+  int grid;                 /* CTAs of the persistent kernel (warp-specialized
+                               fp32: workers, two per 384-thread CTA)         */
   int ctas_per_sm;          /* resident CTAs per SM actually used             */
   int max_ctas_per_sm;      /* occupancy limit of the selected kernel         */
   int cc_major, cc_minor;
