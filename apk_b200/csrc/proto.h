@@ -80,6 +80,15 @@ struct StreamProto {
   const unsigned* order;  // [tiles] visit order as tm * tiles_n + tn (nullptr = grouped raster)
   unsigned* done;         // [n_panels * n_cb] finished tiles per C block
   int* ack;               // mapped host memory [n_panels * n_cb]: C block complete
+  // K slices (warp-specialized fp32 kernel only; 0 or 1 = whole K).  With
+  // ksplit = 2 the operands move as K halves: ready flags are indexed
+  // panel * ksplit + slice, order[] entries are (tile * ksplit + slice), and
+  // a tile runs as two chained jobs: slice 0 leaves its accumulators in
+  // part[] and raises part_ready once per compute warp, slice 1 starts from
+  // them.  Each element sees the same FMA sequence as an unsplit tile.
+  int ksplit;
+  float* part;            // [tiles][BM * BN] slice-0 accumulators, row-major per tile
+  int* part_ready;        // [tiles] compute warps of slice 0 that stored theirs
 };
 
 // Count a finished background tile of a streamed run; the last tile of a C
@@ -101,6 +110,20 @@ __device__ __forceinline__ void stream_tile(const StreamProto& st, int tile, int
   const int o = (int)st.order[tile];
   tm = o / tiles_n;
   tn = o - tm * tiles_n;
+}
+
+// K slices of a streamed run (1 unless the host split K).
+__device__ __forceinline__ int stream_ksplit(const StreamProto& st) { return st.ksplit > 1 ? st.ksplit : 1; }
+
+// Tile coordinates and K slice of a streamed run's visit slot.
+__device__ __forceinline__ void stream_job(const StreamProto& st, int slot, int tiles_n, int& tm, int& tn,
+                                           int& slice) {
+  const int ks = stream_ksplit(st);
+  const int o = (int)st.order[slot];
+  slice = o % ks;
+  const int t = o / ks;
+  tm = t / tiles_n;
+  tn = t - tm * tiles_n;
 }
 
 // One heterogeneous background task: C window = A window *

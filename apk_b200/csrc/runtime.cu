@@ -146,7 +146,10 @@ struct apk_ctx {
   unsigned* h_order = nullptr;
   int stream_cap = 0;       // capacity of d_ready (panels + column panels)
   int pack_cap = 0;         // capacity of d_pdone / h_pack (C blocks)
-  int order_cap = 0;        // capacity of d_order / h_order (tiles)
+  int order_cap = 0;        // capacity of d_order / h_order (visit slots)
+  float* d_part = nullptr;  // K-slice hand-off accumulators of a streamed run
+  int* d_part_ready = nullptr;
+  int part_cap = 0;         // capacity of d_part / d_part_ready (tiles)
   StreamProto st_cfg{};     // copied into the launch's parameters (zeros = resident operands)
   cudaEvent_t ev_start = nullptr, ev_done = nullptr;
   bool running = false;
@@ -542,6 +545,8 @@ apk_status apk_destroy(apk_ctx* ctx) {
   F(ctx->d_ready);
   F(ctx->d_pdone);
   F(ctx->d_order);
+  F(ctx->d_part);
+  F(ctx->d_part_ready);
   if (ctx->h_pack) cudaFreeHost(ctx->h_pack);
   if (ctx->h_order) cudaFreeHost(ctx->h_order);
   if (ctx->h_one) cudaFreeHost(ctx->h_one);
@@ -1059,6 +1064,15 @@ apk_status gemm_streamed(apk_ctx* ctx, const char* A, const char* B, float* C) {
   const int nb = n_units / b_units;
   const int cb_tn = std::max(1, b_units / tn_units), n_cb = (tiles_n + cb_tn - 1) / cb_tn;
   const int nblk = np * n_cb, ntiles = tiles_m * tiles_n;
+  // The warp-specialized fp32 kernel takes K in two chained slices: both
+  // operands move as K halves, all slice-0 jobs first, so slice-0 tiles
+  // compute while the second half is still being copied and the tiles the
+  // last copies unlock need half a tile's time (4096^3: modelled 4.13 ->
+  // 3.52 ms per call).  Other kernels, or an odd or short K, take whole K.
+  const int nk = K / ctx->cfg.k_tile;
+  const int ks = (ctx->cfg.dtype == APK_F32 && use_ws(ctx) && nk % 2 == 0 && nk >= 4) ? 2 : 1;
+  const int kh = K / ks;  // K elements per slice
+  const int nslots = ntiles * ks;
   if (!ctx->h2dstream) {
     APK_CU(cudaStreamCreateWithFlags(&ctx->h2dstream, cudaStreamNonBlocking));
     APK_CU(cudaStreamCreateWithFlags(&ctx->d2hstream, cudaStreamNonBlocking));
@@ -1066,11 +1080,20 @@ apk_status gemm_streamed(apk_ctx* ctx, const char* A, const char* B, float* C) {
     APK_CU(cudaHostAlloc(&ctx->h_one, sizeof(int), cudaHostAllocPortable));
     *ctx->h_one = 1;
   }
-  if (ctx->stream_cap < np + nb) {
+  if (ctx->stream_cap < (np + nb) * ks) {
     if (ctx->d_ready) cudaFree(ctx->d_ready);
     ctx->d_ready = nullptr;
-    APK_CU(cudaMalloc(&ctx->d_ready, sizeof(int) * (np + nb)));
-    ctx->stream_cap = np + nb;
+    APK_CU(cudaMalloc(&ctx->d_ready, sizeof(int) * (np + nb) * ks));
+    ctx->stream_cap = (np + nb) * ks;
+  }
+  if (ks > 1 && ctx->part_cap < ntiles) {
+    if (ctx->d_part) cudaFree(ctx->d_part);
+    if (ctx->d_part_ready) cudaFree(ctx->d_part_ready);
+    ctx->d_part = nullptr;
+    ctx->d_part_ready = nullptr;
+    APK_CU(cudaMalloc(&ctx->d_part, sizeof(float) * (size_t)ntiles * TM * TN));
+    APK_CU(cudaMalloc(&ctx->d_part_ready, sizeof(int) * ntiles));
+    ctx->part_cap = ntiles;
   }
   if (ctx->pack_cap < nblk) {
     if (ctx->d_pdone) cudaFree(ctx->d_pdone);
@@ -1082,49 +1105,62 @@ apk_status gemm_streamed(apk_ctx* ctx, const char* A, const char* B, float* C) {
     APK_CU(cudaHostGetDevicePointer(reinterpret_cast<void**>(&ctx->d_pack_mapped), ctx->h_pack, 0));
     ctx->pack_cap = nblk;
   }
-  if (ctx->order_cap < ntiles) {
+  if (ctx->order_cap < nslots) {
     if (ctx->d_order) cudaFree(ctx->d_order);
     if (ctx->h_order) cudaFreeHost(ctx->h_order);
     ctx->d_order = nullptr;
     ctx->h_order = nullptr;
-    APK_CU(cudaMalloc(&ctx->d_order, sizeof(unsigned) * ntiles));
-    APK_CU(cudaHostAlloc(&ctx->h_order, sizeof(unsigned) * ntiles, cudaHostAllocPortable));
-    ctx->order_cap = ntiles;
+    APK_CU(cudaMalloc(&ctx->d_order, sizeof(unsigned) * nslots));
+    APK_CU(cudaHostAlloc(&ctx->h_order, sizeof(unsigned) * nslots, cudaHostAllocPortable));
+    ctx->order_cap = nslots;
   }
   const StreamPlan plan = plan_stream(tiles_m, tiles_n, panel_tm, np, nb, tn_units, n_units, b_units,
-                                      (double)TM * K * es, (double)128 * K * es);
+                                      (double)TM * kh * es, (double)128 * kh * es);
   if ((int)plan.order.size() != ntiles)
     return fail(ctx, APK_EINVAL, "stream plan covers %d of %d tiles", (int)plan.order.size(), ntiles);
-  // the previous call's copies have completed (its streams were synchronised)
-  memcpy(ctx->h_order, plan.order.data(), sizeof(unsigned) * ntiles);
+  // the previous call's copies have completed (its streams were synchronised).
+  // Slot order: every tile's slice 0, then every tile's slice 1, each in the
+  // plan's order (a slice-1 job's predecessor is always popped before it).
+  for (int h = 0; h < ks; ++h)
+    for (int i = 0; i < ntiles; ++i) ctx->h_order[(size_t)h * ntiles + i] = plan.order[i] * ks + h;
   volatile int* ack = ctx->h_pack;
   for (int i = 0; i < nblk; ++i) ack[i] = 0;
   std::atomic_thread_fence(std::memory_order_seq_cst);
   cudaStream_t hs = ctx->h2dstream, ds = ctx->d2hstream;
-  APK_CU(cudaMemsetAsync(ctx->d_ready, 0, sizeof(int) * (np + nb), hs));
+  APK_CU(cudaMemsetAsync(ctx->d_ready, 0, sizeof(int) * (np + nb) * ks, hs));
   APK_CU(cudaMemsetAsync(ctx->d_pdone, 0, sizeof(unsigned) * nblk, hs));
-  APK_CU(cudaMemcpyAsync(ctx->d_order, ctx->h_order, sizeof(unsigned) * ntiles, cudaMemcpyHostToDevice, hs));
+  if (ks > 1) APK_CU(cudaMemsetAsync(ctx->d_part_ready, 0, sizeof(int) * ntiles, hs));
+  APK_CU(cudaMemcpyAsync(ctx->d_order, ctx->h_order, sizeof(unsigned) * nslots, cudaMemcpyHostToDevice, hs));
   APK_CU(cudaEventRecord(ctx->ev_reset, hs));
   char* dA = static_cast<char*>(ctx->dA);
   char* dB = static_cast<char*>(ctx->dB);
   const size_t bw = (size_t)128 * b_units * es;  // bytes per B panel row
-  for (const int c : plan.copies) {
-    if (c >= 0) {
-      const size_t r0 = (size_t)c * panel_tm * TM;
-      const size_t rows = std::min((size_t)M - r0, (size_t)panel_tm * TM);
-      APK_CU(cudaMemcpyAsync(dA + r0 * K * es, A + r0 * K * es, rows * K * es, cudaMemcpyHostToDevice, hs));
-      APK_CU(cudaMemcpyAsync(ctx->d_ready + c, ctx->h_one, sizeof(int), cudaMemcpyHostToDevice, hs));
-    } else {
-      const int j = -c - 1;
-      APK_CU(cudaMemcpy2DAsync(dB + j * bw, (size_t)N * es, B + j * bw, (size_t)N * es, bw, K,
-                               cudaMemcpyHostToDevice, hs));
-      APK_CU(cudaMemcpyAsync(ctx->d_ready + np + j, ctx->h_one, sizeof(int), cudaMemcpyHostToDevice, hs));
+  for (int h = 0; h < ks; ++h) {
+    const size_t ka = (size_t)h * kh * es;  // byte offset of the slice in an A row
+    const size_t kb = (size_t)h * kh * N * es;  // byte offset of the slice's first B row
+    for (const int c : plan.copies) {
+      if (c >= 0) {
+        const size_t r0 = (size_t)c * panel_tm * TM;
+        const size_t rows = std::min((size_t)M - r0, (size_t)panel_tm * TM);
+        if (ks == 1)
+          APK_CU(cudaMemcpyAsync(dA + r0 * K * es, A + r0 * K * es, rows * K * es, cudaMemcpyHostToDevice, hs));
+        else
+          APK_CU(cudaMemcpy2DAsync(dA + r0 * K * es + ka, (size_t)K * es, A + r0 * K * es + ka, (size_t)K * es,
+                                   (size_t)kh * es, rows, cudaMemcpyHostToDevice, hs));
+        APK_CU(cudaMemcpyAsync(ctx->d_ready + c * ks + h, ctx->h_one, sizeof(int), cudaMemcpyHostToDevice, hs));
+      } else {
+        const int j = -c - 1;
+        APK_CU(cudaMemcpy2DAsync(dB + kb + j * bw, (size_t)N * es, B + kb + j * bw, (size_t)N * es, bw, kh,
+                                 cudaMemcpyHostToDevice, hs));
+        APK_CU(cudaMemcpyAsync(ctx->d_ready + (np + j) * ks + h, ctx->h_one, sizeof(int), cudaMemcpyHostToDevice,
+                               hs));
+      }
     }
   }
 
   StreamProto st{};
   st.a_ready = ctx->d_ready;
-  st.b_ready = ctx->d_ready + np;
+  st.b_ready = ctx->d_ready + np * ks;  // flags are [panel * ks + slice]
   st.b_units = b_units;
   st.panel_tm = panel_tm;
   st.n_panels = np;
@@ -1133,10 +1169,13 @@ apk_status gemm_streamed(apk_ctx* ctx, const char* A, const char* B, float* C) {
   st.order = ctx->d_order;
   st.done = ctx->d_pdone;
   st.ack = ctx->d_pack_mapped;
+  st.ksplit = ks;
+  st.part = ks > 1 ? ctx->d_part : nullptr;
+  st.part_ready = ks > 1 ? ctx->d_part_ready : nullptr;
   ctx->st_cfg = st;
   APK_CU(cudaStreamWaitEvent(ctx->kstream, ctx->ev_reset, 0));
   const int poll = ctx->dAu ? (int)ctx->cfg.poll : APK_POLL_OFF;
-  apk_status s = launch_impl(ctx, (unsigned long long)ntiles, poll, ctx->kstream, true);
+  apk_status s = launch_impl(ctx, (unsigned long long)nslots, poll, ctx->kstream, true);
   ctx->st_cfg = StreamProto{};
   if (s != APK_OK) return s;
   ctx->running = true;

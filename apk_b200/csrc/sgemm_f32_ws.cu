@@ -69,7 +69,10 @@ constexpr int PROD_REGS = 56, COMP_REGS = 224, LAUNCH_REGS = 168;
 static_assert(128 * PROD_REGS + 256 * COMP_REGS <= NT * LAUNCH_REGS, "setmaxnreg split exceeds the launch's registers");
 
 enum : int { T_BG = 1, T_URG = 2, T_SUSPEND = 3, T_STOP = 4 };
-enum : int { F_FIRST = 1, F_LAST = 2, F_RESUME = 4 };
+// F_CHAIN: the first stage of a K slice after the first, whose accumulators
+// start from the previous slice's (streamed runs); F_HANDOFF: the last
+// stage of a K slice before the last, which leaves them there.
+enum : int { F_FIRST = 1, F_LAST = 2, F_RESUME = 4, F_CHAIN = 8, F_HANDOFF = 16 };
 
 struct Tag {
   int kind, flags, c, row0, col0, e, item, pad;
@@ -120,6 +123,23 @@ __device__ __forceinline__ bool bwait(uint64_t* bar, uint32_t parity, const F32P
   }
 }
 
+// Bounded wait for a global counter to reach target (acquire), giving up
+// when another role aborted.
+__device__ __forceinline__ bool wait_count(const int* c, int target, const F32Params& p, Shared& sh) {
+  const long long t0 = globaltimer_ns();
+  while (true) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
+    if (v >= target) return true;
+    if (vload(&sh.abort)) return false;
+    if (globaltimer_ns() - t0 > p.wait_limit_ns) {
+      vstore(&sh.abort, 1);
+      report_status(p.ev.status, DEV_WAIT_TIMEOUT_SPIN, p.ev.abort_word);
+      return false;
+    }
+  }
+}
+
 __device__ __forceinline__ void bwait_unwind(uint64_t* bar, uint32_t parity, long long limit) {
   const long long t0 = globaltimer_ns();
   while (!mbar_try_wait(bar, parity))
@@ -164,7 +184,10 @@ __device__ __forceinline__ void kpair(const float* __restrict__ As, const float*
   }
 }
 
-template <int POLL, int DISC, bool ORACLE>
+// KS: the instantiation for streamed runs with K slices (F_CHAIN /
+// F_HANDOFF).  The resident instantiations carry none of that code, which
+// changes how the compiler schedules the mainloop (-5% measured).
+template <int POLL, int DISC, bool ORACLE, bool KS>
 __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring_all = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -259,6 +282,8 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
       // Background tile in progress: its geometry and next stage to issue.
       unsigned long long bg_task = 0;
       int bg_row0 = 0, bg_col0 = 0, bg_c = 0, bg_nk = 0;
+      int bg_k0 = 0;  // first K stage of the tile's slice
+      int bg_xf = 0;  // F_CHAIN on its first stage / F_HANDOFF on its last (K slices)
       bool bg_open = false;  // the tile has stages issued and not all consumed
       // Observe generation f at a poll site and pop urgent work items; with
       // background stages in flight the first item is preceded by the skip
@@ -334,9 +359,11 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
               if (n <= -2) resume = true;
             }
           }
-          const int flags = (bg_c == 0 ? F_FIRST : 0) | (bg_c == bg_nk - 1 ? F_LAST : 0) | (resume ? F_RESUME : 0);
+          const int flags = (bg_c == 0 ? F_FIRST | (bg_xf & F_CHAIN) : 0) |
+                            (bg_c == bg_nk - 1 ? F_LAST | (bg_xf & F_HANDOFF) : 0) | (resume ? F_RESUME : 0);
           resume = false;
-          if (!emit(T_BG, flags, bg_c, bg_row0, bg_col0, 0, 0, bg_task, &p.tmA, &p.tmB, bg_c * BK)) return false;
+          if (!emit(T_BG, flags, bg_c, bg_row0, bg_col0, 0, 0, bg_task, &p.tmA, &p.tmB, (bg_k0 + bg_c) * BK))
+            return false;
           ++bg_c;
         }
         return true;
@@ -380,24 +407,32 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
         if (f < 0 || vload(&sh.abort)) break;
         if (POLL != POLL_OFF && f != lastSeen && handle(f, -1) == -1) break;
         if (task >= p.q.num_tasks) break;
-        const int tile = (int)(task % (unsigned long long)p.total_tiles);
-        int tm, tn;
+        const int ks = KS ? stream_ksplit(p.st) : 1;
+        const int tile = (int)(task % (unsigned long long)(p.total_tiles * ks));
+        int tm, tn, slice = 0;
         if (p.st.order != nullptr)
-          stream_tile(p.st, tile, p.tiles_n, tm, tn);
+          stream_job(p.st, tile, p.tiles_n, tm, tn, slice);
         else
           tile_coords(tile, p.total_tiles / p.tiles_n, p.tiles_n, 8, tm, tn);
-        // streamed operands: the tile's A row panel and B column panel must
-        // have landed before its first TMA load
-        if (p.st.a_ready != nullptr &&
-            !wait_ready2(&p.st.a_ready[tm / p.st.panel_tm], &p.st.b_ready[tn / p.st.b_units], p.wait_limit_ns)) {
+        // streamed operands: the slice of the tile's A row panel and B
+        // column panel must have landed before its first TMA load
+        if (p.st.a_ready != nullptr && !wait_ready2(&p.st.a_ready[(tm / p.st.panel_tm) * ks + slice],
+                                                    &p.st.b_ready[(tn / p.st.b_units) * ks + slice], p.wait_limit_ns)) {
           vstore(&sh.abort, 1);
           report_status(p.ev.status, DEV_WAIT_TIMEOUT_SPIN, p.ev.abort_word);
           break;
         }
+        // a later K slice starts from the accumulators its predecessor left:
+        // every compute warp of that job has stored its share.  The
+        // predecessor was popped earlier (the visit order lists every
+        // slice-0 job first) and waits on nothing this worker does.
+        if (KS && slice > 0 && !wait_count(&p.st.part_ready[tm * p.tiles_n + tn], 4 * slice, p, sh)) break;
         bg_task = task;
         bg_row0 = tm * BM;
         bg_col0 = tn * BN;
-        bg_nk = p.nk;
+        bg_nk = p.nk / ks;
+        bg_k0 = slice * bg_nk;
+        bg_xf = (slice > 0 ? F_CHAIN : 0) | (slice < ks - 1 ? F_HANDOFF : 0);
         bg_c = 0;
         bg_open = true;
         ok = emit_rest(false);
@@ -473,15 +508,28 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
       }
       bool compute = true;
       if (kind == T_BG) {
-        if (flags & F_RESUME) {
-          // the checkpointed accumulators; cur is this warp's own cursor,
-          // kept across the urgent items (a re-issue from stage 0 also
-          // carries F_FIRST, which must not reset it)
+        if (flags & (KS ? F_RESUME | F_CHAIN : F_RESUME)) {
+          // RESUME: the checkpointed accumulators; cur is this warp's own
+          // cursor, kept across the urgent items (a re-issue from stage 0
+          // also carries F_FIRST, which must not reset it).  CHAIN (first
+          // stage of a later K slice): the previous slice's accumulators,
+          // stored by another worker, so the loads skip L1.
+          // (slab: one float4 per (i, q) and thread; hand-off block: the
+          // C tile layout, row stride BN)
+          const float4* src = slab + gtid;
+          int si = 4 * 128, sq = 128;
+          if (KS && !(flags & F_RESUME)) {
+            cur = 0;
+            const int tid = (vload(&gs.tag[s].row0) / BM) * p.tiles_n + vload(&gs.tag[s].col0) / BN;
+            src = reinterpret_cast<const float4*>(p.st.part + (size_t)tid * (BM * BN) + arow0 * BN + bcol);
+            si = 4 * BN / 4;
+            sq = 32 / 4;
+          }
 #pragma unroll
           for (int i = 0; i < 8; ++i)
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              const float4 v = slab[(i * 4 + q) * 128 + gtid];
+              const float4 v = KS ? __ldcg(&src[i * si + q * sq]) : src[i * si + q * sq];
               acc[i][4 * q] = v.x;
               acc[i][4 * q + 1] = v.y;
               acc[i][4 * q + 2] = v.z;
@@ -520,15 +568,34 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
         }
         if (kind == T_BG) cur = tc + 1;
       }
-      const bool done_tile = (flags & F_LAST) && (kind == T_URG || (compute && cur == p.nk));
+      // a background stage is computed only in cursor order, so computing
+      // the F_LAST one completes the tile (or its K slice)
+      const bool done_tile = (flags & F_LAST) && (kind == T_URG || (compute && (KS || cur == p.nk)));
       if (done_tile) {
         const Tag& t = gs.tag[s];
         const int row0 = vload(&t.row0), col0 = vload(&t.col0), e = vload(&t.e);
         // ---- epilogue: this warp's 32 rows of the tile ----
-        if (kind == T_BG) {
+        if (kind == T_BG && !KS) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             float* crow = p.C + (size_t)(row0 + arow0 + 4 * i) * p.ldc + col0 + bcol;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              *reinterpret_cast<float4*>(crow + 32 * q) =
+                  make_float4(acc[i][4 * q], acc[i][4 * q + 1], acc[i][4 * q + 2], acc[i][4 * q + 3]);
+          }
+        } else if (kind == T_BG) {
+          // the tile's C block, or for a K slice before the last the tile's
+          // hand-off block (the same layout with a row stride of BN)
+          float* cb = p.C + (size_t)row0 * p.ldc + col0;
+          size_t ld = p.ldc;
+          if (flags & F_HANDOFF) {
+            cb = p.st.part + (size_t)((row0 / BM) * p.tiles_n + col0 / BN) * (BM * BN);
+            ld = BN;
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float* crow = cb + (size_t)(arow0 + 4 * i) * ld + bcol;
 #pragma unroll
             for (int q = 0; q < 4; ++q)
               *reinterpret_cast<float4*>(crow + 32 * q) =
@@ -552,6 +619,8 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
         }
         __threadfence();  // the tile's stores are visible before it is counted
         __syncwarp();
+        if (KS && lane == 0 && kind == T_BG && (flags & F_HANDOFF))
+          atomicAdd(&p.st.part_ready[(row0 / BM) * p.tiles_n + col0 / BN], 1);  // this warp's share is out
         // the fourth warp to finish does the accounting.  A background tile
         // counts on the group's counter: a warp that skipped its last stage
         // behind a yield stores it after the resume, in another slot.  An
@@ -561,11 +630,13 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
         if (lane == 0 && atomicAdd(cnt, 1) == 3) {
           *cnt = 0;
           if (kind == T_BG) {
-            ++gs.tiles;
             if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[t.task], 1);
-            count_trigger(p.ev);
-            if (p.st.done != nullptr)
-              stream_tile_done(p.st, p.total_tiles / p.tiles_n, p.tiles_n, row0 / BM, col0 / BN);
+            if (!KS || !(flags & F_HANDOFF)) {  // the tile is complete
+              ++gs.tiles;
+              count_trigger(p.ev);
+              if (p.st.done != nullptr)
+                stream_tile_done(p.st, p.total_tiles / p.tiles_n, p.tiles_n, row0 / BM, col0 / BN);
+            }
           } else {
             if (ORACLE) atomicAdd(&p.ev.uexec[e], 1);
             atomicMax(&p.ev.done_ns[e], (unsigned long long)globaltimer_ns());
@@ -595,13 +666,14 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
 // Host-side dispatch.
 
 template <int POLL, int DISC, bool ORACLE>
-static const void* kernel_ptr() {
-  return reinterpret_cast<const void*>(&sgemm_ws<POLL, DISC, ORACLE>);
+static const void* kernel_ptr(bool ks) {
+  return ks ? reinterpret_cast<const void*>(&sgemm_ws<POLL, DISC, ORACLE, true>)
+            : reinterpret_cast<const void*>(&sgemm_ws<POLL, DISC, ORACLE, false>);
 }
 
-static const void* select_kernel(int poll, int disc, bool oracle) {
+static const void* select_kernel(int poll, int disc, bool oracle, bool ks) {
 #define APK_SEL(PL, DS, OR) \
-  if (poll == PL && disc == DS && oracle == OR) return kernel_ptr<PL, DS, OR>();
+  if (poll == PL && disc == DS && oracle == OR) return kernel_ptr<PL, DS, OR>(ks);
   APK_SEL(POLL_OFF, DISC_DRAIN, false)
   APK_SEL(POLL_OFF, DISC_DRAIN, true)
   APK_SEL(POLL_BOUNDARY, DISC_DRAIN, false)
@@ -624,27 +696,32 @@ size_t params_bytes() { return sizeof(F32Params); }
 // count below the setmaxnreg split, or not one CTA per SM).
 cudaError_t prepare(int poll, int disc, bool oracle, int* ok) {
   *ok = 0;
-  const void* k = select_kernel(poll, disc, oracle);
-  if (!k) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
-  if (e != cudaSuccess) return e;
-  cudaFuncAttributes fa;
-  e = cudaFuncGetAttributes(&fa, k);
-  if (e != cudaSuccess) return e;
-  int occ = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, NT, SMEM_BYTES);
-  if (e != cudaSuccess) return e;
-  // setmaxnreg.inc waits for registers the block does not have if the launch
-  // gave it fewer than the split assumes: never launch that
-  *ok = (fa.numRegs >= LAUNCH_REGS && occ == 1) ? 1 : 0;
+  int good = 1;
+  for (const bool ks : {false, true}) {  // resident and K-sliced streamed runs
+    const void* k = select_kernel(poll, disc, oracle, ks);
+    if (!k) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, k);
+    if (e != cudaSuccess) return e;
+    int occ = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, NT, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    // setmaxnreg.inc waits for registers the block does not have if the
+    // launch gave it fewer than the split assumes: never launch that
+    if (!(fa.numRegs >= LAUNCH_REGS && occ == 1)) good = 0;
+  }
+  *ok = good;
   return cudaSuccess;
 }
 
-// workers = the runtime's grid (2 per CTA).
+// workers = the runtime's grid (2 per CTA).  prm.st.ksplit > 1 selects the
+// K-sliced instantiation.
 cudaError_t launch(const F32Params& prm, int workers, int poll, int disc, bool oracle, cudaStream_t stream) {
-  const void* k = select_kernel(poll, disc, oracle);
+  const void* k = select_kernel(poll, disc, oracle, prm.st.ksplit > 1);
   if (!k || workers % G != 0) return cudaErrorInvalidValue;
   void* args[] = {const_cast<F32Params*>(&prm)};
   return cudaLaunchKernel(k, dim3(workers / G), dim3(NT), args, SMEM_BYTES, stream);
