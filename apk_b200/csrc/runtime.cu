@@ -165,6 +165,11 @@ struct apk_ctx {
   bool ownAu = false, ownBu = false;
   float* dCu = nullptr;  // (max_events + 1) slots
   size_t cu_slot = 0;
+  // urgent output slots [0, cu_dirty) may hold values (fresh allocation or
+  // the split-K sums of the previous launch's events); the device-set events
+  // the last launch could raise
+  int cu_dirty = 0;
+  int dev_events_last = 0;
 
   // control
   Ctrl* d_ctrl = nullptr;   // main launch
@@ -748,6 +753,7 @@ apk_status apk_set_urgent(apk_ctx* ctx, const void* A, const void* B, int M, int
   if (ctx->dCu) cudaFree(ctx->dCu);
   ctx->cu_slot = (size_t)M * N;
   APK_CU(cudaMalloc(&ctx->dCu, sizeof(float) * ctx->cu_slot * (ctx->cfg.max_events + 1)));
+  ctx->cu_dirty = ctx->cfg.max_events + 1;
   ctx->Mu = M;
   ctx->Nu = N;
   ctx->Ku = K;
@@ -841,7 +847,16 @@ apk_status reset_logs(apk_ctx* ctx, unsigned long long num_tasks) {
   APK_CU(cudaMemsetAsync(ctx->d_uexec, 0, sizeof(int) * E, s));
   APK_CU(cudaMemsetAsync(ctx->d_tiles, 0, sizeof(unsigned long long) * G, s));
   APK_CU(cudaMemsetAsync(ctx->d_slab_hdr, 0, sizeof(long long) * 4 * G, s));
-  if (ctx->dCu) APK_CU(cudaMemsetAsync(ctx->dCu, 0, sizeof(float) * ctx->cu_slot * (E + 1), s));
+  // every urgent output slot starts the launch at zero (split-K items add
+  // into it).  Only slots a previous launch could have written are cleared:
+  // events it raised are bounded by the host injections (n_injected, reset
+  // below) or by the device schedule it ran with.
+  if (ctx->dCu) {
+    const int used = std::min(E + 1, std::max({ctx->cu_dirty, ctx->n_injected.load(), ctx->dev_events_last}));
+    if (used > 0) APK_CU(cudaMemsetAsync(ctx->dCu, 0, sizeof(float) * ctx->cu_slot * used, s));
+    ctx->cu_dirty = 0;
+  }
+  ctx->dev_events_last = ctx->cfg.set_mode == APK_SET_DEVICE ? ctx->n_sched + ctx->n_count : 0;
   // verification launches pre-fill C with 0xFF bytes (NaN) so a tile that
   // never runs fails loudly (src/persistent.cu:156-160)
   if (ctx->cfg.oracle && ctx->dC && !ctx->task_mode)
