@@ -264,7 +264,11 @@ apk_status apk_read_run_stats(apk_ctx* ctx, apk_run_stats* st);
 
 /* One synchronous GEMM through the persistent kernel: upload (host
  * buffers), drain every tile once, download.  Replaces one pass of
- * src/persistent.cu:155-172. */
+ * src/persistent.cu:155-172.  From host buffers the copies overlap the
+ * kernel (operand panels in, finished C blocks out); with the
+ * warp-specialized fp32 kernel K is taken in two chained slices.  C is
+ * bitwise equal to a resident drain of the same operands either way.
+ * run_stats.tiles_done counts tiles, not slices. */
 apk_status apk_gemm(apk_ctx* ctx, const void* A, const void* B, void* C, int M, int N, int K,
                     apk_mem_kind kind);
 
