@@ -65,6 +65,43 @@ def test_streamed_gemm_ragged_shapes(libapk, shape):
     _check(C, oracle.gemm_f64(A, B), K)
 
 
+def test_streamed_k_slices_under_stage_yields(libapk):
+    """apk_gemm from host memory takes K in two chained slices (slice 1
+    starts from the accumulators slice 0 handed off).  Device-set yields
+    every 20 us checkpoint jobs of both slices mid-pipeline; C must still be
+    bitwise equal to a resident drain, every (tile, slice) job run exactly
+    once, every urgent output correct."""
+    M = N = K = 2048
+    A, B = oracle.gen_uniform(M, N, K, 31)
+    Au, Bu, refu = _urgent_ref()
+    ntiles = (M // 128) * (N // 128)
+    with _ctx(poll="off") as c:
+        c.set_background(A, B)
+        c.launch(ntiles)
+        c.wait(60)
+        C0 = c.read_output()
+    nev = 40
+    offs = (np.arange(nev, dtype=np.int64) + 1) * 20_000
+    with _ctx(poll="stage", set_mode="device", oracle=True) as c:
+        c.set_urgent(Au, Bu)
+        c.schedule_device_events(offs)
+        C = c.gemm(A, B)
+        ev = c.read_events()
+        st = c.run_stats()
+        ex, ue = c.read_oracle(2 * ntiles)
+        outs = [c.read_urgent_output(e) for e in range(nev) if ev["claimer"][e]]
+        uitems = (U_M // 128) * (U_N // 128) * c.cfg.urgent_split_k
+    fired = int(np.count_nonzero(ev["set_ns"][:nev]))
+    assert fired >= 10 and st["yields"] > 0 and st["device_status"] == 0
+    assert st["tiles_done"] == ntiles  # tiles, not slices
+    assert np.array_equal(C.view(np.uint32), C0.view(np.uint32)), "K-sliced streamed run not bitwise"
+    assert np.all(ex == 1), "a (tile, slice) job ran other than once"
+    for Cu in outs:
+        _check(Cu, refu, U_K)
+    v = oracle.exactly_once(ex, ue[:fired], ev["claimer"][:fired], ev["set_ns"][:fired], uitems, fired)
+    assert v["pass"], v
+
+
 def test_fp32_kernels_bitwise_equal(libapk):
     """The warp-specialized and the block-synchronous fp32 kernels run the
     same FMA sequence per element: bitwise-equal C, both within tolerance."""
