@@ -110,6 +110,7 @@ SIGNATURES = {
     "apk_read_oracle": (c_int, [P, P, P]),
     "apk_read_run_stats": (c_int, [P, ctypes.POINTER(RunStats)]),
     "apk_gemm": (c_int, [P, P, P, P, c_int, c_int, c_int, c_int]),
+    "apk_probe_copy": (c_int, [P, P, P, P, c_int, P]),
     "apk_run_latency": (c_int, [P, ctypes.POINTER(LatencyConfig), ctypes.POINTER(LatencyResult)]),
     "apk_probe_visibility": (c_int, [P, c_int, P]),
     "apk_run_visibility": (c_int, [P, ctypes.POINTER(VisibilityConfig), ctypes.POINTER(VisibilityResult), P, P]),
@@ -125,6 +126,8 @@ SIGNATURES = {
                              c_int, P]),
     "apk_shard_tasks": (c_int, [P, c_int, c_int, c_int, P]),
     "apk_sgemm_f32_noalloc": (c_int, [P, P, P, c_int, c_int, c_int, c_int, P]),
+    "apk_sgemm_f32_noalloc_status": (c_int, [P, ctypes.POINTER(c_int)]),
+    "apk_sgemm_f32_noalloc_selftest": (c_int, [c_ll, P]),
     "apk_fill_uniform": (None, [c_uint, P, c_size_t, P, c_size_t]),
     "apk_fill_normal_bf16": (None, [c_ull, P, c_size_t]),
     "apk_round_bf16": (None, [P, P, c_size_t]),

@@ -99,7 +99,11 @@ __device__ __forceinline__ void stream_tile_done(const StreamProto& st, int tile
   const int cols = tiles_n - cb * st.cb_tn < st.cb_tn ? tiles_n - cb * st.cb_tn : st.cb_tn;
   const int b = pn * st.n_cb + cb;
   if (atomicAdd(&st.done[b], 1u) + 1u == (unsigned)(rows * cols)) {
-    // mapped host memory: the store is pushed out by a system-scope fence
+    // the host reads the block with a copy engine once it sees the ack in
+    // mapped host memory: a system-scope fence orders every tile's C stores
+    // (each made visible at GPU scope before it was counted) before the ack,
+    // and a second one pushes the ack out now
+    __threadfence_system();
     *reinterpret_cast<volatile int*>(&st.ack[b]) = 1;
     __threadfence_system();
   }

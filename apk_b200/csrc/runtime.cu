@@ -1221,10 +1221,17 @@ apk_status gemm_streamed(apk_ctx* ctx, const char* A, const char* B, float* C) {
       if (ended) {
         for (int blk = 0; blk < nblk && out == APK_OK; ++blk)
           if (!sent[blk]) out = fail(ctx, APK_EDEVICE, "kernel ended without finishing C block %d", blk);
-      } else if (cudaEventQuery(ctx->ev_done) == cudaSuccess) {
-        // one more scan sees every ack the finished kernel wrote
-        std::atomic_thread_fence(std::memory_order_seq_cst);
-        ended = true;
+      } else {
+        const cudaError_t q = cudaEventQuery(ctx->ev_done);
+        if (q == cudaSuccess) {
+          // one more scan sees every ack the finished kernel wrote
+          std::atomic_thread_fence(std::memory_order_seq_cst);
+          ended = true;
+        } else if (q != cudaErrorNotReady) {
+          // a sticky error (failed launch, faulted kernel): no further ack
+          // will come and every later query fails the same way
+          out = fail(ctx, APK_ECUDA, "streamed GEMM kernel failed: %s", cudaGetErrorString(q));
+        }
       }
     }
   }
@@ -1471,6 +1478,36 @@ apk_status apk_gemm(apk_ctx* ctx, const void* A, const void* B, void* C, int M, 
   APK_CU(cudaStreamSynchronize(ctx->kstream));
   ctx->running = false;
   return read_status(ctx);
+}
+
+apk_status apk_probe_copy(apk_ctx* ctx, const void* A, const void* B, void* C, int reps, double* out_ms) {
+  if (!ctx || !A || !B || !C || reps <= 0 || !out_ms) return APK_EINVAL;
+  if (ctx->running) return fail(ctx, APK_ESTATE, "probe needs an idle device");
+  const size_t es = esize_of(ctx->cfg.dtype);
+  const size_t ab = es * ctx->M * ctx->K, bb = es * (size_t)ctx->K * ctx->N, cb = 4ull * ctx->M * ctx->N;
+  if (!ctx->h2dstream || !ctx->ownA || !ctx->ownB || !ctx->ownC || ctx->capA < ab || ctx->capB < bb ||
+      ctx->capC < cb)
+    return fail(ctx, APK_ESTATE, "needs a previous apk_gemm from host memory on this context");
+  APK_CU(cudaSetDevice(ctx->cfg.device));
+  cudaStream_t hs = ctx->h2dstream, ds = ctx->d2hstream;
+  std::vector<double> t[3];
+  for (int r = 0; r < reps; ++r)
+    for (int m = 0; m < 3; ++m) {  // 0: A and B in, 1: C out, 2: both at once
+      const long long t0 = host_now_ns();
+      if (m != 1) {
+        APK_CU(cudaMemcpyAsync(ctx->dA, A, ab, cudaMemcpyHostToDevice, hs));
+        APK_CU(cudaMemcpyAsync(ctx->dB, B, bb, cudaMemcpyHostToDevice, hs));
+      }
+      if (m != 0) APK_CU(cudaMemcpyAsync(C, ctx->dC, cb, cudaMemcpyDeviceToHost, ds));
+      APK_CU(cudaStreamSynchronize(hs));
+      APK_CU(cudaStreamSynchronize(ds));
+      t[m].push_back((double)(host_now_ns() - t0) / 1e6);
+    }
+  for (int m = 0; m < 3; ++m) {
+    std::sort(t[m].begin(), t[m].end());
+    out_ms[m] = t[m][t[m].size() / 2];
+  }
+  return APK_OK;
 }
 
 // ------------------------------------------------------------------ harness

@@ -672,11 +672,17 @@ cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool orac
 // the process exits.  Its device address is obtained with
 // cudaGetSymbolAddress at the first call on each device (with that device
 // current); that first call should therefore come before any stream capture.
-// Every call shares the array and it keeps the last call's contents: the
-// queue header is cleared on the caller's stream before each launch, so
-// calls issued in order on one stream are independent, while calls that
-// overlap on the GPU (different streams, or other devices' contexts sharing
-// nothing but this code) race on the same scratch and must not be issued.
+// Every call on one device shares that device's array and it keeps the last
+// call's contents: the queue header is cleared on the caller's stream before
+// each launch, so calls issued in order on one stream are independent, while
+// calls that overlap on the same device (for example on two streams) race on
+// the same scratch and must not be issued.  Calls on different devices use
+// different instances of the array and do not interact.
+//
+// The device status word sits in the same header.  A kernel whose bounded
+// wait ran out (2 s) records a code there and leaves C incomplete; since the
+// call itself is asynchronous, apk_sgemm_f32_noalloc_status reads the word
+// back after the caller's stream has drained (no allocation either).
 // ===========================================================================
 #include <cstdio>
 #include <cstring>
@@ -692,11 +698,16 @@ namespace {
 
 constexpr size_t kNoAllocScratchBytes = 16384;  // stated maximum
 constexpr size_t kNoAllocHeaderBytes = 256;
+// 2016 per-CTA counters.  The kernel fits at most 2 CTAs per SM (97 KB of
+// shared memory each), so residency -- checked first -- stays far below this
+// on a B200 (296); the size check guards parts with more than 1008 SMs.
 constexpr int kNoAllocMaxGrid = (int)((kNoAllocScratchBytes - kNoAllocHeaderBytes) / sizeof(unsigned long long));
+static_assert(kNoAllocMaxGrid >= 2 * 148, "the static scratch must cover a B200's full residency");
 
 struct NoAllocHeader {
   unsigned long long next_task, start_min, end_max, yields;
   int exited, abort_word, status, flag;
+  int never_set;  // a word no code path writes (the status path's self-test)
 };
 static_assert(sizeof(NoAllocHeader) <= kNoAllocHeaderBytes, "header must fit");
 
@@ -719,15 +730,29 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 }  // namespace f32
 }  // namespace apk
 
-extern "C" apk_status apk_sgemm_f32_noalloc(const float* A, const float* B, float* C, int M, int N, int K,
-                                            int grid, void* stream) {
-  using namespace apk;
-  using namespace apk::f32;
-  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0 || M % 128 || N % 128 || K % 32) return APK_EINVAL;
-  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(C)) & 15)
-    return APK_EINVAL;
+namespace apk {
+namespace f32 {
+namespace {
+
+// A bounded spin on a word nothing writes: it gives up after limit_ns and
+// records DEV_WAIT_TIMEOUT_SPIN in the status word, exactly as a kernel
+// whose mbarrier wait ran out does.
+__global__ void noalloc_spin_kernel(const int* word, long long limit_ns, int* status) {
+  if (threadIdx.x != 0) return;
+  const long long t0 = globaltimer_ns();
+  while (flag_load(word) != 1)
+    if (globaltimer_ns() - t0 > limit_ns) {
+      atomicCAS(status, 0, DEV_WAIT_TIMEOUT_SPIN);
+      return;
+    }
+}
+
+// One-time set-up on the current device (the scratch array's device
+// address, the kernel's shared-memory attribute, the SM count).  Returns
+// the device's record, or nullptr on a CUDA failure.
+NoAllocDevice* noalloc_device() {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return APK_ECUDA;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
   NoAllocDevice& d = g_noalloc_dev[dev];
   {
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
@@ -735,18 +760,18 @@ extern "C" apk_status apk_sgemm_f32_noalloc(const float* A, const float* B, floa
       // one-time set-up on this device (it is current): the scratch array's
       // device address, the kernel's shared-memory attribute, SM count
       void* ptr = nullptr;
-      if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return APK_ECUDA;
+      if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return nullptr;
       int maxc = 0;
-      if (prepare(POLL_OFF, DISC_DRAIN, false, 32, SCHED_QUEUE, &maxc) != cudaSuccess || maxc < 1) return APK_ECUDA;
+      if (prepare(POLL_OFF, DISC_DRAIN, false, 32, SCHED_QUEUE, &maxc) != cudaSuccess || maxc < 1) return nullptr;
       int sms = 0;
-      if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return APK_ECUDA;
+      if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return nullptr;
       if (!g_noalloc_encode) {
         void* fn = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) !=
                 cudaSuccess ||
             q != cudaDriverEntryPointSuccess || !fn)
-          return APK_ECUDA;
+          return nullptr;
         g_noalloc_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
       }
       d.scratch = static_cast<unsigned char*>(ptr);
@@ -755,6 +780,23 @@ extern "C" apk_status apk_sgemm_f32_noalloc(const float* A, const float* B, floa
       d.ready = true;
     }
   }
+  return &d;
+}
+
+}  // namespace
+}  // namespace f32
+}  // namespace apk
+
+extern "C" apk_status apk_sgemm_f32_noalloc(const float* A, const float* B, float* C, int M, int N, int K,
+                                            int grid, void* stream) {
+  using namespace apk;
+  using namespace apk::f32;
+  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0 || M % 128 || N % 128 || K % 32) return APK_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(C)) & 15)
+    return APK_EINVAL;
+  NoAllocDevice* dp = noalloc_device();
+  if (dp == nullptr) return APK_ECUDA;
+  NoAllocDevice& d = *dp;
   const int resident = d.sms * d.max_ctas_per_sm;
   if (grid <= 0) grid = resident;
   if (grid > resident) return APK_EINVAL;  // CTAs beyond residency never start
@@ -809,4 +851,29 @@ extern "C" apk_status apk_sgemm_f32_noalloc(const float* A, const float* B, floa
   if (cudaMemsetAsync(&h->start_min, 0xFF, sizeof(h->start_min), s) != cudaSuccess) return APK_ECUDA;
   if (launch(p, grid, POLL_OFF, DISC_DRAIN, false, 32, SCHED_QUEUE, s) != cudaSuccess) return APK_ECUDA;
   return APK_OK;
+}
+
+extern "C" apk_status apk_sgemm_f32_noalloc_status(void* stream, int* device_status) {
+  using namespace apk::f32;
+  if (!device_status) return APK_EINVAL;
+  NoAllocDevice* d = noalloc_device();
+  if (d == nullptr) return APK_ECUDA;
+  if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return APK_ECUDA;
+  const NoAllocHeader* h = reinterpret_cast<const NoAllocHeader*>(d->scratch);
+  // a 4-byte copy into the caller's variable: no buffer is allocated
+  if (cudaMemcpy(device_status, &h->status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return APK_ECUDA;
+  return APK_OK;
+}
+
+extern "C" apk_status apk_sgemm_f32_noalloc_selftest(long long limit_ns, void* stream) {
+  using namespace apk;
+  using namespace apk::f32;
+  if (limit_ns <= 0 || limit_ns > 10000000000LL) return APK_EINVAL;
+  NoAllocDevice* d = noalloc_device();
+  if (d == nullptr) return APK_ECUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  NoAllocHeader* h = reinterpret_cast<NoAllocHeader*>(d->scratch);
+  if (cudaMemsetAsync(d->scratch, 0, kNoAllocHeaderBytes, s) != cudaSuccess) return APK_ECUDA;
+  noalloc_spin_kernel<<<1, 32, 0, s>>>(&h->never_set, limit_ns, &h->status);
+  return cudaGetLastError() == cudaSuccess ? APK_OK : APK_ECUDA;
 }

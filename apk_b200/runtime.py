@@ -295,6 +295,13 @@ class Context:
         self.M, self.N, self.K = M, N, K
         return C
 
+    def probe_copy(self, A: np.ndarray, B: np.ndarray, C: np.ndarray, reps: int = 5) -> dict:
+        """Copy ceiling of gemm() from these host buffers (no kernel): ms of
+        A+B in, C out, and both at once (medians over reps)."""
+        out = np.zeros(3, np.float64)
+        self._check(self._lib.apk_probe_copy(self._h, _ptr(A), _ptr(B), _ptr(C), reps, _ptr(out)))
+        return {"h2d_ms": float(out[0]), "d2h_ms": float(out[1]), "both_ms": float(out[2])}
+
     def gemm_device(self, A_ptr: int, B_ptr: int, C_ptr: int, M: int, N: int, K: int):
         self._check(self._lib.apk_gemm(self._h, ctypes.c_void_p(A_ptr), ctypes.c_void_p(B_ptr),
                                        ctypes.c_void_p(C_ptr), M, N, K, L.APK_MEM_DEVICE))

@@ -10,18 +10,36 @@ synthetic, no dataset involved.
 A step is one launch of the persistent kernel: it drains background tiles
 (task t computes tile t mod 1024) while `--events-per-step` urgent GEMMs are
 injected by the host (flag stored with cudaMemcpyAsync on a high-priority
-control stream), then the host stops it.  value = the
+control stream); the launch is bounded and ends by itself.  value = the
 background GEMM's TFLOP/s over the timed steps (FLOPs of completed tiles /
 CUDA-event time of the launches, summed over ranks and divided by the max
-over ranks); the urgent preemption latencies of all timed events are
-reported beside it.  e2e = the same metric through the public API with
-host buffers: apk_gemm over pinned host A, B -> C (H2D + drain + D2H).
+over ranks); latency_us holds the urgent preemption latencies of all timed
+events.  e2e = the same metric through the public API with host buffers:
+apk_gemm over pinned host A, B -> C (H2D + drain + D2H), with the plain copy
+ceiling of the same buffers beside it.
+
+Every rank also runs the configs[4] leg (`config4`): 2^20 heterogeneous bf16
+GEMM tasks from one seed, LPT-sharded over the ranks, each rank draining its
+shard undisturbed and under a 2 kHz Poisson urgent stream; exactly-once over
+the union of shards, corrupted half-tiles and urgent claims are checked on
+the host after timing.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    python bench.py --case drain-f32|drain-bf16|tasks-bf16 [...]   # one small case, for ncu
+
+Definitions of the latency keys: preempt = host store of the yield flag ->
+host sees the device's claim ack (mapped memory, host clock, no clock
+mapping); urgent_done = host store -> host sees the last urgent item's ack;
+dev_* = globaltimer intervals from the first CTA to observe the flag
+(claim after it, spread of observations, done after claim);
+device_set.* = CTA 0 sets the flag on a schedule, so set -> claim / last
+observer / done share one clock (the reference's primary instrument,
+src/yield.cu:186-195).
 """
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -35,6 +53,14 @@ M = N = K = 4096
 U = 256
 METRIC = "urgent-task p50/p99 preempt latency (us); background GEMM TFLOPS (% of peak)"
 SMS_B200 = 148
+# DRAM bytes (read + write) per 128x128x4096 tile of the warp-specialized
+# fp32 kernel: one ncu capture of a 4096^3 drain (1024 tiles) measured
+# 363.2 MB read + 54.8 MB written, i.e. 417.9 MB / 1024 tiles.  Command:
+#   ncu --set full --clock-control none -k regex:sgemm_ws -s 1 -c 1 \
+#       python bench.py --case drain-f32 --n 4096
+# A constant, so a stale value shows up beside the profile it came from
+# rather than silently; re-capture after any change to the kernel.
+F32WS_DRAM_BYTES_PER_TILE = 408132
 
 
 def parse():
@@ -46,6 +72,15 @@ def parse():
     ap.add_argument("--events-per-step", type=int, default=200)
     ap.add_argument("--period-us", type=float, default=1000.0)
     ap.add_argument("--no-extras", action="store_true", help="skip overhead/baseline/cpu legs")
+    ap.add_argument("--no-config4", action="store_true", help="skip the configs[4] task-queue leg")
+    ap.add_argument("--config4-tasks", type=int, default=1 << 20)
+    # one small case for profilers (ncu): a few bounded launches, no timing contract
+    ap.add_argument("--case", default=None, choices=["drain-f32", "drain-bf16", "tasks-bf16"])
+    ap.add_argument("--n", type=int, default=0, help="--case drain-*: n^3 background")
+    ap.add_argument("--reps", type=int, default=0, help="--case: launches")
+    ap.add_argument("--poll", default="stage", choices=("off", "boundary", "stage"))
+    ap.add_argument("--kernel", default="auto", help="--case drain-f32: auto|ws|sync; drain-bf16: auto|pair|single")
+    ap.add_argument("--tasks", type=int, default=1 << 16, help="--case tasks-bf16: task count")
     return ap.parse_args()
 
 
@@ -62,18 +97,21 @@ def pct(v, q):
     return v[min(int(q * len(v)), len(v) - 1)] if v else None
 
 
+def r3(x):
+    return None if x is None else round(float(x), 3)
+
+
 # ---------------------------------------------------------------- dist
 def dist_setup(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
-        import datetime
-
         import torch.distributed as dist
-        # control plane only (barriers, max/sum of per-rank results): the
-        # timed path has no collective, each rank drains its own shard
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+        # control plane only (barriers, max/sum of per-rank results, the
+        # exactly-once union after timing): the timed path has no
+        # collective, each rank drains its own work
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
     return world, rank, local
 
 
@@ -93,34 +131,13 @@ def allgather_obj(world, obj):
 
 
 # ---------------------------------------------------------------- cpu legs
-def cpu_gemm_sample(target_s: float = 8.0):
-    """The reference's float64 loop (oracle port of src/persistent.cu:221-227),
-    row-parallel on every host thread, on a row band of the 4096^3 workload
-    sized to about target_s seconds.  Returns (TFLOP/s, rows, threads, secs)."""
-    import oracle
-    A, B = oracle.gen_uniform(M, N, K, 21)
-    th = oracle.max_threads()
-    import numpy as np
-    rows = max(th, 8)
-    while True:
-        t = time.perf_counter()
-        _ = oracle_gemm_band(oracle, A, B, rows, th)
-        dt = time.perf_counter() - t
-        if dt > 0.5 or rows >= M:
-            break
-        rows = min(M, rows * 4)
-    rows = int(min(M, max(th, rows * target_s / max(dt, 1e-3))))
-    t = time.perf_counter()
-    oracle_gemm_band(oracle, A, B, rows, th)
-    dt = time.perf_counter() - t
-    del np
-    return 2.0 * rows * N * K / dt / 1e12, rows, th, dt
-
-
-def oracle_gemm_band(oracle, A, B, rows, th):
-    import numpy as np
-    Ab = np.ascontiguousarray(A[:rows])
-    return oracle.gemm_f64_omp(Ab, B, th)
+def host_cores() -> int:
+    """Host threads this process may run on (set explicitly: torchrun exports
+    OMP_NUM_THREADS=1, which must not decide the all-cores figure)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 def cpu_desc():
@@ -133,48 +150,149 @@ def cpu_desc():
     return "unknown"
 
 
+def ref_loop_rows(oracle, A, B, rows):
+    """The reference's float64 host loop (src/persistent.cu:221-227) as
+    shipped: one thread, i-k-j order, on the first `rows` rows of A."""
+    return oracle.gemm_f64_rows(A, B, 0, rows)
+
+
+def size_rows(fn, target_s, lo=8):
+    """Rows of the 4096^3 product that take about target_s through fn."""
+    rows = lo
+    while True:
+        t = time.perf_counter()
+        fn(rows)
+        dt = time.perf_counter() - t
+        if dt > 0.3 or rows >= M:
+            break
+        rows = min(M, rows * 4)
+    return int(min(M, max(lo, rows * target_s / max(dt, 1e-3))))
+
+
+def cpu_single_core(oracle, A, B, target_s=8.0):
+    """(TFLOP/s, rows, seconds) of the reference's loop on one core."""
+    rows = size_rows(lambda r: ref_loop_rows(oracle, A, B, r), target_s)
+    t = time.perf_counter()
+    ref_loop_rows(oracle, A, B, rows)
+    dt = time.perf_counter() - t
+    return 2.0 * rows * N * K / dt / 1e12, rows, dt
+
+
+def cpu_all_cores(oracle, A, B, target_s=4.0):
+    """The same loop row-parallel (OpenMP) on every host thread this process
+    may use: a labelled side figure, not the baseline."""
+    import numpy as np
+    th = host_cores()
+    run = lambda r: oracle.gemm_f64_omp(np.ascontiguousarray(A[:r]), B, th)  # noqa: E731
+    rows = size_rows(run, target_s, lo=th)
+    t = time.perf_counter()
+    run(rows)
+    dt = time.perf_counter() - t
+    return 2.0 * rows * N * K / dt / 1e12, rows, th, dt
+
+
 def run_reference(args, world, rank):
-    """Reference arm: the reference's own CPU implementation of the path (its
-    float64 host GEMM, as the oracle port) on all host threads."""
+    """Reference arm: the reference's CPU implementation of the path (its
+    float64 host GEMM, src/persistent.cu:221-227, as the oracle port) exactly
+    as shipped -- single-threaded -- on a row band of the configs[1] product
+    per step.  The same single-core measurement at every N: rank 0 runs it,
+    the other ranks exit without work.  The OpenMP all-cores form is
+    reported beside it under all_cores."""
     if rank != 0:
         return
     import oracle
     A, B = oracle.gen_uniform(M, N, K, 21)
-    th = oracle.max_threads()
-    # size one step to ~2 s of work so K+W steps end within a few minutes
-    rows = max(th, 16)
-    t = time.perf_counter()
-    oracle_gemm_band(oracle, A, B, rows, th)
-    dt = time.perf_counter() - t
-    rows = int(min(M, max(th, rows * 2.0 / max(dt, 1e-3))))
+    # size one step to ~2 s of single-core work so K+W steps end in minutes
+    rows = size_rows(lambda r: ref_loop_rows(oracle, A, B, r), 2.0)
     for _ in range(args.warmup):
-        oracle_gemm_band(oracle, A, B, rows, th)
+        ref_loop_rows(oracle, A, B, rows)
     times = []
     for _ in range(args.steps):
         t = time.perf_counter()
-        oracle_gemm_band(oracle, A, B, rows, th)
+        ref_loop_rows(oracle, A, B, rows)
         times.append(time.perf_counter() - t)
     tot = sum(times)
     val = 2.0 * rows * N * K * len(times) / tot / 1e12
+    allc, arows, th, adt = cpu_all_cores(oracle, A, B)
+    sample = f"{rows} of {M} rows of the 4096^3 float64 product per step, one thread"
     line = {
         "impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot / len(times) * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic (srand(21)/rand() uniform[-1,1], src/persistent.cu:132-135)",
-        "config": {"workload": "configs[1] background GEMM fp32 4096^3 as the reference's float64 host "
+        "config": {"workload": "configs[1] background GEMM fp32 4096^3 through the reference's float64 host "
                                "loop (src/persistent.cu:221-227), row band per step",
-                   "rows_per_step": rows, "M": M, "N": N, "K": K},
-        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": th, "kind": "port",
-                         "sample": f"{rows} of {M} rows of the 4096^3 product per step, OpenMP row-parallel",
+                   "rows_per_step": rows, "M": M, "N": N, "K": K,
+                   "ranks": "rank 0 alone, the same single-core measurement at every N"},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": 1, "kind": "port", "sample": sample,
                          "cpu": cpu_desc()},
+        "all_cores": {"value": allc, "unit": "TFLOP/s", "cores": th, "kind": "port",
+                      "sample": f"{arrows} rows, OpenMP row-parallel, {adt:.1f} s"},
         "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- cases
+def run_case(args):
+    """One small bounded case for a profiler: --reps launches of one drain
+    (fp32 or bf16 n^3 background, or a configs[4] task list), each printing
+    its launch time.  Under ncu skip the first launch (`-s 1`) so the
+    captured one runs with warm tensor maps and caches; the launches are
+    bounded, so a serialised capture never waits for a host flag."""
+    import apk_b200
+    if args.case == "tasks-bf16":
+        import numpy as np
+        from apk_b200.runtime import POOL, gen_tasks
+        tasks, n_chk = gen_tasks(args.tasks, 21)
+        flops = float((2.0 * tasks["m"].astype(np.float64) * tasks["n"] * tasks["k"]).sum())
+        A = apk_b200.fill_normal_bf16((POOL["a_rows"], POOL["a_cols"]), 101)
+        B = apk_b200.fill_normal_bf16((POOL["b_rows"], POOL["b_cols"]), 102)
+        Au = apk_b200.fill_normal_bf16((256, 256), 31)
+        Bu = apk_b200.fill_normal_bf16((256, 256), 32)
+        with apk_b200.Context(dtype="bf16", poll=args.poll, urgent_split_k=1,
+                              bf16_kernel=args.kernel if args.kernel != "auto" else "auto") as c:
+            c.set_task_pool(A, B, POOL["c_rows"], POOL["c_cols"])
+            c.set_urgent(Au, Bu)
+            nw = c.set_tasks(tasks, n_chk)
+            for _ in range(args.reps or 3):
+                c.launch(nw)
+                c.wait(120)
+                st = c.run_stats()
+                print("tasks-bf16 %d tasks poll=%s: %.3f ms, %.1f TFLOP/s, %d halves" % (
+                    args.tasks, args.poll, st["launch_ms"], flops / st["launch_ms"] / 1e9, st["tiles_done"]),
+                    flush=True)
+        return
+    bf16 = args.case == "drain-bf16"
+    n = args.n or (6144 if bf16 else 4096)
+    reps = args.reps or (3 if bf16 else 2)
+    if bf16:
+        A = apk_b200.fill_normal_bf16((n, n), 21)
+        B = apk_b200.fill_normal_bf16((n, n), 22)
+        Au = apk_b200.fill_normal_bf16((256, 256), 31)
+        Bu = apk_b200.fill_normal_bf16((256, 256), 32)
+        kw = {"dtype": "bf16", "bf16_kernel": args.kernel}
+    else:
+        A, B = apk_b200.fill_uniform(n, n, n, 21)
+        Au, Bu = apk_b200.fill_uniform(256, 256, 256, 99)
+        kw = {"dtype": "f32", "f32_kernel": args.kernel}
+    with apk_b200.Context(poll=args.poll, urgent_split_k=1, **kw) as c:
+        c.set_background(A, B)
+        c.set_urgent(Au, Bu)
+        info = c.info
+        tiles = (n // info["tile_m"]) * (-(-n // info["tile_n"]))
+        for _ in range(reps):
+            c.launch(tiles)
+            c.wait(60)
+            st = c.run_stats()
+            print("%s %d^3 poll=%s: %.3f ms, %.1f TFLOP/s, %d tiles" % (
+                args.case, n, args.poll, st["launch_ms"], 2.0 * n ** 3 / st["launch_ms"] / 1e9,
+                st["tiles_done"]), flush=True)
+
+
 # ---------------------------------------------------------------- extras
-def device_set_latency(apk_b200, np, dev, A, B, Au, Bu, bg_tasks, events=200):
+def device_set_latency(apk_b200, dev, A, B, Au, Bu, bg_tasks, events=200):
     """configs[1] with the reference's primary instrument: CTA 0 sets the
     flag at scheduled globaltimer instants (src/yield.cu:186-195), so set,
     observation, claim and completion share one clock."""
@@ -183,18 +301,17 @@ def device_set_latency(apk_b200, np, dev, A, B, Au, Bu, bg_tasks, events=200):
         c.set_urgent(Au, Bu)
         r = c.run_latency(events=events, period_us=1000, seed=7, warmup_events=10, settle_ms=2.0,
                           bg_tasks=bg_tasks)
-    keys = ("n", "unclaimed", "anomalies", "claim_p50_us", "claim_p99_us", "last_obs_p50_us",
-            "last_obs_p99_us", "done_p50_us", "done_p99_us", "bg_tflops")
-    return {k: r[k] for k in keys}
+    return {"n": r["n"], "unclaimed": r["unclaimed"], "claim_p50": r3(r["claim_p50_us"]),
+            "claim_p99": r3(r["claim_p99_us"]), "last_obs_p50": r3(r["last_obs_p50_us"]),
+            "last_obs_p99": r3(r["last_obs_p99_us"]), "done_p50": r3(r["done_p50_us"]),
+            "done_p99": r3(r["done_p99_us"])}
 
 
 def bf16_config2(apk_b200, np, dev):
-    """bf16 8192^3, N(0,1) rounded to bf16, K-tile 64 (the
-    reference's shape is 256x128 tiles in a 4-stage ring; this kernel runs
-    256x256 tiles in a 3-stage ring of the same 192 KB): throughput of the
-    uninterrupted drain, then a drain with device-set yields at random
-    pipeline stages whose output must be bitwise identical to the
-    uninterrupted one."""
+    """bf16 8192^3, N(0,1) rounded to bf16, K-tile 64:
+    throughput of the uninterrupted drain, then a drain with device-set
+    yields at random pipeline stages whose output must be bitwise identical
+    to the uninterrupted one."""
     n = 8192
     A = apk_b200.fill_normal_bf16((n, n), 21)
     B = apk_b200.fill_normal_bf16((n, n), 22)
@@ -223,27 +340,11 @@ def bf16_config2(apk_b200, np, dev):
     fired = int(np.count_nonzero(ev["set_ns"][:nev]))
     cl = [(ev["claim_ns"][e] - ev["set_ns"][e]) / 1e3 for e in range(fired) if ev["claimer"][e]]
     dn = [(ev["done_ns"][e] - ev["set_ns"][e]) / 1e3 for e in range(fired) if ev["done_ns"][e]]
-    mid = sum(1 for e in range(fired) if ev["claimer"][e] and ev["claim_site"][e] > 0)
-    return {"tflops_median": tf, "pct_of_measured_peak": tf / peak * 100.0, "peak_tflops": peak,
-            "ms_median": med, "yield_run": {
-                "events_fired": fired, "checkpoints": st["yields"], "mid_pipeline_claims": mid,
-                "bitwise_equal_to_uninterrupted": bool(np.array_equal(C.view(np.uint32), C0.view(np.uint32))),
-                "claim_p50_us": pct(cl, 0.5), "claim_p99_us": pct(cl, 0.99),
-                "done_p50_us": pct(dn, 0.5), "done_p99_us": pct(dn, 0.99),
-                "tflops_with_yields": st["bg_tflops"], "checkpoint": ckpt_stats(st)}}
-
-
-def ckpt_stats(st):
-    """Checkpoint traffic of a bf16 yield run: bytes moved between TMEM and
-    the slab, mean CTA wall time per checkpoint and the CTA's GB/s."""
     y = max(int(st["yields"]), 1)
-    out = {}
-    for k in ("spill", "restore"):
-        b, ns = int(st[f"ckpt_{k}_bytes"]), int(st[f"ckpt_{k}_ns"])
-        out[f"{k}_bytes"] = b
-        out[f"{k}_us_mean"] = ns / y / 1e3
-        out[f"{k}_gbs_per_cta"] = b / ns if ns > 0 else None
-    return out
+    return {"tflops": r3(tf), "pct_of_peak": r3(tf / peak * 100.0), "fired": fired, "ckpts": int(st["yields"]),
+            "bitwise": bool(np.array_equal(C.view(np.uint32), C0.view(np.uint32))),
+            "claim_p50": r3(pct(cl, 0.5)), "done_p50": r3(pct(dn, 0.5)),
+            "spill_us": r3(st["ckpt_spill_ns"] / y / 1e3), "restore_us": r3(st["ckpt_restore_ns"] / y / 1e3)}
 
 
 # ---------------------------------------------------------------- our arm
@@ -313,7 +414,6 @@ def run_ours(args, world, rank, local):
     clocks = ClockSampler(dev)
     barrier(world)
     clocks.start()
-    wall0 = time.perf_counter()
     flops = 0.0
     tiles = 0
     launch_ms = []
@@ -327,8 +427,7 @@ def run_ours(args, world, rank, local):
         launch_ms.append(st["launch_ms"])
         yields += st["yields"]
         for k in lats:
-            lats[k] = lats[k] + lat[k] if isinstance(lats[k], list) else lats[k] + lat[k]
-    wall = time.perf_counter() - wall0
+            lats[k] = lats[k] + lat[k]
     barrier(world)
     clk = clocks.stop()
 
@@ -340,15 +439,18 @@ def run_ours(args, world, rank, local):
     hB[:] = B
     for _ in range(2):
         ctx.gemm(hA, hB, hC)
+    barrier(world)  # every rank's copies contend for the host at once, as in the timed steps
     e2e_t = []
     for _ in range(max(3, args.steps)):
         t = time.perf_counter()
         ctx.gemm(hA, hB, hC)
         e2e_t.append(time.perf_counter() - t)
     e2e_tf = 2.0 * M * N * K / statistics.median(e2e_t) / 1e12
-    # single-pass kernel time for the roofline: one 4096^3 drain with the
-    # operands already resident (apk_gemm from host memory streams them in
-    # while the kernel runs, so its launch time includes the transfers)
+    # the copy ceiling: the same buffers and copy streams, no kernel, all
+    # ranks at once (PCIe and host memory are shared between the GPUs)
+    barrier(world)
+    cp = ctx.probe_copy(hA, hB, hC, reps=5)
+    # single-pass kernel time: one 4096^3 drain with the operands resident
     ctx.set_background(A, B)
     ctx.launch((M // info["tile_m"]) * (N // info["tile_n"]))
     ctx.wait(60)
@@ -357,18 +459,26 @@ def run_ours(args, world, rank, local):
     extras = {}
     if not args.no_extras:
         on_ms, off_ms = ctx.run_overhead(info["grid"] * 12, reps=3)
-        extras["poll_cost_pct"] = (on_ms / off_ms - 1.0) * 100.0
-        extras["drain_ms_poll_on"] = on_ms
-        extras["drain_ms_poll_off"] = off_ms
+        extras["poll_cost_pct"] = r3((on_ms / off_ms - 1.0) * 100.0)
         base = ctx.run_baseline(1024, trials=20, seed=21)
-        extras["no_preemption_e2e_us"] = {"p50": pct(list(base), 0.5), "p99": pct(list(base), 0.99)}
+        extras["no_preempt_us"] = {"p50": r3(pct(list(base), 0.5)), "p99": r3(pct(list(base), 0.99))}
     ctx.close()
     if not args.no_extras:
-        extras["device_set"] = device_set_latency(apk_b200, np, dev, A, B, Au, Bu, bg_tasks)
+        extras["device_set"] = device_set_latency(apk_b200, dev, A, B, Au, Bu, bg_tasks)
         extras["bf16_config2"] = bf16_config2(apk_b200, np, dev)
 
-    res = {"flops": flops, "launch_s": sum(launch_ms) / 1e3, "lats": lats, "wall": wall, "clk": clk,
-           "e2e_tf": e2e_tf, "extras": extras, "info": info, "yields": yields,
+    c4 = None
+    if not args.no_config4:
+        from apk_b200 import config4
+        barrier(world)  # the shards drain concurrently on all GPUs
+        c4_res, ex0, ex1 = config4.run_rank(dev, world, rank, args.config4_tasks)
+        counts = config4.union_counts(world, ex0, ex1)
+        c4_all = allgather_obj(world, c4_res)
+        if rank == 0:
+            c4 = config4.summarize(c4_all, counts, args.config4_tasks)
+
+    res = {"flops": flops, "launch_s": sum(launch_ms) / 1e3, "lats": lats, "clk": clk,
+           "e2e_tf": e2e_tf, "copy": cp, "extras": extras, "info": info, "yields": yields,
            "one_pass_ms": one_pass["launch_ms"], "one_pass_tiles": one_pass["tiles_done"],
            "tiles": tiles, "launch_ms": launch_ms}
     allr = allgather_obj(world, res)
@@ -386,85 +496,75 @@ def run_ours(args, world, rank, local):
         anomalies += r["lats"]["anomalies"]
     clk = allr[0]["clk"]
     sm_mhz = clk.get("sm_mhz") or 1965.0
-    fp32_peak_nominal = SMS_B200 * 128 * 2 * 1965e6 / 1e12
     fp32_peak_clock = SMS_B200 * 128 * 2 * sm_mhz * 1e6 / 1e12
-    per_gpu = value / world
     # the dominant kernel's launches inside the timed region (rank 0): the
     # algorithmic FLOPs of the tiles they completed / their summed
     # CUDA-event durations, i.e. FLOPs per launch / average launch time
     r0 = allr[0]
+    nl = max(1, len(r0["launch_ms"]))
     achieved = 2.0 * 128 * 128 * K * r0["tiles"] / (sum(r0["launch_ms"]) / 1e3) / 1e12
     one_drain = 2.0 * 128 * 128 * K * r0["one_pass_tiles"] / (r0["one_pass_ms"] / 1e3) / 1e12
-    # DRAM bytes per launch: the ncu capture's per-tile traffic (read + write)
-    # scaled to the average tiles of a timed launch
-    traffic = None
-    tp = os.path.join(ROOT, "profiles", "sgemm_f32_ws_4096.md")
-    if os.path.exists(tp):
-        for ln in open(tp):
-            if ln.startswith("dram_bytes_per_tile:"):
-                traffic = float(ln.split(":", 1)[1]) * r0["tiles"] / max(1, len(r0["launch_ms"]))
+    gemm_flop = 2.0 * M * N * K
+    copy_ceiling = sum(gemm_flop / (r["copy"]["h2d_ms"] / 1e3) / 1e12 for r in allr)
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": tmax * 1e3 / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "configs[1]: persistent fp32 SGEMM 4096^3 background, 128x128 tiles, K-tile 32, "
-                               "full residency; urgent fp32 256^3 injected by the host (flag via cudaMemcpyAsync) at a "
-                               "uniform time in every 1 ms period",
-                   "M": M, "N": N, "K": K, "urgent": [U, U, U], "events_per_step": args.events_per_step,
-                   "period_us": args.period_us, "grid": allr[0]["info"]["grid"],
-                   "ctas_per_sm": allr[0]["info"]["ctas_per_sm"], "poll": "stage", "set": "host_memcpy",
-                   "urgent_split_k": 8, "l2": "inputs larger than L2: A+B+C = 192 MB > 126 MB",
-                   "parallelism": f"{world} independent replicas (no collectives)"},
-        "latency_us": {
-            "events": len(L["claim_after_first_obs"]) + unclaimed, "unclaimed": unclaimed, "anomalies": anomalies,
-            "preempt_p50": pct(L["rt_claim"], 0.5), "preempt_p99": pct(L["rt_claim"], 0.99),
-            "urgent_done_p50": pct(L["rt_done"], 0.5), "urgent_done_p99": pct(L["rt_done"], 0.99),
-            "device_claim_after_first_observer_p50": pct(L["claim_after_first_obs"], 0.5),
-            "device_claim_after_first_observer_p99": pct(L["claim_after_first_obs"], 0.99),
-            "device_observation_spread_p50": pct(L["spread"], 0.5),
-            "device_observation_spread_p99": pct(L["spread"], 0.99),
-            "device_done_after_claim_p50": pct(L["done_after_claim"], 0.5),
-            "device_done_after_claim_p99": pct(L["done_after_claim"], 0.99),
-            "definition": "preempt = host store of the yield flag -> host sees the device's claim ack (the "
-                          "first popper of the urgent work, acked through mapped memory), host clock, no "
-                          "clock mapping; urgent_done = host store -> host sees the last urgent item's ack; "
-                          "device_* are globaltimer intervals from the first CTA to observe the flag "
-                          "(src/yield.cu:148-153); extras.device_set measures set->claim in one clock",
-        },
-        "bg_pct_of_fp32_peak": {"nominal_1965MHz": per_gpu / fp32_peak_nominal * 100.0,
-                                "at_measured_clock": per_gpu / fp32_peak_clock * 100.0},
-        "yields": sum(r["yields"] for r in allr),
+        "gpu_launches": args.steps,
+        "config": {"workload": "configs[1]: fp32 4096^3 persistent SGEMM background, 128x128 tiles, K-tile 32, "
+                               "full residency; urgent fp32 256^3 host-injected once per 1 ms",
+                   "events_per_step": args.events_per_step, "grid": r0["info"]["grid"],
+                   "ctas_per_sm": r0["info"]["ctas_per_sm"], "poll": "stage", "set": "host_memcpy",
+                   "urgent_split_k": 8, "l2": "inputs > L2 (A+B+C 192 MB)",
+                   "parallelism": f"{world} ranks, no collectives; configs[1] per rank, configs[4] sharded"},
         "roofline": {"bound": "fp32_fma", "achieved": achieved, "peak": fp32_peak_clock, "unit": "TFLOP/s",
-                     "frac": achieved / fp32_peak_clock, "traffic": traffic,
-                     "peak_source": f"148 SMs x 128 FP32 lanes x 2 x {sm_mhz:.0f} MHz (median SM clock sampled "
-                                    "under load); MEASURED_PEAKS.json has no FP32 CUDA-core figure",
-                     "kernel": "apk::f32ws::sgemm_ws<POLL_STAGE, DRAIN>: the timed steps' bounded launches "
-                               "(4096^3 background tiles under urgent injections)",
-                     "launches": len(r0["launch_ms"]), "tiles_per_launch": r0["tiles"] / max(1, len(r0["launch_ms"])),
-                     "one_drain_tflops": one_drain},
+                     "frac": achieved / fp32_peak_clock,
+                     "traffic": F32WS_DRAM_BYTES_PER_TILE * r0["tiles"] / nl,
+                     "peak_source": f"148 SMs x 128 lanes x 2 x {sm_mhz:.0f} MHz (sampled); no FP32 figure "
+                                    "in MEASURED_PEAKS.json",
+                     "kernel": "f32ws::sgemm_ws<POLL_STAGE,DRAIN>", "launches": nl,
+                     "tiles_per_launch": r0["tiles"] / nl, "one_drain_tflops": r3(one_drain)},
+        "clocks": clk,
         "e2e": {"value": sum(r["e2e_tf"] for r in allr), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": 2 * M * K * 4, "d2h_bytes_per_step": M * N * 4,
-                "path": "apk_gemm with pinned host A, B -> C: A row panels and B column panels stream in "
-                        "(interleaved) while the persistent kernel runs, C blocks stream back as they finish"},
-        "gpu_launches": args.steps,
-        "clocks": clk,
+                "copy_ceiling": r3(copy_ceiling),
+                "copy_ms": {k: r3(r0["copy"][k]) for k in ("h2d_ms", "d2h_ms", "both_ms")}},
         "gpu": gpu_identity(local),
         "extras": allr[0]["extras"],
     }
-    if rank == 0 and world == 1 and not args.no_extras:
+    if world == 1 and not args.no_extras:
         try:
-            v, rows, th, dt = cpu_gemm_sample()
-            line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": th, "kind": "port",
-                                    "sample": f"{rows} of {M} rows of the 4096^3 float64 product "
-                                              f"({dt:.1f} s), OpenMP row-parallel restatement of "
-                                              "src/persistent.cu:221-227", "cpu": cpu_desc()}
+            import oracle
+            Ao, Bo = oracle.gen_uniform(M, N, K, 21)
+            v, rows, dt = cpu_single_core(oracle, Ao, Bo)
+            line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+                                    "sample": f"{rows} of {M} rows of the 4096^3 float64 product ({dt:.1f} s), "
+                                              "the reference's loop single-threaded as shipped",
+                                    "cpu": cpu_desc()}
+            va, ra, th, dta = cpu_all_cores(oracle, Ao, Bo)
+            line["cpu_all_cores"] = {"value": va, "unit": "TFLOP/s", "cores": th, "kind": "port",
+                                     "sample": f"{ra} rows, OpenMP row-parallel ({dta:.1f} s)"}
         except Exception as e:  # the GPU number stands without it
             line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+    if c4 is not None:
+        line["config4"] = {k: (r3(v) if isinstance(v, float) else v) for k, v in c4.items()}
+    line["latency_us"] = {
+        "events": len(L["claim_after_first_obs"]) + unclaimed, "unclaimed": unclaimed, "anomalies": anomalies,
+        "preempt_p50": r3(pct(L["rt_claim"], 0.5)), "preempt_p99": r3(pct(L["rt_claim"], 0.99)),
+        "urgent_done_p50": r3(pct(L["rt_done"], 0.5)), "urgent_done_p99": r3(pct(L["rt_done"], 0.99)),
+        "dev_claim_p50": r3(pct(L["claim_after_first_obs"], 0.5)),
+        "dev_claim_p99": r3(pct(L["claim_after_first_obs"], 0.99)),
+        "dev_spread_p50": r3(pct(L["spread"], 0.5)), "dev_spread_p99": r3(pct(L["spread"], 0.99)),
+        "dev_done_p50": r3(pct(L["done_after_claim"], 0.5)), "dev_done_p99": r3(pct(L["done_after_claim"], 0.99)),
+    }
     print(json.dumps(line), flush=True)
 
 
 def main():
     args = parse()
+    if args.case:
+        run_case(args)
+        return
     world, rank, local = dist_setup(args)
     try:
         if args.impl == "reference":

@@ -272,6 +272,15 @@ apk_status apk_read_run_stats(apk_ctx* ctx, apk_run_stats* st);
 apk_status apk_gemm(apk_ctx* ctx, const void* A, const void* B, void* C, int M, int N, int K,
                     apk_mem_kind kind);
 
+/* Copy ceiling of apk_gemm from host memory: the host buffers, device
+ * buffers and copy streams of this context's last host-memory apk_gemm,
+ * with no kernel.  out_ms[0]: A and B host->device; out_ms[1]: C
+ * device->host; out_ms[2]: both at once on their two streams (medians of
+ * reps, host clock around the stream synchronisations).  2*M*N*K /
+ * out_ms[0] bounds what apk_gemm can reach from host memory.  No reference
+ * counterpart (the reference times no transfer). */
+apk_status apk_probe_copy(apk_ctx* ctx, const void* A, const void* B, void* C, int reps, double* out_ms);
+
 /* ---- harness modes (the reference binaries' --mode switches) ---------- */
 
 typedef struct apk_latency_config {
@@ -468,9 +477,29 @@ int apk_shard_tasks(const apk_task* tasks, int n, int world, int rank, int* idx)
  * call is asynchronous on `stream` (a cudaStream_t, NULL = the legacy
  * default stream).  Every call shares the array: calls issued in order on
  * one stream are independent (the queue header is cleared on that stream
- * first), calls that overlap on the GPU race and must not be made. */
+ * first), calls that overlap on the same device (e.g. on two streams) race
+ * and must not be made; each device has its own array.  A bounded device
+ * wait that runs out (2 s) leaves C incomplete and is not visible in the
+ * return code, which comes back before the kernel runs: read it with
+ * apk_sgemm_f32_noalloc_status. */
 apk_status apk_sgemm_f32_noalloc(const float* A, const float* B, float* C, int M, int N, int K, int grid,
                                  void* stream);
+
+/* Device status of the last apk_sgemm_f32_noalloc call on the current
+ * device: synchronizes `stream` (the call's stream), then copies the status
+ * word out of the static scratch into *device_status -- 0, or the code of
+ * the wait that ran out (3 = a spin, 1 = a pipeline-stage wait).  Allocates
+ * nothing.  Calls overlapping on the device would overwrite the word; the
+ * next apk_sgemm_f32_noalloc clears it.  No counterpart in the reference
+ * (its waits are unbounded). */
+apk_status apk_sgemm_f32_noalloc_status(void* stream, int* device_status);
+
+/* Failure-path self-test of the status word above: queues on `stream` a
+ * bounded spin on a scratch word nothing sets, which gives up after
+ * limit_ns (at most 10 s) and records 3 (DEV_WAIT_TIMEOUT_SPIN) as a
+ * timed-out GEMM would.  apk_sgemm_f32_noalloc_status then reports it; the
+ * device stays usable.  Allocates nothing.  No counterpart in the reference. */
+apk_status apk_sgemm_f32_noalloc_selftest(long long limit_ns, void* stream);
 
 /* ---- data and memory helpers ----------------------------------------- */
 

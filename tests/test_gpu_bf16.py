@@ -77,14 +77,15 @@ def test_config2_shape_sampled_rows(libapk):
     _check_rows(C, A, B, [(0, 8), (255, 2), (4096 + 128, 8), (M - 8, 8)])
 
 
-def _yield_run(poll, nev=30, gap_ns=20_000, discipline="drain"):
-    M = N = K = 4096
+def _yield_run(poll, nev=30, gap_ns=20_000, discipline="drain", n=4096, drains=0):
+    M = N = K = n
     A, B = _normal((M, K), 21), _normal((K, N), 22)
     Au, Bu = _normal((256, 256), 31), _normal((256, 256), 32)
     with _ctx(poll="off") as c:
         Cref = c.gemm(A, B)
-    with _ctx(poll=poll, set_mode="device", oracle=True, discipline=discipline) as c:
-        ntasks = 1024
+    with _ctx(poll=poll, set_mode="device", oracle=True, discipline=discipline, max_events=max(64, nev + 8)) as c:
+        # task t computes tile t mod tiles: 1024 tasks, or whole drains of C
+        ntasks = drains * (M // c.info["tile_m"]) * (N // c.info["tile_n"]) if drains else 1024
         c.set_background(A, B)
         c.set_urgent(Au, Bu)
         c.schedule_device_events((np.arange(nev, dtype=np.int64) + 1) * gap_ns)
@@ -125,6 +126,27 @@ def test_stage_checkpoint_resume_is_bitwise(libapk):
     for Cu in r["outs"]:
         mr, bad, nans = oracle.check(Cu, r["refu"], TOL)
         assert bad == 0 and nans == 0
+    f = r["fired"]
+    v = oracle.exactly_once(r["ex"], r["ue"][:f], ev["claimer"][:f], ev["set_ns"][:f], r["uitems"], f)
+    assert v["pass"], v
+
+
+def test_config2_full_shape_stage_yields_bitwise(libapk):
+    """configs[2] at its own size, 8192^3: yields at random pipeline stages
+    (40 device-set events 15 us apart, inside two ~0.7 ms drains), including
+    buffer-conflicting ones; the resumed output is bitwise equal to the
+    uninterrupted run, every tile and urgent item ran exactly once and every
+    urgent output matches float64."""
+    r = _yield_run("stage", nev=40, gap_ns=15_000, n=8192, drains=2)
+    ev = r["ev"]
+    assert r["fired"] >= 20 and r["st"]["yields"] > 0
+    claimed = [e for e in range(r["fired"]) if ev["claimer"][e]]
+    assert any(ev["claim_site"][e] > 0 for e in claimed), "no mid-pipeline claim"
+    assert any(ev["inflight"][e] > 0 for e in claimed), "no buffer-conflicting yield"
+    assert np.array_equal(r["C"].view(np.uint32), r["Cref"].view(np.uint32)), "resume not bitwise"
+    for Cu in r["outs"]:
+        mr, bad, nans = oracle.check(Cu, r["refu"], TOL)
+        assert bad == 0 and nans == 0, f"urgent: {bad} bad, max rel {mr:.3e}"
     f = r["fired"]
     v = oracle.exactly_once(r["ex"], r["ue"][:f], ev["claimer"][:f], ev["set_ns"][:f], r["uitems"], f)
     assert v["pass"], v

@@ -123,3 +123,18 @@ def test_urgent_preemption_keeps_checksums_bitwise(whole_run):
     for Cu in outs:
         assert oracle.check(Cu, refu, oracle.BF16_TOL)[1] == 0
     assert all(ue[e] == items for e in range(fired) if ev["claimer"][e])
+
+
+def test_config4_poisson_host_stream_2e16_tasks(libapk):
+    """configs[4] on 2^16 tasks with its own arrival process: urgent 256^3
+    GEMMs injected by the host as a 2 kHz Poisson stream while the shard
+    drains.  Every half-tile runs exactly once in both drains, no half-tile's
+    checksum changes under preemption, every arrival is claimed and its
+    urgent output is complete (src/yield.cu:576-667 verdict)."""
+    from apk_b200 import config4
+    res, ex0, ex1 = config4.run_rank(0, 1, 0, n_tasks=1 << 16, seed=SEED, rate_hz=2000.0)
+    out = config4.summarize([res], config4.union_counts(1, ex0, ex1), 1 << 16)
+    assert out["exactly_once"], res
+    assert out["corrupted"] == 0
+    assert out["arrivals"] >= 20 and out["urgent_claimed"] == out["arrivals"], res
+    assert out["urgent_outputs_ok"] and out["checkpoints"] > 0

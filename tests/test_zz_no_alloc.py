@@ -58,7 +58,8 @@ def test_noalloc_rejects_beyond_limits(libapk):
     dB = torch.zeros((32, 128), dtype=torch.float32, device="cuda")
     dC = torch.zeros((128, 128), dtype=torch.float32, device="cuda")
     p = [ctypes.c_void_p(t.data_ptr()) for t in (dA, dB, dC)]
-    # a grid whose per-CTA counters exceed the static scratch array
+    # a grid beyond the kernel's residency (2 CTAs per SM) is refused before
+    # the scratch-size check, whose 2016-CTA limit no B200 grid reaches
     assert libapk.apk_sgemm_f32_noalloc(*p, 128, 128, 32, 100000, None) == 1  # APK_EINVAL
     # a shape that is not tile-aligned
     assert libapk.apk_sgemm_f32_noalloc(*p, 100, 128, 32, 0, None) == 1
@@ -66,3 +67,32 @@ def test_noalloc_rejects_beyond_limits(libapk):
     assert libapk.apk_sgemm_f32_noalloc(*p, 128, 128, 32, 0, None) == 0
     torch.cuda.synchronize()
     assert float(dC.abs().sum()) == 0.0
+    st = ctypes.c_int(-1)
+    assert libapk.apk_sgemm_f32_noalloc_status(None, ctypes.byref(st)) == 0
+    assert st.value == 0
+
+
+def test_noalloc_status_reports_a_wait_that_ran_out(libapk):
+    """A kernel whose bounded wait gives up leaves C incomplete while the
+    asynchronous call has already returned APK_OK: the status query must show
+    it.  The self-test queues the same kind of bounded spin on a scratch word
+    nothing sets (no fault, no hang: it gives up after 50 ms), then a normal
+    call clears the word again."""
+    import torch
+
+    st = ctypes.c_int(-1)
+    assert libapk.apk_sgemm_f32_noalloc_selftest(50_000_000, None) == 0
+    assert libapk.apk_sgemm_f32_noalloc_status(None, ctypes.byref(st)) == 0
+    assert st.value == 3  # DEV_WAIT_TIMEOUT_SPIN
+
+    A, B = oracle.gen_uniform(256, 256, 128, 5)
+    dA = torch.from_numpy(A).cuda()
+    dB = torch.from_numpy(B).cuda()
+    dC = torch.full((256, 256), float("nan"), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    assert libapk.apk_sgemm_f32_noalloc(ctypes.c_void_p(dA.data_ptr()), ctypes.c_void_p(dB.data_ptr()),
+                                        ctypes.c_void_p(dC.data_ptr()), 256, 256, 128, 0, None) == 0
+    assert libapk.apk_sgemm_f32_noalloc_status(None, ctypes.byref(st)) == 0
+    assert st.value == 0
+    mr, bad, nans = oracle.check(dC.cpu().numpy(), oracle.gemm_f64(A, B), oracle.fp32_tol(128))
+    assert bad == 0 and nans == 0, f"{bad} bad, {nans} NaN, max rel {mr:.3e}"
