@@ -40,7 +40,7 @@ class DeviceInfo(ctypes.Structure):
     _fields_ = [("sms", c_int), ("grid", c_int), ("ctas_per_sm", c_int), ("max_ctas_per_sm", c_int),
                 ("cc_major", c_int), ("cc_minor", c_int), ("smem_per_cta", c_int),
                 ("threads_per_cta", c_int), ("tile_m", c_int), ("tile_n", c_int), ("k_tile", c_int),
-                ("stages", c_int), ("name", ctypes.c_char * 128)]
+                ("stages", c_int), ("name", ctypes.c_char * 128), ("slot_k", c_int)]
 
 
 class EventLog(ctypes.Structure):

@@ -337,7 +337,8 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
       }
       bool resume = false;
       for (int c = 0; c < nk && ok; ++c) {
-        if (POLL == POLL_STAGE) {
+        // a yield site every poll_every ring slots (one K-tile)
+        if (POLL == POLL_STAGE && (p.poll_every <= 1 || c % p.poll_every == 0)) {
           const int fs = vload(&sh.gen);
           if (fs < 0) {
             ok = false;  // stop sentinel: abandon the tile

@@ -365,7 +365,8 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
       }
       bool resume = false;
       for (int c = 0; c < p.nk && ok; ++c) {
-        if (POLL == POLL_STAGE) {
+        // a yield site every poll_every ring slots (one K-tile)
+        if (POLL == POLL_STAGE && (p.poll_every <= 1 || c % p.poll_every == 0)) {
           const int fs = vload(&sh.gen);
           if (fs < 0) {
             ok = false;

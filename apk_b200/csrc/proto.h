@@ -150,7 +150,10 @@ struct F32Params {
   CUtensorMap tmAu;  // urgent A
   CUtensorMap tmBu;  // urgent B
   float* C;
-  int ldc, tiles_n, total_tiles, nk;   // nk = K / BK
+  int ldc, tiles_n, total_tiles, nk;   // nk = K / BK (ring slots per tile)
+  int poll_every;                      // ring slots per stage-level yield site:
+                                       // the K-tile (depth between yield sites)
+                                       // over the ring slot's K depth
   float* Cu;                           // urgent output, one slot per event
   long long cu_stride;                 // floats between event slots
   int ldcu, utiles_n, usplit, unk, uitems;  // unk = stages per urgent item
@@ -167,6 +170,16 @@ struct F32Params {
   QueueProto q;
   StreamProto st;
 };
+
+// A kernel geometry as the host sees it: output tile, threads per CTA, the
+// K depth and count of the ring slots, the K depth of one A box, dynamic
+// shared memory.  fp32 block-synchronous geometries (sgemm_f32.cu): L32 and
+// L64 (128x128 tiles, 32- or 64-deep slots), M (64x128) and S (32x128) for
+// 4 and 8 resident CTAs per SM.
+struct GeoInfo {
+  int tile_m, tile_n, threads, slot_k, stages, a_box_k, smem_bytes;
+};
+enum F32Geo : int { F32_GEO_L32 = 0, F32_GEO_L64 = 1, F32_GEO_M = 2, F32_GEO_S = 3 };
 
 // Visibility microbenchmark parameters (the flag-notification probe of
 // src/yield.cu:227-293, decoupled from tile work).

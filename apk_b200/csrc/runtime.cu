@@ -23,12 +23,10 @@
 
 namespace apk {
 namespace f32 {
-cudaError_t prepare(int poll, int disc, bool oracle, int bk, int sched, int* max_ctas_per_sm);
-cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int bk, int sched,
+cudaError_t prepare(int poll, int disc, bool oracle, int geo, int sched, int* max_ctas_per_sm);
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int geo, int sched,
                    cudaStream_t stream);
-int smem_bytes(int bk);
-int stages(int bk);
-int threads();
+GeoInfo geo_info(int geo);
 size_t params_bytes();
 }  // namespace f32
 namespace bf16pair {
@@ -126,6 +124,11 @@ struct apk_ctx {
   // block-synchronous kernel for experiments that compare grids slot by slot
   bool ws_ok = false;
   bool sync_only = false;
+  // geometry and ring: fp32 block-synchronous tile geometry (F32Geo), the K
+  // depth of one ring slot and the slots per stage-level yield site
+  int f32_geo = F32_GEO_L32;
+  int slot_k = 32;
+  int poll_every = 1;
   // bf16: the CTA-pair kernel can run every poll variant this context
   // launches with every SM in a pair
   bool pair_ok = false;
@@ -275,8 +278,12 @@ size_t esize_of(apk_dtype d) { return d == APK_BF16 ? 2 : 4; }
 // Output tiles: fp32 128x128; bf16 256 rows by 256 columns, the last tile of
 // a row 128 wide when the width is an odd multiple of 128.
 bool use_pair(const apk_ctx* ctx);
-int tile_rows(const apk_ctx* ctx) { return ctx->cfg.dtype == APK_F32 ? 128 : 256; }
-int tile_cols(const apk_ctx* ctx) { return ctx->cfg.dtype == APK_F32 ? 128 : use_pair(ctx) ? 512 : 256; }
+int tile_rows(const apk_ctx* ctx) {
+  return ctx->cfg.dtype == APK_F32 ? f32::geo_info(ctx->f32_geo).tile_m : 256;
+}
+int tile_cols(const apk_ctx* ctx) {
+  return ctx->cfg.dtype == APK_F32 ? f32::geo_info(ctx->f32_geo).tile_n : use_pair(ctx) ? 512 : 256;
+}
 int tiles_across(const apk_ctx* ctx, int n) { return (n + tile_cols(ctx) - 1) / tile_cols(ctx); }
 
 apk_status upload(apk_ctx* ctx, void** dst, bool* own, size_t* cap, const void* src, size_t bytes,
@@ -305,22 +312,22 @@ apk_status prepare_kernel(apk_ctx* ctx, int poll) {
   int maxc = 0;
   cudaError_t e;
   if (ctx->cfg.dtype == APK_F32)
-    e = f32::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->cfg.k_tile, ctx->cfg.scheduler, &maxc);
+    e = f32::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->f32_geo, ctx->cfg.scheduler, &maxc);
   else
-    e = bf16::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->cfg.k_tile, &maxc);
+    e = bf16::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->slot_k, &maxc);
   if (e != cudaSuccess)
     return fail(ctx, APK_EUNSUPPORTED, "kernel variant unavailable (dtype %d poll %d disc %d oracle %d k_tile %d): %s",
                 ctx->cfg.dtype, poll, ctx->cfg.discipline, ctx->cfg.oracle, ctx->cfg.k_tile,
                 cudaGetErrorString(e));
   if (maxc < 1) return fail(ctx, APK_EUNSUPPORTED, "kernel does not fit on an SM");
   ctx->max_ctas_per_sm = maxc;
-  if (ctx->cfg.dtype == APK_F32 && ctx->cfg.scheduler == APK_SCHED_QUEUE && ctx->cfg.k_tile == 32) {
+  if (ctx->cfg.dtype == APK_F32 && ctx->cfg.scheduler == APK_SCHED_QUEUE && ctx->f32_geo == F32_GEO_L32) {
     int ok = 0;
     e = f32ws::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, &ok);
     if (e != cudaSuccess) ok = 0;
     ctx->ws_ok = ctx->ws_ok && ok;
   }
-  if (ctx->cfg.dtype == APK_BF16 && ctx->cfg.k_tile == 64) {
+  if (ctx->cfg.dtype == APK_BF16 && ctx->slot_k == 64) {
     int pairs = 0;
     e = bf16pair::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->sms, &pairs);
     if (e != cudaSuccess) pairs = 0;
@@ -334,7 +341,7 @@ apk_status prepare_kernel(apk_ctx* ctx, int poll) {
 // CTA per SM over every SM; the one-CTA kernel runs everything else.
 bool use_pair(const apk_ctx* ctx) {
   return ctx->cfg.dtype == APK_BF16 && ctx->pair_ok && ctx->cfg.bf16_kernel != APK_BF16_SINGLE &&
-         !ctx->task_mode && ctx->cfg.k_tile == 64 && ctx->grid == ctx->sms && ctx->N % 256 == 0 &&
+         !ctx->task_mode && ctx->slot_k == 64 && ctx->grid == ctx->sms && ctx->N % 256 == 0 &&
          ctx->Nu % 256 == 0;
 }
 
@@ -346,7 +353,7 @@ bool use_pair(const apk_ctx* ctx) {
 bool use_ws(const apk_ctx* ctx) {
   return ctx->cfg.dtype == APK_F32 && ctx->ws_ok && !ctx->sync_only && ctx->cfg.f32_kernel != APK_F32_BLOCK_SYNC &&
          ctx->cfg.scheduler == APK_SCHED_QUEUE &&
-         ctx->cfg.k_tile == 32 && ctx->grid == ctx->sms * f32ws::workers_per_cta();
+         ctx->f32_geo == F32_GEO_L32 && ctx->grid == ctx->sms * f32ws::workers_per_cta();
 }
 
 }  // namespace
@@ -392,11 +399,26 @@ apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
   if (c.urgent_split_k < 1) c.urgent_split_k = 1;
   if (c.wait_limit_ns <= 0) c.wait_limit_ns = 2000000000LL;
   if (c.k_tile == 0) c.k_tile = c.dtype == APK_BF16 ? 64 : 32;
-  if (c.k_tile != 32 && c.k_tile != 64) {
-    fail(ctx, APK_EINVAL, "k_tile must be 32 or 64");
+  if (c.k_tile != 32 && c.k_tile != 64 && c.k_tile != 128) {
+    fail(ctx, APK_EINVAL, "k_tile must be 32, 64 or 128");
     *out = ctx;
     return APK_EINVAL;
   }
+  // Geometry and ring.  The K-tile is the K depth between two stage-level
+  // yield sites; each kernel moves it through ring slots of its own depth
+  // (fp32 128x128 tiles: 32, or 64 at one CTA per SM; 64x128 and 32x128
+  // tiles for 4 and 8 CTAs per SM: 16; bf16: 64, or 32 for K-tile 32) and
+  // polls every k_tile / slot_k slots.
+  if (c.dtype == APK_F32) {
+    ctx->f32_geo = c.ctas_per_sm >= 8   ? F32_GEO_S
+                   : c.ctas_per_sm >= 4 ? F32_GEO_M
+                   : (c.ctas_per_sm == 1 && c.k_tile >= 64) ? F32_GEO_L64
+                                                             : F32_GEO_L32;
+    ctx->slot_k = f32::geo_info(ctx->f32_geo).slot_k;
+  } else {
+    ctx->slot_k = c.k_tile == 32 ? 32 : 64;
+  }
+  ctx->poll_every = c.k_tile / ctx->slot_k;
   if (c.discipline == APK_DISC_POISON && c.poll == APK_POLL_OFF) {
     fail(ctx, APK_EINVAL, "the poison discipline needs a poll mode");
     *out = ctx;
@@ -576,13 +598,14 @@ apk_status apk_get_info(apk_ctx* ctx, apk_device_info* info) {
     info->threads_per_cta = f32ws::threads();
     info->tile_m = 128;
     info->tile_n = 128;
-    info->stages = f32::stages(ctx->cfg.k_tile);
+    info->stages = f32::geo_info(F32_GEO_L32).stages;
   } else if (ctx->cfg.dtype == APK_F32) {
-    info->smem_per_cta = f32::smem_bytes(ctx->cfg.k_tile);
-    info->threads_per_cta = f32::threads();
-    info->tile_m = 128;
-    info->tile_n = 128;
-    info->stages = f32::stages(ctx->cfg.k_tile);
+    const GeoInfo g = f32::geo_info(ctx->f32_geo);
+    info->smem_per_cta = g.smem_bytes;
+    info->threads_per_cta = g.threads;
+    info->tile_m = g.tile_m;
+    info->tile_n = g.tile_n;
+    info->stages = g.stages;
   } else if (use_pair(ctx)) {
     info->smem_per_cta = bf16pair::smem_bytes();
     info->threads_per_cta = bf16pair::threads();
@@ -590,13 +613,14 @@ apk_status apk_get_info(apk_ctx* ctx, apk_device_info* info) {
     info->tile_n = 512;  // one tile per CTA pair
     info->stages = bf16pair::stages();
   } else {
-    info->smem_per_cta = bf16::smem_bytes(ctx->cfg.k_tile);
+    info->smem_per_cta = bf16::smem_bytes(ctx->slot_k);
     info->threads_per_cta = bf16::threads();
     info->tile_m = 256;
     info->tile_n = 256;
-    info->stages = bf16::stages(ctx->cfg.k_tile);
+    info->stages = bf16::stages(ctx->slot_k);
   }
   info->k_tile = ctx->cfg.k_tile;
+  info->slot_k = ctx->slot_k;
   snprintf(info->name, sizeof info->name, "%s", ctx->name);
   return APK_OK;
 }
@@ -740,10 +764,10 @@ apk_status apk_set_urgent(apk_ctx* ctx, const void* A, const void* B, int M, int
   if (ctx->running) return fail(ctx, APK_ESTATE, "set_urgent while a launch runs");
   const int split = ctx->cfg.urgent_split_k;
   const int tm = ctx->cfg.dtype == APK_F32 ? 128 : 256;
-  if (M <= 0 || N <= 0 || K <= 0 || M % tm || N % 128 || K % (ctx->cfg.k_tile * split))
+  if (M <= 0 || N <= 0 || K <= 0 || M % tm || N % 128 || K % (ctx->slot_k * split))
     return fail(ctx, APK_EINVAL,
-                "urgent shape %dx%dx%d: M a multiple of %d, N of 128, K of k_tile*split (%d)", M, N, K,
-                tm, ctx->cfg.k_tile * split);
+                "urgent shape %dx%dx%d: M a multiple of %d, N of 128, K of slot depth*split (%d)", M, N, K,
+                tm, ctx->slot_k * split);
   APK_CU(cudaSetDevice(ctx->cfg.device));
   const size_t es = esize_of(ctx->cfg.dtype);
   size_t capAu = 0, capBu = 0;
@@ -920,19 +944,24 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
   cudaError_t e;
   if (record) APK_CU(cudaEventRecord(ctx->ev_start, stream));
   const bool f32 = ctx->cfg.dtype == APK_F32;
-  const int bk = ctx->cfg.k_tile;
+  const int bk = ctx->slot_k;  // K depth of one ring slot
   const int tm = tile_rows(ctx);
   F32Params p;
   memset(&p, 0, sizeof p);
   {
-    // fp32: A as [128 rows][32 k] boxes (128B swizzle), B as [BK k][128 n]
-    // boxes (no swizzle).  bf16: A as [128 rows][BK k] boxes, one swizzle
-    // span per row (128B for BK 64, 64B for BK 32), and B as [BK k][64 n]
-    // boxes, 128B swizzled (the tcgen05 canonical K- / MN-major atoms).
+    // fp32: A as [tile rows][32 or 16 k] boxes (128B or 64B swizzle: one
+    // swizzle span per row), B as [BK k][tile cols] boxes (no swizzle); the
+    // warp-specialized kernel uses the 128x128 / 32 ones.  bf16: A as
+    // [<=128 rows][BK k] boxes, one swizzle span per row (128B for BK 64,
+    // 64B for BK 32), and B as [BK k][64 n] boxes, 128B swizzled (the
+    // tcgen05 canonical K- / MN-major atoms).
     const CUtensorMapDataType dt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     const int es = f32 ? 4 : 2;
-    const int a_box_k = f32 ? 32 : bk, b_box_n = f32 ? 128 : 64;
-    const CUtensorMapSwizzle asw = (f32 || bk == 64) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    const GeoInfo fg = f32::geo_info(ctx->f32_geo);
+    const int a_box_k = f32 ? fg.a_box_k : bk, b_box_n = f32 ? fg.tile_n : 64;
+    const int a_box_m = f32 ? fg.tile_m : 128;
+    const CUtensorMapSwizzle asw = (f32 ? a_box_k == 32 : bk == 64) ? CU_TENSOR_MAP_SWIZZLE_128B
+                                                                    : CU_TENSOR_MAP_SWIZZLE_64B;
     const CUtensorMapSwizzle bsw = f32 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B;
     apk_status t;
     // task mode: the maps cover the operand pools, tasks are windows of them
@@ -941,10 +970,10 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
     const void* srcB = tk ? ctx->dBpool : ctx->dB;
     const long long ar = tk ? ctx->a_rows : ctx->M, ac = tk ? ctx->a_cols : ctx->K;
     const long long br = tk ? ctx->b_rows : ctx->K, bc = tk ? ctx->b_cols : ctx->N;
-    if ((t = make_tmap(ctx, &p.tmA, srcA, dt, es, ar, ac, a_box_k, 128, asw)) != APK_OK) return t;
+    if ((t = make_tmap(ctx, &p.tmA, srcA, dt, es, ar, ac, a_box_k, a_box_m, asw)) != APK_OK) return t;
     if ((t = make_tmap(ctx, &p.tmB, srcB, dt, es, br, bc, b_box_n, bk, bsw)) != APK_OK) return t;
     if (ctx->dAu) {
-      if ((t = make_tmap(ctx, &p.tmAu, ctx->dAu, dt, es, ctx->Mu, ctx->Ku, a_box_k, 128, asw)) != APK_OK)
+      if ((t = make_tmap(ctx, &p.tmAu, ctx->dAu, dt, es, ctx->Mu, ctx->Ku, a_box_k, a_box_m, asw)) != APK_OK)
         return t;
       if ((t = make_tmap(ctx, &p.tmBu, ctx->dBu, dt, es, ctx->Ku, ctx->Nu, b_box_n, bk, bsw)) != APK_OK) return t;
     } else {
@@ -976,6 +1005,7 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
   p.usplit = ctx->cfg.urgent_split_k;
   p.unk = ctx->Ku ? ctx->Ku / bk / p.usplit : 0;
   p.uitems = (ctx->Mu / tm) * p.utiles_n * p.usplit;
+  p.poll_every = ctx->poll_every;
   p.slab = ctx->d_slab;
   p.slab_hdr = ctx->d_slab_hdr;
   p.wait_limit_ns = ctx->cfg.wait_limit_ns;
@@ -986,7 +1016,7 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
     e = f32ws::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, stream);
   else if (f32)
     e = f32::launch(p, ctx->cfg.scheduler == APK_SCHED_CLC ? (int)num_tasks : ctx->grid, poll,
-                    ctx->cfg.discipline, ctx->cfg.oracle != 0, bk, ctx->cfg.scheduler, stream);
+                    ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->f32_geo, ctx->cfg.scheduler, stream);
   else if (use_pair(ctx))
     e = bf16pair::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, stream);
   else
@@ -1084,7 +1114,7 @@ apk_status gemm_streamed(apk_ctx* ctx, const char* A, const char* B, float* C) {
   // compute while the second half is still being copied and the tiles the
   // last copies unlock need half a tile's time (4096^3: modelled 4.13 ->
   // 3.52 ms per call).  Other kernels, or an odd or short K, take whole K.
-  const int nk = K / ctx->cfg.k_tile;
+  const int nk = K / ctx->slot_k;
   const int ks = (ctx->cfg.dtype == APK_F32 && use_ws(ctx) && nk % 2 == 0 && nk >= 4) ? 2 : 1;
   const int kh = K / ks;  // K elements per slice
   const int nslots = ntiles * ks;
@@ -1449,6 +1479,25 @@ apk_status apk_gemm(apk_ctx* ctx, const void* A, const void* B, void* C, int M, 
   if (ctx->cfg.dtype == APK_BF16 && M % 256) return fail(ctx, APK_EINVAL, "bf16 M must be a multiple of 256");
   const size_t es = esize_of(ctx->cfg.dtype);
   apk_status s;
+  if (kind == APK_MEM_HOST && ctx->cfg.dtype == APK_F32 &&
+      (ctx->f32_geo == F32_GEO_M || ctx->f32_geo == F32_GEO_S)) {
+    // the 4- and 8-CTA-per-SM fp32 geometries are not streamed: whole
+    // operands in, one resident drain, C out
+    if ((s = upload(ctx, &ctx->dA, &ctx->ownA, &ctx->capA, A, es * M * K, kind)) != APK_OK) return s;
+    if ((s = upload(ctx, &ctx->dB, &ctx->ownB, &ctx->capB, B, es * (size_t)K * N, kind)) != APK_OK) return s;
+    if ((s = upload(ctx, &ctx->dC, &ctx->ownC, &ctx->capC, nullptr, 4ull * M * N, kind)) != APK_OK) return s;
+    ctx->M = M;
+    ctx->N = N;
+    ctx->K = K;
+    const unsigned long long tiles = (unsigned long long)(M / tile_rows(ctx)) * tiles_across(ctx, N);
+    const int poll = ctx->dAu ? (int)ctx->cfg.poll : APK_POLL_OFF;
+    if ((s = launch_impl(ctx, tiles, poll, ctx->kstream, true)) != APK_OK) return s;
+    ctx->running = true;
+    APK_CU(cudaMemcpyAsync(C, ctx->dC, 4ull * M * N, cudaMemcpyDeviceToHost, ctx->kstream));
+    APK_CU(cudaStreamSynchronize(ctx->kstream));
+    ctx->running = false;
+    return read_status(ctx);
+  }
   if (kind == APK_MEM_HOST) {
     // device buffers only: the operands stream in while the kernel runs
     if ((s = upload(ctx, &ctx->dA, &ctx->ownA, &ctx->capA, nullptr, es * M * K, kind)) != APK_OK) return s;
@@ -1770,7 +1819,7 @@ apk_status run_reserved_impl(apk_ctx* ctx, unsigned long long num_tasks, int res
   // urgent GEMM's tiles on a max-priority stream (src/urgent_baseline.cu:101-112)
   F32Params up;
   memset(&up, 0, sizeof up);
-  const int bk = ctx->cfg.k_tile;
+  const int bk = 32;  // the urgent kernel runs the 128x128 tiles with 32-deep slots
   apk_status t;
   if ((t = make_tmap(ctx, &up.tmA, ctx->dAu, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ctx->Mu, ctx->Ku, 32, 128,
                      CU_TENSOR_MAP_SWIZZLE_128B)) != APK_OK)
@@ -1786,6 +1835,7 @@ apk_status run_reserved_impl(apk_ctx* ctx, unsigned long long num_tasks, int res
   up.tiles_n = ctx->Nu / 128;
   up.total_tiles = utiles;
   up.nk = ctx->Ku / bk;
+  up.poll_every = 1;
   up.Cu = up.C;
   up.ldcu = ctx->Nu;
   up.usplit = 1;
@@ -1839,7 +1889,8 @@ apk_status run_reserved_impl(apk_ctx* ctx, unsigned long long num_tasks, int res
     const long long t0 = host_now_ns();
     spin_until_ns(t0 + (long long)delay_ns);
     const long long ta = host_now_ns();
-    cudaError_t e = f32::launch(up, utiles, APK_POLL_OFF, APK_DISC_DRAIN, false, bk, APK_SCHED_QUEUE, ctx->ustream);
+    cudaError_t e = f32::launch(up, utiles, APK_POLL_OFF, APK_DISC_DRAIN, false, F32_GEO_L32, APK_SCHED_QUEUE,
+                                ctx->ustream);
     if (e != cudaSuccess) return fail(ctx, APK_ECUDA, "urgent launch failed: %s", cudaGetErrorString(e));
     APK_CU(cudaStreamSynchronize(ctx->ustream));
     const long long td = host_now_ns();
@@ -1866,8 +1917,8 @@ apk_status apk_run_visibility(apk_ctx* ctx, const apk_visibility_config* vc, apk
   const unsigned long long min_n4 = 2ull * vis::loads_per_iter() * stride;
   if (n4 < min_n4) n4 = min_n4;
   // the studied kernel's shared memory per CTA keeps the residency the same
-  const int smem = std::max(4 * NT, ctx->cfg.dtype == APK_F32 ? f32::smem_bytes(ctx->cfg.k_tile)
-                                                               : bf16::smem_bytes(ctx->cfg.k_tile));
+  const int smem = std::max(4 * NT, ctx->cfg.dtype == APK_F32 ? f32::geo_info(ctx->f32_geo).smem_bytes
+                                                               : bf16::smem_bytes(ctx->slot_k));
   std::mt19937 rng(vc->seed);
   std::uniform_real_distribution<double> gap((double)vc->gap_min_ns, (double)vc->gap_max_ns);
   std::vector<long long> sched(E);

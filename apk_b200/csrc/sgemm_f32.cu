@@ -46,51 +46,80 @@
 namespace apk {
 namespace f32 {
 
-constexpr int BM = 128, BN = 128, NT = 128;
-
-template <int BK>
-struct Cfg {
-  static constexpr int STAGES = (BK == 32) ? 3 : 2;
-  static constexpr int A_BYTES = BM * BK * 4;
-  static constexpr int B_BYTES = BK * BN * 4;
+// Tile geometries.  NT = BM threads: warp w owns output rows 32w .. 32w+31;
+// thread (w, lane) holds rows 32w + lane/8 + 4i (i < 8) and columns
+// (lane%8)*4 + 32q + 0..3 (q < BN/32): an 8 x BN/8 register micro-tile.
+// SUB: K depth of one A box (32: 128-byte rows with the 128-byte swizzle;
+// 16: 64-byte rows with the 64-byte swizzle); BK: K depth of one ring slot
+// (a multiple of SUB); S: ring slots; MINB: resident CTAs per SM the
+// register budget is compiled for.
+//   L32: 128x128 tiles, 32-deep slots, 3 slots (97 KB): 2 CTAs per SM
+//   L64: 128x128 tiles, 64-deep slots, 2 slots (129 KB): 1 CTA per SM
+//   M:   64x128 tiles (two warps), 16-deep slots, 4 slots (49 KB): 4 CTAs
+//        per SM
+//   S:   32x128 tiles (one warp), 16-deep slots, 2 slots (21 KB): 8 CTAs
+//        per SM
+// Every geometry keeps the 8x16 micro-tile and thus at most 2 x 128
+// threads' worth of registers per SM (255 per thread): at 4 and 8 CTAs per
+// SM the CTA shrinks to two warps or one.  (64x64 and 128x64 tiles with 8x8
+// micro-tiles, tried first, spilled at the 128 registers a thread gets
+// there: the kernel's control state takes about 100.)
+// Yield sites are every poll_every slots: the K-tile (the K depth between
+// two sites) over BK.
+template <int BM_, int BN_, int SUB_, int BK_, int S_, int MINB_>
+struct Geo {
+  static constexpr int BM = BM_, BN = BN_, NT = BM_, SUB = SUB_, BK = BK_, S = S_, MINB = MINB_;
+  static constexpr int NQ = BN / 32;  // float4 column groups per thread
+  static constexpr int A_BYTES = BM * BK * 4, B_BYTES = BK * BN * 4;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+  static constexpr int SMEM_BYTES = S * STAGE_BYTES + 1024;
+  static_assert(BK % SUB == 0 && (SUB == 32 || SUB == 16), "A boxes are 32 or 16 deep");
 };
+using GeoL32 = Geo<128, 128, 32, 32, 3, 2>;
+using GeoL64 = Geo<128, 128, 32, 64, 2, 1>;
+using GeoM = Geo<64, 128, 16, 16, 4, 4>;
+using GeoS = Geo<32, 128, 16, 16, 2, 8>;
+enum GeoId : int { GEO_L32 = F32_GEO_L32, GEO_L64 = F32_GEO_L64, GEO_M = F32_GEO_M, GEO_S = F32_GEO_S };
 
-// One K-tile of the 128x128 tile: acc[i][j] += A[r_i][k] * B[k][c_j] for k
-// in increasing order.  Thread (warp w, lane l): rows r_i = 32w + (l>>3) +
-// 4i (i < 8), columns c_j = (l&7)*4 + 32(j/4) + j%4 (j < 16); a warp owns 32
-// full-width rows.  A is read two k at a time (float2 per row) and B one k
-// at a time (four float4, each row segment one 128-byte wavefront).  The
-// FMAs are packed in pairs of adjacent columns with __ffma2_rn: each lane of
-// the pair is the same round-to-nearest FMA as fmaf, so every sum and its k
-// order is exactly that of scalar FMAs, while 64 instructions per k carry
-// 128 FMAs -- half the issue slots, which is what lets 8 warps per SM keep
-// the FP32 pipe fed (the 8x8 scalar tiling at 16 warps per SM was
-// issue-bound at ~60% of the pipe).
-// kpair: two k (one k-pair kp) of one 32-deep sub-tile.
+// Physical 16-byte chunk of logical chunk kc in A row 32w + ty + 4i: the
+// 128-byte swizzle XORs the chunk with (row & 7) = ty + 4(i & 1); the
+// 64-byte swizzle with ((row >> 1) & 3) = (ty >> 1) + 2(i & 1).
+template <class GE>
+__device__ __forceinline__ int a_chunk(int kc, int ty, int i) {
+  if constexpr (GE::SUB == 32) return kc ^ (ty + 4 * (i & 1));
+  else return kc ^ ((ty >> 1) + 2 * (i & 1));
+}
+
+// One k-pair kp of one SUB-deep A box: acc[i][j] += A[r_i][k] * B[k][c_j]
+// for its two k in increasing order.  A is read two k at a time (float2 per
+// row) and B one k at a time (BN/32 float4, each row segment one 128-byte
+// wavefront).  The FMAs are packed in pairs of adjacent columns with
+// __ffma2_rn: each lane of the pair is the same round-to-nearest FMA as
+// fmaf, so every sum and its k order is exactly that of scalar FMAs, while
+// one instruction carries two FMAs -- half the issue slots, which is what
+// lets 8 warps per SM keep the FP32 pipe fed (the 8x8 scalar tiling at 16
+// warps per SM was issue-bound at ~60% of the pipe).
+template <class GE>
 __device__ __forceinline__ void kpair(const float* __restrict__ Asub, const float* __restrict__ Bsub,
-                                      float (&acc)[8][16], int arow0, int ty, int bcol, int kp) {
+                                      float (&acc)[8][4 * GE::NQ], int arow0, int ty, int bcol, int kp) {
   const int kc = kp >> 1, half = kp & 1;
   float2 a[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    // row r = arow0 + 4i; (r & 7) == ty + 4*(i&1) because arow0 = 32*w + ty
-    const int sw = kc ^ (ty + 4 * (i & 1));
-    a[i] = *reinterpret_cast<const float2*>(Asub + (arow0 + 4 * i) * 32 + (sw << 2) + 2 * half);
-  }
+  for (int i = 0; i < 8; ++i)
+    a[i] = *reinterpret_cast<const float2*>(Asub + (arow0 + 4 * i) * GE::SUB + (a_chunk<GE>(kc, ty, i) << 2) +
+                                            2 * half);
 #pragma unroll
   for (int kk = 0; kk < 2; ++kk) {
-    const float* brow = Bsub + (kp * 2 + kk) * BN + bcol;
-    float4 b[4];
+    const float* brow = Bsub + (kp * 2 + kk) * GE::BN + bcol;
+    float4 b[GE::NQ];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) b[q] = *reinterpret_cast<const float4*>(brow + 32 * q);
+    for (int q = 0; q < GE::NQ; ++q) b[q] = *reinterpret_cast<const float4*>(brow + 32 * q);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float av = kk == 0 ? a[i].x : a[i].y;
       const float2 ad = make_float2(av, av);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < GE::NQ; ++q) {
         float2 c0 = make_float2(acc[i][4 * q], acc[i][4 * q + 1]);
         float2 c1 = make_float2(acc[i][4 * q + 2], acc[i][4 * q + 3]);
         c0 = __ffma2_rn(ad, make_float2(b[q].x, b[q].y), c0);
@@ -105,45 +134,44 @@ __device__ __forceinline__ void kpair(const float* __restrict__ Asub, const floa
 }
 
 // poll: when non-null (tid 0 of a background stage), the yield flag is
-// loaded into pend two k-pairs before the end of the stage, so the value the
-// next stage barrier publishes is a fraction of a stage old while the load
+// loaded into pend two k-pairs before the end of the slot, so the value the
+// next slot barrier publishes is a fraction of a slot old while the load
 // latency still hides under the remaining FMAs.
-template <int BK>
-__device__ __forceinline__ void compute_stage(const float* __restrict__ As,
-                                              const float* __restrict__ Bs, float (&acc)[8][16],
-                                              int arow0, int ty, int bcol, bool poll,
+template <class GE>
+__device__ __forceinline__ void compute_stage(const float* __restrict__ As, const float* __restrict__ Bs,
+                                              float (&acc)[8][4 * GE::NQ], int arow0, int ty, int bcol, bool poll,
                                               const int* flag, int& pend) {
+  constexpr int KP = GE::SUB / 2;
 #pragma unroll
-  for (int sub = 0; sub < BK / 32; ++sub) {
-    const float* Asub = As + sub * (BM * 32);
-    const float* Bsub = Bs + sub * 32 * BN;
+  for (int sub = 0; sub < GE::BK / GE::SUB; ++sub) {
+    const float* Asub = As + sub * (GE::BM * GE::SUB);
+    const float* Bsub = Bs + sub * GE::SUB * GE::BN;
     // not unrolled: unrolled by two the loop ran faster in a mainloop probe
     // (56.4 against 52.1 TFLOP/s, operands resident in shared memory) but
     // with this kernel's control state it exceeds 255 registers and spills
 #pragma unroll 1
-    for (int kp = 0; kp < 14; ++kp) kpair(Asub, Bsub, acc, arow0, ty, bcol, kp);
+    for (int kp = 0; kp < KP - 2; ++kp) kpair<GE>(Asub, Bsub, acc, arow0, ty, bcol, kp);
     // the poll sits between two loops, not behind a per-iteration branch
-    if (sub == BK / 32 - 1 && poll) pend = flag_load(flag);
+    if (sub == GE::BK / GE::SUB - 1 && poll) pend = flag_load(flag);
     // keeps the two loops apart when there is no poll (POLL_OFF), so that
     // variant is the polling code minus the load, not a re-fused loop whose
     // speed measured 39.7 or 42.1 TFLOP/s depending on the B200 it ran on
     asm volatile("" ::: "memory");
 #pragma unroll 1
-    for (int kp = 14; kp < 16; ++kp) kpair(Asub, Bsub, acc, arow0, ty, bcol, kp);
+    for (int kp = KP - 2; kp < KP; ++kp) kpair<GE>(Asub, Bsub, acc, arow0, ty, bcol, kp);
   }
 }
 
-template <int BK>
-__device__ __forceinline__ void issue_stage(uint8_t* smem, uint64_t* full, uint32_t seq,
-                                            const CUtensorMap* tA, const CUtensorMap* tB,
-                                            int row0, int col0, int k0) {
-  using C = Cfg<BK>;
-  const int slot = seq % C::STAGES;
-  float* a = reinterpret_cast<float*>(smem + slot * C::A_BYTES);
-  float* b = reinterpret_cast<float*>(smem + C::STAGES * C::A_BYTES + slot * C::B_BYTES);
-  mbar_arrive_expect_tx(&full[slot], C::STAGE_BYTES);
+template <class GE>
+__device__ __forceinline__ void issue_stage(uint8_t* smem, uint64_t* full, uint32_t seq, const CUtensorMap* tA,
+                                            const CUtensorMap* tB, int row0, int col0, int k0) {
+  const int slot = seq % GE::S;
+  float* a = reinterpret_cast<float*>(smem + slot * GE::A_BYTES);
+  float* b = reinterpret_cast<float*>(smem + GE::S * GE::A_BYTES + slot * GE::B_BYTES);
+  mbar_arrive_expect_tx(&full[slot], GE::STAGE_BYTES);
 #pragma unroll
-  for (int sub = 0; sub < BK / 32; ++sub) tma_load_2d(a + sub * BM * 32, tA, k0 + sub * 32, row0, &full[slot]);
+  for (int sub = 0; sub < GE::BK / GE::SUB; ++sub)
+    tma_load_2d(a + sub * GE::BM * GE::SUB, tA, k0 + sub * GE::SUB, row0, &full[slot]);
   tma_load_2d(b, tB, col0, k0, &full[slot]);
 }
 
@@ -156,10 +184,9 @@ __device__ __forceinline__ void issue_stage(uint8_t* smem, uint64_t* full, uint3
 enum Sched : int { SCHED_QUEUE = 0, SCHED_CLC = 1 };
 constexpr unsigned long long NO_TASK = ~0ull;
 
-template <int POLL, int DISC, bool ORACLE, int BK, int SCHED>
-__global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant__ F32Params p) {
-  using C = Cfg<BK>;
-  constexpr int S = C::STAGES;
+template <int POLL, int DISC, bool ORACLE, class GE, int SCHED>
+__global__ void __launch_bounds__(GE::NT, GE::MINB) sgemm_persistent(const __grid_constant__ F32Params p) {
+  constexpr int S = GE::S, BM = GE::BM, BN = GE::BN, NT = GE::NT, BK = GE::BK, NQ = GE::NQ, NJ = 4 * GE::NQ;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full[S];
@@ -263,7 +290,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
   uint32_t P = 0, Q = 0;  // issued / consumed stage sequence numbers (uniform)
   bool bad = false;       // this thread saw a wait time out
   int pend = 0;           // tid 0: last flag value loaded inside a stage
-  float acc[8][16];
+  float acc[8][NJ];
 
   // Job state (uniform).  A job is a background tile or one urgent item;
   // both run through the single mainloop below.
@@ -300,7 +327,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
     if (tid == 0) {
       const CUtensorMap* tA = urgent ? &p.tmAu : &p.tmA;
       const CUtensorMap* tB = urgent ? &p.tmBu : &p.tmB;
-      for (int s = 0; s < n; ++s) issue_stage<BK>(smem, full, P + s, tA, tB, row0, col0, (kst0 + from + s) * BK);
+      for (int s = 0; s < n; ++s) issue_stage<GE>(smem, full, P + s, tA, tB, row0, col0, (kst0 + from + s) * BK);
     }
     P += n;
   };
@@ -358,12 +385,12 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
         // checkpoint: drain in-flight stages, park the accumulators
         drain();
         if (bg_active) {
-          float4* s4 = reinterpret_cast<float4*>(p.slab) + (size_t)cta() * 32 * NT;
+          float4* s4 = reinterpret_cast<float4*>(p.slab) + (size_t)cta() * (BM * BN / 4);
 #pragma unroll
           for (int i = 0; i < 8; ++i)
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              s4[(i * 4 + q) * NT + tid] =
+            for (int q = 0; q < NQ; ++q)
+              s4[(i * NQ + q) * NT + tid] =
                   make_float4(acc[i][4 * q], acc[i][4 * q + 1], acc[i][4 * q + 2], acc[i][4 * q + 3]);
           if (tid == 0) {
             s_bgRow0 = row0;
@@ -391,7 +418,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 16; ++j) acc[i][j] = 0.f;
+        for (int j = 0; j < NJ; ++j) acc[i][j] = 0.f;
       __syncthreads();  // the slot refilled first was read by the previous job
       prime(0);
     } else if (bg_active) {
@@ -404,12 +431,12 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
         c = s_bgC;
         kst0 = 0;
         nk = p.nk;
-        const float4* s4 = reinterpret_cast<const float4*>(p.slab) + (size_t)cta() * 32 * NT;
+        const float4* s4 = reinterpret_cast<const float4*>(p.slab) + (size_t)cta() * (BM * BN / 4);
 #pragma unroll
         for (int i = 0; i < 8; ++i)
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float4 v = s4[(i * 4 + q) * NT + tid];
+          for (int q = 0; q < NQ; ++q) {
+            const float4 v = s4[(i * NQ + q) * NT + tid];
             acc[i][4 * q] = v.x;
             acc[i][4 * q + 1] = v.y;
             acc[i][4 * q + 2] = v.z;
@@ -471,7 +498,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 16; ++j) acc[i][j] = 0.f;
+        for (int j = 0; j < NJ; ++j) acc[i][j] = 0.f;
       // streamed operands: the tile's A row panel and B column panel must
       // have landed before its first TMA load
       if (p.st.a_ready != nullptr && tid == 0 &&
@@ -488,10 +515,11 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
     for (; c < nk; ++c) {
       bool ys = false;
       if (POLL == POLL_STAGE && !urgent && tid == 0) {
-        const int fs = pend;  // loaded near the end of the previous stage
+        const int fs = pend;  // loaded near the end of the previous slot
         setter();
         s_f = fs;
-        ys = fs != s_lastSeen;
+        // a yield site every poll_every slots (one K-tile)
+        ys = fs != s_lastSeen && (p.poll_every <= 1 || c % p.poll_every == 0);
       }
       // frees the slot refilled below (read by every thread one stage ago)
       const int y = __syncthreads_or(ys || bad);
@@ -501,14 +529,14 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
       }
       if (c + S - 1 < nk) {
         if (tid == 0)
-          issue_stage<BK>(smem, full, P, urgent ? &p.tmAu : &p.tmA, urgent ? &p.tmBu : &p.tmB, row0, col0,
+          issue_stage<GE>(smem, full, P, urgent ? &p.tmAu : &p.tmA, urgent ? &p.tmBu : &p.tmB, row0, col0,
                           (kst0 + c + S - 1) * BK);
         ++P;
       }
       if (!mbar_wait(&full[Q % S], (Q / S) & 1, p.wait_limit_ns)) bad = true;
       const int slot = Q % S;
-      const float* As = reinterpret_cast<const float*>(smem + slot * C::A_BYTES);
-      const float* Bs = reinterpret_cast<const float*>(smem + S * C::A_BYTES + slot * C::B_BYTES);
+      const float* As = reinterpret_cast<const float*>(smem + slot * GE::A_BYTES);
+      const float* Bs = reinterpret_cast<const float*>(smem + S * GE::A_BYTES + slot * GE::B_BYTES);
       if (DISC == DISC_POISON && urgent && c == 0) {
         // detector control: one wrong staged value in each urgent item
         if (tid == 0) {
@@ -517,7 +545,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
         }
         __syncthreads();
       }
-      compute_stage<BK>(As, Bs, acc, arow0, ty, bcol, POLL == POLL_STAGE && !urgent && tid == 0, p.ev.flag,
+      compute_stage<GE>(As, Bs, acc, arow0, ty, bcol, POLL == POLL_STAGE && !urgent && tid == 0, p.ev.flag,
                         pend);
       ++Q;
     }
@@ -532,7 +560,7 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
       for (int i = 0; i < 8; ++i) {
         float* crow = p.C + (size_t)(row0 + arow0 + 4 * i) * p.ldc + col0 + bcol;
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+        for (int q = 0; q < NQ; ++q)
           *reinterpret_cast<float4*>(crow + 32 * q) =
               make_float4(acc[i][4 * q], acc[i][4 * q + 1], acc[i][4 * q + 2], acc[i][4 * q + 3]);
       }
@@ -553,12 +581,12 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
         float* crow = Cu + (size_t)(row0 + arow0 + 4 * i) * p.ldcu + col0 + bcol;
         if (p.usplit == 1) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
+          for (int q = 0; q < NQ; ++q)
             *reinterpret_cast<float4*>(crow + 32 * q) =
                 make_float4(acc[i][4 * q], acc[i][4 * q + 1], acc[i][4 * q + 2], acc[i][4 * q + 3]);
         } else {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) atomicAdd(crow + 32 * (j >> 2) + (j & 3), acc[i][j]);
+          for (int j = 0; j < NJ; ++j) atomicAdd(crow + 32 * (j >> 2) + (j & 3), acc[i][j]);
         }
       }
       __syncthreads();  // whole item written before it is counted
@@ -596,18 +624,19 @@ __global__ void __launch_bounds__(NT, 2) sgemm_persistent(const __grid_constant_
   }
 }
 
-// Host-side dispatch over the template instantiations.
+// Host-side dispatch over the template instantiations.  geo: GEO_L32,
+// GEO_L64, GEO_M, GEO_S (the Geo aliases above).
 
-template <int POLL, int DISC, bool ORACLE, int BK, int SCHED>
+template <int POLL, int DISC, bool ORACLE, class GE, int SCHED>
 static const void* kernel_ptr() {
-  return reinterpret_cast<const void*>(&sgemm_persistent<POLL, DISC, ORACLE, BK, SCHED>);
+  return reinterpret_cast<const void*>(&sgemm_persistent<POLL, DISC, ORACLE, GE, SCHED>);
 }
 
-static const void* select_kernel(int poll, int disc, bool oracle, int bk, int sched) {
+static const void* select_kernel(int poll, int disc, bool oracle, int geo, int sched) {
 #define APK_SEL(PL, DS, OR, SC)                                                    \
   if (poll == PL && disc == DS && oracle == OR && sched == SC) {                  \
-    if (bk == 32) return kernel_ptr<PL, DS, OR, 32, SC>();                       \
-    if (bk == 64) return kernel_ptr<PL, DS, OR, 64, SC>();                       \
+    if (geo == GEO_L32) return kernel_ptr<PL, DS, OR, GeoL32, SC>();             \
+    if (geo == GEO_L64) return kernel_ptr<PL, DS, OR, GeoL64, SC>();             \
   }
   APK_SEL(POLL_OFF, DISC_DRAIN, false, SCHED_QUEUE)
   APK_SEL(POLL_OFF, DISC_DRAIN, true, SCHED_QUEUE)
@@ -625,31 +654,57 @@ static const void* select_kernel(int poll, int disc, bool oracle, int bk, int sc
   APK_SEL(POLL_STAGE, DISC_DRAIN, false, SCHED_CLC)
   APK_SEL(POLL_STAGE, DISC_DRAIN, true, SCHED_CLC)
 #undef APK_SEL
+  // the multi-CTA geometries (queue scheduler): the scaling surface's 4 and
+  // 8 CTAs per SM
+#define APK_SEL(PL, DS, OR)                                                    \
+  if (poll == PL && disc == DS && oracle == OR && sched == SCHED_QUEUE) {      \
+    if (geo == GEO_M) return kernel_ptr<PL, DS, OR, GeoM, SCHED_QUEUE>();      \
+    if (geo == GEO_S) return kernel_ptr<PL, DS, OR, GeoS, SCHED_QUEUE>();      \
+  }
+  APK_SEL(POLL_OFF, DISC_DRAIN, false)
+  APK_SEL(POLL_OFF, DISC_DRAIN, true)
+  APK_SEL(POLL_BOUNDARY, DISC_DRAIN, false)
+  APK_SEL(POLL_STAGE, DISC_DRAIN, false)
+  APK_SEL(POLL_STAGE, DISC_DRAIN, true)
+  APK_SEL(POLL_STAGE, DISC_POISON, false)
+#undef APK_SEL
   return nullptr;
 }
 
-int smem_bytes(int bk) { return bk == 32 ? Cfg<32>::SMEM_BYTES : Cfg<64>::SMEM_BYTES; }
-int stages(int bk) { return bk == 32 ? Cfg<32>::STAGES : Cfg<64>::STAGES; }
-int threads() { return NT; }
+template <class GE>
+static GeoInfo info_of() {
+  return GeoInfo{GE::BM, GE::BN, GE::NT, GE::BK, GE::S, GE::SUB, GE::SMEM_BYTES};
+}
+
+GeoInfo geo_info(int geo) {
+  switch (geo) {
+    case GEO_L64: return info_of<GeoL64>();
+    case GEO_M: return info_of<GeoM>();
+    case GEO_S: return info_of<GeoS>();
+    default: return info_of<GeoL32>();
+  }
+}
 size_t params_bytes() { return sizeof(F32Params); }
 
-cudaError_t prepare(int poll, int disc, bool oracle, int bk, int sched, int* max_ctas_per_sm) {
-  const void* k = select_kernel(poll, disc, oracle, bk, sched);
+cudaError_t prepare(int poll, int disc, bool oracle, int geo, int sched, int* max_ctas_per_sm) {
+  const void* k = select_kernel(poll, disc, oracle, geo, sched);
   if (!k) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(bk));
+  const GeoInfo g = geo_info(geo);
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, g.smem_bytes);
   if (e != cudaSuccess) return e;
   // the whole unified L1 as shared memory, whatever grid an earlier launch used
   e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return e;
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(max_ctas_per_sm, k, NT, smem_bytes(bk));
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(max_ctas_per_sm, k, g.threads, g.smem_bytes);
 }
 
-cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int bk, int sched,
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int geo, int sched,
                    cudaStream_t stream) {
-  const void* k = select_kernel(poll, disc, oracle, bk, sched);
+  const void* k = select_kernel(poll, disc, oracle, geo, sched);
   if (!k) return cudaErrorInvalidValue;
+  const GeoInfo g = geo_info(geo);
   void* args[] = {const_cast<F32Params*>(&prm)};
-  return cudaLaunchKernel(k, dim3(grid), dim3(NT), args, smem_bytes(bk), stream);
+  return cudaLaunchKernel(k, dim3(grid), dim3(g.threads), args, g.smem_bytes, stream);
 }
 
 }  // namespace f32
@@ -762,7 +817,7 @@ NoAllocDevice* noalloc_device() {
       void* ptr = nullptr;
       if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return nullptr;
       int maxc = 0;
-      if (prepare(POLL_OFF, DISC_DRAIN, false, 32, SCHED_QUEUE, &maxc) != cudaSuccess || maxc < 1) return nullptr;
+      if (prepare(POLL_OFF, DISC_DRAIN, false, GEO_L32, SCHED_QUEUE, &maxc) != cudaSuccess || maxc < 1) return nullptr;
       int sms = 0;
       if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return nullptr;
       if (!g_noalloc_encode) {
@@ -831,6 +886,7 @@ extern "C" apk_status apk_sgemm_f32_noalloc(const float* A, const float* B, floa
   p.tiles_n = N / 128;
   p.total_tiles = (M / 128) * (N / 128);
   p.nk = K / 32;
+  p.poll_every = 1;
   p.wait_limit_ns = 2000000000LL;
 
   NoAllocHeader* h = reinterpret_cast<NoAllocHeader*>(d.scratch);
@@ -849,7 +905,7 @@ extern "C" apk_status apk_sgemm_f32_noalloc(const float* A, const float* B, floa
   // written, not accumulated); start_min starts at all-ones for atomicMin
   if (cudaMemsetAsync(d.scratch, 0, kNoAllocHeaderBytes, s) != cudaSuccess) return APK_ECUDA;
   if (cudaMemsetAsync(&h->start_min, 0xFF, sizeof(h->start_min), s) != cudaSuccess) return APK_ECUDA;
-  if (launch(p, grid, POLL_OFF, DISC_DRAIN, false, 32, SCHED_QUEUE, s) != cudaSuccess) return APK_ECUDA;
+  if (launch(p, grid, POLL_OFF, DISC_DRAIN, false, GEO_L32, SCHED_QUEUE, s) != cudaSuccess) return APK_ECUDA;
   return APK_OK;
 }
 

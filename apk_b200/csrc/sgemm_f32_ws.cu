@@ -344,12 +344,14 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
       };
 
       // Issue the open tile's stages bg_c .. bg_nk-1.  Under POLL_STAGE the
-      // flag is watched while each slot frees; a yield there checkpoints the
+      // flag is watched while each yield site's slot frees (one every
+      // poll_every slots); a yield there checkpoints the
       // tile and moves bg_c back to the warps' smallest cursor, and the next
       // stage issued carries RESUME.  False on stop or abort.
       auto emit_rest = [&](bool resume) -> bool {
         while (bg_c < bg_nk) {
-          if (POLL == POLL_STAGE) {
+          // a yield site every poll_every slots (one K-tile)
+          if (POLL == POLL_STAGE && (p.poll_every <= 1 || bg_c % p.poll_every == 0)) {
             if (wait_watch(&gs.empty[P % S], ((P / S) & 1) ^ 1) < 0) return false;
             const int fs = vload(&sh.gen);
             if (fs < 0) return false;  // stop sentinel: abandon the tile

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define APK_ABI_VERSION 3
+#define APK_ABI_VERSION 4
 #define APK_TASKS_UNBOUNDED 0xFFFFFFFFFFFFFFFFull
 
 typedef enum apk_status {
@@ -110,10 +110,18 @@ typedef enum apk_bf16_kernel {
 typedef struct apk_config {
   int device;
   apk_dtype dtype;
-  int ctas_per_sm;          /* 0 = as many as fit (full residency)            */
+  int ctas_per_sm;          /* 0 = as many as fit (full residency).  fp32: 4
+                               or 8 select 64x128 or 32x128 output tiles (a
+                               CTA of two warps or one, 16-deep ring slots);
+                               bf16: 2, 4 or 8 select 256x128, 128x128 or
+                               64x128 tiles with one TMEM buffer each, so
+                               that many CTAs fit on an SM                    */
   int grid;                 /* 0 = SMs * ctas_per_sm                          */
-  int k_tile;               /* 32 or 64; 0 = the dtype's default (fp32 32,
-                               bf16 64)                                       */
+  int k_tile;               /* 32, 64 or 128: the K depth between two
+                               stage-level yield sites (the pipeline stage);
+                               0 = the dtype's default (fp32 32, bf16 64).
+                               The ring moves it in slots of the kernel's own
+                               depth (apk_device_info.slot_k)                 */
   apk_poll_mode poll;
   apk_discipline discipline;
   apk_set_mode set_mode;
@@ -155,6 +163,8 @@ typedef struct apk_device_info {
                                          odd multiple of 128), or 256x512 per
                                          CTA pair with the CTA-pair kernel    */
   char name[128];
+  int slot_k;               /* (ABI 4) K depth of one ring slot; a stage-level
+                               yield site comes every k_tile / slot_k slots  */
 } apk_device_info;
 apk_status apk_get_info(apk_ctx* ctx, apk_device_info* info);
 

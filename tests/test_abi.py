@@ -34,7 +34,7 @@ def test_python_binding_covers_header():
 
 
 def test_abi_version(libapk):
-    assert libapk.apk_abi_version() == 3
+    assert libapk.apk_abi_version() == 4
 
 
 def test_config_defaults(libapk):
