@@ -42,6 +42,13 @@
 //   * every mbarrier wait is bounded; a timeout raises a CTA abort flag and
 //     the device status word, every role unwinds, outstanding MMAs and TMA
 //     loads are waited for (bounded) and TMEM is freed before exit.
+//   * geometries (class BG below): STD is everything above; the N
+//     geometries serve 2, 4 and 8 resident CTAs per SM (the scaling
+//     surface's cells): narrow jobs only (BM x 128 output tiles, one MMA of
+//     M = 128, N = BM per 16-deep k-step), one TMEM buffer of BM columns
+//     (256 / 128 / 64: the SM's 512 columns shared by 2 / 4 / 8 CTAs) and
+//     four epilogue warps, one per TMEM lane quadrant.  The CTAs sharing an
+//     SM overlap each other's epilogues with their MMAs.
 #include <string>
 
 #include "../../include/apk.h"
@@ -52,38 +59,62 @@
 namespace apk {
 namespace bf16 {
 
-constexpr int BM = 256, BN = 256, BNH = 128;
-constexpr int EPI_WARPS = 8;                     // warps 2-9
-constexpr int CTRL_WARP = 2 + EPI_WARPS;         // warp 10
-constexpr int NT = 32 * (CTRL_WARP + 1);         // 11 warps
-
-// The TMA ring for a K-tile of BK (64 or 32): A as two [128 rows][BK k] boxes
-// (K-major: 128-byte swizzle for BK 64, 64-byte for BK 32, one row = one
-// swizzle span) and B as four [BK k][64 n] boxes (MN-major, 128-byte
-// swizzle).  BK 64: 3 slots of 64 KB; BK 32: 7 slots of 32 KB -- 192 or
-// 224 KB of operands in flight.
-template <int BK>
-struct Ring {
-  static constexpr int S = BK == 64 ? 3 : 7;
-  static constexpr int A_HALF = 128 * BK * 2;            // one [128][BK] bf16 box
-  static constexpr int A_BYTES = 2 * A_HALF;
-  static constexpr int B_CHUNK = BK * 64 * 2;            // one [BK k][64 n] box
-  static constexpr int B_BYTES = 4 * B_CHUNK;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // a narrow job loads A + 2 chunks
-  static constexpr int SMEM_BYTES = S * STAGE_BYTES + 1024;
-  static constexpr uint32_t A_LAYOUT = BK == 64 ? tc::LAYOUT_SW128 : tc::LAYOUT_SW64;
-  static constexpr uint32_t A_SBO = BK * 2 * 8;          // 8 rows of one swizzle span
-};
-constexpr int S_MAX = 7;
+constexpr int BNH = 128;                         // columns of one accumulator (a narrow job)
 constexpr int RING = 8;                          // epilogue job ring
 constexpr int RASTER_GROUP = 8;                  // tile-rows per raster group
-// Each 256x128 half of the C tile is computed transposed, D = C_half^T
-// (128 x 256): the MMA's A operand is the half's [64 k][128 n] B columns
-// (MN-major), its B operand the [256 m][64 k] A tile (K-major).  One M=128,
+constexpr int S_MAX = 7;
+
+// Kernel geometry.  BM: output tile rows (the MMA's N: one M=128, N=BM
+// instruction per 128-column half and 16-deep k-step); NBUF: TMEM buffers of
+// BM columns (STD: two, a wide 256x256 job takes both); EPI: epilogue warps;
+// BK: K depth of a ring slot; S: slots; MINB: resident CTAs per SM; LDX:
+// TMEM columns per epilogue load (x8 where registers are scarce).
+//
+// The TMA ring for a K-tile of BK (64 or 32): A as [<=128 rows][BK k] boxes
+// (K-major: 128-byte swizzle for BK 64, 64-byte for BK 32, one row = one
+// swizzle span) and B as [BK k][64 n] boxes (MN-major, 128-byte swizzle),
+// four for a wide job, two for a narrow one.
+template <int BM_, int NBUF_, int EPI_, int BK_, int S_, int MINB_, int LDX_>
+struct BG {
+  static constexpr int BM = BM_, NBUF = NBUF_, EPI = EPI_, BK = BK_, S = S_, MINB = MINB_, LDX = LDX_;
+  static constexpr bool WIDE = NBUF == 2;        // 256-wide jobs (STD)
+  static constexpr int BN = WIDE ? 256 : BNH;    // output tile columns
+  static constexpr int CTRL_WARP = 2 + EPI;
+  static constexpr int NT = 32 * (CTRL_WARP + 1);
+  static constexpr int TMEM_COLS = NBUF * BM;
+  static constexpr int BPH = BM / 32;            // 32-row epilogue blocks per 128-column half
+  static constexpr int A_BOX_ROWS = BM < 128 ? BM : 128;
+  static constexpr int A_HALF = A_BOX_ROWS * BK * 2;       // one A box
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_CHUNK = BK * 64 * 2;               // one [BK k][64 n] box
+  static constexpr int B_BYTES = (WIDE ? 4 : 2) * B_CHUNK;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // a narrow STD job loads A + 2 chunks
+  static constexpr int SMEM_BYTES = S * STAGE_BYTES + 1024;
+  static constexpr uint32_t A_LAYOUT = BK == 64 ? tc::LAYOUT_SW128 : tc::LAYOUT_SW64;
+  static constexpr uint32_t A_SBO = BK * 2 * 8;  // 8 rows of one swizzle span
+  static_assert(S <= S_MAX && BM % 64 == 0 && (EPI == 8 || EPI == 4) && (LDX == 32 || LDX == 8), "geometry");
+};
+// STD: the configs[2] / configs[4] kernel, one CTA per SM
+using BgStd64 = BG<256, 2, 8, 64, 3, 1, 32>;
+using BgStd32 = BG<256, 2, 8, 32, 7, 1, 32>;
+// multi-CTA geometries: 2 CTAs (256x128 tiles, 96 KB), 4 (128x128, 48 KB),
+// 8 (64x128, 24 KB); 224 threads x 4 or x 8 leave 72 or 32 registers a
+// thread, so those two load TMEM eight columns at a time
+using BgN256x64 = BG<256, 1, 4, 64, 2, 2, 32>;
+using BgN256x32 = BG<256, 1, 4, 32, 4, 2, 32>;
+using BgN128 = BG<128, 1, 4, 32, 3, 4, 8>;
+using BgN64 = BG<64, 1, 4, 32, 2, 8, 8>;
+
+// Each 128-column half of the C tile is computed transposed, D = C_half^T
+// (128 x BM): the MMA's A operand is the half's [BK k][128 n] B columns
+// (MN-major), its B operand the [BM m][BK k] A tile (K-major).  One M=128,
 // N=256 instruction per half and 16-deep k-step reads 12 KB of shared memory
 // per 2^19 MACs where two M=128, N=128 instructions (one per 128-row half)
 // would read 16 KB.
-constexpr uint32_t IDESC = tc::idesc_bf16_f32(128, 256, /*A MN-major*/ true, /*B MN-major*/ false);
+template <class G>
+__host__ __device__ constexpr uint32_t idesc() {
+  return tc::idesc_bf16_f32(128, G::BM, /*A MN-major*/ true, /*B MN-major*/ false);
+}
 // A task tile with only 128 valid rows (m an odd multiple of 128) multiplies
 // just those: N = 128, one A box per stage (9.5% of configs[4]'s MMA work
 // went to rows no one stores).
@@ -102,6 +133,7 @@ struct EpiJob {
   unsigned long long task;
 };
 
+template <int EPI>
 struct __align__(16) Shared {
   StageTag tag[S_MAX];
   EpiJob epi[RING];
@@ -115,7 +147,7 @@ struct __align__(16) Shared {
   int prod_done;  // producer finished: the control warp may exit
   int consumed;   // stages consumed by the MMA warp (for the in-flight log)
   int epi_cnt[RING];
-  double chk_part[RING][2][EPI_WARPS];  // per-warp sum(c^2) of each 256x128 half of a task tile
+  double chk_part[RING][2][EPI];  // per-warp sum(c^2) of each 256x128 half of a task tile
   unsigned long long tiles;
 };
 
@@ -123,7 +155,8 @@ __device__ __forceinline__ int vload(const int* p) { return *reinterpret_cast<co
 __device__ __forceinline__ void vstore(int* p, int v) { *reinterpret_cast<volatile int*>(p) = v; }
 
 // Bounded mbarrier wait that also gives up when another role aborted.
-__device__ __noinline__ bool bwait(uint64_t* bar, uint32_t parity, const F32Params& p, Shared& sh) {
+template <class SH>
+__device__ __noinline__ bool bwait(uint64_t* bar, uint32_t parity, const F32Params& p, SH& sh) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = globaltimer_ns();
   int n = 0;
@@ -149,14 +182,16 @@ __device__ __noinline__ void bwait_unwind(uint64_t* bar, uint32_t parity, long l
     if (globaltimer_ns() - t0 > limit) return;
 }
 
-template <int POLL, int DISC, bool ORACLE, int BK>
-__global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_constant__ F32Params p) {
-  using R = Ring<BK>;
-  constexpr int S = R::S, A_HALF = R::A_HALF, A_BYTES = R::A_BYTES, B_CHUNK = R::B_CHUNK;
-  constexpr int STAGE_BYTES = R::STAGE_BYTES;
+template <int POLL, int DISC, bool ORACLE, class G>
+__global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __grid_constant__ F32Params p) {
+  using R = G;
+  constexpr int S = G::S, A_HALF = G::A_HALF, A_BYTES = G::A_BYTES, B_CHUNK = G::B_CHUNK, BK = G::BK;
+  constexpr int STAGE_BYTES = G::STAGE_BYTES, BM = G::BM, BN = G::BN, EPI_WARPS = G::EPI;
+  constexpr int CTRL_WARP = G::CTRL_WARP, BPH = G::BPH;
+  constexpr uint32_t IDESC = idesc<G>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ Shared sh;
+  __shared__ Shared<G::EPI> sh;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int cta = blockIdx.x;
@@ -166,7 +201,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
       mbar_init(&sh.full[s], 1);
       mbar_init(&sh.empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < G::NBUF; ++b) {
       mbar_init(&sh.tfull[b], 1);
       mbar_init(&sh.tempty[b], EPI_WARPS);
       mbar_init(&sh.tres[b], EPI_WARPS);
@@ -190,7 +225,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
     atomicMin(p.q.start_min, (unsigned long long)globaltimer_ns());
   }
   if (warp == 1) {
-    tc::tmem_alloc(&sh.tmem_base, 512);
+    tc::tmem_alloc(&sh.tmem_base, G::TMEM_COLS);
     tc::tmem_relinquish();
   }
   tc::fence_before_sync();
@@ -224,7 +259,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         mbar_arrive_expect_tx(&sh.full[s], (half ? A_HALF : A_BYTES) + nb_chunks * B_CHUNK);
         uint8_t* st = stages + s * STAGE_BYTES;
         tma_load_2d(st, tA, ak, ar0, &sh.full[s]);
-        if (!half) tma_load_2d(st + A_HALF, tA, ak, ar0 + 128, &sh.full[s]);
+        if (BM > 128 && !half) tma_load_2d(st + A_HALF, tA, ak, ar0 + 128, &sh.full[s]);
         for (int b = 0; b < nb_chunks; ++b) tma_load_2d(st + A_BYTES + b * B_CHUNK, tB, bc0 + 64 * b, bk, &sh.full[s]);
       } else {
         mbar_arrive(&sh.full[s]);  // control slot: no data
@@ -260,7 +295,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
           ++n;
           const int t = it / p.usplit, ks = it % p.usplit;
           const int r0 = (t / p.utiles_n) * BM, c0 = (t % p.utiles_n) * BN;
-          const int wide = c0 + BN <= p.ldcu ? F_WIDE : 0;
+          const int wide = G::WIDE && c0 + BN <= p.ldcu ? F_WIDE : 0;
           for (int c = 0; c < p.unk; ++c) {
             const int kk = (ks * p.unk + c) * BK;
             if (!emit(T_URG, (c == 0 ? F_FIRST : 0) | (c == p.unk - 1 ? F_LAST : 0) | wide, r0, c0, e, it, 0,
@@ -305,7 +340,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         bk0 = td.b_k0;
         nk = td.k / BK;
         mvalid = (td.m - tm * BM) < BM ? (td.m - tm * BM) : BM;
-        wide = !(td.flags & APK_TASK_NARROW) && (tn + 2) * BNH <= td.n ? F_WIDE : 0;
+        wide = G::WIDE && !(td.flags & APK_TASK_NARROW) && (tn + 2) * BNH <= td.n ? F_WIDE : 0;
         // checksum / oracle index of the tile's first 256x128 half
         tag_task = (unsigned long long)(td.chk_base + (long long)tm * (td.n / BNH) + tn);
       } else {
@@ -320,7 +355,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         ak0 = bk0 = 0;
         nk = p.nk;
         mvalid = BM;
-        wide = col0 + BN <= p.ldc ? F_WIDE : 0;
+        wide = G::WIDE && col0 + BN <= p.ldc ? F_WIDE : 0;
         // streamed operands: the A row panel and the B column panel(s) of
         // the tile must have landed before its first TMA load
         if (p.st.a_ready != nullptr) {
@@ -354,7 +389,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
           }
         }
         const int flags = (c == 0 ? F_FIRST : 0) | (c == nk - 1 ? F_LAST : 0) | (resume ? F_RESUME : 0) | wide |
-                          (mvalid <= BNH ? F_HALF : 0);
+                          (BM == 256 && mvalid <= BNH ? F_HALF : 0);
         resume = false;
         // e carries the valid rows of the tile, task the oracle / checksum index
         if (!emit(T_BG, flags, row0, col0, mvalid, 0, tag_task, &p.tmA, &p.tmB, ar0, bc0, ak0 + c * BK,
@@ -409,9 +444,9 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
       }
       if (t.flags & (F_FIRST | F_RESUME)) {
         // a narrow job takes the next buffer, a wide one both
-        cwide = (t.flags & F_WIDE) ? 1 : 0;
+        cwide = (G::WIDE && (t.flags & F_WIDE)) ? 1 : 0;
         cur = cwide ? 0 : nb;
-        nb = cwide ? 0 : nb ^ 1;
+        nb = (cwide || G::NBUF == 1) ? 0 : nb ^ 1;
         bool ok = true;
         for (int b = cur; b <= (cwide ? 1 : cur) && ok; ++b) {
           ok = bwait(&sh.tempty[b], (ub[b] & 1) ^ 1, p, sh);
@@ -433,7 +468,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         fence_proxy_async_smem();
       }
       const uint32_t sa = smem_u32(st), sb = smem_u32(st + A_BYTES);
-      const uint32_t d0 = tbase + (uint32_t)cur * 256;
+      const uint32_t d0 = tbase + (uint32_t)cur * BM;
 #pragma unroll
       for (int kk = 0; kk < BK / 16; ++kk) {
         // MMA A = B tile rows kk*16.. (MN-major: 64-column chunks LBO apart,
@@ -444,8 +479,8 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         const uint64_t bdesc = tc::smem_desc(sa + kk * 32, 16, R::A_SBO, R::A_LAYOUT);
         const uint32_t idesc = (t.flags & F_HALF) ? IDESC_HALF : IDESC;
         tc::mma_bf16(d0, tc::smem_desc(sb + kk * 2048, B_CHUNK, 1024, tc::LAYOUT_SW128), bdesc, idesc, acc);
-        if (cwide)
-          tc::mma_bf16(d0 + 256, tc::smem_desc(sb + 2 * B_CHUNK + kk * 2048, B_CHUNK, 1024, tc::LAYOUT_SW128),
+        if (G::WIDE && cwide)
+          tc::mma_bf16(d0 + BM, tc::smem_desc(sb + 2 * B_CHUNK + kk * 2048, B_CHUNK, 1024, tc::LAYOUT_SW128),
                        bdesc, idesc, acc);
       }
       tc::commit(&sh.empty[s]);  // frees the slot once these MMAs have read it
@@ -461,8 +496,12 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
     bwait_unwind(&sh.drain, 0, p.wait_limit_ns);
   } else if (warp >= 2 && warp < CTRL_WARP) {
     // ================================ epilogue ================================
+    // A 32-row block (32 TMEM columns of one quadrant) moves as 32 / LDX
+    // units of LDX columns; with 8 epilogue warps the quadrant's two warps
+    // take alternate blocks (GS = 2), with 4 one warp takes them all.
+    constexpr int LDX = G::LDX, UPB = 32 / LDX, GS = EPI_WARPS / 4;
     const int q = warp & 3;          // TMEM lane quadrant this warp may access
-    const int g = (warp - 2) >> 2;   // which of the quadrant's two warps: 32-row blocks g, g+2, ...
+    const int g = (warp - 2) >> 2;   // which of the quadrant's warps: blocks g, g + GS, ...
     const int ew = (warp - 2);       // epilogue warp index (checksum slot)
     uint32_t Y = 0, eb[2] = {0, 0};
     const uint32_t tbase = sh.tmem_base;
@@ -476,30 +515,38 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         if (lane == 0) mbar_arrive(&sh.eempty[sl]);
         break;
       }
-      // TMEM holds each 256x128 half of the tile transposed: lane = C column
-      // (32q + lane of this warp's quadrant, plus 128 in the second half),
-      // column = C row.  Block bb = (hh, blk) covers C rows blk*32 ..
+      // TMEM holds each 128-column half of the tile transposed: lane = C
+      // column (32q + lane of this warp's quadrant, plus 128 in the second
+      // half), column = C row.  Block bb = (hh, blk) covers C rows blk*32 ..
       // blk*32+31 of half hh, one register per row; a wide job's second half
-      // sits in the next 256 TMEM columns.
-      const uint32_t tcol = tbase + ((uint32_t)(32 * q) << 16) + (uint32_t)j.buf * 256;
+      // sits in the next BM TMEM columns.
+      const uint32_t tcol = tbase + ((uint32_t)(32 * q) << 16) + (uint32_t)j.buf * BM;
       const int nh = j.wide ? 2 : 1;
-      auto slab_blk = [&](int hh, int blk) { return slab + (size_t)((hh * 8 + blk) * 4 + q) * 1024; };
+      const int lim = BPH * nh;  // blocks of the job
+      auto slab_blk = [&](int hh, int blk) { return slab + (size_t)((hh * BPH + blk) * 4 + q) * 1024; };
+      // unit u = block * UPB + sub: TMEM columns blk*32 + sub*LDX .. + LDX of half hh
+      auto ucol = [&](int u) {
+        const int bb = u / UPB;
+        return tcol + (uint32_t)((bb / BPH) * BM + (bb % BPH) * 32 + (u % UPB) * LDX);
+      };
       if (j.action == E_RESTORE) {
         const long long r0 = globaltimer_ns();
 #pragma unroll 1
-        for (int bb = g; bb < 8 * nh; bb += 2) {
-          const int hh = bb >> 3, blk = bb & 7;
-          const float4* s4 = reinterpret_cast<const float4*>(slab_blk(hh, blk));
-          uint32_t v[32];
+        for (int bb = g; bb < lim; bb += GS) {
+#pragma unroll 1
+          for (int sub = 0; sub < UPB; ++sub) {
+            const float4* s4 = reinterpret_cast<const float4*>(slab_blk(bb / BPH, bb % BPH));
+            uint32_t v[LDX];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 x = s4[i * 32 + lane];
-            v[4 * i] = __float_as_uint(x.x);
-            v[4 * i + 1] = __float_as_uint(x.y);
-            v[4 * i + 2] = __float_as_uint(x.z);
-            v[4 * i + 3] = __float_as_uint(x.w);
+            for (int i = 0; i < LDX / 4; ++i) {
+              const float4 x = s4[(sub * (LDX / 4) + i) * 32 + lane];
+              v[4 * i] = __float_as_uint(x.x);
+              v[4 * i + 1] = __float_as_uint(x.y);
+              v[4 * i + 2] = __float_as_uint(x.z);
+              v[4 * i + 3] = __float_as_uint(x.w);
+            }
+            tc::st_32x32b<LDX>(ucol(bb * UPB + sub), v);
           }
-          tc::st_32x32b_x32(tcol + hh * 256 + blk * 32, v);
         }
         tc::wait_st();
         tc::fence_before_sync();
@@ -507,9 +554,9 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         if (lane == 0) {
           mbar_arrive(&sh.tres[j.buf]);
           if (p.q.ckpt != nullptr) {
-            // this warp moved 4 * nh blocks of 32 x 32 floats from the slab
+            // this warp moved lim / GS blocks of 32 x 32 floats from the slab
             atomicAdd(&p.q.ckpt[2], (unsigned long long)(globaltimer_ns() - r0));
-            atomicAdd(&p.q.ckpt[3], (unsigned long long)nh * 4 * 4096);
+            atomicAdd(&p.q.ckpt[3], (unsigned long long)(lim / GS) * 4096);
           }
         }
       } else {
@@ -521,54 +568,56 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
         // lane (256 terms, ~1e-6 relative) keeps the double conversions off
         // the path that frees TMEM, the lanes and warps add up in double
         float csum[2] = {0.0f, 0.0f};
-        // This warp's blocks bb = g, g+2, ... (< 8 * nh); rows past the task's
+        // This warp's blocks bb = g, g+GS, ... (< lim); rows past the task's
         // m (a 128-row task in a 256-row tile) are neither stored nor summed.
-        // Software-pipelined: the next block's tcgen05.ld is issued before
-        // the current block's stores, and TMEM is released as soon as the
-        // last block is in registers, before its stores.
-        const int lim = 8 * nh;
-        auto valid = [&](int bb) { return !(j.action == E_STORE_C && (bb & 7) * 32 >= j.e); };
-        auto next = [&](int bb) {
-          bb += 2;
-          while (bb < lim && !valid(bb)) bb += 2;
-          return bb;
+        // Software-pipelined: the next unit's tcgen05.ld is issued before
+        // the current unit's stores, and TMEM is released as soon as the
+        // last unit is in registers, before its stores.
+        constexpr int ULIM = 1 << 30;
+        auto valid = [&](int bb) { return !(j.action == E_STORE_C && (bb % BPH) * 32 >= j.e); };
+        auto next = [&](int u) {
+          if (u % UPB != UPB - 1) return u + 1;
+          int bb = u / UPB + GS;
+          while (bb < lim && !valid(bb)) bb += GS;
+          return bb < lim ? bb * UPB : ULIM;
         };
-        auto tload = [&](int bb, uint32_t(&v)[32]) { tc::ld_32x32b_x32(tcol + (bb >> 3) * 256 + (bb & 7) * 32, v); };
-        auto consume = [&](int bb, const uint32_t(&v)[32]) {
-          const int hh = bb >> 3, blk = bb & 7;
+        auto consume = [&](int u, const uint32_t(&v)[LDX]) {
+          const int bb = u / UPB, sub = u % UPB, hh = bb / BPH, blk = bb % BPH;
           if (j.action == E_SPILL) {
             float4* s4 = reinterpret_cast<float4*>(slab_blk(hh, blk));
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              s4[i * 32 + lane] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                                              __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+            for (int i = 0; i < LDX / 4; ++i)
+              s4[(sub * (LDX / 4) + i) * 32 + lane] =
+                  make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                              __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
             return;
           }
-          // register i -> C row blk*32+i, lane -> C column: each store
-          // instruction writes one contiguous 128-byte row segment
+          // register i -> C row blk*32 + sub*LDX + i, lane -> C column: each
+          // store instruction writes one contiguous 128-byte row segment
           const int col = j.col0 + BNH * hh + 32 * q + lane;
+          const int row = j.row0 + blk * 32 + sub * LDX;
           if (j.action == E_STORE_C) {
-            float* dst = p.C + (size_t)(j.row0 + blk * 32) * p.ldc + col;
+            float* dst = p.C + (size_t)row * p.ldc + col;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) dst[(size_t)i * p.ldc] = __uint_as_float(v[i]);
+            for (int i = 0; i < LDX; ++i) dst[(size_t)i * p.ldc] = __uint_as_float(v[i]);
             if (p.task_mode) {
               // one running sum per half, blocks in order, rows in order
               float cs = hh == 0 ? csum[0] : csum[1];
 #pragma unroll
-              for (int i = 0; i < 32; ++i) {
+              for (int i = 0; i < LDX; ++i) {
                 const float x = __uint_as_float(v[i]);
                 cs = fmaf(x, x, cs);
               }
               if (hh == 0) csum[0] = cs; else csum[1] = cs;
             }
           } else {
-            float* dst = p.Cu + (size_t)j.e * p.cu_stride + (size_t)(j.row0 + blk * 32) * p.ldcu + col;
+            float* dst = p.Cu + (size_t)j.e * p.cu_stride + (size_t)row * p.ldcu + col;
             if (p.usplit == 1) {
 #pragma unroll
-              for (int i = 0; i < 32; ++i) dst[(size_t)i * p.ldcu] = __uint_as_float(v[i]);
+              for (int i = 0; i < LDX; ++i) dst[(size_t)i * p.ldcu] = __uint_as_float(v[i]);
             } else {
 #pragma unroll
-              for (int i = 0; i < 32; ++i) atomicAdd(dst + (size_t)i * p.ldcu, __uint_as_float(v[i]));
+              for (int i = 0; i < LDX; ++i) atomicAdd(dst + (size_t)i * p.ldcu, __uint_as_float(v[i]));
             }
           }
         };
@@ -580,26 +629,28 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
             mbar_arrive(&sh.tempty[j.buf]);
             if (j.wide) mbar_arrive(&sh.tempty[1]);  // a wide job held both buffers (buf 0 and 1)
             if (j.action == E_SPILL && p.q.ckpt != nullptr) {
-              // TMEM free again: this warp's 4 * nh blocks are in registers
+              // TMEM free again: this warp's lim / GS blocks are in registers
               atomicAdd(&p.q.ckpt[0], (unsigned long long)(globaltimer_ns() - s0));
-              atomicAdd(&p.q.ckpt[1], (unsigned long long)nh * 4 * 4096);
+              atomicAdd(&p.q.ckpt[1], (unsigned long long)(lim / GS) * 4096);
             }
           }
           released = true;
         };
-        uint32_t va[32], vb[32];
-        int cur = valid(g) ? g : next(g);
-        if (cur < lim) tload(cur, va);
-        while (cur < lim) {
+        uint32_t va[LDX], vb[LDX];
+        int bb0 = g;
+        while (bb0 < lim && !valid(bb0)) bb0 += GS;
+        int cur = bb0 < lim ? bb0 * UPB : ULIM;
+        if (cur != ULIM) tc::ld_32x32b<LDX>(ucol(cur), va);
+        while (cur != ULIM) {
           tc::wait_ld();
           int nxt = next(cur);
-          if (nxt < lim) tload(nxt, vb); else release();
+          if (nxt != ULIM) tc::ld_32x32b<LDX>(ucol(nxt), vb); else release();
           consume(cur, va);
           cur = nxt;
-          if (cur >= lim) break;
+          if (cur == ULIM) break;
           tc::wait_ld();
           nxt = next(cur);
-          if (nxt < lim) tload(nxt, va); else release();
+          if (nxt != ULIM) tc::ld_32x32b<LDX>(ucol(nxt), va); else release();
           consume(cur, vb);
           cur = nxt;
         }
@@ -676,7 +727,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
   if (warp == 1) {
     __syncwarp();
     tc::fence_after_sync();
-    tc::tmem_dealloc(sh.tmem_base, 512);
+    tc::tmem_dealloc(sh.tmem_base, G::TMEM_COLS);
   }
   if (tid == 0) {
     p.q.tiles_done[cta] = sh.tiles;
@@ -687,16 +738,17 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_persistent(const __grid_const
 
 // ---------------------------------------------------------------------------
 
-template <int POLL, int DISC, bool ORACLE, int BK>
+template <int POLL, int DISC, bool ORACLE, class G>
 static const void* kernel_ptr() {
-  return reinterpret_cast<const void*>(&gemm_bf16_persistent<POLL, DISC, ORACLE, BK>);
+  return reinterpret_cast<const void*>(&gemm_bf16_persistent<POLL, DISC, ORACLE, G>);
 }
 
-static const void* select_kernel(int poll, int disc, bool oracle, int bk) {
-#define APK_SEL(PL, DS, OR)                                     \
-  if (poll == PL && disc == DS && oracle == OR) {              \
-    if (bk == 64) return kernel_ptr<PL, DS, OR, 64>();         \
-    if (bk == 32) return kernel_ptr<PL, DS, OR, 32>();         \
+// geo: BF16_GEO_* (proto.h)
+static const void* select_kernel(int poll, int disc, bool oracle, int geo) {
+#define APK_SEL(PL, DS, OR)                                                 \
+  if (poll == PL && disc == DS && oracle == OR) {                          \
+    if (geo == BF16_GEO_STD64) return kernel_ptr<PL, DS, OR, BgStd64>();   \
+    if (geo == BF16_GEO_STD32) return kernel_ptr<PL, DS, OR, BgStd32>();   \
   }
   APK_SEL(POLL_OFF, DISC_DRAIN, false)
   APK_SEL(POLL_OFF, DISC_DRAIN, true)
@@ -707,33 +759,72 @@ static const void* select_kernel(int poll, int disc, bool oracle, int bk) {
   APK_SEL(POLL_STAGE, DISC_POISON, false)
   APK_SEL(POLL_STAGE, DISC_POISON, true)
 #undef APK_SEL
+  // the multi-CTA geometries: the variants the scaling surface and its tests use
+#define APK_SEL(PL, DS, OR)                                                    \
+  if (poll == PL && disc == DS && oracle == OR) {                             \
+    if (geo == BF16_GEO_N256x64) return kernel_ptr<PL, DS, OR, BgN256x64>();  \
+    if (geo == BF16_GEO_N256x32) return kernel_ptr<PL, DS, OR, BgN256x32>();  \
+    if (geo == BF16_GEO_N128) return kernel_ptr<PL, DS, OR, BgN128>();        \
+    if (geo == BF16_GEO_N64) return kernel_ptr<PL, DS, OR, BgN64>();          \
+  }
+  APK_SEL(POLL_OFF, DISC_DRAIN, false)
+  APK_SEL(POLL_OFF, DISC_DRAIN, true)
+  APK_SEL(POLL_BOUNDARY, DISC_DRAIN, false)
+  APK_SEL(POLL_STAGE, DISC_DRAIN, false)
+  APK_SEL(POLL_STAGE, DISC_DRAIN, true)
+  APK_SEL(POLL_STAGE, DISC_POISON, false)
+#undef APK_SEL
   return nullptr;
 }
 
-int smem_bytes(int bk) { return bk == 32 ? Ring<32>::SMEM_BYTES : Ring<64>::SMEM_BYTES; }
-int stages(int bk) { return bk == 32 ? Ring<32>::S : Ring<64>::S; }
-int threads() { return NT; }
-int epi_warps() { return EPI_WARPS; }
+template <class G>
+static GeoInfo info_of() {
+  return GeoInfo{G::BM, G::BN, G::NT, G::BK, G::S, G::BK, G::SMEM_BYTES};
+}
+
+GeoInfo geo_info(int geo) {
+  switch (geo) {
+    case BF16_GEO_STD32: return info_of<BgStd32>();
+    case BF16_GEO_N256x64: return info_of<BgN256x64>();
+    case BF16_GEO_N256x32: return info_of<BgN256x32>();
+    case BF16_GEO_N128: return info_of<BgN128>();
+    case BF16_GEO_N64: return info_of<BgN64>();
+    default: return info_of<BgStd64>();
+  }
+}
+static int tmem_cols(int geo) {
+  switch (geo) {
+    case BF16_GEO_N256x64: case BF16_GEO_N256x32: return BgN256x64::TMEM_COLS;
+    case BF16_GEO_N128: return BgN128::TMEM_COLS;
+    case BF16_GEO_N64: return BgN64::TMEM_COLS;
+    default: return BgStd64::TMEM_COLS;
+  }
+}
+int epi_warps(int geo) { return geo == BF16_GEO_STD64 || geo == BF16_GEO_STD32 ? BgStd64::EPI : BgN128::EPI; }
 size_t params_bytes() { return sizeof(F32Params); }
 
-cudaError_t prepare(int poll, int disc, bool oracle, int bk, int* max_ctas_per_sm) {
-  const void* k = select_kernel(poll, disc, oracle, bk);
+cudaError_t prepare(int poll, int disc, bool oracle, int geo, int* max_ctas_per_sm) {
+  const void* k = select_kernel(poll, disc, oracle, geo);
   if (!k) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(bk));
+  const GeoInfo g = geo_info(geo);
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, g.smem_bytes);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return e;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(max_ctas_per_sm, k, NT, smem_bytes(bk));
-  // each CTA allocates all 512 TMEM columns: never more than one per SM
-  if (e == cudaSuccess && *max_ctas_per_sm > 1) *max_ctas_per_sm = 1;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(max_ctas_per_sm, k, g.threads, g.smem_bytes);
+  // a CTA allocates TMEM_COLS of the SM's 512 TMEM columns: never more CTAs
+  // per SM than fit (an allocation would wait for another CTA's release)
+  const int tmem_cap = 512 / tmem_cols(geo);
+  if (e == cudaSuccess && *max_ctas_per_sm > tmem_cap) *max_ctas_per_sm = tmem_cap;
   return e;
 }
 
-cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int bk, cudaStream_t stream) {
-  const void* k = select_kernel(poll, disc, oracle, bk);
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int geo, cudaStream_t stream) {
+  const void* k = select_kernel(poll, disc, oracle, geo);
   if (!k) return cudaErrorInvalidValue;
+  const GeoInfo g = geo_info(geo);
   void* args[] = {const_cast<F32Params*>(&prm)};
-  return cudaLaunchKernel(k, dim3(grid), dim3(NT), args, smem_bytes(bk), stream);
+  return cudaLaunchKernel(k, dim3(grid), dim3(g.threads), args, g.smem_bytes, stream);
 }
 
 }  // namespace bf16

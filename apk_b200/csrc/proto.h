@@ -180,6 +180,13 @@ struct GeoInfo {
   int tile_m, tile_n, threads, slot_k, stages, a_box_k, smem_bytes;
 };
 enum F32Geo : int { F32_GEO_L32 = 0, F32_GEO_L64 = 1, F32_GEO_M = 2, F32_GEO_S = 3 };
+// bf16 one-CTA kernel geometries (gemm_bf16.cu): STD (256x256 tiles, one CTA
+// per SM, 64- or 32-deep slots) and N256 / N128 / N64 (256x128, 128x128,
+// 64x128 tiles for 2, 4 and 8 resident CTAs per SM).
+enum BF16Geo : int {
+  BF16_GEO_STD64 = 0, BF16_GEO_STD32 = 1, BF16_GEO_N256x64 = 2, BF16_GEO_N256x32 = 3, BF16_GEO_N128 = 4,
+  BF16_GEO_N64 = 5
+};
 
 // Visibility microbenchmark parameters (the flag-notification probe of
 // src/yield.cu:227-293, decoupled from tile work).

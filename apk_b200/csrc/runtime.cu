@@ -52,12 +52,10 @@ int threads();
 int loads_per_iter();
 }  // namespace vis
 namespace bf16 {
-cudaError_t prepare(int poll, int disc, bool oracle, int bk, int* max_ctas_per_sm);
-cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int bk, cudaStream_t stream);
-int smem_bytes(int bk);
-int stages(int bk);
-int threads();
-int epi_warps();
+cudaError_t prepare(int poll, int disc, bool oracle, int geo, int* max_ctas_per_sm);
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int geo, cudaStream_t stream);
+GeoInfo geo_info(int geo);
+int epi_warps(int geo);
 size_t params_bytes();
 }  // namespace bf16
 }  // namespace apk
@@ -127,6 +125,7 @@ struct apk_ctx {
   // geometry and ring: fp32 block-synchronous tile geometry (F32Geo), the K
   // depth of one ring slot and the slots per stage-level yield site
   int f32_geo = F32_GEO_L32;
+  int bf16_geo = BF16_GEO_STD64;
   int slot_k = 32;
   int poll_every = 1;
   // bf16: the CTA-pair kernel can run every poll variant this context
@@ -279,10 +278,12 @@ size_t esize_of(apk_dtype d) { return d == APK_BF16 ? 2 : 4; }
 // a row 128 wide when the width is an odd multiple of 128.
 bool use_pair(const apk_ctx* ctx);
 int tile_rows(const apk_ctx* ctx) {
-  return ctx->cfg.dtype == APK_F32 ? f32::geo_info(ctx->f32_geo).tile_m : 256;
+  return ctx->cfg.dtype == APK_F32 ? f32::geo_info(ctx->f32_geo).tile_m : bf16::geo_info(ctx->bf16_geo).tile_m;
 }
 int tile_cols(const apk_ctx* ctx) {
-  return ctx->cfg.dtype == APK_F32 ? f32::geo_info(ctx->f32_geo).tile_n : use_pair(ctx) ? 512 : 256;
+  return ctx->cfg.dtype == APK_F32 ? f32::geo_info(ctx->f32_geo).tile_n
+         : use_pair(ctx)           ? 512
+                                   : bf16::geo_info(ctx->bf16_geo).tile_n;
 }
 int tiles_across(const apk_ctx* ctx, int n) { return (n + tile_cols(ctx) - 1) / tile_cols(ctx); }
 
@@ -314,7 +315,7 @@ apk_status prepare_kernel(apk_ctx* ctx, int poll) {
   if (ctx->cfg.dtype == APK_F32)
     e = f32::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->f32_geo, ctx->cfg.scheduler, &maxc);
   else
-    e = bf16::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->slot_k, &maxc);
+    e = bf16::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->bf16_geo, &maxc);
   if (e != cudaSuccess)
     return fail(ctx, APK_EUNSUPPORTED, "kernel variant unavailable (dtype %d poll %d disc %d oracle %d k_tile %d): %s",
                 ctx->cfg.dtype, poll, ctx->cfg.discipline, ctx->cfg.oracle, ctx->cfg.k_tile,
@@ -327,7 +328,7 @@ apk_status prepare_kernel(apk_ctx* ctx, int poll) {
     if (e != cudaSuccess) ok = 0;
     ctx->ws_ok = ctx->ws_ok && ok;
   }
-  if (ctx->cfg.dtype == APK_BF16 && ctx->slot_k == 64) {
+  if (ctx->cfg.dtype == APK_BF16 && ctx->bf16_geo == BF16_GEO_STD64) {
     int pairs = 0;
     e = bf16pair::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->sms, &pairs);
     if (e != cudaSuccess) pairs = 0;
@@ -341,7 +342,7 @@ apk_status prepare_kernel(apk_ctx* ctx, int poll) {
 // CTA per SM over every SM; the one-CTA kernel runs everything else.
 bool use_pair(const apk_ctx* ctx) {
   return ctx->cfg.dtype == APK_BF16 && ctx->pair_ok && ctx->cfg.bf16_kernel != APK_BF16_SINGLE &&
-         !ctx->task_mode && ctx->slot_k == 64 && ctx->grid == ctx->sms && ctx->N % 256 == 0 &&
+         !ctx->task_mode && ctx->bf16_geo == BF16_GEO_STD64 && ctx->grid == ctx->sms && ctx->N % 256 == 0 &&
          ctx->Nu % 256 == 0;
 }
 
@@ -416,7 +417,12 @@ apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
                                                              : F32_GEO_L32;
     ctx->slot_k = f32::geo_info(ctx->f32_geo).slot_k;
   } else {
-    ctx->slot_k = c.k_tile == 32 ? 32 : 64;
+    const bool k32 = c.k_tile == 32;
+    ctx->bf16_geo = c.ctas_per_sm >= 8   ? BF16_GEO_N64
+                    : c.ctas_per_sm >= 4 ? BF16_GEO_N128
+                    : c.ctas_per_sm >= 2 ? (k32 ? BF16_GEO_N256x32 : BF16_GEO_N256x64)
+                                         : (k32 ? BF16_GEO_STD32 : BF16_GEO_STD64);
+    ctx->slot_k = bf16::geo_info(ctx->bf16_geo).slot_k;
   }
   ctx->poll_every = c.k_tile / ctx->slot_k;
   if (c.discipline == APK_DISC_POISON && c.poll == APK_POLL_OFF) {
@@ -613,11 +619,12 @@ apk_status apk_get_info(apk_ctx* ctx, apk_device_info* info) {
     info->tile_n = 512;  // one tile per CTA pair
     info->stages = bf16pair::stages();
   } else {
-    info->smem_per_cta = bf16::smem_bytes(ctx->slot_k);
-    info->threads_per_cta = bf16::threads();
-    info->tile_m = 256;
-    info->tile_n = 256;
-    info->stages = bf16::stages(ctx->slot_k);
+    const GeoInfo g = bf16::geo_info(ctx->bf16_geo);
+    info->smem_per_cta = g.smem_bytes;
+    info->threads_per_cta = g.threads;
+    info->tile_m = g.tile_m;
+    info->tile_n = g.tile_n;
+    info->stages = g.stages;
   }
   info->k_tile = ctx->cfg.k_tile;
   info->slot_k = ctx->slot_k;
@@ -689,6 +696,8 @@ apk_status apk_set_tasks(apk_ctx* ctx, const apk_task* tasks, int n, long long n
   if (!ctx || !tasks || n <= 0 || n_chk <= 0) return APK_EINVAL;
   if (ctx->running) return fail(ctx, APK_ESTATE, "set_tasks while a launch runs");
   if (!ctx->dApool) return fail(ctx, APK_ESTATE, "no task pool set");
+  if (ctx->bf16_geo != BF16_GEO_STD64 && ctx->bf16_geo != BF16_GEO_STD32)
+    return fail(ctx, APK_EUNSUPPORTED, "task mode runs the one-CTA-per-SM bf16 geometry (ctas_per_sm 0 or 1)");
   // a work-list entry packs task (20 bits), tile row and the tile's first
   // 128-column block (6 bits each); a tile is 256x256, or 256x128 where the
   // task's n ends 128 columns into it.  Checksums and oracle counters are
@@ -959,7 +968,7 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
     const int es = f32 ? 4 : 2;
     const GeoInfo fg = f32::geo_info(ctx->f32_geo);
     const int a_box_k = f32 ? fg.a_box_k : bk, b_box_n = f32 ? fg.tile_n : 64;
-    const int a_box_m = f32 ? fg.tile_m : 128;
+    const int a_box_m = f32 ? fg.tile_m : std::min(128, bf16::geo_info(ctx->bf16_geo).tile_m);
     const CUtensorMapSwizzle asw = (f32 ? a_box_k == 32 : bk == 64) ? CU_TENSOR_MAP_SWIZZLE_128B
                                                                     : CU_TENSOR_MAP_SWIZZLE_64B;
     const CUtensorMapSwizzle bsw = f32 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B;
@@ -1020,7 +1029,7 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
   else if (use_pair(ctx))
     e = bf16pair::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, stream);
   else
-    e = bf16::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, bk, stream);
+    e = bf16::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->bf16_geo, stream);
   if (e != cudaSuccess) return fail(ctx, APK_ECUDA, "kernel launch failed: %s", cudaGetErrorString(e));
   if (record) APK_CU(cudaEventRecord(ctx->ev_done, stream));
   return APK_OK;
@@ -1446,7 +1455,8 @@ apk_status apk_read_run_stats(apk_ctx* ctx, apk_run_stats* st) {
     st->ckpt_restore_bytes = cb.ckpt[3];
     // (the pair kernel: 16 warps over two CTAs spill side by side; bytes
     // cover the pair)
-    const unsigned long long w = use_pair(ctx) ? 2ull * bf16pair::epi_warps() : (unsigned long long)bf16::epi_warps();
+    const unsigned long long w =
+        use_pair(ctx) ? 2ull * bf16pair::epi_warps() : (unsigned long long)bf16::epi_warps(ctx->bf16_geo);
     st->ckpt_spill_ns = (long long)(cb.ckpt[0] / w);
     st->ckpt_restore_ns = (long long)(cb.ckpt[2] / w);
   }
@@ -1918,7 +1928,7 @@ apk_status apk_run_visibility(apk_ctx* ctx, const apk_visibility_config* vc, apk
   if (n4 < min_n4) n4 = min_n4;
   // the studied kernel's shared memory per CTA keeps the residency the same
   const int smem = std::max(4 * NT, ctx->cfg.dtype == APK_F32 ? f32::geo_info(ctx->f32_geo).smem_bytes
-                                                               : bf16::smem_bytes(ctx->slot_k));
+                                                               : bf16::geo_info(ctx->bf16_geo).smem_bytes);
   std::mt19937 rng(vc->seed);
   std::uniform_real_distribution<double> gap((double)vc->gap_min_ns, (double)vc->gap_max_ns);
   std::vector<long long> sched(E);

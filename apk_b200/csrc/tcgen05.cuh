@@ -100,6 +100,31 @@ __device__ __forceinline__ void st_32x32b_x32(uint32_t taddr, const uint32_t (&v
       : "memory");
 }
 
+__device__ __forceinline__ void ld_32x32b_x8(uint32_t taddr, uint32_t (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr)
+               : "memory");
+}
+
+__device__ __forceinline__ void st_32x32b_x8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
+// x32 or x8 by the array's size (the epilogue's unit width)
+template <int W>
+__device__ __forceinline__ void ld_32x32b(uint32_t taddr, uint32_t (&v)[W]) {
+  if constexpr (W == 32) ld_32x32b_x32(taddr, v);
+  else ld_32x32b_x8(taddr, v);
+}
+template <int W>
+__device__ __forceinline__ void st_32x32b(uint32_t taddr, const uint32_t (&v)[W]) {
+  if constexpr (W == 32) st_32x32b_x32(taddr, v);
+  else st_32x32b_x8(taddr, v);
+}
+
 __device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 

@@ -139,3 +139,29 @@ def test_bf16_k_tile_128_stage_yields_bitwise(libapk, bf16_kernel):
     r = _bf16_yield_run(128, bf16_kernel=bf16_kernel)
     assert r["info"]["slot_k"] == 64
     _check_bf16_yield(r, 128)
+
+
+@pytest.mark.parametrize("cps,k_tile", [(2, 64), (2, 32), (4, 64), (8, 128)])
+def test_bf16_multi_cta_geometries_bitwise(libapk, cps, k_tile):
+    import apk_b200
+    M, N, K = 512, 384, 512
+    A = apk_b200.fill_normal_bf16((M, K), 1)
+    B = apk_b200.fill_normal_bf16((K, N), 2)
+    with _ctx(dtype="bf16", poll="off", bf16_kernel="single") as c:
+        C0 = c.gemm(A, B)
+    with _ctx(dtype="bf16", poll="stage", ctas_per_sm=cps, k_tile=k_tile, oracle=True, urgent_split_k=1) as c:
+        info = c.info
+        assert info["ctas_per_sm"] == cps and info["grid"] == cps * info["sms"]
+        assert (info["tile_m"], info["tile_n"]) == ({2: 256, 4: 128, 8: 64}[cps], 128)
+        C = c.gemm(A, B)
+    assert np.array_equal(C.view(np.uint32), C0.view(np.uint32))
+    ref = oracle.gemm_f64_bf16_rows(A, B, 0, M)
+    mr, bad, nans = oracle.check(C, ref, oracle.BF16_TOL)
+    assert bad == 0 and nans == 0, f"{bad} bad, {nans} NaN, max rel {mr:.3e}"
+
+
+@pytest.mark.parametrize("cps,k_tile", [(2, 64), (4, 128), (8, 32)])
+def test_bf16_multi_cta_stage_yields_bitwise(libapk, cps, k_tile):
+    r = _bf16_yield_run(k_tile, ctas_per_sm=cps)
+    assert r["info"]["ctas_per_sm"] == cps
+    _check_bf16_yield(r, k_tile)
