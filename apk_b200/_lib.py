@@ -56,7 +56,7 @@ class RunStats(ctypes.Structure):
                 ("bg_flops", c_double), ("bg_tflops", c_double), ("exited", c_int),
                 ("device_status", c_int), ("launch_ms", c_double),
                 ("ckpt_spill_bytes", c_ull), ("ckpt_restore_bytes", c_ull),
-                ("ckpt_spill_ns", c_ll), ("ckpt_restore_ns", c_ll)]
+                ("ckpt_spill_ns", c_ll), ("ckpt_restore_ns", c_ll), ("parks", c_ull)]
 
 
 class LatencyConfig(ctypes.Structure):

@@ -21,9 +21,11 @@ feasible cell
   settles near 1.4 GHz); the short ABAB drains of the poll cost run at burst
   clocks.  SM clocks and throttle reasons are sampled during each.
 
-A cell the kernels cannot run is reported with the reason instead of
-numbers (a CTA count above what the register file, TMEM or shared memory
-admits, a K-tile whose ring does not fit).  One JSON line per cell, then a
+Every cell has a geometry: 4 and 8 fp32 CTAs per SM run 64x128 and 32x128
+tiles, 2 / 4 / 8 bf16 CTAs run 256x128 / 128x128 / 64x128 tiles with one
+TMEM buffer each, and the K-tile is the K depth between two yield sites,
+moved through each kernel's own ring slots.  A cell whose CTAs would not
+all fit on an SM is reported with the occupancy limit instead of numbers.  One JSON line per cell, then a
 summary table.  Each cell runs in a process of its own, so that no cell's
 timing depends on the device allocations and kernels of the cells before
 it.
@@ -38,7 +40,6 @@ import sys
 
 CTAS = (1, 2, 4, 8)
 KTILES = (32, 64, 128)
-KTILES_BUILT = (32, 64)
 SHAPES = ((4096, 4096, 4096), (16384, 1024, 4096))
 URGENT = 256
 
@@ -51,20 +52,22 @@ def _operands(apk_b200, dtype, M, N, K):
     return A, B, Au, Bu
 
 
+def geometry(dtype, cps):
+    """The tile geometry each cell runs (the runtime picks it from
+    ctas_per_sm; restated here for the report)."""
+    if dtype == "f32":
+        return {1: "128x128 tiles, 128-thread CTAs", 2: "128x128 tiles, two workers per 384-thread CTA",
+                4: "64x128 tiles, 64-thread CTAs", 8: "32x128 tiles, 32-thread CTAs"}[cps]
+    return {1: "256x512 tiles on CTA pairs (K-tile >= 64) / 256x256 (K-tile 32)",
+            2: "256x128 tiles, 256 TMEM columns", 4: "128x128 tiles, 128 TMEM columns",
+            8: "64x128 tiles, 64 TMEM columns"}[cps]
+
+
 def _infeasible_reason(dtype, cps, kt, info):
-    if kt not in KTILES_BUILT:
-        ring = "two 128-row x 128-k fp32 stages need 256 KB" if dtype == "f32" else \
-            "one 256x256 x 128-k bf16 stage needs 128 KB, no room for a second"
-        return f"K-tile {kt}: {ring} of the 227 KB of shared memory per SM"
+    """None when the cell runs as asked; else why the runtime could not place
+    cps CTAs of the cell's geometry on an SM (its occupancy limit)."""
     if info is not None and info["ctas_per_sm"] != cps:
-        if dtype == "bf16":
-            why = "each CTA allocates all 512 TMEM columns and 230 KB of shared memory"
-        elif kt == 64:
-            why = "each CTA's two 64 KB stages take 129 KB of the 227 KB of shared memory"
-        else:
-            why = ("each 128-thread CTA holds ~232 registers per thread (29.7K of the SM's 64K) and 97 KB "
-                   "of shared memory")
-        return f"{cps} CTAs/SM: at most {info['max_ctas_per_sm']} fit ({why})"
+        return f"{cps} CTAs/SM: at most {info['max_ctas_per_sm']} of this geometry fit ({geometry(dtype, cps)})"
     return None
 
 
@@ -72,10 +75,7 @@ def run_cell(apk_b200, dtype, cps, kt, shape, events, warmup, seed, operands):
     from apk_b200.clocks import ClockSampler
     M, N, K = shape
     cell = {"dtype": dtype, "ctas_per_sm": cps, "k_tile": kt, "shape": [M, N, K]}
-    if kt not in KTILES_BUILT:
-        cell["infeasible"] = _infeasible_reason(dtype, cps, kt, None)
-        return cell
-    # fp32 urgent items are one K-stage each (configs[1]: split-K 8 at K-tile 32)
+    # fp32 urgent items are one K-tile each (configs[1]: split-K 8 at K-tile 32)
     split = URGENT // kt if dtype == "f32" else 1
     with apk_b200.Context(dtype=dtype, ctas_per_sm=cps, k_tile=kt, poll="stage", set_mode="device",
                           max_events=events + 8, urgent_split_k=split) as c:
@@ -112,6 +112,7 @@ def run_cell(apk_b200, dtype, cps, kt, shape, events, warmup, seed, operands):
         yields = c.run_stats()["yields"]
     cell.update({
         "grid": info["grid"], "tile": [info["tile_m"], info["tile_n"]], "stages": info["stages"],
+        "slot_k": info["slot_k"], "yield_site_every_slots": kt // info["slot_k"],
         "kernel": ("warp-specialized (2 workers per 384-thread CTA)" if info["threads_per_cta"] == 384 else
                    f"{info['threads_per_cta']}-thread CTAs"),
         "urgent_split_k": split,
@@ -156,18 +157,14 @@ def main():
         for shape in SHAPES:
             for cps in CTAS:
                 for kt in KTILES:
-                    if kt not in KTILES_BUILT:
-                        cell = {"dtype": dtype, "ctas_per_sm": cps, "k_tile": kt, "shape": list(shape),
-                                "infeasible": _infeasible_reason(dtype, cps, kt, None)}
-                    else:
-                        spec = ",".join(map(str, (dtype, cps, kt) + shape))
-                        out = subprocess.run(
-                            [sys.executable, "-m", "apk_b200.config3", "--cell", spec, "--events", str(args.events),
-                             "--warmup", str(args.warmup), "--seed", str(args.seed)],
-                            capture_output=True, text=True)
-                        if out.returncode != 0:
-                            raise RuntimeError(f"cell {spec} failed:\n{out.stdout}\n{out.stderr}")
-                        cell = json.loads(out.stdout.strip().splitlines()[-1])
+                    spec = ",".join(map(str, (dtype, cps, kt) + shape))
+                    out = subprocess.run(
+                        [sys.executable, "-m", "apk_b200.config3", "--cell", spec, "--events", str(args.events),
+                         "--warmup", str(args.warmup), "--seed", str(args.seed)],
+                        capture_output=True, text=True)
+                    if out.returncode != 0:
+                        raise RuntimeError(f"cell {spec} failed:\n{out.stdout}\n{out.stderr}")
+                    cell = json.loads(out.stdout.strip().splitlines()[-1])
                     cells.append(cell)
                     print(json.dumps(cell), flush=True)
     ran = [c for c in cells if "infeasible" not in c]

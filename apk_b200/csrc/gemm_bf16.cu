@@ -141,6 +141,12 @@ struct __align__(16) Shared {
   uint64_t tfull[2], tempty[2], tres[2];
   uint64_t efull[RING], eempty[RING];
   uint64_t drain;
+  // cluster launch control: the answer of the one request kept in flight,
+  // its barrier, and this CTA's resident slot (the index of its logs,
+  // counters and slab); under the queue scheduler slot = blockIdx.x
+  uint4 clc_resp;
+  uint64_t clc_bar;
+  int slot;
   uint32_t tmem_base;
   int abort;      // CTA-local: some role's bounded wait gave up
   int gen;        // latest yield-flag value seen by the control warp (-1 stop)
@@ -182,8 +188,18 @@ __device__ __noinline__ void bwait_unwind(uint64_t* bar, uint32_t parity, long l
     if (globaltimer_ns() - t0 > limit) return;
 }
 
-template <int POLL, int DISC, bool ORACLE, class G>
+// Work distribution: SCH_QUEUE = persistent grid popping the global fetch-add
+// counter; SCH_CLC = one CTA per task, each running CTA taking
+// not-yet-launched CTAs' tasks with cluster launch control (one request in
+// flight, issued one tile ahead); when the hardware declines a request (a
+// higher-priority stream's kernel waits for SMs) the CTA exits at its next
+// tile boundary and frees its SM.
+enum : int { SCH_QUEUE = 0, SCH_CLC = 1 };
+constexpr unsigned long long NO_TASK = ~0ull;
+
+template <int POLL, int DISC, bool ORACLE, class G, int SCHED = SCH_QUEUE>
 __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __grid_constant__ F32Params p) {
+  constexpr bool CLC = SCHED == SCH_CLC;
   using R = G;
   constexpr int S = G::S, A_HALF = G::A_HALF, A_BYTES = G::A_BYTES, B_CHUNK = G::B_CHUNK, BK = G::BK;
   constexpr int STAGE_BYTES = G::STAGE_BYTES, BM = G::BM, BN = G::BN, EPI_WARPS = G::EPI;
@@ -194,9 +210,14 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
   __shared__ Shared<G::EPI> sh;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int cta = blockIdx.x;
 
   if (tid == 0) {
+    if constexpr (CLC) {
+      mbar_init(&sh.clc_bar, 1);
+      sh.slot = slot_claim(p.q.slot_bits, p.q.nslots, p.wait_limit_ns);
+    } else {
+      sh.slot = (int)blockIdx.x;
+    }
     for (int s = 0; s < S; ++s) {
       mbar_init(&sh.full[s], 1);
       mbar_init(&sh.empty[s], 1);
@@ -231,6 +252,9 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
+  // per-CTA logs, counters and the slab are indexed by the resident slot
+  const int cta = sh.slot;
+  const int gridw = CLC ? p.q.nslots : (int)gridDim.x;
 
   if (warp == 0 && lane == 0) {
     // ================================ producer ================================
@@ -273,7 +297,7 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
     auto handle = [&](int f, int site, bool partial) -> int {
       const int fc = f < p.ev.max_events ? f : p.ev.max_events;
       const long long g = globaltimer_ns();
-      for (int e = lastSeen; e < fc; ++e) p.ev.obs_ns[(size_t)e * gridDim.x + cta] = g;
+      for (int e = lastSeen; e < fc; ++e) p.ev.obs_ns[(size_t)e * gridw + cta] = g;
       const int old = lastSeen;
       lastSeen = f;
       int n = 0;
@@ -294,8 +318,8 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
           }
           ++n;
           const int t = it / p.usplit, ks = it % p.usplit;
-          const int r0 = (t / p.utiles_n) * BM, c0 = (t % p.utiles_n) * BN;
-          const int wide = G::WIDE && c0 + BN <= p.ldcu ? F_WIDE : 0;
+          const int r0 = (t / p.utiles_n) * BM, c0 = (t % p.utiles_n) * (p.narrow_all ? BNH : BN);
+          const int wide = G::WIDE && !p.narrow_all && c0 + BN <= p.ldcu ? F_WIDE : 0;
           for (int c = 0; c < p.unk; ++c) {
             const int kk = (ks * p.unk + c) * BK;
             if (!emit(T_URG, (c == 0 ? F_FIRST : 0) | (c == p.unk - 1 ? F_LAST : 0) | wide, r0, c0, e, it, 0,
@@ -310,11 +334,46 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
     // the queue is popped one task ahead: the atomic's round trip overlaps
     // the current tile's stage issue instead of stalling the ring at every
     // tile boundary (a popped task is kept across a yield and run after it)
-    unsigned long long next_task = atomicAdd(p.q.next_task, 1ull);
+    // CLC: the task of the request answered at this boundary, asked for one
+    // tile earlier (the first is this CTA's own index)
+    uint32_t clc_phase = 0;
+    bool clc_inflight = false;
+    auto clc_issue = [&]() {
+      mbar_arrive_expect_tx(&sh.clc_bar, 16);
+      clc_try_cancel(&sh.clc_resp, &sh.clc_bar);
+      clc_inflight = true;
+    };
+    auto clc_answer = [&]() -> unsigned long long {
+      clc_inflight = false;
+      if (!mbar_wait(&sh.clc_bar, clc_phase, p.wait_limit_ns)) {
+        report_status(p.ev.status, DEV_WAIT_TIMEOUT_SPIN, p.ev.abort_word);
+        return NO_TASK;
+      }
+      clc_phase ^= 1u;
+      unsigned x = 0;
+      return clc_query(&sh.clc_resp, &x) ? (unsigned long long)x : NO_TASK;
+    };
+    if (CLC) {
+      // a CTA launched mid-run takes the generations raised before it as
+      // seen: their urgent work was popped by the CTAs that observed them
+      const int f0 = flag_load(p.ev.flag);
+      lastSeen = f0 > 0 ? f0 : 0;
+      if (cta < 0) {  // no resident slot came free (cannot happen while residency holds)
+        report_status(p.ev.status, DEV_BAD_CONFIG, p.ev.abort_word);
+        ok = false;
+      }
+    }
+    unsigned long long next_task = CLC ? (unsigned long long)blockIdx.x : atomicAdd(p.q.next_task, 1ull);
+    if (CLC && ok) clc_issue();
     while (ok) {
       // ---- tile boundary: take the popped background task ----
       const unsigned long long task = next_task;
-      if (task < p.q.num_tasks) next_task = atomicAdd(p.q.next_task, 1ull);
+      if (CLC) {
+        next_task = clc_inflight ? clc_answer() : NO_TASK;
+        if (next_task != NO_TASK) clc_issue();
+      } else if (task < p.q.num_tasks) {
+        next_task = atomicAdd(p.q.next_task, 1ull);
+      }
       int f = vload(&sh.gen);
       if (f < 0 || vload(&sh.abort)) break;
       if (POLL != POLL_OFF && f != lastSeen)
@@ -351,11 +410,11 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
         else
           tile_coords(tile, p.total_tiles / p.tiles_n, p.tiles_n, RASTER_GROUP, tm, tn);
         row0 = ar0 = tm * BM;
-        col0 = bc0 = tn * BN;
+        col0 = bc0 = tn * (p.narrow_all ? BNH : BN);
         ak0 = bk0 = 0;
         nk = p.nk;
         mvalid = BM;
-        wide = G::WIDE && col0 + BN <= p.ldc ? F_WIDE : 0;
+        wide = G::WIDE && !p.narrow_all && col0 + BN <= p.ldc ? F_WIDE : 0;
         // streamed operands: the A row panel and the B column panel(s) of
         // the tile must have landed before its first TMA load
         if (p.st.a_ready != nullptr) {
@@ -398,6 +457,9 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
       }
     }
     emit(T_STOP, 0, 0, 0, 0, 0, 0, nullptr, nullptr, 0, 0, 0, 0);
+    // a CLC answer still in flight (a stopped or aborted run) lands before
+    // shared memory goes away; a task it took is dropped with the run
+    if (CLC && clc_inflight) mbar_wait(&sh.clc_bar, clc_phase, p.wait_limit_ns);
     vstore(&sh.prod_done, 1);
     // TMA loads still in flight (only when unwinding) must land before exit
     for (uint32_t q = (uint32_t)vload(&sh.consumed); q < P; ++q)
@@ -407,8 +469,11 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
     // TMEM buffer use: ub[b] counts the jobs that took buffer b (the
     // epilogue frees it with one tempty phase per job), rb[b] the restores
     // into it.  cur / cwide: buffer and width of the job being fed.
+    // parked: the buffer holding a suspended narrow background job's
+    // accumulator (park mode), -1 when none; while one is parked every other
+    // job takes the other buffer.
     uint32_t Q = 0, X = 0, ub[2] = {0, 0}, rb[2] = {0, 0};
-    int nb = 0, cur = 0, cwide = 0;
+    int nb = 0, cur = 0, cwide = 0, parked = -1;
     const uint32_t tbase = sh.tmem_base;
     auto post = [&](int action, int buf, int wide, const StageTag& t) -> bool {
       const int sl = X % RING;
@@ -435,18 +500,33 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
         break;
       }
       if (t.kind == T_SUSPEND) {
-        if (!post(E_SPILL, cur, cwide, t)) break;
-        tc::commit(&sh.tfull[cur]);
+        if (G::NBUF == 2 && p.park && !cwide) {
+          // park: the accumulator stays in its buffer, nothing is spilled;
+          // the stages consumed so far have all been committed in order, so
+          // the resumed MMAs continue the same sequence
+          parked = cur;
+          nb = cur ^ 1;
+          if (p.q.ckpt != nullptr) atomicAdd(&p.q.ckpt[4], 1ull);
+        } else {
+          if (!post(E_SPILL, cur, cwide, t)) break;
+          tc::commit(&sh.tfull[cur]);
+        }
         mbar_arrive(&sh.empty[s]);
         ++Q;
         vstore(&sh.consumed, (int)Q);
         continue;
       }
-      if (t.flags & (F_FIRST | F_RESUME)) {
+      if (G::NBUF == 2 && (t.flags & F_RESUME) && parked >= 0) {
+        // resume the parked job in place: no buffer to take, nothing to restore
+        cur = parked;
+        cwide = 0;
+        parked = -1;
+        nb = cur ^ 1;
+      } else if (t.flags & (F_FIRST | F_RESUME)) {
         // a narrow job takes the next buffer, a wide one both
         cwide = (G::WIDE && (t.flags & F_WIDE)) ? 1 : 0;
         cur = cwide ? 0 : nb;
-        nb = (cwide || G::NBUF == 1) ? 0 : nb ^ 1;
+        nb = (cwide || G::NBUF == 1 || parked >= 0) ? (parked >= 0 ? parked ^ 1 : 0) : nb ^ 1;
         bool ok = true;
         for (int b = cur; b <= (cwide ? 1 : cur) && ok; ++b) {
           ok = bwait(&sh.tempty[b], (ub[b] & 1) ^ 1, p, sh);
@@ -685,7 +765,8 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
                 ++sh.tiles;
                 if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[j.task], 1);
                 if (p.st.done != nullptr)  // every warp fenced its stores above
-                  stream_tile_done(p.st, p.total_tiles / p.tiles_n, p.tiles_n, j.row0 / BM, j.col0 / BN);
+                  stream_tile_done(p.st, p.total_tiles / p.tiles_n, p.tiles_n, j.row0 / BM,
+                                   j.col0 / (p.narrow_all ? BNH : BN));
               }
               count_trigger(p.ev);
             } else {
@@ -703,8 +784,14 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
     }
   } else if (warp == CTRL_WARP && lane == 0) {
     // ================================ control =================================
+    // device setter: the CTA in slot 0 (under CLC its state passes from one
+    // slot-0 holder to the next)
     int nextEv = 0;
     long long gBase = 0;
+    if (CLC && cta == 0 && p.q.setter_state != nullptr) {
+      nextEv = (int)p.q.setter_state[0];
+      gBase = p.q.setter_state[1];
+    }
     while (!vload(&sh.prod_done) && !vload(&sh.abort)) {
       int f = POLL != POLL_OFF ? flag_load(p.ev.flag) : 0;
       if (*reinterpret_cast<volatile int*>(p.ev.abort_word)) f = -1;
@@ -720,6 +807,10 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
       vstore(&sh.gen, f);
       __nanosleep(64);
     }
+    if (CLC && cta == 0 && p.q.setter_state != nullptr) {
+      p.q.setter_state[0] = nextEv;
+      p.q.setter_state[1] = gBase;
+    }
   }
 
   tc::fence_before_sync();
@@ -730,21 +821,44 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
     tc::tmem_dealloc(sh.tmem_base, G::TMEM_COLS);
   }
   if (tid == 0) {
-    p.q.tiles_done[cta] = sh.tiles;
+    if (CLC) {
+      if (cta >= 0) atomicAdd(&p.q.tiles_done[cta], sh.tiles);
+    } else {
+      p.q.tiles_done[cta] = sh.tiles;
+    }
     atomicMax(p.q.end_max, (unsigned long long)globaltimer_ns());
     atomicAdd(p.q.exited, 1);
+    if (CLC && cta >= 0) {
+      __threadfence();
+      slot_release(p.q.slot_bits, cta);  // last: the slot's logs are written
+    }
   }
 }
 
 // ---------------------------------------------------------------------------
 
-template <int POLL, int DISC, bool ORACLE, class G>
+template <int POLL, int DISC, bool ORACLE, class G, int SCHED = SCH_QUEUE>
 static const void* kernel_ptr() {
-  return reinterpret_cast<const void*>(&gemm_bf16_persistent<POLL, DISC, ORACLE, G>);
+  return reinterpret_cast<const void*>(&gemm_bf16_persistent<POLL, DISC, ORACLE, G, SCHED>);
 }
 
-// geo: BF16_GEO_* (proto.h)
-static const void* select_kernel(int poll, int disc, bool oracle, int geo) {
+// geo: BF16_GEO_* (proto.h); sched: SCH_QUEUE or SCH_CLC (the one-CTA-per-SM
+// geometries, drain discipline)
+static const void* select_kernel(int poll, int disc, bool oracle, int geo, int sched) {
+  if (sched == SCH_CLC) {
+#define APK_SEL(PL, OR)                                                                          \
+  if (poll == PL && disc == DISC_DRAIN && oracle == OR) {                                       \
+    if (geo == BF16_GEO_STD64) return kernel_ptr<PL, DISC_DRAIN, OR, BgStd64, SCH_CLC>();       \
+    if (geo == BF16_GEO_STD32) return kernel_ptr<PL, DISC_DRAIN, OR, BgStd32, SCH_CLC>();       \
+  }
+    APK_SEL(POLL_OFF, false)
+    APK_SEL(POLL_OFF, true)
+    APK_SEL(POLL_BOUNDARY, false)
+    APK_SEL(POLL_STAGE, false)
+    APK_SEL(POLL_STAGE, true)
+#undef APK_SEL
+    return nullptr;
+  }
 #define APK_SEL(PL, DS, OR)                                                 \
   if (poll == PL && disc == DS && oracle == OR) {                          \
     if (geo == BF16_GEO_STD64) return kernel_ptr<PL, DS, OR, BgStd64>();   \
@@ -803,8 +917,8 @@ static int tmem_cols(int geo) {
 int epi_warps(int geo) { return geo == BF16_GEO_STD64 || geo == BF16_GEO_STD32 ? BgStd64::EPI : BgN128::EPI; }
 size_t params_bytes() { return sizeof(F32Params); }
 
-cudaError_t prepare(int poll, int disc, bool oracle, int geo, int* max_ctas_per_sm) {
-  const void* k = select_kernel(poll, disc, oracle, geo);
+cudaError_t prepare(int poll, int disc, bool oracle, int geo, int sched, int* max_ctas_per_sm) {
+  const void* k = select_kernel(poll, disc, oracle, geo, sched);
   if (!k) return cudaErrorInvalidValue;
   const GeoInfo g = geo_info(geo);
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, g.smem_bytes);
@@ -819,8 +933,9 @@ cudaError_t prepare(int poll, int disc, bool oracle, int geo, int* max_ctas_per_
   return e;
 }
 
-cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int geo, cudaStream_t stream) {
-  const void* k = select_kernel(poll, disc, oracle, geo);
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int geo, int sched,
+                   cudaStream_t stream) {
+  const void* k = select_kernel(poll, disc, oracle, geo, sched);
   if (!k) return cudaErrorInvalidValue;
   const GeoInfo g = geo_info(geo);
   void* args[] = {const_cast<F32Params*>(&prm)};

@@ -165,6 +165,11 @@ struct F32Params {
   const TaskDesc* tasks;
   double* chk;
   int task_mode;
+  // bf16 one-CTA kernel: narrow_all runs background and urgent work as
+  // 256x128 jobs (each holds one of the two TMEM buffers); park keeps a
+  // yielding background job's accumulator in its buffer (the urgent items
+  // use the other one) instead of spilling it to the slab
+  int narrow_all, park;
   long long wait_limit_ns;
   EventProto ev;
   QueueProto q;

@@ -52,8 +52,9 @@ int threads();
 int loads_per_iter();
 }  // namespace vis
 namespace bf16 {
-cudaError_t prepare(int poll, int disc, bool oracle, int geo, int* max_ctas_per_sm);
-cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int geo, cudaStream_t stream);
+cudaError_t prepare(int poll, int disc, bool oracle, int geo, int sched, int* max_ctas_per_sm);
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int geo, int sched,
+                   cudaStream_t stream);
 GeoInfo geo_info(int geo);
 int epi_warps(int geo);
 size_t params_bytes();
@@ -82,7 +83,7 @@ struct Ctrl {
   unsigned long long end_max;
   unsigned long long yields;
   unsigned long long completed;  // completed background tiles (count triggers)
-  unsigned long long ckpt[4];    // checkpoint spill ns, bytes, restore ns, bytes
+  unsigned long long ckpt[5];    // checkpoint spill ns, bytes, restore ns, bytes; TMEM parks
   int exited;
   int abort_word;
   int status;
@@ -277,12 +278,18 @@ size_t esize_of(apk_dtype d) { return d == APK_BF16 ? 2 : 4; }
 // Output tiles: fp32 128x128; bf16 256 rows by 256 columns, the last tile of
 // a row 128 wide when the width is an odd multiple of 128.
 bool use_pair(const apk_ctx* ctx);
+// bf16 NARROW / NARROW_SPILL: 256x128 jobs in the one-CTA kernel
+bool narrow_jobs(const apk_ctx* ctx) {
+  return ctx->cfg.dtype == APK_BF16 &&
+         (ctx->cfg.bf16_kernel == APK_BF16_NARROW || ctx->cfg.bf16_kernel == APK_BF16_NARROW_SPILL);
+}
 int tile_rows(const apk_ctx* ctx) {
   return ctx->cfg.dtype == APK_F32 ? f32::geo_info(ctx->f32_geo).tile_m : bf16::geo_info(ctx->bf16_geo).tile_m;
 }
 int tile_cols(const apk_ctx* ctx) {
   return ctx->cfg.dtype == APK_F32 ? f32::geo_info(ctx->f32_geo).tile_n
          : use_pair(ctx)           ? 512
+         : narrow_jobs(ctx)        ? 128
                                    : bf16::geo_info(ctx->bf16_geo).tile_n;
 }
 int tiles_across(const apk_ctx* ctx, int n) { return (n + tile_cols(ctx) - 1) / tile_cols(ctx); }
@@ -315,7 +322,7 @@ apk_status prepare_kernel(apk_ctx* ctx, int poll) {
   if (ctx->cfg.dtype == APK_F32)
     e = f32::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->f32_geo, ctx->cfg.scheduler, &maxc);
   else
-    e = bf16::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->bf16_geo, &maxc);
+    e = bf16::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->bf16_geo, ctx->cfg.scheduler, &maxc);
   if (e != cudaSuccess)
     return fail(ctx, APK_EUNSUPPORTED, "kernel variant unavailable (dtype %d poll %d disc %d oracle %d k_tile %d): %s",
                 ctx->cfg.dtype, poll, ctx->cfg.discipline, ctx->cfg.oracle, ctx->cfg.k_tile,
@@ -328,7 +335,7 @@ apk_status prepare_kernel(apk_ctx* ctx, int poll) {
     if (e != cudaSuccess) ok = 0;
     ctx->ws_ok = ctx->ws_ok && ok;
   }
-  if (ctx->cfg.dtype == APK_BF16 && ctx->bf16_geo == BF16_GEO_STD64) {
+  if (ctx->cfg.dtype == APK_BF16 && ctx->bf16_geo == BF16_GEO_STD64 && ctx->cfg.scheduler == APK_SCHED_QUEUE) {
     int pairs = 0;
     e = bf16pair::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->sms, &pairs);
     if (e != cudaSuccess) pairs = 0;
@@ -341,7 +348,8 @@ apk_status prepare_kernel(apk_ctx* ctx, int poll) {
 // (no task list) whose N and urgent N are multiples of 256, K-tile 64, one
 // CTA per SM over every SM; the one-CTA kernel runs everything else.
 bool use_pair(const apk_ctx* ctx) {
-  return ctx->cfg.dtype == APK_BF16 && ctx->pair_ok && ctx->cfg.bf16_kernel != APK_BF16_SINGLE &&
+  return ctx->cfg.dtype == APK_BF16 && ctx->pair_ok && ctx->cfg.scheduler == APK_SCHED_QUEUE &&
+         (ctx->cfg.bf16_kernel == APK_BF16_AUTO || ctx->cfg.bf16_kernel == APK_BF16_PAIR) &&
          !ctx->task_mode && ctx->bf16_geo == BF16_GEO_STD64 && ctx->grid == ctx->sms && ctx->N % 256 == 0 &&
          ctx->Nu % 256 == 0;
 }
@@ -435,8 +443,12 @@ apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
     *out = ctx;
     return APK_EINVAL;
   }
-  if (c.scheduler == APK_SCHED_CLC && (c.dtype != APK_F32 || c.discipline != APK_DISC_DRAIN)) {
-    fail(ctx, APK_EUNSUPPORTED, "the cluster-launch-control scheduler is built for fp32 with the drain discipline");
+  if (c.scheduler == APK_SCHED_CLC &&
+      (c.discipline != APK_DISC_DRAIN || (c.dtype == APK_BF16 && c.ctas_per_sm > 1) ||
+       (c.dtype == APK_F32 && c.ctas_per_sm > 2))) {
+    fail(ctx, APK_EUNSUPPORTED,
+         "the cluster-launch-control scheduler is built for the drain discipline and the 128x128 fp32 / one-CTA bf16 "
+         "geometries");
     *out = ctx;
     return APK_EUNSUPPORTED;
   }
@@ -464,6 +476,8 @@ apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
   }
   ctx->ctas_per_sm = c.ctas_per_sm > 0 ? std::min(c.ctas_per_sm, ctx->max_ctas_per_sm) : ctx->max_ctas_per_sm;
   ctx->grid = c.grid > 0 ? c.grid : ctx->sms * ctx->ctas_per_sm;
+  if (narrow_jobs(ctx) && ctx->bf16_geo != BF16_GEO_STD64 && ctx->bf16_geo != BF16_GEO_STD32)
+    return fail(ctx, APK_EUNSUPPORTED, "the NARROW bf16 kernels run one CTA per SM (ctas_per_sm 0 or 1)");
   if (c.dtype == APK_BF16 && c.bf16_kernel == APK_BF16_PAIR && !use_pair(ctx))
     return fail(ctx, APK_EUNSUPPORTED,
                 "the CTA-pair bf16 kernel needs K-tile 64, one CTA on each of an even number of SMs and "
@@ -1015,6 +1029,8 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
   p.unk = ctx->Ku ? ctx->Ku / bk / p.usplit : 0;
   p.uitems = (ctx->Mu / tm) * p.utiles_n * p.usplit;
   p.poll_every = ctx->poll_every;
+  p.narrow_all = narrow_jobs(ctx) ? 1 : 0;
+  p.park = ctx->cfg.dtype == APK_BF16 && ctx->cfg.bf16_kernel == APK_BF16_NARROW ? 1 : 0;
   p.slab = ctx->d_slab;
   p.slab_hdr = ctx->d_slab_hdr;
   p.wait_limit_ns = ctx->cfg.wait_limit_ns;
@@ -1029,7 +1045,8 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
   else if (use_pair(ctx))
     e = bf16pair::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, stream);
   else
-    e = bf16::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->bf16_geo, stream);
+    e = bf16::launch(p, clc ? (int)num_tasks : ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0,
+                     ctx->bf16_geo, ctx->cfg.scheduler, stream);
   if (e != cudaSuccess) return fail(ctx, APK_ECUDA, "kernel launch failed: %s", cudaGetErrorString(e));
   if (record) APK_CU(cudaEventRecord(ctx->ev_done, stream));
   return APK_OK;
@@ -1459,6 +1476,7 @@ apk_status apk_read_run_stats(apk_ctx* ctx, apk_run_stats* st) {
         use_pair(ctx) ? 2ull * bf16pair::epi_warps() : (unsigned long long)bf16::epi_warps(ctx->bf16_geo);
     st->ckpt_spill_ns = (long long)(cb.ckpt[0] / w);
     st->ckpt_restore_ns = (long long)(cb.ckpt[2] / w);
+    st->parks = cb.ckpt[4];
   }
   if (ctx->task_mode) {
     // tiles differ in size: a complete drain did every task's 2*m*n*k; a

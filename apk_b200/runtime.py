@@ -22,7 +22,7 @@ _SET = {"device": L.APK_SET_DEVICE, "host_mapped": L.APK_SET_HOST_MAPPED,
 _DTYPE = {"f32": L.APK_F32, "bf16": L.APK_BF16}
 _SCHED = {"queue": L.APK_SCHED_QUEUE, "clc": L.APK_SCHED_CLC}
 _F32K = {"auto": 0, "ws": 1, "sync": 2}
-_BF16K = {"auto": 0, "pair": 1, "single": 2}
+_BF16K = {"auto": 0, "pair": 1, "single": 2, "narrow": 3, "narrow_spill": 4}
 
 
 class ApkError(RuntimeError):

@@ -73,7 +73,8 @@ typedef enum apk_mem_kind { APK_MEM_HOST = 0, APK_MEM_DEVICE = 1 } apk_mem_kind;
 
 /* How background tasks reach CTAs.  QUEUE: a persistent grid of resident
  * CTAs popping a global fetch-add counter (src/persistent.cu:51-79).  CLC
- * (fp32, drain discipline, bounded launches only): one CTA per task, running
+ * (fp32 128x128 tiles and the one-CTA bf16 kernel, task mode included; drain
+ * discipline, bounded launches only): one CTA per task, running
  * CTAs take not-yet-launched CTAs' tasks through Blackwell cluster launch
  * control; when the hardware declines (a higher-priority stream's kernel is
  * waiting) CTAs exit and free their SMs, and the rest of the grid launches
@@ -104,7 +105,15 @@ typedef enum apk_f32_kernel {
 typedef enum apk_bf16_kernel {
   APK_BF16_AUTO = 0,
   APK_BF16_PAIR = 1,
-  APK_BF16_SINGLE = 2
+  APK_BF16_SINGLE = 2,
+  /* (ABI 4) one CTA per SM, every background and urgent job 256x128 (one
+   * of the two 256-column TMEM buffers each, so a job's epilogue overlaps
+   * the next job's MMAs).  NARROW parks a yielding background job's
+   * accumulator in its buffer while the urgent items use the other one:
+   * nothing is spilled or restored.  NARROW_SPILL checkpoints it to the
+   * slab like the other kernels (the comparison arm). */
+  APK_BF16_NARROW = 3,
+  APK_BF16_NARROW_SPILL = 4
 } apk_bf16_kernel;
 
 typedef struct apk_config {
@@ -269,6 +278,8 @@ typedef struct apk_run_stats {
    * tcgen05.st complete).  bytes / ns = a CTA's checkpoint GB/s. */
   unsigned long long ckpt_spill_bytes, ckpt_restore_bytes;
   long long ckpt_spill_ns, ckpt_restore_ns;
+  unsigned long long parks;          /* (ABI 4) bf16 NARROW: checkpoints kept in
+                                        TMEM instead of spilled               */
 } apk_run_stats;
 apk_status apk_read_run_stats(apk_ctx* ctx, apk_run_stats* st);
 

@@ -290,3 +290,101 @@ def test_k_tile_32_stage_yield_bitwise(libapk):
         assert bad == 0 and nans == 0
     v = oracle.exactly_once(ex, ue[:fired], ev["claimer"][:fired], ev["set_ns"][:fired], 1, fired)
     assert v["pass"], v
+
+
+@pytest.mark.parametrize("kernel", ["narrow", "narrow_spill"])
+def test_narrow_jobs_park_or_spill_bitwise(libapk, kernel):
+    """256x128 background and urgent jobs, each in one of the two TMEM
+    buffers.  NARROW parks a yielding background job's accumulator in its
+    buffer while the urgent items run in the other (no spill or restore
+    bytes); NARROW_SPILL checkpoints it to the slab.  Either way the resumed
+    MMAs continue the same sequence: C bitwise equal to the one-CTA
+    kernel's uninterrupted drain, every urgent output within 1e-2 of
+    float64, exactly once."""
+    M = N = K = 4096
+    A, B = _normal((M, K), 21), _normal((K, N), 22)
+    Au, Bu = _normal((256, 256), 31), _normal((256, 256), 32)
+    refu = oracle.gemm_f64_bf16_rows(Au, Bu, 0, 256)
+    with _ctx(poll="off", bf16_kernel="single") as c:
+        C0 = c.gemm(A, B)
+    nev = 30
+    with _ctx(poll="stage", set_mode="device", oracle=True, bf16_kernel=kernel, max_events=64) as c:
+        info = c.info
+        assert (info["tile_m"], info["tile_n"]) == (256, 128)
+        ntasks = 8 * (M // 256) * (N // 128)
+        c.set_background(A, B)
+        c.set_urgent(Au, Bu)
+        c.schedule_device_events((np.arange(nev, dtype=np.int64) + 1) * 20_000)
+        c.launch(ntasks)
+        c.wait(60)
+        C = c.read_output()
+        ev = c.read_events()
+        st = c.run_stats()
+        ex, ue = c.read_oracle(ntasks)
+        fired = int(np.count_nonzero(ev["set_ns"][:nev]))
+        outs = [c.read_urgent_output(e) for e in range(fired) if ev["claimer"][e]]
+    assert fired >= 10 and st["yields"] > 0
+    if kernel == "narrow":
+        assert st["parks"] == st["yields"] and st["ckpt_spill_bytes"] == 0 and st["ckpt_restore_bytes"] == 0
+    else:
+        assert st["parks"] == 0 and st["ckpt_spill_bytes"] == st["yields"] * 256 * 128 * 4
+    assert np.array_equal(C.view(np.uint32), C0.view(np.uint32)), "resume not bitwise"
+    for Cu in outs:
+        mr, bad, nans = oracle.check(Cu, refu, TOL)
+        assert bad == 0 and nans == 0, f"urgent: {bad} bad, max rel {mr:.3e}"
+    v = oracle.exactly_once(ex, ue[:fired], ev["claimer"][:fired], ev["set_ns"][:fired], 2, fired)
+    assert v["pass"], v
+
+
+def test_clc_scheduler_drain_exactly_once_bitwise(libapk):
+    """bf16 under cluster launch control: one CTA per task, running CTAs
+    take the pending ones; every task exactly once and C bitwise equal to
+    the queue-scheduled one-CTA kernel's."""
+    M, N, K = 2048, 2048, 1024
+    A, B = _normal((M, K), 51), _normal((K, N), 52)
+    with _ctx(poll="off", bf16_kernel="single") as c:
+        C0 = c.gemm(A, B)
+    ntasks = 3 * (M // 256) * (N // 256)
+    with _ctx(poll="off", oracle=True, scheduler="clc") as c:
+        C = c.gemm(A, B)
+        st = c.run_stats()
+        c.set_background(A, B)
+        c.launch(ntasks)
+        c.wait(30)
+        ex, _ = c.read_oracle(ntasks)
+    assert np.array_equal(C.view(np.uint32), C0.view(np.uint32))
+    assert st["tiles_done"] == (M // 256) * (N // 256) and st["device_status"] == 0
+    assert np.all(ex == 1)
+
+
+def test_clc_stage_yields_bitwise(libapk):
+    """bf16 CLC with per-stage device-set yields: checkpoints resume
+    bitwise; every task and urgent item exactly once."""
+    M = N = K = 4096
+    A, B = _normal((M, K), 21), _normal((K, N), 22)
+    Au, Bu = _normal((256, 256), 31), _normal((256, 256), 32)
+    refu = oracle.gemm_f64_bf16_rows(Au, Bu, 0, 256)
+    with _ctx(poll="off", bf16_kernel="single") as c:
+        C0 = c.gemm(A, B)
+    nev = 30
+    with _ctx(poll="stage", set_mode="device", oracle=True, scheduler="clc", max_events=64) as c:
+        ntasks = 8 * (M // 256) * (N // 256)
+        c.set_background(A, B)
+        c.set_urgent(Au, Bu)
+        c.schedule_device_events((np.arange(nev, dtype=np.int64) + 1) * 20_000)
+        c.launch(ntasks)
+        c.wait(60)
+        C = c.read_output()
+        ev = c.read_events()
+        st = c.run_stats()
+        ex, ue = c.read_oracle(ntasks)
+        fired = int(np.count_nonzero(ev["set_ns"][:nev]))
+        outs = [c.read_urgent_output(e) for e in range(fired) if ev["claimer"][e]]
+    assert fired >= 10 and st["yields"] > 0 and st["device_status"] == 0
+    assert any(ev["claim_site"][e] > 0 for e in range(fired) if ev["claimer"][e]), "no mid-pipeline claim"
+    assert np.array_equal(C.view(np.uint32), C0.view(np.uint32)), "resume not bitwise"
+    for Cu in outs:
+        mr, bad, nans = oracle.check(Cu, refu, TOL)
+        assert bad == 0 and nans == 0
+    v = oracle.exactly_once(ex, ue[:fired], ev["claimer"][:fired], ev["set_ns"][:fired], 1, fired)
+    assert v["pass"], v

@@ -138,3 +138,17 @@ def test_config4_poisson_host_stream_2e16_tasks(libapk):
     assert out["corrupted"] == 0
     assert out["arrivals"] >= 20 and out["urgent_claimed"] == out["arrivals"], res
     assert out["urgent_outputs_ok"] and out["checkpoints"] > 0
+
+
+def test_clc_scheduler_task_queue_bitwise(whole_run):
+    """The task list under cluster launch control (one CTA per work entry):
+    every half-tile exactly once, checksums bitwise equal to the queue run."""
+    tasks, n_chk = whole_run["tasks"], whole_run["n_chk"]
+    with _ctx(poll="off", oracle=True, scheduler="clc") as c:
+        _run(c, whole_run["A"], whole_run["B"], whole_run["pool"], tasks, n_chk)
+        chk = c.read_checksums()
+        ex, _ = c.read_oracle(n_chk)
+        st = c.run_stats()
+    assert st["device_status"] == 0
+    assert np.all(ex == 1)
+    assert np.array_equal(chk.view(np.uint64), whole_run["chk"].view(np.uint64))
