@@ -637,7 +637,7 @@ apk_status apk_get_info(apk_ctx* ctx, apk_device_info* info) {
     info->smem_per_cta = g.smem_bytes;
     info->threads_per_cta = g.threads;
     info->tile_m = g.tile_m;
-    info->tile_n = g.tile_n;
+    info->tile_n = tile_cols(ctx);  // 128 for the NARROW kernels' 256x128 jobs
     info->stages = g.stages;
   }
   info->k_tile = ctx->cfg.k_tile;
