@@ -54,10 +54,10 @@ def test_quantiles_known_answer():
     assert sp["spread_p50_us"] == 99.0 and sp["first_p50_us"] == 1.0
 
 
-def test_maxofn_predicts_iid_maxima():
+def test_independent_max_model_predicts_iid_maxima():
     rng = np.random.default_rng(21)
     rows = rng.exponential(2.0, size=(4000, 16)).tolist()
-    m = obs.maxofn(rows)
+    m = obs.independent_max_model(rows)
     for q in m["quantiles"][:3]:
         assert abs(q["predicted_us"] - q["measured_us"]) / q["measured_us"] < 0.08, q
 
