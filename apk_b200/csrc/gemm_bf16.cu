@@ -49,6 +49,7 @@
 //     (256 / 128 / 64: the SM's 512 columns shared by 2 / 4 / 8 CTAs) and
 //     four epilogue warps, one per TMEM lane quadrant.  The CTAs sharing an
 //     SM overlap each other's epilogues with their MMAs.
+#include <algorithm>
 #include <string>
 
 #include "../../include/apk.h"
@@ -925,12 +926,33 @@ cudaError_t prepare(int poll, int disc, bool oracle, int geo, int sched, int* ma
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return e;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(max_ctas_per_sm, k, g.threads, g.smem_bytes);
-  // a CTA allocates TMEM_COLS of the SM's 512 TMEM columns: never more CTAs
-  // per SM than fit (an allocation would wait for another CTA's release)
+  // Residency from the kernel's own resources.  The occupancy calculator
+  // answers 1 for every kernel that allocates tensor memory (on B200 with
+  // driver 580 even 32 threads and no shared memory gave 1), while the
+  // hardware places 2, 4 and 8 of the multi-CTA geometries on one SM: in a
+  // launch of that many CTAs per SM every CTA observed a device-set event
+  // within 4 us of its raise.  So the count is computed here: shared memory
+  // (with the per-CTA reservation), registers (allocated per warp in units of
+  // 256), threads, and the CTA's share of the SM's 512 TMEM columns (an
+  // allocation beyond them would wait for another CTA's release).
+  cudaFuncAttributes fa;
+  if ((e = cudaFuncGetAttributes(&fa, k)) != cudaSuccess) return e;
+  int dev = 0, smem_sm = 0, smem_rsv = 0, thr_sm = 0, regs_sm = 0, blk_sm = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev)) != cudaSuccess ||
+      (e = cudaDeviceGetAttribute(&smem_rsv, cudaDevAttrReservedSharedMemoryPerBlock, dev)) != cudaSuccess ||
+      (e = cudaDeviceGetAttribute(&thr_sm, cudaDevAttrMaxThreadsPerMultiProcessor, dev)) != cudaSuccess ||
+      (e = cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev)) != cudaSuccess ||
+      (e = cudaDeviceGetAttribute(&blk_sm, cudaDevAttrMaxBlocksPerMultiprocessor, dev)) != cudaSuccess)
+    return e;
+  const int warps = (g.threads + 31) / 32;
+  const int regs_per_warp = ((fa.numRegs * 32 + 255) / 256) * 256;
+  const int by_smem = smem_sm / (g.smem_bytes + (int)fa.sharedSizeBytes + smem_rsv);
+  const int by_regs = regs_per_warp > 0 ? regs_sm / (regs_per_warp * warps) : blk_sm;
+  const int by_threads = thr_sm / g.threads;
   const int tmem_cap = 512 / tmem_cols(geo);
-  if (e == cudaSuccess && *max_ctas_per_sm > tmem_cap) *max_ctas_per_sm = tmem_cap;
-  return e;
+  *max_ctas_per_sm = std::min(std::min(std::min(by_smem, by_regs), std::min(by_threads, blk_sm)), tmem_cap);
+  return cudaSuccess;
 }
 
 cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, int geo, int sched,
