@@ -431,10 +431,15 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
         }
       }
       bool resume = false;
+      // the control warp's flag copy is read one slot ahead: the shared
+      // load's latency overlaps the previous slot's issue instead of sitting
+      // on the producer's path (with 32-deep slots the producer is the
+      // critical path: reading it at the site cost ~10% of the drain)
+      int fs_next = POLL == POLL_STAGE ? vload(&sh.gen) : 0;
       for (int c = 0; c < nk && ok; ++c) {
         // a yield site every poll_every ring slots (one K-tile)
         if (POLL == POLL_STAGE && (p.poll_every <= 1 || c % p.poll_every == 0)) {
-          const int fs = vload(&sh.gen);
+          const int fs = fs_next;
           if (fs < 0) {
             ok = false;  // stop sentinel: abandon the tile
             break;
@@ -452,6 +457,7 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
                           (BM == 256 && mvalid <= BNH ? F_HALF : 0);
         resume = false;
         // e carries the valid rows of the tile, task the oracle / checksum index
+        if (POLL == POLL_STAGE) fs_next = vload(&sh.gen);
         if (!emit(T_BG, flags, row0, col0, mvalid, 0, tag_task, &p.tmA, &p.tmB, ar0, bc0, ak0 + c * BK,
                   bk0 + c * BK))
           ok = false;
@@ -793,6 +799,13 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
       nextEv = (int)p.q.setter_state[0];
       gBase = p.q.setter_state[1];
     }
+    // one poller per CTA: with c CTAs per SM each polls every 64*c ns, so an
+    // SM loads the flag at the same rate whatever c is (8 CTAs per SM polling
+    // every 64 ns each cost a third of the drain: 1184 pollers on one line)
+    unsigned nsm;
+    asm volatile("mov.u32 %0, %%nsmid;" : "=r"(nsm));
+    const int per_sm = nsm > 0 && gridw > (int)nsm ? gridw / (int)nsm : 1;
+    const unsigned sleep_ns = 64u * (unsigned)per_sm;
     while (!vload(&sh.prod_done) && !vload(&sh.abort)) {
       int f = POLL != POLL_OFF ? flag_load(p.ev.flag) : 0;
       if (*reinterpret_cast<volatile int*>(p.ev.abort_word)) f = -1;
@@ -806,7 +819,7 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
         }
       }
       vstore(&sh.gen, f);
-      __nanosleep(64);
+      __nanosleep(sleep_ns);
     }
     if (CLC && cta == 0 && p.q.setter_state != nullptr) {
       p.q.setter_state[0] = nextEv;
