@@ -65,17 +65,23 @@ constexpr int T = 4 * S;
 constexpr int RASTER_GROUP = 8;
 // D = C_cols^T: MMA A = the B columns (MN-major), MMA B = the A rows (K-major)
 constexpr uint32_t IDESC = tc::idesc_bf16_f32(256, 256, true, false);
+// a task tile with 128 valid rows: N = 128, each CTA staging 64 of them
+constexpr uint32_t IDESC_HALF = tc::idesc_bf16_f32(256, 128, true, false);
 
 enum : int { T_BG = 1, T_URG = 2, T_SUSPEND = 3, T_STOP = 4 };
-enum : int { F_FIRST = 1, F_LAST = 2, F_RESUME = 4, F_WIDE = 8 };
+enum : int { F_FIRST = 1, F_LAST = 2, F_RESUME = 4, F_WIDE = 8, F_HALF = 16 };
 enum : int { E_STORE_C = 1, E_STORE_U = 2, E_SPILL = 3, E_RESTORE = 4, E_EXIT = 5 };
 
+// row0 / col0: the job's output origin; e: the urgent event, or for a
+// background job its valid rows; ncols: its valid columns (512 for a wide
+// pair tile, 256, or 128 for a task tile whose n ends 128 columns in: the
+// peer's half is computed but not stored)
 struct StageTag {
-  int kind, flags, row0, col0, e, item, k, pad;
+  int kind, flags, row0, col0, e, item, k, ncols;
   unsigned long long task;
 };
 struct EpiJob {
-  int action, buf, wide, row0, col0, e, item, pad;
+  int action, buf, wide, row0, col0, e, item, ncols;
   unsigned long long task;
 };
 
@@ -93,6 +99,10 @@ struct __align__(16) Shared {
   int prod_done;
   int consumed;
   int epi_cnt[RING];
+  // task mode: this CTA's 8 epilogue warps' sum(c^2) partials of its 128
+  // columns of a job and their count (the CTA's own accounting)
+  double chk_part[RING][EPI_WARPS];
+  int cta_cnt[RING];
   unsigned long long tiles;
 };
 
@@ -157,12 +167,13 @@ __device__ __forceinline__ void tma_load_pair(void* dst, const CUtensorMap* tm, 
       "l"(tm), "r"(x), "r"(y), "r"(bar)
       : "memory");
 }
-__device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
+__device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t acc,
+                                         uint32_t idesc = IDESC) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(acc)
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
       : "memory");
 }
 // one arrival on the barrier (either CTA) once this thread's pair MMAs completed
@@ -221,6 +232,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
       mbar_init(&sh.efull[r], 1);
       mbar_init(&sh.eempty[r], 2 * EPI_WARPS);
       sh.epi_cnt[r] = 0;
+      sh.cta_cnt[r] = 0;
     }
     mbar_init(&sh.drain, 1);
     fence_mbar_init();
@@ -252,14 +264,23 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
     uint32_t P = 0;
     int lastSeen = 0;
     bool ok = true;
+    // One slot: the job's output origin (row0, col0) and bookkeeping travel
+    // with the tag; the leader loads A rows from ar0 and B columns from bc0
+    // at k offsets ak / bk (they differ in task mode, where A, B and C are
+    // windows of pools), the peer A rows from ar0 + 128 (+ 64 for a
+    // 128-row task tile, whose N = 128 MMAs take 64 rows from each CTA).
     auto emit = [&](int kind, int flags, int row0, int col0, int e, int item, unsigned long long task,
-                    const CUtensorMap* tA, const CUtensorMap* tB, int k) -> bool {
+                    const CUtensorMap* tA, const CUtensorMap* tB, int ar0, int bc0, int ak, int bk,
+                    int ncols) -> bool {
       // first the peer's copy of the tag, into its tag ring: the peer then
       // issues its loads the moment its slot frees, in step with the
-      // leader's own
+      // leader's own.  {kind | flags << 8 | (bk - ak) << 16, peer A row,
+      // B column base, ak}
       const int ti = P % T;
-      st_async_v4(mapa(&sh.ptag[ti], 1), make_uint4((uint32_t)kind | ((uint32_t)flags << 8), (uint32_t)row0,
-                                                    (uint32_t)col0, (uint32_t)k),
+      const int peer_ar0 = ar0 + ((flags & F_HALF) ? 64 : 128);
+      st_async_v4(mapa(&sh.ptag[ti], 1),
+                  make_uint4((uint32_t)kind | ((uint32_t)flags << 8) | ((uint32_t)(bk - ak) << 16),
+                             (uint32_t)peer_ar0, (uint32_t)bc0, (uint32_t)ak),
                   mapa(&sh.tagfull[ti], 1));
       const int s = P % S;
       if (!bwait(&sh.empty[s], ((P / S) & 1) ^ 1, p, sh)) return false;
@@ -270,16 +291,17 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
       t.col0 = col0;
       t.e = e;
       t.item = item;
-      t.k = k;
+      t.k = ak;
+      t.ncols = ncols;
       t.task = task;
       if (tA != nullptr) {
         const int nb = (flags & F_WIDE) ? 4 : 2;
         mbar_arrive_expect_tx(&sh.full[s], 2 * (A_BYTES + nb * B_CHUNK));
         uint8_t* st = stages + s * STAGE_BYTES;
         const uint32_t fb = mapa(&sh.full[s], 0);
-        tma_load_pair(st, tA, k, row0, fb);
+        tma_load_pair(st, tA, ak, ar0, fb);
         for (int b = 0; b < nb; ++b)
-          tma_load_pair(st + A_BYTES + b * B_CHUNK, tB, col0 + 256 * (b >> 1) + 64 * (b & 1), k, fb);
+          tma_load_pair(st + A_BYTES + b * B_CHUNK, tB, bc0 + 256 * (b >> 1) + 64 * (b & 1), bk, fb);
       } else {
         mbar_arrive(&sh.full[s]);  // control slot: no data
       }
@@ -310,7 +332,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
             if (p.ev.ack != nullptr) ack_host(&p.ev.ack[2 * e]);
           }
           if (n == 0 && partial) {
-            if (!emit(T_SUSPEND, 0, 0, 0, 0, 0, 0, nullptr, nullptr, 0)) return -1;
+            if (!emit(T_SUSPEND, 0, 0, 0, 0, 0, 0, nullptr, nullptr, 0, 0, 0, 0, 0)) return -1;
             atomicAdd(p.q.yields, 1ull);
           }
           ++n;
@@ -320,7 +342,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
           for (int c = 0; c < p.unk; ++c) {
             const int kk = (ks * p.unk + c) * BK;
             if (!emit(T_URG, (c == 0 ? F_FIRST : 0) | (c == p.unk - 1 ? F_LAST : 0) | wide, r0, c0, e, it, 0,
-                      &p.tmAu, &p.tmBu, kk))
+                      &p.tmAu, &p.tmBu, r0, c0, kk, kk, wide ? 512 : 256))
               return -1;
           }
         }
@@ -340,14 +362,42 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
           break;
         }
       if (task >= p.q.num_tasks) break;
-      const int tile = (int)(task % (unsigned long long)p.total_tiles);
-      int tm, tn;
-      if (p.st.order != nullptr)
-        stream_tile(p.st, tile, p.tiles_n, tm, tn);
-      else
-        tile_coords(tile, p.total_tiles / p.tiles_n, p.tiles_n, RASTER_GROUP, tm, tn);
-      const int row0 = tm * BM, col0 = tn * BN;
-      const int wide = col0 + BN <= p.ldc ? F_WIDE : 0;
+      // job geometry: output origin, operand origins and k offsets, K steps,
+      // valid rows and columns, width (wide = 512 columns over two
+      // accumulators, else 256 in one)
+      int row0, col0, ar0, bc0, ak0 = 0, bk0 = 0, nk = p.nk, mvalid = BM, wide = 0, ncols;
+      unsigned long long tag_task = task;
+      int tm = 0, tn = 0;
+      if (p.task_mode) {
+        // work entry: task, tile row, first 128-column block of the tile;
+        // every task tile is a 256x256 pair job (a tile whose n ends 128
+        // columns in computes the peer's half without storing it)
+        const unsigned w = p.work[task];
+        const TaskDesc td = p.tasks[w >> 12];
+        tm = (w >> 6) & 63;
+        tn = w & 63;
+        row0 = td.c_row0 + tm * BM;
+        col0 = td.c_col0 + tn * 128;
+        ar0 = td.a_row0 + tm * BM;
+        bc0 = td.b_col0 + tn * 128;
+        ak0 = td.a_k0;
+        bk0 = td.b_k0;
+        nk = td.k / BK;
+        mvalid = (td.m - tm * BM) < BM ? (td.m - tm * BM) : BM;
+        ncols = (tn + 2) * 128 <= td.n ? 256 : 128;
+        // checksum / oracle index of the tile's first 256x128 half
+        tag_task = (unsigned long long)(td.chk_base + (long long)tm * (td.n / 128) + tn);
+      } else {
+        const int tile = (int)(task % (unsigned long long)p.total_tiles);
+        if (p.st.order != nullptr)
+          stream_tile(p.st, tile, p.tiles_n, tm, tn);
+        else
+          tile_coords(tile, p.total_tiles / p.tiles_n, p.tiles_n, RASTER_GROUP, tm, tn);
+        row0 = ar0 = tm * BM;
+        col0 = bc0 = tn * BN;
+        wide = col0 + BN <= p.ldc ? F_WIDE : 0;
+        ncols = wide ? 512 : 256;
+      }
       if (p.st.a_ready != nullptr) {
         // every 128-column B unit of the tile must have landed
         const int* ar = &p.st.a_ready[tm / p.st.panel_tm];
@@ -364,7 +414,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
         }
       }
       bool resume = false;
-      for (int c = 0; c < p.nk && ok; ++c) {
+      for (int c = 0; c < nk && ok; ++c) {
         // a yield site every poll_every ring slots (one K-tile)
         if (POLL == POLL_STAGE && (p.poll_every <= 1 || c % p.poll_every == 0)) {
           const int fs = vload(&sh.gen);
@@ -381,12 +431,15 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
             if (n > 0 && c > 0) resume = true;
           }
         }
-        const int flags = (c == 0 ? F_FIRST : 0) | (c == p.nk - 1 ? F_LAST : 0) | (resume ? F_RESUME : 0) | wide;
+        const int flags = (c == 0 ? F_FIRST : 0) | (c == nk - 1 ? F_LAST : 0) | (resume ? F_RESUME : 0) | wide |
+                          (mvalid <= 128 ? F_HALF : 0);
         resume = false;
-        if (!emit(T_BG, flags, row0, col0, 0, 0, task, &p.tmA, &p.tmB, c * BK)) ok = false;
+        if (!emit(T_BG, flags, row0, col0, mvalid, 0, tag_task, &p.tmA, &p.tmB, ar0, bc0, ak0 + c * BK,
+                  bk0 + c * BK, ncols))
+          ok = false;
       }
     }
-    emit(T_STOP, 0, 0, 0, 0, 0, 0, nullptr, nullptr, 0);
+    emit(T_STOP, 0, 0, 0, 0, 0, 0, nullptr, nullptr, 0, 0, 0, 0, 0);
     vstore(&sh.prod_done, 1);
     // loads still in flight (only when unwinding) land before teardown
     for (uint32_t q = (uint32_t)vload(&sh.consumed); q < P; ++q)
@@ -397,7 +450,6 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
     // that read the slot's previous use have completed (its empty barrier,
     // committed by the leader's MMA warp).
     uint32_t P = 0;
-    const uint32_t rowoff = 128;
     while (true) {
       const int ti = P % T, s = P % S;
       // this entry's phase: our arrival plus the leader's 16-byte store
@@ -406,9 +458,10 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
       const uint4 w = sh.ptag[ti];
       StageTag t;
       t.kind = (int)(w.x & 0xFF);
-      t.flags = (int)(w.x >> 8);
-      t.row0 = (int)w.y;
-      t.col0 = (int)w.z;
+      t.flags = (int)((w.x >> 8) & 0xFF);
+      const int dk = (int)(int16_t)(w.x >> 16);  // B's k offset minus A's
+      t.row0 = (int)w.y;                         // this CTA's first A row
+      t.col0 = (int)w.z;                         // the job's B column base
       t.k = (int)w.w;
       if (t.kind == T_STOP) break;
       if (t.kind == T_BG || t.kind == T_URG) {
@@ -418,16 +471,17 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
         if (t.kind == T_BG && (t.flags & F_FIRST) && p.st.a_ready != nullptr) {
           // the leader saw the panels land; order this CTA's loads after it
           const int u0 = t.col0 / 128;
-          if (!wait_ready2(&p.st.a_ready[(t.row0 / BM) / p.st.panel_tm],
+          if (!wait_ready2(&p.st.a_ready[((t.row0 - 128) / BM) / p.st.panel_tm],
                            &p.st.b_ready[(u0 + ((t.flags & F_WIDE) ? 3 : 1)) / p.st.b_units], p.wait_limit_ns))
             break;
         }
         const int nb = (t.flags & F_WIDE) ? 4 : 2;
         uint8_t* st = stages + s * STAGE_BYTES;
         const uint32_t fb = mapa(&sh.full[s], 0);
-        tma_load_pair(st, tA, t.k, t.row0 + rowoff, fb);
+        tma_load_pair(st, tA, t.k, t.row0, fb);
         for (int b = 0; b < nb; ++b)
-          tma_load_pair(st + A_BYTES + b * B_CHUNK, tB, t.col0 + 256 * (b >> 1) + 128 + 64 * (b & 1), t.k, fb);
+          tma_load_pair(st + A_BYTES + b * B_CHUNK, tB, t.col0 + 256 * (b >> 1) + 128 + 64 * (b & 1), t.k + dk,
+                        fb);
       }
       ++P;
     }
@@ -447,6 +501,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
       j.col0 = t.col0;
       j.e = t.e;
       j.item = t.item;
+      j.ncols = t.ncols;
       j.task = t.task;
       const uint32_t pj = mapa(&j, 1);
       st_cluster_u32(pj + offsetof(EpiJob, action), (uint32_t)action);
@@ -456,6 +511,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
       st_cluster_u32(pj + offsetof(EpiJob, col0), (uint32_t)t.col0);
       st_cluster_u32(pj + offsetof(EpiJob, e), (uint32_t)t.e);
       st_cluster_u32(pj + offsetof(EpiJob, item), (uint32_t)t.item);
+      st_cluster_u32(pj + offsetof(EpiJob, ncols), (uint32_t)t.ncols);
       st_cluster_u64(pj + offsetof(EpiJob, task), t.task);
       mbar_arrive(&sh.efull[sl]);
       arrive_cluster(mapa(&sh.efull[sl], 1));
@@ -510,7 +566,8 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
       for (int kk = 0; kk < BK / 16; ++kk) {
         const uint32_t acc = (kk > 0 || !(t.flags & F_FIRST)) ? 1u : 0u;
         const uint64_t bdesc = tc::smem_desc(sa + kk * 32, 16, 1024, tc::LAYOUT_SW128);
-        mma_pair(d0, tc::smem_desc(sb + kk * 2048, B_CHUNK, 1024, tc::LAYOUT_SW128), bdesc, acc);
+        mma_pair(d0, tc::smem_desc(sb + kk * 2048, B_CHUNK, 1024, tc::LAYOUT_SW128), bdesc, acc,
+                 (t.flags & F_HALF) ? IDESC_HALF : IDESC);
         if (cwide)
           mma_pair(d0 + 256, tc::smem_desc(sb + 2 * B_CHUNK + kk * 2048, B_CHUNK, 1024, tc::LAYOUT_SW128), bdesc,
                    acc);
@@ -584,6 +641,18 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
         tc::fence_after_sync();
         const long long s0 = globaltimer_ns();
         const int lim = 8 * nh;
+        // rows past the job's valid rows, and this CTA's columns when the
+        // job's valid columns end before them, are neither stored nor summed
+        const bool cols_ok = 128 * (int)rank < j.ncols;
+        auto valid = [&](int bb) { return !(j.action == E_STORE_C && ((bb & 7) * 32 >= j.e || !cols_ok)); };
+        auto next = [&](int bb) {
+          bb += 2;
+          while (bb < lim && !valid(bb)) bb += 2;
+          return bb;
+        };
+        // task mode: this lane's sum(c^2) of its column, rows in order, in
+        // fp32 (the same order and grouping as the one-CTA kernel)
+        float csum = 0.0f;
         auto tload = [&](int bb, uint32_t(&v)[32]) { tc::ld_32x32b_x32(tcol + (bb >> 3) * 256 + (bb & 7) * 32, v); };
         auto consume = [&](int bb, const uint32_t(&v)[32]) {
           const int hh = bb >> 3, blk = bb & 7;
@@ -600,6 +669,13 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
             float* dst = p.C + (size_t)(j.row0 + blk * 32) * p.ldc + col;
 #pragma unroll
             for (int i = 0; i < 32; ++i) dst[(size_t)i * p.ldc] = __uint_as_float(v[i]);
+            if (p.task_mode) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const float x = __uint_as_float(v[i]);
+                csum = fmaf(x, x, csum);
+              }
+            }
           } else {
             float* dst = p.Cu + (size_t)j.e * p.cu_stride + (size_t)(j.row0 + blk * 32) * p.ldcu + col;
             if (p.usplit == 1) {
@@ -611,6 +687,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
             }
           }
         };
+        bool released = false;
         auto release = [&]() {
           tc::fence_before_sync();
           __syncwarp();
@@ -622,35 +699,58 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
               atomicAdd(&p.q.ckpt[1], (unsigned long long)nh * 4 * 4096);
             }
           }
+          released = true;
         };
         uint32_t va[32], vb[32];
-        int cur = g;
-        tload(cur, va);
+        int cur = valid(g) ? g : next(g);
+        if (cur < lim) tload(cur, va);
         while (cur < lim) {
           tc::wait_ld();
-          int nxt = cur + 2;
+          int nxt = next(cur);
           if (nxt < lim) tload(nxt, vb); else release();
           consume(cur, va);
           cur = nxt;
           if (cur >= lim) break;
           tc::wait_ld();
-          nxt = cur + 2;
+          nxt = next(cur);
           if (nxt < lim) tload(nxt, va); else release();
           consume(cur, vb);
           cur = nxt;
         }
+        if (!released) release();  // no block of this warp had valid rows
         if (j.action != E_SPILL) {
-          // the job's stores are visible before it is counted; the last of
-          // the pair's 16 epilogue warps does the accounting
+          if (p.task_mode && j.action == E_STORE_C) {
+            double sd = (double)csum;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sd += __shfl_xor_sync(0xffffffffu, sd, o);
+            if (lane == 0) sh.chk_part[sl][warp - 2] = sd;
+          }
+          // the job's stores are visible before it is counted
           __threadfence();
           __syncwarp();
+          if (p.task_mode && j.action == E_STORE_C && lane == 0 &&
+              atomicAdd(&sh.cta_cnt[sl], 1) == EPI_WARPS - 1) {
+            // task mode: the last of this CTA's 8 warps accounts for its
+            // 128-column half (checksum in the fixed warp order)
+            sh.cta_cnt[sl] = 0;
+            if (cols_ok) {
+              double sum = 0.0;
+              for (int w = 0; w < EPI_WARPS; ++w) sum += sh.chk_part[sl][w];
+              p.chk[j.task + rank] = sum;
+              ++sh.tiles;
+              if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[j.task + rank], 1);
+            }
+          }
+          // the last of the pair's 16 epilogue warps does the job's accounting
           if (lane == 0 && atom_add_cluster(mapa(&sh.epi_cnt[sl], 0), 1u) == 2 * EPI_WARPS - 1) {
             st_cluster_u32(mapa(&sh.epi_cnt[sl], 0), 0u);
             if (j.action == E_STORE_C) {
-              atom_add_cluster_u64(mapa(&sh.tiles, 0), 1ull);
-              if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[j.task], 1);
-              if (p.st.done != nullptr)
-                stream_tile_done(p.st, p.total_tiles / p.tiles_n, p.tiles_n, j.row0 / BM, j.col0 / BN);
+              if (!p.task_mode) {
+                atom_add_cluster_u64(mapa(&sh.tiles, 0), 1ull);
+                if (ORACLE && p.q.exec_count != nullptr) atomicAdd(&p.q.exec_count[j.task], 1);
+                if (p.st.done != nullptr)
+                  stream_tile_done(p.st, p.total_tiles / p.tiles_n, p.tiles_n, j.row0 / BM, j.col0 / BN);
+              }
               count_trigger(p.ev);
             } else {
               if (ORACLE) atomicAdd(&p.ev.uexec[j.e], 1);
@@ -701,7 +801,8 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
   __syncwarp();
   cluster_sync();
   if (tid == 0) {
-    p.q.tiles_done[cta] = leader ? sh.tiles : 0ull;
+    // task mode: each CTA counted its own 128-column halves
+    p.q.tiles_done[cta] = (leader || p.task_mode) ? sh.tiles : 0ull;
     atomicMax(p.q.end_max, (unsigned long long)globaltimer_ns());
     atomicAdd(p.q.exited, 1);
   }

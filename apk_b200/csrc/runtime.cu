@@ -344,15 +344,18 @@ apk_status prepare_kernel(apk_ctx* ctx, int poll) {
   return APK_OK;
 }
 
-// The bf16 launch runs the CTA-pair kernel for a plain background GEMM
-// (no task list) whose N and urgent N are multiples of 256, K-tile 64, one
-// CTA per SM over every SM; the one-CTA kernel runs everything else.
-bool use_pair(const apk_ctx* ctx) {
+// The bf16 launch runs the CTA-pair kernel for a task list, or a plain
+// background GEMM whose N is a multiple of 256, when the urgent N is one too,
+// K-tile is 64 or 128, one CTA per SM over every SM; the one-CTA kernel runs
+// everything else.
+// (task lists included: every task tile is a 256x256 pair job, the
+// peer's half of a tile whose n ends 128 columns in computed and not stored)
+bool pair_capable(const apk_ctx* ctx) {
   return ctx->cfg.dtype == APK_BF16 && ctx->pair_ok && ctx->cfg.scheduler == APK_SCHED_QUEUE &&
          (ctx->cfg.bf16_kernel == APK_BF16_AUTO || ctx->cfg.bf16_kernel == APK_BF16_PAIR) &&
-         !ctx->task_mode && ctx->bf16_geo == BF16_GEO_STD64 && ctx->grid == ctx->sms && ctx->N % 256 == 0 &&
-         ctx->Nu % 256 == 0;
+         ctx->bf16_geo == BF16_GEO_STD64 && ctx->grid == ctx->sms && ctx->Nu % 256 == 0;
 }
+bool use_pair(const apk_ctx* ctx) { return pair_capable(ctx) && (ctx->task_mode || ctx->N % 256 == 0); }
 
 // The fp32 launch runs the warp-specialized kernel (one 384-thread CTA per
 // SM, two 128x128 workers) at full residency of the default schedule: queue
@@ -731,7 +734,9 @@ apk_status apk_set_tasks(apk_ctx* ctx, const apk_task* tasks, int n, long long n
         d.c_col0 + d.n > ctx->c_cols || tiles_m > 63 || tiles_n > 63 || d.chk_base < 0 ||
         d.chk_base + (long long)tiles_m * tiles_n > n_chk)
       return fail(ctx, APK_EINVAL, "task %d does not fit the pools / checksum array", t);
-    const int step = (d.flags & APK_TASK_NARROW) ? 1 : 2;
+    // 256x128 jobs for APK_TASK_NARROW tasks -- except on CTA pairs, whose
+    // jobs are 256 wide
+    const int step = ((d.flags & APK_TASK_NARROW) && !pair_capable(ctx)) ? 1 : 2;
     for (int tm = 0; tm < tiles_m; ++tm)
       for (int tn = 0; tn < tiles_n; tn += step)
         work.push_back(((unsigned)t << 12) | ((unsigned)tm << 6) | (unsigned)tn);

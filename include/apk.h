@@ -98,10 +98,12 @@ typedef enum apk_f32_kernel {
 
 /* bf16 kernel.  PAIR: clusters of two CTAs compute 256x512 output tiles
  * with cta_group::2 MMAs (each CTA stages half the operands and holds half
- * the accumulators); it serves a plain background GEMM (no task list) with
- * N and the urgent N multiples of 256, K-tile 64, one CTA per SM.  SINGLE:
- * one CTA per 256x256 tile; serves every shape, task mode and K-tile 32.
- * AUTO picks PAIR where it applies.  info.tile_n reports 512 for PAIR. */
+ * the accumulators); it serves a background GEMM with N a multiple of 256 and
+ * task lists (256x256 jobs, one accumulator per CTA, so a job's epilogue
+ * overlaps the next job's MMAs), the urgent N a multiple of 256, K-tile 64 or
+ * 128, one CTA per SM.  SINGLE: one CTA per 256x256 tile; serves every shape,
+ * task mode and K-tile 32.  AUTO picks PAIR where it applies.  info.tile_n
+ * reports 512 for PAIR. */
 typedef enum apk_bf16_kernel {
   APK_BF16_AUTO = 0,
   APK_BF16_PAIR = 1,
@@ -436,9 +438,10 @@ typedef struct apk_task {
 } apk_task;
 /* task flags: SAMPLED marks a task whose output window no other task touches
  * (set by apk_gen_tasks for spot checks); NARROW runs the task as 256x128
- * tiles, each holding one of the two TMEM accumulator buffers so its
- * epilogue overlaps the next tile's MMAs, instead of 256x256 tiles that hold
- * both (better for short-k tasks, whose epilogue is a larger share). */
+ * tiles in the one-CTA kernel, each holding one of the two TMEM accumulator
+ * buffers so its epilogue overlaps the next tile's MMAs, instead of 256x256
+ * tiles that hold both (the CTA-pair kernel's 256x256 jobs already hold one
+ * buffer each and ignore it). */
 #define APK_TASK_SAMPLED 1
 #define APK_TASK_NARROW 2
 

@@ -152,3 +152,22 @@ def test_clc_scheduler_task_queue_bitwise(whole_run):
     assert st["device_status"] == 0
     assert np.all(ex == 1)
     assert np.array_equal(chk.view(np.uint64), whole_run["chk"].view(np.uint64))
+
+
+def test_pair_and_single_kernels_checksums_bitwise(whole_run):
+    """The task list on CTA pairs (256x256 jobs, 128-row tiles as N = 128
+    pair MMAs, 128-wide edges computed by the pair and stored by the leader
+    only) and on the one-CTA kernel: every half-tile exactly once on both,
+    checksums bitwise equal (same MMA sequence per element, same summation
+    order)."""
+    tasks, n_chk = whole_run["tasks"], whole_run["n_chk"]
+    out = {}
+    for kern in ("pair", "single"):
+        with _ctx(poll="off", oracle=True, bf16_kernel=kern) as c:
+            _run(c, whole_run["A"], whole_run["B"], whole_run["pool"], tasks, n_chk)
+            out[kern] = c.read_checksums()
+            ex, _ = c.read_oracle(n_chk)
+            st = c.run_stats()
+        assert np.all(ex == 1), kern
+        assert st["tiles_done"] == n_chk and st["device_status"] == 0, kern
+    assert np.array_equal(out["pair"].view(np.uint64), out["single"].view(np.uint64))
