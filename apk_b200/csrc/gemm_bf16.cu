@@ -431,15 +431,15 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
         }
       }
       bool resume = false;
-      // the control warp's flag copy is read one slot ahead: the shared
-      // load's latency overlaps the previous slot's issue instead of sitting
-      // on the producer's path (with 32-deep slots the producer is the
-      // critical path: reading it at the site cost ~10% of the drain)
-      int fs_next = POLL == POLL_STAGE ? vload(&sh.gen) : 0;
+      // a yield site every poll_every ring slots (one K-tile), counted down
+      // rather than by a modulo with a run-time divisor on every slot (the
+      // producer is the critical path of the small multi-CTA tiles)
+      int to_site = 0;
       for (int c = 0; c < nk && ok; ++c) {
-        // a yield site every poll_every ring slots (one K-tile)
-        if (POLL == POLL_STAGE && (p.poll_every <= 1 || c % p.poll_every == 0)) {
-          const int fs = fs_next;
+        const bool site = to_site == 0;
+        to_site = site ? p.poll_every - 1 : to_site - 1;
+        if (POLL == POLL_STAGE && site) {
+          const int fs = vload(&sh.gen);
           if (fs < 0) {
             ok = false;  // stop sentinel: abandon the tile
             break;
@@ -457,7 +457,6 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
                           (BM == 256 && mvalid <= BNH ? F_HALF : 0);
         resume = false;
         // e carries the valid rows of the tile, task the oracle / checksum index
-        if (POLL == POLL_STAGE) fs_next = vload(&sh.gen);
         if (!emit(T_BG, flags, row0, col0, mvalid, 0, tag_task, &p.tmA, &p.tmB, ar0, bc0, ak0 + c * BK,
                   bk0 + c * BK))
           ok = false;

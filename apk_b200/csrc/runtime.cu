@@ -355,7 +355,14 @@ bool pair_capable(const apk_ctx* ctx) {
          (ctx->cfg.bf16_kernel == APK_BF16_AUTO || ctx->cfg.bf16_kernel == APK_BF16_PAIR) &&
          ctx->bf16_geo == BF16_GEO_STD64 && ctx->grid == ctx->sms && ctx->Nu % 256 == 0;
 }
-bool use_pair(const apk_ctx* ctx) { return pair_capable(ctx) && (ctx->task_mode || ctx->N % 256 == 0); }
+// Task lists run on pairs only when asked for (APK_BF16_PAIR): their
+// 256-wide pair jobs issue half the MMAs per ring slot of the 256x512 tiles,
+// and on 2^18 configs[4] tasks the pair kernel reached 700 TFLOP/s against
+// 918 for the one-CTA kernel.
+bool use_pair(const apk_ctx* ctx) {
+  return pair_capable(ctx) &&
+         (ctx->task_mode ? ctx->cfg.bf16_kernel == APK_BF16_PAIR : ctx->N % 256 == 0);
+}
 
 // The fp32 launch runs the warp-specialized kernel (one 384-thread CTA per
 // SM, two 128x128 workers) at full residency of the default schedule: queue
@@ -736,7 +743,8 @@ apk_status apk_set_tasks(apk_ctx* ctx, const apk_task* tasks, int n, long long n
       return fail(ctx, APK_EINVAL, "task %d does not fit the pools / checksum array", t);
     // 256x128 jobs for APK_TASK_NARROW tasks -- except on CTA pairs, whose
     // jobs are 256 wide
-    const int step = ((d.flags & APK_TASK_NARROW) && !pair_capable(ctx)) ? 1 : 2;
+    const int step =
+        ((d.flags & APK_TASK_NARROW) && !(pair_capable(ctx) && ctx->cfg.bf16_kernel == APK_BF16_PAIR)) ? 1 : 2;
     for (int tm = 0; tm < tiles_m; ++tm)
       for (int tn = 0; tn < tiles_n; tn += step)
         work.push_back(((unsigned)t << 12) | ((unsigned)tm << 6) | (unsigned)tn);

@@ -98,12 +98,12 @@ typedef enum apk_f32_kernel {
 
 /* bf16 kernel.  PAIR: clusters of two CTAs compute 256x512 output tiles
  * with cta_group::2 MMAs (each CTA stages half the operands and holds half
- * the accumulators); it serves a background GEMM with N a multiple of 256 and
- * task lists (256x256 jobs, one accumulator per CTA, so a job's epilogue
- * overlaps the next job's MMAs), the urgent N a multiple of 256, K-tile 64 or
- * 128, one CTA per SM.  SINGLE: one CTA per 256x256 tile; serves every shape,
- * task mode and K-tile 32.  AUTO picks PAIR where it applies.  info.tile_n
- * reports 512 for PAIR. */
+ * the accumulators); it serves a background GEMM with N a multiple of 256,
+ * the urgent N a multiple of 256, K-tile 64 or 128, one CTA per SM, and --
+ * when asked for by PAIR -- task lists (256x256 jobs, one accumulator per
+ * CTA; slower there than SINGLE).  SINGLE: one CTA per 256x256 tile; serves
+ * every shape, task mode and K-tile 32.  AUTO picks PAIR for a plain
+ * background GEMM where it applies.  info.tile_n reports 512 for PAIR. */
 typedef enum apk_bf16_kernel {
   APK_BF16_AUTO = 0,
   APK_BF16_PAIR = 1,
