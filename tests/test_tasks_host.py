@@ -73,15 +73,20 @@ def _rank_main(rank, world, port, q):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     t, n_chk = gen_tasks(4000, 33)  # every rank derives the same list from the seed
     mine = shard_tasks(t, world, rank)
-    tiles = np.zeros(n_chk, np.int64)
-    for i in mine:  # the global tiles this rank would drain
+    tiles = np.zeros(n_chk, np.int32)
+    for i in mine:  # the global half-tiles this rank's oracle counters would show
         d = t[i]
         nt = ((int(d["m"]) + 255) // 256) * (int(d["n"]) // 128)
         tiles[int(d["chk_base"]):int(d["chk_base"]) + nt] += 1
-    import torch
-    tt = torch.from_numpy(tiles)
-    dist.all_reduce(tt)  # host-side verdict only; not in any data path
-    q.put((rank, int((tt.numpy() == 1).all()), len(mine)))
+    # the bench's host-side union of both drains' counters (uint8 sum over gloo)
+    from apk_b200 import config4
+    counts = config4.union_counts(world, tiles, tiles.copy())
+    # a planted duplicate (rank 0 counts its first half-tile twice) must fail
+    planted = tiles.copy()
+    if rank == 0:
+        planted[int(t[mine[0]]["chk_base"])] += 1
+    dup = config4.union_counts(world, planted, tiles.copy())
+    q.put((rank, int((counts == 1).all() and not (dup == 1).all()), len(mine)))
     dist.destroy_process_group()
 
 
