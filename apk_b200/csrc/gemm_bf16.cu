@@ -244,6 +244,8 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
     tma_prefetch_desc(&p.tmB);
     tma_prefetch_desc(&p.tmAu);
     tma_prefetch_desc(&p.tmBu);
+    tma_prefetch_desc(&p.tmAw);
+    tma_prefetch_desc(&p.tmBw);
     atomicMin(p.q.start_min, (unsigned long long)globaltimer_ns());
   }
   if (warp == 1) {
@@ -283,9 +285,21 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
         const bool half = (flags & F_HALF) != 0;
         mbar_arrive_expect_tx(&sh.full[s], (half ? A_HALF : A_BYTES) + nb_chunks * B_CHUNK);
         uint8_t* st = stages + s * STAGE_BYTES;
-        tma_load_2d(st, tA, ak, ar0, &sh.full[s]);
-        if (BM > 128 && !half) tma_load_2d(st + A_HALF, tA, ak, ar0 + 128, &sh.full[s]);
-        for (int b = 0; b < nb_chunks; ++b) tma_load_2d(st + A_BYTES + b * B_CHUNK, tB, bc0 + 64 * b, bk, &sh.full[s]);
+        // background jobs load A and the job's B chunks as one box each (the
+        // per-box maps serve urgent items, half-row and narrow STD jobs)
+        const bool bg = tA == &p.tmA;
+        if (bg && !half) {
+          tma_load_2d(st, &p.tmAw, ak, ar0, &sh.full[s]);
+        } else {
+          tma_load_2d(st, tA, ak, ar0, &sh.full[s]);
+          if (BM > 128 && !half) tma_load_2d(st + A_HALF, tA, ak, ar0 + 128, &sh.full[s]);
+        }
+        if (bg && nb_chunks == (G::WIDE ? 4 : 2)) {
+          tma_load_3d(st + A_BYTES, &p.tmBw, 0, bk, bc0 / 64, &sh.full[s]);
+        } else {
+          for (int b = 0; b < nb_chunks; ++b)
+            tma_load_2d(st + A_BYTES + b * B_CHUNK, tB, bc0 + 64 * b, bk, &sh.full[s]);
+        }
       } else {
         mbar_arrive(&sh.full[s]);  // control slot: no data
       }
@@ -430,36 +444,53 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
           }
         }
       }
-      bool resume = false;
       // a yield site every poll_every ring slots (one K-tile), counted down
-      // rather than by a modulo with a run-time divisor on every slot (the
-      // producer is the critical path of the small multi-CTA tiles)
-      int to_site = 0;
-      for (int c = 0; c < nk && ok; ++c) {
-        const bool site = to_site == 0;
-        to_site = site ? p.poll_every - 1 : to_site - 1;
-        if (POLL == POLL_STAGE && site) {
-          const int fs = vload(&sh.gen);
-          if (fs < 0) {
-            ok = false;  // stop sentinel: abandon the tile
-            break;
-          }
-          if (fs != lastSeen) {
-            const int n = handle(fs, c, c > 0);
-            if (n < 0) {
-              ok = false;
+      // rather than by a modulo with a run-time divisor on every slot.  The
+      // producer is the critical path of the small tiles and of K-tile 32:
+      // the issue loop only tests the site and leaves it when the
+      // generation moved; the yield itself is handled outside it (inlined
+      // inside, it cost 8-20% of the drain when nothing was raised)
+      bool resume = false, skip = false;
+      int to_site = 0, c = 0;
+      const int fl0 = wide | (BM == 256 && mvalid <= BNH ? F_HALF : 0);
+      while (ok && c < nk) {
+        int fs = 0;
+        bool hit = false;
+        for (; c < nk; ++c) {
+          const bool site = to_site == 0;
+          to_site = site ? p.poll_every - 1 : to_site - 1;
+          if (POLL == POLL_STAGE && site && !skip) {
+            fs = vload(&sh.gen);
+            if (__builtin_expect(fs != lastSeen, 0)) {
+              hit = true;
               break;
             }
-            if (n > 0 && c > 0) resume = true;
+          }
+          skip = false;
+          const int flags = (c == 0 ? F_FIRST : 0) | (c == nk - 1 ? F_LAST : 0) | (resume ? F_RESUME : 0) | fl0;
+          resume = false;
+          // e carries the valid rows of the tile, task the oracle / checksum index
+          if (!emit(T_BG, flags, row0, col0, mvalid, 0, tag_task, &p.tmA, &p.tmB, ar0, bc0, ak0 + c * BK,
+                    bk0 + c * BK)) {
+            ok = false;
+            break;
           }
         }
-        const int flags = (c == 0 ? F_FIRST : 0) | (c == nk - 1 ? F_LAST : 0) | (resume ? F_RESUME : 0) | wide |
-                          (BM == 256 && mvalid <= BNH ? F_HALF : 0);
-        resume = false;
-        // e carries the valid rows of the tile, task the oracle / checksum index
-        if (!emit(T_BG, flags, row0, col0, mvalid, 0, tag_task, &p.tmA, &p.tmB, ar0, bc0, ak0 + c * BK,
-                  bk0 + c * BK))
+        if (!hit) break;
+        if (fs < 0) {
+          ok = false;  // stop sentinel: abandon the tile
+          break;
+        }
+        const int n = handle(fs, c, c > 0);
+        if (n < 0) {
           ok = false;
+          break;
+        }
+        resume = n > 0 && c > 0;
+        // stage c is issued next without testing its site again: its
+        // generation has just been handled
+        to_site = 0;
+        skip = true;
       }
     }
     emit(T_STOP, 0, 0, 0, 0, 0, 0, nullptr, nullptr, 0, 0, 0, 0);
@@ -805,15 +836,21 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
     asm volatile("mov.u32 %0, %%nsmid;" : "=r"(nsm));
     const int per_sm = nsm > 0 && gridw > (int)nsm ? gridw / (int)nsm : 1;
     const unsigned sleep_ns = 64u * (unsigned)per_sm;
+    const int* flag = flag_copy(p.ev, cta);
+    // the abort word is one line every CTA reads: every 16th pass (a stop
+    // also writes -1 into every flag copy); once seen it holds
+    unsigned pass = 0;
+    bool aborted = false;
     while (!vload(&sh.prod_done) && !vload(&sh.abort)) {
-      int f = POLL != POLL_OFF ? flag_load(p.ev.flag) : 0;
-      if (*reinterpret_cast<volatile int*>(p.ev.abort_word)) f = -1;
+      int f = POLL != POLL_OFF ? flag_load(flag) : 0;
+      if ((++pass & 15) == 0 && *reinterpret_cast<volatile int*>(p.ev.abort_word)) aborted = true;
+      if (aborted) f = -1;
       if (cta == 0 && p.ev.sched_ns != nullptr && nextEv < p.ev.n_sched) {
         const long long now = globaltimer_ns();
         if (gBase == 0) gBase = now;
         if (now >= gBase + p.ev.sched_ns[nextEv]) {
           p.ev.set_ns[nextEv] = now;
-          atomicCAS(p.ev.flag, nextEv, nextEv + 1);
+          flag_raise(p.ev, nextEv);
           ++nextEv;
         }
       }

@@ -769,15 +769,21 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
     // ================================ control =================================
     int nextEv = 0;
     long long gBase = 0;
+    const int* flag = flag_copy(p.ev, cta);
+    // the abort word: every 16th pass (a stop also writes -1 into every
+    // flag copy); once seen it holds
+    unsigned pass = 0;
+    bool aborted = false;
     while (!vload(&sh.prod_done) && !vload(&sh.abort)) {
-      int f = POLL != POLL_OFF ? flag_load(p.ev.flag) : 0;
-      if (*reinterpret_cast<volatile int*>(p.ev.abort_word)) f = -1;
+      int f = POLL != POLL_OFF ? flag_load(flag) : 0;
+      if ((++pass & 15) == 0 && *reinterpret_cast<volatile int*>(p.ev.abort_word)) aborted = true;
+      if (aborted) f = -1;
       if (cta == 0 && p.ev.sched_ns != nullptr && nextEv < p.ev.n_sched) {
         const long long now = globaltimer_ns();
         if (gBase == 0) gBase = now;
         if (now >= gBase + p.ev.sched_ns[nextEv]) {
           p.ev.set_ns[nextEv] = now;
-          atomicCAS(p.ev.flag, nextEv, nextEv + 1);
+          flag_raise(p.ev, nextEv);
           ++nextEv;
         }
       }

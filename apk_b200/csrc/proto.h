@@ -14,9 +14,17 @@ enum PollMode : int { POLL_OFF = 0, POLL_BOUNDARY = 1, POLL_STAGE = 2 };
 enum Discipline : int { DISC_DRAIN = 0, DISC_POISON = 2 };
 
 // Yield-event side of the protocol (src/yield.cu:95-102,148-195).
+// The generation is kept in flag_lines copies, one per 128-byte line
+// (flag + FLAG_STRIDE * i); the setter writes every copy and CTA c polls copy
+// c % flag_lines.  1184 CTAs (8 per SM) polling one line every 512 ns cost
+// the drain a fifth of its speed; spread over 32 lines, the cost is that of
+// no flag load at all.
+constexpr int FLAG_LINES = 32, FLAG_STRIDE = 32;
+
 struct EventProto {
   int* flag;                   // generation counter; -1 = stop.  Device memory
                                // or mapped pinned host memory.
+  int flag_lines;              // copies of it at flag + FLAG_STRIDE * i (1: flag only)
   int* abort_word;             // device memory; nonzero makes every CTA exit
   int* status;                 // device memory; first device-side error code
   const long long* sched_ns;   // device setter: cumulative offsets (nullptr = host sets)
@@ -39,6 +47,18 @@ struct EventProto {
   int n_count;
   unsigned long long* completed;
 };
+
+// The copy of the generation CTA (or resident slot) c polls.
+__device__ __forceinline__ const int* flag_copy(const EventProto& ev, int c) {
+  return ev.flag + (ev.flag_lines > 1 ? FLAG_STRIDE * (c % ev.flag_lines) : 0);
+}
+
+// Device setter: raise the generation from `from` to from + 1 in every copy.
+// A compare-and-swap per copy never overwrites the -1 stop sentinel; no
+// result is awaited, so the copies' stores go out back to back.
+__device__ __forceinline__ void flag_raise(const EventProto& ev, int from) {
+  for (int i = 0; i < ev.flag_lines; ++i) atomicCAS(ev.flag + FLAG_STRIDE * i, from, from + 1);
+}
 
 // Background work-queue side (src/persistent.cu:51-79 fetch-add queue).
 struct QueueProto {
@@ -149,6 +169,12 @@ struct F32Params {
   CUtensorMap tmB;   // background B [K][N]  (fp32: BK x 128 boxes; bf16: BK x 64, 128B swizzle)
   CUtensorMap tmAu;  // urgent A
   CUtensorMap tmBu;  // urgent B
+  // bf16 one-CTA kernel, background jobs: A as one box of the tile's rows
+  // (up to 256), B as one 3-D box {64 n, BK k, chunks} of the view
+  // [N/64][K][64] (4 chunks for 256-wide jobs, else 2), so a ring slot takes
+  // two TMA loads; the shared-memory layout is that of the per-box loads
+  CUtensorMap tmAw;
+  CUtensorMap tmBw;
   float* C;
   int ldc, tiles_n, total_tiles, nk;   // nk = K / BK (ring slots per tile)
   int poll_every;                      // ring slots per stage-level yield site:

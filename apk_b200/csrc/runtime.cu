@@ -87,10 +87,15 @@ struct Ctrl {
   int exited;
   int abort_word;
   int status;
-  int flag_dev;  // yield flag in device memory (DEVICE / HOST_MEMCPY modes)
   int never_set; // a word no code path writes (failure-path self-test)
-  int pad;
+  // yield flag in device memory (DEVICE / HOST_MEMCPY modes): copy 0 of the
+  // generation, copies 1..FLAG_LINES-1 on the lines that follow it
+  alignas(128) int flag_dev;
+  int flag_copies[FLAG_LINES * FLAG_STRIDE - 1];
 };
+static_assert(offsetof(Ctrl, flag_copies) + sizeof(int) * (FLAG_LINES * FLAG_STRIDE - 1) ==
+                  offsetof(Ctrl, flag_dev) + sizeof(int) * FLAG_LINES * FLAG_STRIDE,
+              "flag copies follow flag_dev line by line");
 
 // Host-to-globaltimer visibility probe (src/yield.cu:208-214), bounded.
 __global__ void spin_flag_kernel(const int* flag, int target, long long limit_ns, long long* out,
@@ -182,6 +187,7 @@ struct apk_ctx {
   int* h_ack = nullptr;     // mapped pinned [2*max_events]
   int* d_ack_mapped = nullptr;
   int* h_gen = nullptr;     // pinned sources for HOST_MEMCPY stores [max_events + 2]
+  int* h_gen_lines = nullptr;  // the same, FLAG_LINES each: one copy per flag line
 
   // event log (device)
   long long *d_sched = nullptr, *d_set = nullptr, *d_obs = nullptr, *d_claim_ns = nullptr;
@@ -270,6 +276,26 @@ apk_status make_tmap(apk_ctx* ctx, CUtensorMap* tm, const void* base, CUtensorMa
   if (r != CUDA_SUCCESS)
     return fail(ctx, APK_ECUDA, "cuTensorMapEncodeTiled failed (%d) rows=%lld cols=%lld box=%dx%d",
                 (int)r, rows, cols, box_cols, box_rows);
+  return APK_OK;
+}
+
+// 3-D map of a row-major rows x cols matrix seen as [cols/64][rows][64]:
+// box {64, box_rows, chunks} lands chunk-major in shared memory, each chunk
+// the [box_rows][64] block a 2-D map with a 64-column box would load.
+apk_status make_tmap_chunks(apk_ctx* ctx, CUtensorMap* tm, const void* base, CUtensorMapDataType dt, int esize,
+                            long long rows, long long cols, int box_rows, int chunks, CUtensorMapSwizzle sw) {
+  if (ensure_encoder(ctx) != APK_OK) return APK_ECUDA;
+  if (cols % 64 != 0) return fail(ctx, APK_EINVAL, "chunked map: %lld columns not a multiple of 64", cols);
+  cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(cols / 64)};
+  cuuint64_t strides[2] = {(cuuint64_t)cols * esize, (cuuint64_t)64 * esize};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)chunks};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(tm, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(ctx, APK_ECUDA, "cuTensorMapEncodeTiled (3-D) failed (%d) rows=%lld cols=%lld box=64x%dx%d",
+                (int)r, rows, cols, box_rows, chunks);
   return APK_OK;
 }
 
@@ -519,6 +545,7 @@ apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
   APK_CU(cudaHostAlloc(&ctx->h_ack, sizeof(int) * 2 * E, cudaHostAllocMapped));
   APK_CU(cudaHostGetDevicePointer((void**)&ctx->d_ack_mapped, ctx->h_ack, 0));
   APK_CU(cudaHostAlloc(&ctx->h_gen, sizeof(int) * (E + 2), cudaHostAllocDefault));
+  APK_CU(cudaHostAlloc(&ctx->h_gen_lines, sizeof(int) * (E + 2) * FLAG_LINES, cudaHostAllocDefault));
   memset(ctx->h_flag, 0, 64);
   memset(ctx->h_ack, 0, sizeof(int) * 2 * E);
   APK_CU(cudaMalloc(&ctx->d_sched, sizeof(long long) * E));
@@ -593,6 +620,7 @@ apk_status apk_destroy(apk_ctx* ctx) {
   if (ctx->h_flag) cudaFreeHost(ctx->h_flag);
   if (ctx->h_ack) cudaFreeHost(ctx->h_ack);
   if (ctx->h_gen) cudaFreeHost(ctx->h_gen);
+  if (ctx->h_gen_lines) cudaFreeHost(ctx->h_gen_lines);
   if (ctx->kstream) cudaStreamDestroy(ctx->kstream);
   if (ctx->cstream) cudaStreamDestroy(ctx->cstream);
   if (ctx->ustream) cudaStreamDestroy(ctx->ustream);
@@ -859,6 +887,7 @@ void fill_protos(apk_ctx* ctx, unsigned long long num_tasks, EventProto* ev, Que
   memset(ev, 0, sizeof *ev);
   memset(q, 0, sizeof *q);
   ev->flag = flag_ptr;
+  ev->flag_lines = flag_ptr == &cb->flag_dev ? FLAG_LINES : 1;
   ev->abort_word = &cb->abort_word;
   ev->status = &cb->status;
   ev->sched_ns = (ctx->cfg.set_mode == APK_SET_DEVICE && ctx->n_sched > 0) ? ctx->d_sched : nullptr;
@@ -894,7 +923,8 @@ apk_status reset_logs(apk_ctx* ctx, unsigned long long num_tasks) {
   cudaStream_t s = ctx->kstream;
   Ctrl init{};
   init.start_min = ~0ull;
-  APK_CU(cudaMemcpyAsync(ctx->d_ctrl, &init, sizeof init, cudaMemcpyHostToDevice, s));
+  APK_CU(cudaMemcpyAsync(ctx->d_ctrl, &init, offsetof(Ctrl, flag_dev), cudaMemcpyHostToDevice, s));
+  APK_CU(cudaMemsetAsync(&ctx->d_ctrl->flag_dev, 0, sizeof(int) * FLAG_LINES * FLAG_STRIDE, s));
   APK_CU(cudaMemsetAsync(ctx->d_set, 0, sizeof(long long) * E, s));
   APK_CU(cudaMemsetAsync(ctx->d_obs, 0, sizeof(long long) * (size_t)E * G, s));
   APK_CU(cudaMemsetAsync(ctx->d_claim_ns, 0, sizeof(long long) * E, s));
@@ -1008,6 +1038,12 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
     const long long br = tk ? ctx->b_rows : ctx->K, bc = tk ? ctx->b_cols : ctx->N;
     if ((t = make_tmap(ctx, &p.tmA, srcA, dt, es, ar, ac, a_box_k, a_box_m, asw)) != APK_OK) return t;
     if ((t = make_tmap(ctx, &p.tmB, srcB, dt, es, br, bc, b_box_n, bk, bsw)) != APK_OK) return t;
+    if (!f32) {
+      const GeoInfo bg = bf16::geo_info(ctx->bf16_geo);
+      const int chunks = bg.tile_n == 256 ? 4 : 2;
+      if ((t = make_tmap(ctx, &p.tmAw, srcA, dt, es, ar, ac, bk, std::min(256, bg.tile_m), asw)) != APK_OK) return t;
+      if ((t = make_tmap_chunks(ctx, &p.tmBw, srcB, dt, es, br, bc, bk, chunks, bsw)) != APK_OK) return t;
+    }
     if (ctx->dAu) {
       if ((t = make_tmap(ctx, &p.tmAu, ctx->dAu, dt, es, ctx->Mu, ctx->Ku, a_box_k, a_box_m, asw)) != APK_OK)
         return t;
@@ -1330,6 +1366,21 @@ apk_status apk_launch(apk_ctx* ctx, unsigned long long num_tasks) {
   return APK_OK;
 }
 
+namespace {
+// HOST_MEMCPY: the generation goes to every flag line in one copy-engine
+// transfer (4 bytes per 128-byte line) from a pinned slot of its own, so a
+// queued copy never reads a slot the host has moved on from.
+int* stage_flag_lines(apk_ctx* ctx, int slot, int value) {
+  int* src = ctx->h_gen_lines + (size_t)slot * FLAG_LINES;
+  for (int i = 0; i < FLAG_LINES; ++i) src[i] = value;
+  return src;
+}
+cudaError_t copy_flag_lines(apk_ctx* ctx, const int* src) {
+  return cudaMemcpy2DAsync(&ctx->d_ctrl->flag_dev, sizeof(int) * FLAG_STRIDE, src, sizeof(int), sizeof(int),
+                           FLAG_LINES, cudaMemcpyHostToDevice, ctx->cstream);
+}
+}  // namespace
+
 apk_status apk_inject_urgent(apk_ctx* ctx, int* event, long long* host_set_ns) {
   if (!ctx) return APK_EINVAL;
   if (ctx->cfg.set_mode == APK_SET_DEVICE)
@@ -1342,10 +1393,9 @@ apk_status apk_inject_urgent(apk_ctx* ctx, int* event, long long* host_set_ns) {
     *reinterpret_cast<volatile int*>(ctx->h_flag) = gen;
     std::atomic_thread_fence(std::memory_order_seq_cst);
   } else {
-    ctx->h_gen[gen] = gen;
+    int* src = stage_flag_lines(ctx, gen, gen);
     t = host_now_ns();
-    APK_CU(cudaMemcpyAsync(&ctx->d_ctrl->flag_dev, &ctx->h_gen[gen], sizeof(int), cudaMemcpyHostToDevice,
-                           ctx->cstream));
+    APK_CU(copy_flag_lines(ctx, src));
   }
   ctx->host_set[gen - 1] = t;
   ctx->n_injected = gen;
@@ -1378,8 +1428,7 @@ apk_status apk_stop(apk_ctx* ctx) {
     *reinterpret_cast<volatile int*>(ctx->h_flag) = kStop;
     std::atomic_thread_fence(std::memory_order_seq_cst);
   } else {
-    APK_CU(cudaMemcpyAsync(&ctx->d_ctrl->flag_dev, &ctx->h_gen[ctx->cfg.max_events + 1], sizeof(int),
-                           cudaMemcpyHostToDevice, ctx->cstream));
+    APK_CU(copy_flag_lines(ctx, stage_flag_lines(ctx, ctx->cfg.max_events + 1, kStop)));
   }
   // the abort word also stops POLL_OFF kernels at their next tile boundary
   ctx->h_gen[0] = kOne;
@@ -1886,6 +1935,7 @@ apk_status run_reserved_impl(apk_ctx* ctx, unsigned long long num_tasks, int res
   up.slab_hdr = ctx->d_slab_hdr;
   Ctrl* ub = ctx->d_uctrl;
   up.ev.flag = &ub->flag_dev;
+  up.ev.flag_lines = 1;
   up.ev.abort_word = &ub->abort_word;
   up.ev.status = &ub->status;
   up.ev.max_events = 0;

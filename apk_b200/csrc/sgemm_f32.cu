@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(GE::NT, GE::MINB) sgemm_persistent(const __gri
       if (s_gBase == 0) s_gBase = now;
       if (now >= s_gBase + p.ev.sched_ns[nextEv]) {
         p.ev.set_ns[nextEv] = now;
-        atomicCAS(p.ev.flag, nextEv, nextEv + 1);  // never overwrites the -1 sentinel
+        flag_raise(p.ev, nextEv);  // never overwrites the -1 sentinel
         s_nextEv = nextEv + 1;
       }
     }
@@ -463,7 +463,7 @@ __global__ void __launch_bounds__(GE::NT, GE::MINB) sgemm_persistent(const __gri
         fl = s_lastSeen;
         if (POLL == POLL_BOUNDARY) {
           setter();
-          fl = flag_load(p.ev.flag);
+          fl = flag_load(flag_copy(p.ev, cta()));
         }
         if (ab) fl = -1;
         s_f = fl;
@@ -545,8 +545,8 @@ __global__ void __launch_bounds__(GE::NT, GE::MINB) sgemm_persistent(const __gri
         }
         __syncthreads();
       }
-      compute_stage<GE>(As, Bs, acc, arow0, ty, bcol, POLL == POLL_STAGE && !urgent && tid == 0, p.ev.flag,
-                        pend);
+      compute_stage<GE>(As, Bs, acc, arow0, ty, bcol, POLL == POLL_STAGE && !urgent && tid == 0,
+                        flag_copy(p.ev, cta()), pend);
       ++Q;
     }
     if (yielded) {
@@ -891,6 +891,7 @@ extern "C" apk_status apk_sgemm_f32_noalloc(const float* A, const float* B, floa
 
   NoAllocHeader* h = reinterpret_cast<NoAllocHeader*>(d.scratch);
   p.ev.flag = &h->flag;
+  p.ev.flag_lines = 1;
   p.ev.abort_word = &h->abort_word;
   p.ev.status = &h->status;
   p.q.next_task = &h->next_task;
