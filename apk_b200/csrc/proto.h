@@ -53,11 +53,16 @@ __device__ __forceinline__ const int* flag_copy(const EventProto& ev, int c) {
   return ev.flag + (ev.flag_lines > 1 ? FLAG_STRIDE * (c % ev.flag_lines) : 0);
 }
 
-// Device setter: raise the generation from `from` to from + 1 in every copy.
-// A compare-and-swap per copy never overwrites the -1 stop sentinel; no
-// result is awaited, so the copies' stores go out back to back.
+// Device setter: raise the generation from `from` to from + 1 in every copy:
+// plain stores to copies 1.. (a compare-and-swap per copy waited out each
+// one's round trip: the last copy landed ~10 us late), then a compare-and-
+// swap on copy 0, which never overwrites the -1 stop sentinel there.  A stop
+// racing the raise can leave a later copy at the generation; every poller
+// also reads the abort word, which the stop sets too.
 __device__ __forceinline__ void flag_raise(const EventProto& ev, int from) {
-  for (int i = 0; i < ev.flag_lines; ++i) atomicCAS(ev.flag + FLAG_STRIDE * i, from, from + 1);
+  for (int i = 1; i < ev.flag_lines; ++i)
+    asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(ev.flag + FLAG_STRIDE * i), "r"(from + 1) : "memory");
+  atomicCAS(ev.flag, from, from + 1);
 }
 
 // Background work-queue side (src/persistent.cu:51-79 fetch-add queue).

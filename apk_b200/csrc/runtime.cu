@@ -187,7 +187,13 @@ struct apk_ctx {
   int* h_ack = nullptr;     // mapped pinned [2*max_events]
   int* d_ack_mapped = nullptr;
   int* h_gen = nullptr;     // pinned sources for HOST_MEMCPY stores [max_events + 2]
-  int* h_gen_lines = nullptr;  // the same, FLAG_LINES each: one copy per flag line
+  // HOST_MEMCPY flag stores: pinned images of the FLAG_LINES flag lines
+  // (4 KB each), reused in a ring once the copy that read them has run
+  static constexpr int kFlagRing = 16;
+  int* h_flag_ring = nullptr;
+  cudaEvent_t flag_ring_ev[kFlagRing] = {};
+  int flag_ring_next = 0;
+  int flag_lines = 1;  // flag copies of the running launch
 
   // event log (device)
   long long *d_sched = nullptr, *d_set = nullptr, *d_obs = nullptr, *d_claim_ns = nullptr;
@@ -545,7 +551,11 @@ apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
   APK_CU(cudaHostAlloc(&ctx->h_ack, sizeof(int) * 2 * E, cudaHostAllocMapped));
   APK_CU(cudaHostGetDevicePointer((void**)&ctx->d_ack_mapped, ctx->h_ack, 0));
   APK_CU(cudaHostAlloc(&ctx->h_gen, sizeof(int) * (E + 2), cudaHostAllocDefault));
-  APK_CU(cudaHostAlloc(&ctx->h_gen_lines, sizeof(int) * (E + 2) * FLAG_LINES, cudaHostAllocDefault));
+  APK_CU(cudaHostAlloc(&ctx->h_flag_ring, sizeof(int) * apk_ctx::kFlagRing * FLAG_LINES * FLAG_STRIDE,
+                       cudaHostAllocDefault));
+  memset(ctx->h_flag_ring, 0, sizeof(int) * apk_ctx::kFlagRing * FLAG_LINES * FLAG_STRIDE);
+  for (int i = 0; i < apk_ctx::kFlagRing; ++i)
+    APK_CU(cudaEventCreateWithFlags(&ctx->flag_ring_ev[i], cudaEventDisableTiming));
   memset(ctx->h_flag, 0, 64);
   memset(ctx->h_ack, 0, sizeof(int) * 2 * E);
   APK_CU(cudaMalloc(&ctx->d_sched, sizeof(long long) * E));
@@ -620,7 +630,9 @@ apk_status apk_destroy(apk_ctx* ctx) {
   if (ctx->h_flag) cudaFreeHost(ctx->h_flag);
   if (ctx->h_ack) cudaFreeHost(ctx->h_ack);
   if (ctx->h_gen) cudaFreeHost(ctx->h_gen);
-  if (ctx->h_gen_lines) cudaFreeHost(ctx->h_gen_lines);
+  for (int i = 0; i < apk_ctx::kFlagRing; ++i)
+    if (ctx->flag_ring_ev[i]) cudaEventDestroy(ctx->flag_ring_ev[i]);
+  if (ctx->h_flag_ring) cudaFreeHost(ctx->h_flag_ring);
   if (ctx->kstream) cudaStreamDestroy(ctx->kstream);
   if (ctx->cstream) cudaStreamDestroy(ctx->cstream);
   if (ctx->ustream) cudaStreamDestroy(ctx->ustream);
@@ -887,7 +899,11 @@ void fill_protos(apk_ctx* ctx, unsigned long long num_tasks, EventProto* ev, Que
   memset(ev, 0, sizeof *ev);
   memset(q, 0, sizeof *q);
   ev->flag = flag_ptr;
-  ev->flag_lines = flag_ptr == &cb->flag_dev ? FLAG_LINES : 1;
+  // the copies pay where 4 or 8 CTAs per SM poll (1184 pollers on one line
+  // cost those drains a fifth of their speed); at 1 or 2 a single word is
+  // polled and stored (a 4-byte copy lands ~1.5 us before a 4 KB one)
+  ev->flag_lines = flag_ptr == &cb->flag_dev && ctx->ctas_per_sm >= 4 ? FLAG_LINES : 1;
+  ctx->flag_lines = ev->flag_lines;
   ev->abort_word = &cb->abort_word;
   ev->status = &cb->status;
   ev->sched_ns = (ctx->cfg.set_mode == APK_SET_DEVICE && ctx->n_sched > 0) ? ctx->d_sched : nullptr;
@@ -1367,17 +1383,26 @@ apk_status apk_launch(apk_ctx* ctx, unsigned long long num_tasks) {
 }
 
 namespace {
-// HOST_MEMCPY: the generation goes to every flag line in one copy-engine
-// transfer (4 bytes per 128-byte line) from a pinned slot of its own, so a
-// queued copy never reads a slot the host has moved on from.
-int* stage_flag_lines(apk_ctx* ctx, int slot, int value) {
-  int* src = ctx->h_gen_lines + (size_t)slot * FLAG_LINES;
-  for (int i = 0; i < FLAG_LINES; ++i) src[i] = value;
-  return src;
+// HOST_MEMCPY: the generation goes to every flag line in one contiguous
+// copy-engine transfer of the 4 KB of lines (a 2-D copy of one word per
+// line took ~4 us longer to land).  The pinned image comes from a ring;
+// a slot is rewritten only after the copy that read it has run.
+cudaError_t stage_flag_lines(apk_ctx* ctx, int value, int** src) {
+  const int slot = ctx->flag_ring_next;
+  ctx->flag_ring_next = (slot + 1) % apk_ctx::kFlagRing;
+  cudaError_t e = cudaEventSynchronize(ctx->flag_ring_ev[slot]);
+  if (e != cudaSuccess) return e;
+  int* img = ctx->h_flag_ring + (size_t)slot * FLAG_LINES * FLAG_STRIDE;
+  for (int i = 0; i < FLAG_LINES; ++i) img[i * FLAG_STRIDE] = value;
+  *src = img;
+  return cudaSuccess;
 }
 cudaError_t copy_flag_lines(apk_ctx* ctx, const int* src) {
-  return cudaMemcpy2DAsync(&ctx->d_ctrl->flag_dev, sizeof(int) * FLAG_STRIDE, src, sizeof(int), sizeof(int),
-                           FLAG_LINES, cudaMemcpyHostToDevice, ctx->cstream);
+  const size_t bytes = ctx->flag_lines > 1 ? sizeof(int) * FLAG_LINES * FLAG_STRIDE : sizeof(int);
+  cudaError_t e = cudaMemcpyAsync(&ctx->d_ctrl->flag_dev, src, bytes, cudaMemcpyHostToDevice, ctx->cstream);
+  if (e != cudaSuccess) return e;
+  const int slot = (ctx->flag_ring_next + apk_ctx::kFlagRing - 1) % apk_ctx::kFlagRing;
+  return cudaEventRecord(ctx->flag_ring_ev[slot], ctx->cstream);
 }
 }  // namespace
 
@@ -1393,7 +1418,8 @@ apk_status apk_inject_urgent(apk_ctx* ctx, int* event, long long* host_set_ns) {
     *reinterpret_cast<volatile int*>(ctx->h_flag) = gen;
     std::atomic_thread_fence(std::memory_order_seq_cst);
   } else {
-    int* src = stage_flag_lines(ctx, gen, gen);
+    int* src = nullptr;
+    APK_CU(stage_flag_lines(ctx, gen, &src));
     t = host_now_ns();
     APK_CU(copy_flag_lines(ctx, src));
   }
@@ -1428,7 +1454,9 @@ apk_status apk_stop(apk_ctx* ctx) {
     *reinterpret_cast<volatile int*>(ctx->h_flag) = kStop;
     std::atomic_thread_fence(std::memory_order_seq_cst);
   } else {
-    APK_CU(copy_flag_lines(ctx, stage_flag_lines(ctx, ctx->cfg.max_events + 1, kStop)));
+    int* src = nullptr;
+    APK_CU(stage_flag_lines(ctx, kStop, &src));
+    APK_CU(copy_flag_lines(ctx, src));
   }
   // the abort word also stops POLL_OFF kernels at their next tile boundary
   ctx->h_gen[0] = kOne;

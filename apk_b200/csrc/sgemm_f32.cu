@@ -140,7 +140,7 @@ __device__ __forceinline__ void kpair(const float* __restrict__ Asub, const floa
 template <class GE>
 __device__ __forceinline__ void compute_stage(const float* __restrict__ As, const float* __restrict__ Bs,
                                               float (&acc)[8][4 * GE::NQ], int arow0, int ty, int bcol, bool poll,
-                                              const int* flag, int& pend) {
+                                              const int* flag, const int* const* flag_at, int& pend) {
   constexpr int KP = GE::SUB / 2;
 #pragma unroll
   for (int sub = 0; sub < GE::BK / GE::SUB; ++sub) {
@@ -152,7 +152,11 @@ __device__ __forceinline__ void compute_stage(const float* __restrict__ As, cons
 #pragma unroll 1
     for (int kp = 0; kp < KP - 2; ++kp) kpair<GE>(Asub, Bsub, acc, arow0, ty, bcol, kp);
     // the poll sits between two loops, not behind a per-iteration branch
-    if (sub == GE::BK / GE::SUB - 1 && poll) pend = flag_load(flag);
+    // 4 or 8 CTAs per SM poll their flag copy, whose address the CTA keeps in
+    // shared memory (flag_at), read only on this branch so that no register
+    // holds it through the loop; at 1 or 2 the launch keeps one copy, the
+    // flag itself (a kernel parameter, no register either)
+    if (sub == GE::BK / GE::SUB - 1 && poll) pend = flag_load(GE::MINB >= 4 ? *flag_at : flag);
     // keeps the two loops apart when there is no poll (POLL_OFF), so that
     // variant is the polling code minus the load, not a re-fused loop whose
     // speed measured 39.7 or 42.1 TFLOP/s depending on the B200 it ran on
@@ -198,6 +202,7 @@ __global__ void __launch_bounds__(GE::NT, GE::MINB) sgemm_persistent(const __gri
   __shared__ __align__(8) uint64_t s_clcBar;
   __shared__ unsigned long long s_clcNext;
   __shared__ int s_clcInFlight, s_slot;
+  __shared__ const int* s_flag;  // the flag copy this CTA polls
   __shared__ uint32_t s_clcPhase;
   // Bookkeeping touched only by tid 0, or needed only across a job switch,
   // lives in shared memory: as per-thread locals it costs every thread
@@ -243,6 +248,7 @@ __global__ void __launch_bounds__(GE::NT, GE::MINB) sgemm_persistent(const __gri
     tma_prefetch_desc(&p.tmB);
     tma_prefetch_desc(&p.tmAu);
     tma_prefetch_desc(&p.tmBu);
+    if constexpr (GE::MINB >= 4) s_flag = flag_copy(p.ev, s_slot < 0 ? 0 : s_slot);
     atomicMin(p.q.start_min, (unsigned long long)globaltimer_ns());
   }
   __syncthreads();
@@ -308,7 +314,10 @@ __global__ void __launch_bounds__(GE::NT, GE::MINB) sgemm_persistent(const __gri
       if (s_gBase == 0) s_gBase = now;
       if (now >= s_gBase + p.ev.sched_ns[nextEv]) {
         p.ev.set_ns[nextEv] = now;
-        flag_raise(p.ev, nextEv);  // never overwrites the -1 sentinel
+        // 1 or 2 CTAs per SM: the launch keeps one flag copy; the loop over
+        // copies, compiled into those kernels, cost them 8% of their speed
+        if constexpr (GE::MINB >= 4) flag_raise(p.ev, nextEv);  // never overwrites the -1 sentinel
+        else atomicCAS(p.ev.flag, nextEv, nextEv + 1);
         s_nextEv = nextEv + 1;
       }
     }
@@ -463,7 +472,7 @@ __global__ void __launch_bounds__(GE::NT, GE::MINB) sgemm_persistent(const __gri
         fl = s_lastSeen;
         if (POLL == POLL_BOUNDARY) {
           setter();
-          fl = flag_load(flag_copy(p.ev, cta()));
+          fl = flag_load(GE::MINB >= 4 ? s_flag : p.ev.flag);
         }
         if (ab) fl = -1;
         s_f = fl;
@@ -545,8 +554,8 @@ __global__ void __launch_bounds__(GE::NT, GE::MINB) sgemm_persistent(const __gri
         }
         __syncthreads();
       }
-      compute_stage<GE>(As, Bs, acc, arow0, ty, bcol, POLL == POLL_STAGE && !urgent && tid == 0,
-                        flag_copy(p.ev, cta()), pend);
+      compute_stage<GE>(As, Bs, acc, arow0, ty, bcol, POLL == POLL_STAGE && !urgent && tid == 0, p.ev.flag, &s_flag,
+                        pend);
       ++Q;
     }
     if (yielded) {

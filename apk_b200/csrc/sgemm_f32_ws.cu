@@ -446,24 +446,19 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
         bwait_unwind(&gs.full[q % S], (q / S) & 1, p.wait_limit_ns);
     } else if (warp == G && lane == 0) {
       // ============================== control ===============================
+      // one CTA per SM: the launch keeps one flag copy (ev.flag_lines == 1)
       int nextEv = 0;
       long long gBase = 0;
-      const int* flag = flag_copy(p.ev, blockIdx.x);
-      // the abort word: every 16th pass (a stop also writes -1 into every
-      // flag copy); once seen it holds
-      unsigned pass = 0;
-      bool aborted = false;
       while (vload(&sh.prod_done) < G && !vload(&sh.abort)) {
-        int f = POLL != POLL_OFF ? flag_load(flag) : 0;
-        if ((++pass & 15) == 0 && *reinterpret_cast<volatile int*>(p.ev.abort_word)) aborted = true;
-        if (aborted) f = -1;
+        int f = POLL != POLL_OFF ? flag_load(p.ev.flag) : 0;
+        if (*reinterpret_cast<volatile int*>(p.ev.abort_word)) f = -1;
         // device-set events (src/yield.cu:186-195): worker 0's CTA
         if (blockIdx.x == 0 && p.ev.sched_ns != nullptr && nextEv < p.ev.n_sched) {
           const long long now = globaltimer_ns();
           if (gBase == 0) gBase = now;
           if (now >= gBase + p.ev.sched_ns[nextEv]) {
             p.ev.set_ns[nextEv] = now;
-            flag_raise(p.ev, nextEv);  // never overwrites the -1 sentinel
+            atomicCAS(p.ev.flag, nextEv, nextEv + 1);  // never overwrites the -1 sentinel
             ++nextEv;
           }
         }
