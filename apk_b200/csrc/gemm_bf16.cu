@@ -498,8 +498,13 @@ __global__ void __launch_bounds__(G::NT, G::MINB) gemm_bf16_persistent(const __g
     // shared memory goes away; a task it took is dropped with the run
     if (CLC && clc_inflight) mbar_wait(&sh.clc_bar, clc_phase, p.wait_limit_ns);
     vstore(&sh.prod_done, 1);
-    // TMA loads still in flight (only when unwinding) must land before exit
-    for (uint32_t q = (uint32_t)vload(&sh.consumed); q < P; ++q)
+    // TMA loads still in flight (only when unwinding) must land before exit.
+    // Only the last S stages can be: an older one's slot was reused, so its
+    // loads landed and its barrier has moved on; waiting on its parity could
+    // match a later phase that never comes.  (The consumer publishes
+    // `consumed` late -- after posting an epilogue job -- so it may lag P by
+    // a whole ring.)
+    for (uint32_t q = max((uint32_t)vload(&sh.consumed), P >= (uint32_t)S ? P - S : 0u); q < P; ++q)
       bwait_unwind(&sh.full[q % S], (q / S) & 1, p.wait_limit_ns);
   } else if (warp == 1 && lane == 0) {
     // ================================== MMA ===================================

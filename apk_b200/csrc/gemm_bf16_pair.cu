@@ -44,14 +44,12 @@
 namespace apk {
 namespace bf16pair {
 
-constexpr int BM = 256, BN = 512, BK = 64, S = 4;
+constexpr int BM = 256, BN = 512, BK = 64;
 constexpr int EPI_WARPS = 8;
 constexpr int CTRL_WARP = 2 + EPI_WARPS;
 constexpr int NT = 32 * (CTRL_WARP + 1);
 constexpr int A_BYTES = 128 * BK * 2;         // this CTA's 128 A rows
 constexpr int B_CHUNK = BK * 64 * 2;          // one [64 k][64 n] box
-constexpr int STAGE_BYTES = A_BYTES + 4 * B_CHUNK;
-constexpr int SMEM_BYTES = S * STAGE_BYTES + 1024;
 constexpr int RING = 8;
 // Peer tag ring.  The leader stores stage P's tag in entry P % T after its
 // wait for stage P-1's slot, i.e. after the MMAs of stage P-1-S completed;
@@ -61,7 +59,21 @@ constexpr int RING = 8;
 // acknowledgment (a SUSPEND slot is always followed by urgent data stages).
 // A release-ordered acknowledgment from the peer cost ~1400 cycles a stage
 // and starved the ring.
-constexpr int T = 4 * S;
+//
+// Ring geometry: S slots of A + NCH B chunks.  A plain run's 512-wide pair
+// tiles take four chunks a slot (4 x 48 KB); task lists, whose pair jobs are
+// at most 256 wide, take two (6 x 32 KB): a short task's stage holds half the
+// MMA work of a wide one, and four slots of it did not cover the load
+// latency (the task kernel streamed at two thirds of the one-CTA kernel's
+// rate).
+template <int S_, int NCH_>
+struct PG {
+  static constexpr int S = S_, NCH = NCH_, T = 4 * S_;
+  static constexpr int STAGE_BYTES = A_BYTES + NCH_ * B_CHUNK;
+  static constexpr int SMEM_BYTES = S_ * STAGE_BYTES + 1024;
+};
+using PgPlain = PG<4, 4>;
+using PgTasks = PG<6, 2>;
 constexpr int RASTER_GROUP = 8;
 // D = C_cols^T: MMA A = the B columns (MN-major), MMA B = the A rows (K-major)
 constexpr uint32_t IDESC = tc::idesc_bf16_f32(256, 256, true, false);
@@ -85,6 +97,7 @@ struct EpiJob {
   unsigned long long task;
 };
 
+template <int S, int T>
 struct __align__(16) Shared {
   StageTag tag[S];   // the leader's MMA reads the slot's tag here
   uint4 ptag[T];     // the peer's copy {kind | flags << 8, row0, col0, k}, stored by the leader
@@ -184,7 +197,8 @@ __device__ __forceinline__ void commit_pair(uint32_t bar) {
 
 // Bounded wait on a barrier of this CTA (remote arrivals: cluster-scope
 // acquire); also gives up when another role of this CTA aborted.
-__device__ __forceinline__ bool bwait(uint64_t* bar, uint32_t parity, const F32Params& p, Shared& sh) {
+template <class SH>
+__device__ __forceinline__ bool bwait(uint64_t* bar, uint32_t parity, const F32Params& p, SH& sh) {
   if (try_wait_cluster(bar, parity)) return true;
   const long long t0 = globaltimer_ns();
   int n = 0;
@@ -207,11 +221,12 @@ __device__ __forceinline__ void bwait_unwind(uint64_t* bar, uint32_t parity, lon
     if (globaltimer_ns() - t0 > limit) return;
 }
 
-template <int POLL, int DISC, bool ORACLE>
+template <int POLL, int DISC, bool ORACLE, class PGEO>
 __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ F32Params p) {
+  constexpr int S = PGEO::S, T = PGEO::T, NCH = PGEO::NCH, STAGE_BYTES = PGEO::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ Shared sh;
+  __shared__ Shared<S, T> sh;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int cta = blockIdx.x;
   const uint32_t rank = cluster_rank();
@@ -295,7 +310,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
       t.ncols = ncols;
       t.task = task;
       if (tA != nullptr) {
-        const int nb = (flags & F_WIDE) ? 4 : 2;
+        const int nb = (NCH == 4 && (flags & F_WIDE)) ? 4 : 2;
         mbar_arrive_expect_tx(&sh.full[s], 2 * (A_BYTES + nb * B_CHUNK));
         uint8_t* st = stages + s * STAGE_BYTES;
         const uint32_t fb = mapa(&sh.full[s], 0);
@@ -441,8 +456,13 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
     }
     emit(T_STOP, 0, 0, 0, 0, 0, 0, nullptr, nullptr, 0, 0, 0, 0, 0);
     vstore(&sh.prod_done, 1);
-    // loads still in flight (only when unwinding) land before teardown
-    for (uint32_t q = (uint32_t)vload(&sh.consumed); q < P; ++q)
+    // TMA loads still in flight (only when unwinding) must land before exit.
+    // Only the last S stages can be: an older one's slot was reused, so its
+    // loads landed and its barrier has moved on; waiting on its parity could
+    // match a later phase that never comes.  (The consumer publishes
+    // `consumed` late -- after posting an epilogue job -- so it may lag P by
+    // a whole ring.)
+    for (uint32_t q = max((uint32_t)vload(&sh.consumed), P >= (uint32_t)S ? P - S : 0u); q < P; ++q)
       bwait_unwind(&sh.full[q % S], (q / S) & 1, p.wait_limit_ns);
   } else if (warp == 0 && lane == 0) {
     // ============================= peer producer =============================
@@ -475,7 +495,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
                            &p.st.b_ready[(u0 + ((t.flags & F_WIDE) ? 3 : 1)) / p.st.b_units], p.wait_limit_ns))
             break;
         }
-        const int nb = (t.flags & F_WIDE) ? 4 : 2;
+        const int nb = (NCH == 4 && (t.flags & F_WIDE)) ? 4 : 2;
         uint8_t* st = stages + s * STAGE_BYTES;
         const uint32_t fb = mapa(&sh.full[s], 0);
         tma_load_pair(st, tA, t.k, t.row0, fb);
@@ -537,7 +557,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
         continue;
       }
       if (t.flags & (F_FIRST | F_RESUME)) {
-        cwide = (t.flags & F_WIDE) ? 1 : 0;
+        cwide = (NCH == 4 && (t.flags & F_WIDE)) ? 1 : 0;
         cur = cwide ? 0 : nb;
         nb = cwide ? 0 : nb ^ 1;
         bool ok = true;
@@ -568,7 +588,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
         const uint64_t bdesc = tc::smem_desc(sa + kk * 32, 16, 1024, tc::LAYOUT_SW128);
         mma_pair(d0, tc::smem_desc(sb + kk * 2048, B_CHUNK, 1024, tc::LAYOUT_SW128), bdesc, acc,
                  (t.flags & F_HALF) ? IDESC_HALF : IDESC);
-        if (cwide)
+        if (NCH == 4 && cwide)
           mma_pair(d0 + 256, tc::smem_desc(sb + 2 * B_CHUNK + kk * 2048, B_CHUNK, 1024, tc::LAYOUT_SW128), bdesc,
                    acc);
       }
@@ -816,14 +836,16 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
 
 // ---------------------------------------------------------------------------
 
-template <int POLL, int DISC, bool ORACLE>
+template <int POLL, int DISC, bool ORACLE, class PGEO>
 static const void* kernel_ptr() {
-  return reinterpret_cast<const void*>(&gemm_bf16_pair<POLL, DISC, ORACLE>);
+  return reinterpret_cast<const void*>(&gemm_bf16_pair<POLL, DISC, ORACLE, PGEO>);
 }
 
-static const void* select_kernel(int poll, int disc, bool oracle) {
-#define APK_SEL(PL, DS, OR) \
-  if (poll == PL && disc == DS && oracle == OR) return kernel_ptr<PL, DS, OR>();
+// tasks: the task-list ring geometry (PgTasks), else PgPlain
+static const void* select_kernel(int poll, int disc, bool oracle, bool tasks) {
+#define APK_SEL(PL, DS, OR)                                                   \
+  if (poll == PL && disc == DS && oracle == OR)                               \
+    return tasks ? kernel_ptr<PL, DS, OR, PgTasks>() : kernel_ptr<PL, DS, OR, PgPlain>();
   APK_SEL(POLL_OFF, DISC_DRAIN, false)
   APK_SEL(POLL_OFF, DISC_DRAIN, true)
   APK_SEL(POLL_BOUNDARY, DISC_DRAIN, false)
@@ -836,21 +858,28 @@ static const void* select_kernel(int poll, int disc, bool oracle) {
   return nullptr;
 }
 
-int smem_bytes() { return SMEM_BYTES; }
-int stages() { return S; }
+int smem_bytes(bool tasks) { return tasks ? PgTasks::SMEM_BYTES : PgPlain::SMEM_BYTES; }
+int stages(bool tasks) { return tasks ? PgTasks::S : PgPlain::S; }
 int threads() { return NT; }
 int epi_warps() { return EPI_WARPS; }
 size_t params_bytes() { return sizeof(F32Params); }
 
 // *pairs = clusters of two that can be resident at once (0: the kernel does
 // not run here).
+// Both ring geometries are prepared: a context learns of a task list after
+// it is created.
 cudaError_t prepare(int poll, int disc, bool oracle, int sms, int* pairs) {
   *pairs = 0;
-  const void* k = select_kernel(poll, disc, oracle);
-  if (!k) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  const void* k = select_kernel(poll, disc, oracle, false);
+  const void* kt = select_kernel(poll, disc, oracle, true);
+  if (!k || !kt) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, PgPlain::SMEM_BYTES);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(kt, cudaFuncAttributeMaxDynamicSharedMemorySize, PgTasks::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(kt, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute at[1];
@@ -860,14 +889,21 @@ cudaError_t prepare(int poll, int disc, bool oracle, int sms, int* pairs) {
   at[0].val.clusterDim.z = 1;
   cfg.gridDim = dim3(sms - (sms & 1));
   cfg.blockDim = dim3(NT);
-  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.dynamicSmemBytes = PgPlain::SMEM_BYTES;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  return cudaOccupancyMaxActiveClusters(pairs, k, &cfg);
+  e = cudaOccupancyMaxActiveClusters(pairs, k, &cfg);
+  if (e != cudaSuccess) return e;
+  int tpairs = 0;
+  cfg.dynamicSmemBytes = PgTasks::SMEM_BYTES;
+  e = cudaOccupancyMaxActiveClusters(&tpairs, kt, &cfg);
+  if (tpairs < *pairs) *pairs = tpairs;
+  return e;
 }
 
 cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, cudaStream_t stream) {
-  const void* k = select_kernel(poll, disc, oracle);
+  const bool tasks = prm.task_mode != 0;
+  const void* k = select_kernel(poll, disc, oracle, tasks);
   if (!k || grid % 2) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute at[1];
@@ -877,7 +913,7 @@ cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool orac
   at[0].val.clusterDim.z = 1;
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(NT);
-  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.dynamicSmemBytes = tasks ? PgTasks::SMEM_BYTES : PgPlain::SMEM_BYTES;
   cfg.stream = stream;
   cfg.attrs = at;
   cfg.numAttrs = 1;

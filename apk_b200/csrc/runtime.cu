@@ -32,8 +32,8 @@ size_t params_bytes();
 namespace bf16pair {
 cudaError_t prepare(int poll, int disc, bool oracle, int sms, int* pairs);
 cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, cudaStream_t stream);
-int smem_bytes();
-int stages();
+int smem_bytes(bool tasks);
+int stages(bool tasks);
 int threads();
 int epi_warps();
 size_t params_bytes();
@@ -677,11 +677,11 @@ apk_status apk_get_info(apk_ctx* ctx, apk_device_info* info) {
     info->tile_n = g.tile_n;
     info->stages = g.stages;
   } else if (use_pair(ctx)) {
-    info->smem_per_cta = bf16pair::smem_bytes();
+    info->smem_per_cta = bf16pair::smem_bytes(ctx->task_mode);
     info->threads_per_cta = bf16pair::threads();
     info->tile_m = 256;
     info->tile_n = 512;  // one tile per CTA pair
-    info->stages = bf16pair::stages();
+    info->stages = bf16pair::stages(ctx->task_mode);
   } else {
     const GeoInfo g = bf16::geo_info(ctx->bf16_geo);
     info->smem_per_cta = g.smem_bytes;

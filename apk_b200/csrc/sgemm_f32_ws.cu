@@ -441,8 +441,10 @@ __global__ void __launch_bounds__(NT, 1) sgemm_ws(const __grid_constant__ F32Par
       }
       emit(T_STOP, 0, 0, 0, 0, 0, 0, 0, nullptr, nullptr, 0);
       atomicAdd(&sh.prod_done, 1);
-      // TMA loads still in flight (only when unwinding) must land before exit
-      for (uint32_t q = (uint32_t)vload(&gs.consumed); q < P; ++q)
+      // TMA loads still in flight (only when unwinding) must land before
+      // exit; only the last S stages can be (an older slot was reused, its
+      // barrier has moved on and its parity could match a later phase)
+      for (uint32_t q = max((uint32_t)vload(&gs.consumed), P >= (uint32_t)S ? P - S : 0u); q < P; ++q)
         bwait_unwind(&gs.full[q % S], (q / S) & 1, p.wait_limit_ns);
     } else if (warp == G && lane == 0) {
       // ============================== control ===============================

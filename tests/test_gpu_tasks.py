@@ -99,14 +99,19 @@ def test_two_shards_reproduce_checksums_bitwise(whole_run):
     assert np.array_equal(merged.view(np.uint64), whole_run["chk"].view(np.uint64))
 
 
-def test_urgent_preemption_keeps_checksums_bitwise(whole_run):
+@pytest.mark.parametrize("kern", ["auto", "pair"])
+def test_urgent_preemption_keeps_checksums_bitwise(whole_run, kern):
+    """Device-set yields every 50 us while the task list drains, on the
+    one-CTA kernel and on CTA pairs (6-slot task ring): every half-tile
+    exactly once, checksums bitwise equal to the undisturbed run, every
+    claimed event's urgent output complete and correct."""
     tasks, n_chk = whole_run["tasks"], whole_run["n_chk"]
     import apk_b200
     Au = apk_b200.fill_normal_bf16((256, 256), 31)
     Bu = apk_b200.fill_normal_bf16((256, 256), 32)
     refu = oracle.gemm_f64_bf16_rows(Au, Bu, 0, 256)
     nev = 40
-    with _ctx(poll="stage", set_mode="device", oracle=True, max_events=64) as c:
+    with _ctx(poll="stage", set_mode="device", oracle=True, max_events=64, bf16_kernel=kern) as c:
         c.set_urgent(Au, Bu)
         c.schedule_device_events((np.arange(nev, dtype=np.int64) + 1) * 50_000)
         _run(c, whole_run["A"], whole_run["B"], whole_run["pool"], tasks, n_chk)
