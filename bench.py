@@ -60,7 +60,7 @@ SMS_B200 = 148
 #       python bench.py --case drain-f32 --n 4096
 # A constant, so a stale value shows up beside the profile it came from
 # rather than silently; re-capture after any change to the kernel.
-F32WS_DRAM_BYTES_PER_TILE = 408132
+F32WS_DRAM_BYTES_PER_TILE = 393618
 
 
 def parse():
