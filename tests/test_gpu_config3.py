@@ -165,3 +165,31 @@ def test_bf16_multi_cta_stage_yields_bitwise(libapk, cps, k_tile):
     r = _bf16_yield_run(k_tile, ctas_per_sm=cps)
     assert r["info"]["ctas_per_sm"] == cps
     _check_bf16_yield(r, k_tile)
+
+
+@pytest.mark.parametrize("dtype,cps", [("f32", 4), ("f32", 8), ("bf16", 4), ("bf16", 8)])
+def test_host_set_events_with_flag_copies(libapk, dtype, cps):
+    """At 4 and 8 CTAs per SM the yield flag lives in 32 cache-line copies
+    (CTA c polls copy c % 32): the host setter writes every copy in one
+    copy-engine transfer and the stop writes -1 into all of them.  Host-set
+    events on an unbounded launch stopped after the last one: every event
+    claimed, none missed by any CTA, and the launch ends on the stop."""
+    import apk_b200
+    if dtype == "f32":
+        A, B = oracle.gen_uniform(2048, 2048, 2048, 21)
+        Au, Bu = oracle.gen_uniform(256, 256, 256, 99)
+        kw = {"urgent_split_k": 8}
+    else:
+        A = apk_b200.fill_normal_bf16((4096, 4096), 21)
+        B = apk_b200.fill_normal_bf16((4096, 4096), 22)
+        Au = apk_b200.fill_normal_bf16((256, 256), 31)
+        Bu = apk_b200.fill_normal_bf16((256, 256), 32)
+        kw = {"dtype": "bf16", "urgent_split_k": 1}
+    with _ctx(poll="stage", set_mode="host_memcpy", ctas_per_sm=cps, max_events=128, **kw) as c:
+        assert c.info["ctas_per_sm"] == cps
+        c.set_background(A, B)
+        c.set_urgent(Au, Bu)
+        r = c.run_latency(events=60, period_us=500, seed=5, warmup_events=10, probe_reps=0)
+        st = c.run_stats()
+    assert r["n"] == 50 and r["unclaimed"] == 0 and r["anomalies"] == 0, r
+    assert st["device_status"] == 0
