@@ -227,7 +227,7 @@ def run_reference(args, world, rank):
         "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": 1, "kind": "port", "sample": sample,
                          "cpu": cpu_desc()},
         "all_cores": {"value": allc, "unit": "TFLOP/s", "cores": th, "kind": "port",
-                      "sample": f"{arrows} rows, OpenMP row-parallel, {adt:.1f} s"},
+                      "sample": f"{arows} rows, OpenMP row-parallel, {adt:.1f} s"},
         "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
