@@ -1118,10 +1118,10 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
 }
 
 apk_status read_status(apk_ctx* ctx) {
-  Ctrl cb;
-  APK_CU(cudaMemcpy(&cb, ctx->d_ctrl, sizeof cb, cudaMemcpyDeviceToHost));
-  if (cb.status != 0)
-    return fail(ctx, APK_EDEVICE, "device reported status %d (a bounded wait ran out)", cb.status);
+  int status = 0;  // the word alone: the control block is ~4 KB with the flag lines
+  APK_CU(cudaMemcpy(&status, &ctx->d_ctrl->status, sizeof status, cudaMemcpyDeviceToHost));
+  if (status != 0)
+    return fail(ctx, APK_EDEVICE, "device reported status %d (a bounded wait ran out)", status);
   return APK_OK;
 }
 
@@ -1478,8 +1478,11 @@ apk_status apk_wait(apk_ctx* ctx, long long timeout_ns) {
       ctx->running = false;
       return fail(ctx, APK_ECUDA, "kernel failed: %s", cudaGetErrorString(q));
     }
-    if (host_now_ns() - t0 > timeout_ns) return fail(ctx, APK_ETIMEDOUT, "launch still running");
-    std::this_thread::sleep_for(std::chrono::microseconds(50));
+    const long long waited = host_now_ns() - t0;
+    if (waited > timeout_ns) return fail(ctx, APK_ETIMEDOUT, "launch still running");
+    // poll without sleeping for the first 2 ms (a sleep of 50 us ended short
+    // launches up to ~60 us late), then yield the core between polls
+    if (waited > 2000000) std::this_thread::sleep_for(std::chrono::microseconds(50));
   }
   ctx->running = false;
   APK_CU(cudaGetLastError());
@@ -1546,8 +1549,8 @@ apk_status apk_read_oracle(apk_ctx* ctx, int* exec_counts, int* uexec_counts) {
 apk_status apk_read_run_stats(apk_ctx* ctx, apk_run_stats* st) {
   if (!ctx || !st) return APK_EINVAL;
   if (ctx->running) return fail(ctx, APK_ESTATE, "launch still running");
-  Ctrl cb;
-  APK_CU(cudaMemcpy(&cb, ctx->d_ctrl, sizeof cb, cudaMemcpyDeviceToHost));
+  Ctrl cb;  // the counters precede the flag lines
+  APK_CU(cudaMemcpy(&cb, ctx->d_ctrl, offsetof(Ctrl, flag_dev), cudaMemcpyDeviceToHost));
   std::vector<unsigned long long> t(ctx->last_grid);
   APK_CU(cudaMemcpy(t.data(), ctx->d_tiles, sizeof(unsigned long long) * ctx->last_grid, cudaMemcpyDeviceToHost));
   memset(st, 0, sizeof *st);
