@@ -117,6 +117,11 @@ struct __align__(16) Shared {
   double chk_part[RING][EPI_WARPS];
   int cta_cnt[RING];
   unsigned long long tiles;
+  // the pair's resident slot (logs, counters and slabs of its two CTAs are
+  // at 2 * slot + rank); under CLC the leader's cancellation answer
+  int slot;
+  uint4 clc_resp;
+  uint64_t clc_bar;
 };
 
 __device__ __forceinline__ int vload(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
@@ -221,18 +226,44 @@ __device__ __forceinline__ void bwait_unwind(uint64_t* bar, uint32_t parity, lon
     if (globaltimer_ns() - t0 > limit) return;
 }
 
-template <int POLL, int DISC, bool ORACLE, class PGEO>
+// SCHED: SCH_QUEUE (the atomic queue) or SCH_CLC (one cluster per task:
+// the leader of each running pair cancels a not-yet-launched cluster with
+// clusterlaunchcontrol.try_cancel, without multicast, and takes its task;
+// the peer learns every task from the leader's stage tags as it does under
+// the queue)
+enum : int { SCH_QUEUE = 0, SCH_CLC = 1 };
+constexpr unsigned long long NO_TASK = ~0ull;
+
+template <int POLL, int DISC, bool ORACLE, class PGEO, int SCHED = SCH_QUEUE>
 __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ F32Params p) {
+  constexpr bool CLC = SCHED == SCH_CLC;
   constexpr int S = PGEO::S, T = PGEO::T, NCH = PGEO::NCH, STAGE_BYTES = PGEO::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ Shared<S, T> sh;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int cta = blockIdx.x;
   const uint32_t rank = cluster_rank();
   const bool leader = rank == 0;
 
   if (tid == 0) {
+    if constexpr (CLC) {
+      // the leader claims the pair's slot (one bit per resident pair); the
+      // peer reads it from the leader once the start-up cluster barrier has
+      // shown both CTAs running
+      if (leader) {
+        mbar_init(&sh.clc_bar, 1);
+        int sl = slot_claim(p.q.slot_bits, p.q.nslots / 2, p.wait_limit_ns);
+        sh.abort = 0;
+        if (sl < 0) {  // cannot happen while residency holds: stop the pair at once
+          report_status(p.ev.status, DEV_BAD_CONFIG, p.ev.abort_word);
+          sh.abort = 1;
+          sl = 0;
+        }
+        sh.slot = sl;
+      }
+    } else {
+      sh.slot = (int)blockIdx.x / 2;
+    }
     for (int s = 0; s < S; ++s) {
       mbar_init(&sh.full[s], 1);
       mbar_init(&sh.empty[s], 1);
@@ -251,7 +282,7 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
     }
     mbar_init(&sh.drain, 1);
     fence_mbar_init();
-    sh.abort = 0;
+    if (!CLC || !leader) sh.abort = 0;  // a leader that found no slot stops the pair
     sh.gen = 0;
     sh.prod_done = 0;
     sh.consumed = 0;
@@ -273,6 +304,18 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
   __syncwarp();
   cluster_sync();  // both CTAs' barriers initialised before any remote access
   tc::fence_after_sync();
+  if (CLC && !leader) {
+    if (tid == 0) {
+      uint32_t sl;
+      asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(sl) : "r"(mapa(&sh.slot, 0)) : "memory");
+      sh.slot = (int)sl;
+    }
+    __syncthreads();
+  }
+  // per-CTA logs, counters and the slab: index 2 * slot + rank (the block
+  // index under the queue, where slot = cluster index)
+  const int cta = 2 * sh.slot + (int)rank;
+  const int gridw = CLC ? p.q.nslots : (int)gridDim.x;
 
   if (warp == 0 && lane == 0 && leader) {
     // ============================ leader producer ============================
@@ -329,8 +372,8 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
       const int fc = f < p.ev.max_events ? f : p.ev.max_events;
       const long long g = globaltimer_ns();
       for (int e = lastSeen; e < fc; ++e) {
-        p.ev.obs_ns[(size_t)e * gridDim.x + cta] = g;
-        p.ev.obs_ns[(size_t)e * gridDim.x + cta + 1] = g;
+        p.ev.obs_ns[(size_t)e * gridw + cta] = g;
+        p.ev.obs_ns[(size_t)e * gridw + cta + 1] = g;
       }
       const int old = lastSeen;
       lastSeen = f;
@@ -365,10 +408,41 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
       return n;
     };
 
-    unsigned long long next_task = atomicAdd(p.q.next_task, 1ull);
+    // CLC: the task of the cluster cancelled by the request answered at this
+    // boundary, asked for one tile earlier (the first is the pair's own)
+    uint32_t clc_phase = 0;
+    bool clc_inflight = false;
+    auto clc_issue = [&]() {
+      mbar_arrive_expect_tx(&sh.clc_bar, 16);
+      clc_try_cancel(&sh.clc_resp, &sh.clc_bar);
+      clc_inflight = true;
+    };
+    auto clc_answer = [&]() -> unsigned long long {
+      clc_inflight = false;
+      if (!mbar_wait(&sh.clc_bar, clc_phase, p.wait_limit_ns)) {
+        report_status(p.ev.status, DEV_WAIT_TIMEOUT_SPIN, p.ev.abort_word);
+        return NO_TASK;
+      }
+      clc_phase ^= 1u;
+      unsigned x = 0;
+      return clc_query(&sh.clc_resp, &x) ? (unsigned long long)(x / 2) : NO_TASK;
+    };
+    if (CLC) {
+      // a pair launched mid-run takes the generations raised before it as
+      // seen: their urgent work was popped by the pairs that observed them
+      const int f0 = flag_load(p.ev.flag);
+      lastSeen = f0 > 0 ? f0 : 0;
+    }
+    unsigned long long next_task = CLC ? (unsigned long long)(blockIdx.x / 2) : atomicAdd(p.q.next_task, 1ull);
+    if (CLC && ok && !vload(&sh.abort)) clc_issue();
     while (ok) {
       const unsigned long long task = next_task;
-      if (task < p.q.num_tasks) next_task = atomicAdd(p.q.next_task, 1ull);
+      if (CLC) {
+        next_task = clc_inflight ? clc_answer() : NO_TASK;
+        if (next_task != NO_TASK) clc_issue();
+      } else if (task < p.q.num_tasks) {
+        next_task = atomicAdd(p.q.next_task, 1ull);
+      }
       int f = vload(&sh.gen);
       if (f < 0 || vload(&sh.abort)) break;
       if (POLL != POLL_OFF && f != lastSeen)
@@ -455,6 +529,9 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
       }
     }
     emit(T_STOP, 0, 0, 0, 0, 0, 0, nullptr, nullptr, 0, 0, 0, 0, 0);
+    // a CLC answer still in flight (a stopped or aborted run) lands before
+    // shared memory goes away; a cluster it cancelled is dropped with the run
+    if (CLC && clc_inflight) mbar_wait(&sh.clc_bar, clc_phase, p.wait_limit_ns);
     vstore(&sh.prod_done, 1);
     // TMA loads still in flight (only when unwinding) must land before exit.
     // Only the last S stages can be: an older one's slot was reused, so its
@@ -787,8 +864,14 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
     }
   } else if (warp == CTRL_WARP && lane == 0 && leader) {
     // ================================ control =================================
+    // device setter: the leader in slot 0 (under CLC its state passes from
+    // one slot-0 holder to the next)
     int nextEv = 0;
     long long gBase = 0;
+    if (CLC && cta == 0 && p.q.setter_state != nullptr) {
+      nextEv = (int)p.q.setter_state[0];
+      gBase = p.q.setter_state[1];
+    }
     const int* flag = flag_copy(p.ev, cta);
     // the abort word: every 16th pass (a stop also writes -1 into every
     // flag copy); once seen it holds
@@ -810,6 +893,10 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
       vstore(&sh.gen, f);
       __nanosleep(64);
     }
+    if (CLC && cta == 0 && p.q.setter_state != nullptr) {
+      p.q.setter_state[0] = nextEv;
+      p.q.setter_state[1] = gBase;
+    }
   }
 
   // Teardown: every role of both CTAs is done (MMAs drained by the leader,
@@ -828,21 +915,42 @@ __global__ void __launch_bounds__(NT, 1) gemm_bf16_pair(const __grid_constant__ 
   cluster_sync();
   if (tid == 0) {
     // task mode: each CTA counted its own 128-column halves
-    p.q.tiles_done[cta] = (leader || p.task_mode) ? sh.tiles : 0ull;
+    const unsigned long long mine = (leader || p.task_mode) ? sh.tiles : 0ull;
+    if (CLC) atomicAdd(&p.q.tiles_done[cta], mine);  // the slot's earlier holders counted theirs
+    else p.q.tiles_done[cta] = mine;
     atomicMax(p.q.end_max, (unsigned long long)globaltimer_ns());
     atomicAdd(p.q.exited, 1);
+    if (CLC && leader) {
+      // last: both CTAs' logs are written (the cluster barrier above)
+      __threadfence();
+      slot_release(p.q.slot_bits, sh.slot);
+    }
   }
 }
 
 // ---------------------------------------------------------------------------
 
-template <int POLL, int DISC, bool ORACLE, class PGEO>
+template <int POLL, int DISC, bool ORACLE, class PGEO, int SCHED = SCH_QUEUE>
 static const void* kernel_ptr() {
-  return reinterpret_cast<const void*>(&gemm_bf16_pair<POLL, DISC, ORACLE, PGEO>);
+  return reinterpret_cast<const void*>(&gemm_bf16_pair<POLL, DISC, ORACLE, PGEO, SCHED>);
 }
 
-// tasks: the task-list ring geometry (PgTasks), else PgPlain
-static const void* select_kernel(int poll, int disc, bool oracle, bool tasks) {
+// tasks: the task-list ring geometry (PgTasks), else PgPlain; clc: cluster
+// launch control (plain drains, drain discipline)
+static const void* select_kernel(int poll, int disc, bool oracle, bool tasks, bool clc = false) {
+  if (clc) {
+    if (tasks || disc != DISC_DRAIN) return nullptr;
+#define APK_SELC(PL, OR) \
+  if (poll == PL && oracle == OR) return kernel_ptr<PL, DISC_DRAIN, OR, PgPlain, SCH_CLC>();
+    APK_SELC(POLL_OFF, false)
+    APK_SELC(POLL_OFF, true)
+    APK_SELC(POLL_BOUNDARY, false)
+    APK_SELC(POLL_BOUNDARY, true)
+    APK_SELC(POLL_STAGE, false)
+    APK_SELC(POLL_STAGE, true)
+#undef APK_SELC
+    return nullptr;
+  }
 #define APK_SEL(PL, DS, OR)                                                   \
   if (poll == PL && disc == DS && oracle == OR)                               \
     return tasks ? kernel_ptr<PL, DS, OR, PgTasks>() : kernel_ptr<PL, DS, OR, PgPlain>();
@@ -867,11 +975,12 @@ size_t params_bytes() { return sizeof(F32Params); }
 // *pairs = clusters of two that can be resident at once (0: the kernel does
 // not run here).
 // Both ring geometries are prepared: a context learns of a task list after
-// it is created.
-cudaError_t prepare(int poll, int disc, bool oracle, int sms, int* pairs) {
+// it is created.  clc: the cluster-launch-control kernel instead (plain
+// drains only).
+cudaError_t prepare(int poll, int disc, bool oracle, int sms, int* pairs, bool clc) {
   *pairs = 0;
-  const void* k = select_kernel(poll, disc, oracle, false);
-  const void* kt = select_kernel(poll, disc, oracle, true);
+  const void* k = select_kernel(poll, disc, oracle, false, clc);
+  const void* kt = clc ? k : select_kernel(poll, disc, oracle, true);
   if (!k || !kt) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, PgPlain::SMEM_BYTES);
   if (e != cudaSuccess) return e;
@@ -901,9 +1010,10 @@ cudaError_t prepare(int poll, int disc, bool oracle, int sms, int* pairs) {
   return e;
 }
 
-cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, cudaStream_t stream) {
+// grid: CTAs (two per cluster); under CLC one cluster per task
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, bool clc, cudaStream_t stream) {
   const bool tasks = prm.task_mode != 0;
-  const void* k = select_kernel(poll, disc, oracle, tasks);
+  const void* k = select_kernel(poll, disc, oracle, tasks, clc);
   if (!k || grid % 2) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute at[1];

@@ -30,8 +30,8 @@ GeoInfo geo_info(int geo);
 size_t params_bytes();
 }  // namespace f32
 namespace bf16pair {
-cudaError_t prepare(int poll, int disc, bool oracle, int sms, int* pairs);
-cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, cudaStream_t stream);
+cudaError_t prepare(int poll, int disc, bool oracle, int sms, int* pairs, bool clc);
+cudaError_t launch(const F32Params& prm, int grid, int poll, int disc, bool oracle, bool clc, cudaStream_t stream);
 int smem_bytes(bool tasks);
 int stages(bool tasks);
 int threads();
@@ -367,9 +367,10 @@ apk_status prepare_kernel(apk_ctx* ctx, int poll) {
     if (e != cudaSuccess) ok = 0;
     ctx->ws_ok = ctx->ws_ok && ok;
   }
-  if (ctx->cfg.dtype == APK_BF16 && ctx->bf16_geo == BF16_GEO_STD64 && ctx->cfg.scheduler == APK_SCHED_QUEUE) {
+  if (ctx->cfg.dtype == APK_BF16 && ctx->bf16_geo == BF16_GEO_STD64) {
     int pairs = 0;
-    e = bf16pair::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->sms, &pairs);
+    e = bf16pair::prepare(poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->sms, &pairs,
+                          ctx->cfg.scheduler == APK_SCHED_CLC);
     if (e != cudaSuccess) pairs = 0;
     ctx->pair_ok = ctx->pair_ok && ctx->sms % 2 == 0 && 2 * pairs >= ctx->sms;
   }
@@ -382,15 +383,18 @@ apk_status prepare_kernel(apk_ctx* ctx, int poll) {
 // everything else.
 // (task lists included: every task tile is a 256x256 pair job, the
 // peer's half of a tile whose n ends 128 columns in computed and not stored)
+// Under cluster launch control the pairs run plain drains (one cluster per
+// 256x512 tile); task lists then take the one-CTA kernel.
 bool pair_capable(const apk_ctx* ctx) {
-  return ctx->cfg.dtype == APK_BF16 && ctx->pair_ok && ctx->cfg.scheduler == APK_SCHED_QUEUE &&
+  return ctx->cfg.dtype == APK_BF16 && ctx->pair_ok &&
+         (ctx->cfg.scheduler == APK_SCHED_QUEUE || (ctx->cfg.scheduler == APK_SCHED_CLC && !ctx->task_mode)) &&
          (ctx->cfg.bf16_kernel == APK_BF16_AUTO || ctx->cfg.bf16_kernel == APK_BF16_PAIR) &&
          ctx->bf16_geo == BF16_GEO_STD64 && ctx->grid == ctx->sms && ctx->Nu % 256 == 0;
 }
 // Task lists run on pairs only when asked for (APK_BF16_PAIR): their
-// 256-wide pair jobs issue half the MMAs per ring slot of the 256x512 tiles,
-// and on 2^18 configs[4] tasks the pair kernel reached 700 TFLOP/s against
-// 918 for the one-CTA kernel.
+// 256-wide pair jobs issue one MMA a k-step into one accumulator, and on
+// 2^18 configs[4] tasks the pair kernel reached 760-800 TFLOP/s against
+// 860-910 for the one-CTA kernel.
 bool use_pair(const apk_ctx* ctx) {
   return pair_capable(ctx) &&
          (ctx->task_mode ? ctx->cfg.bf16_kernel == APK_BF16_PAIR : ctx->N % 256 == 0);
@@ -1005,8 +1009,9 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
   }
   if (!ctx->dAu && poll != APK_POLL_OFF) return fail(ctx, APK_ESTATE, "no urgent operands set");
   const bool clc = ctx->cfg.scheduler == APK_SCHED_CLC;
-  if (clc && (num_tasks == APK_TASKS_UNBOUNDED || num_tasks > 0x7fffffffull))
-    return fail(ctx, APK_EINVAL, "the CLC scheduler launches one CTA per task: a bounded launch of < 2^31 tasks");
+  if (clc && (num_tasks == APK_TASKS_UNBOUNDED || num_tasks > 0x3fffffffull))
+    return fail(ctx, APK_EINVAL,
+                "the CLC scheduler launches one CTA (a CTA pair) per task: a bounded launch of < 2^30 tasks");
   apk_status s = reset_logs(ctx, num_tasks);
   if (s != APK_OK) return s;
   int* flag = ctx->cfg.set_mode == APK_SET_HOST_MAPPED ? ctx->d_flag_mapped : &ctx->d_ctrl->flag_dev;
@@ -1108,7 +1113,8 @@ apk_status launch_impl(apk_ctx* ctx, unsigned long long num_tasks, int poll, cud
     e = f32::launch(p, ctx->cfg.scheduler == APK_SCHED_CLC ? (int)num_tasks : ctx->grid, poll,
                     ctx->cfg.discipline, ctx->cfg.oracle != 0, ctx->f32_geo, ctx->cfg.scheduler, stream);
   else if (use_pair(ctx))
-    e = bf16pair::launch(p, ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0, stream);
+    e = bf16pair::launch(p, clc ? 2 * (int)num_tasks : ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0,
+                         clc, stream);
   else
     e = bf16::launch(p, clc ? (int)num_tasks : ctx->grid, poll, ctx->cfg.discipline, ctx->cfg.oracle != 0,
                      ctx->bf16_geo, ctx->cfg.scheduler, stream);

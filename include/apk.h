@@ -73,12 +73,15 @@ typedef enum apk_mem_kind { APK_MEM_HOST = 0, APK_MEM_DEVICE = 1 } apk_mem_kind;
 
 /* How background tasks reach CTAs.  QUEUE: a persistent grid of resident
  * CTAs popping a global fetch-add counter (src/persistent.cu:51-79).  CLC
- * (fp32 128x128 tiles and the one-CTA bf16 kernel, task mode included; drain
- * discipline, bounded launches only): one CTA per task, running
- * CTAs take not-yet-launched CTAs' tasks through Blackwell cluster launch
- * control; when the hardware declines (a higher-priority stream's kernel is
- * waiting) CTAs exit and free their SMs, and the rest of the grid launches
- * later.  The cooperative yield works the same under both. */
+ * (fp32 128x128 tiles, the one-CTA bf16 kernel with task lists included,
+ * and the bf16 CTA pairs for plain drains; drain discipline, bounded
+ * launches of < 2^30 tasks): one CTA -- or one cluster of two -- per task,
+ * running CTAs take not-yet-launched ones' tasks through Blackwell cluster
+ * launch control (on pairs the leader cancels a cluster and relays its
+ * tile to the peer); when the hardware declines (a higher-priority
+ * stream's kernel is waiting) CTAs exit and free their SMs, and the rest of
+ * the grid launches later.  The cooperative yield works the same under
+ * both. */
 typedef enum apk_scheduler { APK_SCHED_QUEUE = 0, APK_SCHED_CLC = 1 } apk_scheduler;
 
 /* fp32 kernel.  WARP_SPECIALIZED: one 384-thread CTA per SM runs two

@@ -336,30 +336,40 @@ def test_narrow_jobs_park_or_spill_bitwise(libapk, kernel):
     assert v["pass"], v
 
 
-def test_clc_scheduler_drain_exactly_once_bitwise(libapk):
-    """bf16 under cluster launch control: one CTA per task, running CTAs
-    take the pending ones; every task exactly once and C bitwise equal to
-    the queue-scheduled one-CTA kernel's."""
+@pytest.mark.parametrize("kern", ["single", "pair"])
+def test_clc_scheduler_drain_exactly_once_bitwise(libapk, kern):
+    """bf16 under cluster launch control: one CTA (or one CTA pair) per
+    task, running CTAs take the pending ones -- on pairs the leader cancels
+    a pending cluster and relays its tile to the peer through the stage
+    tags; every task exactly once and C bitwise equal to the
+    queue-scheduled one-CTA kernel's."""
     M, N, K = 2048, 2048, 1024
     A, B = _normal((M, K), 51), _normal((K, N), 52)
     with _ctx(poll="off", bf16_kernel="single") as c:
         C0 = c.gemm(A, B)
-    ntasks = 3 * (M // 256) * (N // 256)
-    with _ctx(poll="off", oracle=True, scheduler="clc") as c:
+    with _ctx(poll="off", oracle=True, scheduler="clc", bf16_kernel=kern) as c:
+        info = c.info
+        assert info["tile_n"] == (512 if kern == "pair" else 256)
+        tiles = (M // info["tile_m"]) * (N // info["tile_n"])
+        ntasks = 3 * tiles
         C = c.gemm(A, B)
         st = c.run_stats()
         c.set_background(A, B)
         c.launch(ntasks)
         c.wait(30)
         ex, _ = c.read_oracle(ntasks)
+        st2 = c.run_stats()
     assert np.array_equal(C.view(np.uint32), C0.view(np.uint32))
-    assert st["tiles_done"] == (M // 256) * (N // 256) and st["device_status"] == 0
+    assert st["tiles_done"] == tiles and st["device_status"] == 0
+    assert st2["tiles_done"] == ntasks and st2["device_status"] == 0
     assert np.all(ex == 1)
 
 
-def test_clc_stage_yields_bitwise(libapk):
-    """bf16 CLC with per-stage device-set yields: checkpoints resume
-    bitwise; every task and urgent item exactly once."""
+@pytest.mark.parametrize("kern", ["single", "pair"])
+def test_clc_stage_yields_bitwise(libapk, kern):
+    """bf16 CLC with per-stage device-set yields (on pairs: only the leader
+    polls, the peer follows its tags): checkpoints resume bitwise; every
+    task and urgent item exactly once."""
     M = N = K = 4096
     A, B = _normal((M, K), 21), _normal((K, N), 22)
     Au, Bu = _normal((256, 256), 31), _normal((256, 256), 32)
@@ -367,8 +377,10 @@ def test_clc_stage_yields_bitwise(libapk):
     with _ctx(poll="off", bf16_kernel="single") as c:
         C0 = c.gemm(A, B)
     nev = 30
-    with _ctx(poll="stage", set_mode="device", oracle=True, scheduler="clc", max_events=64) as c:
-        ntasks = 8 * (M // 256) * (N // 256)
+    with _ctx(poll="stage", set_mode="device", oracle=True, scheduler="clc", max_events=64, bf16_kernel=kern) as c:
+        info = c.info
+        assert info["tile_n"] == (512 if kern == "pair" else 256)
+        ntasks = 8 * (M // info["tile_m"]) * (N // info["tile_n"])
         c.set_background(A, B)
         c.set_urgent(Au, Bu)
         c.schedule_device_events((np.arange(nev, dtype=np.int64) + 1) * 20_000)
