@@ -344,7 +344,10 @@ def bf16_config2(apk_b200, np, dev):
     out = {"tflops": r3(tf), "pct_of_peak": r3(tf / peak * 100.0), "fired": fired, "ckpts": int(st["yields"]),
            "bitwise": bool(np.array_equal(C.view(np.uint32), C0.view(np.uint32))),
            "claim_p50": r3(pct(cl, 0.5)), "done_p50": r3(pct(dn, 0.5)),
-           "spill_us": r3(st["ckpt_spill_ns"] / y / 1e3), "restore_us": r3(st["ckpt_restore_ns"] / y / 1e3)}
+           "spill_us": r3(st["ckpt_spill_ns"] / y / 1e3), "restore_us": r3(st["ckpt_restore_ns"] / y / 1e3),
+           # TMEM <-> slab bandwidth of one checkpoint (a CTA pair's 512 KB)
+           "spill_gbs": r3(st["ckpt_spill_bytes"] / max(st["ckpt_spill_ns"], 1)),
+           "restore_gbs": r3(st["ckpt_restore_bytes"] / max(st["ckpt_restore_ns"], 1))}
     # the same drain as 256x128 jobs: the yielding accumulator parked in its
     # TMEM buffer against spilled to the slab (urgent done latency, rate)
     for kern in ("narrow", "narrow_spill"):
