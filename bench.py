@@ -131,6 +131,24 @@ def allgather_obj(world, obj):
 
 
 # ---------------------------------------------------------------- cpu legs
+def numa_local_cpus(pci_bus_id: str):
+    """The CPUs this process may use on the NUMA node of the GPU at this PCI
+    address (sysfs local_cpulist), or None when unknown."""
+    try:
+        dom, rest = pci_bus_id.split(":", 1)
+        path = "/sys/bus/pci/devices/%04x:%s/local_cpulist" % (int(dom, 16), rest.lower())
+        with open(path) as f:
+            spec = f.read().strip()
+        cpus = set()
+        for part in spec.split(","):
+            a, _, b = part.partition("-")
+            cpus.update(range(int(a), int(b or a) + 1))
+        cpus &= os.sched_getaffinity(0)
+    except (OSError, ValueError, AttributeError):
+        return None
+    return cpus or None
+
+
 def host_cores() -> int:
     """Host threads this process may run on (set explicitly: torchrun exports
     OMP_NUM_THREADS=1, which must not decide the all-cores figure)."""
@@ -455,10 +473,25 @@ def run_ours(args, world, rank, local):
     barrier(world)
     clk = clocks.stop()
 
-    # e2e through the public API with pinned host buffers
-    hA = apk_b200.pinned_empty((M, K), np.float32)
-    hB = apk_b200.pinned_empty((K, N), np.float32)
-    hC = apk_b200.pinned_empty((M, N), np.float32)
+    # e2e through the public API with pinned host buffers, allocated by this
+    # rank while it runs on its GPU's NUMA node, so the pages land there
+    # (the previous CPU set is restored for the rest of the run)
+    gpu = gpu_identity(local)
+    near = numa_local_cpus(gpu.get("pci_bus_id", ""))
+    prev = os.sched_getaffinity(0) if near else None
+    try:
+        if near:
+            os.sched_setaffinity(0, near)
+        hA = apk_b200.pinned_empty((M, K), np.float32)
+        hB = apk_b200.pinned_empty((K, N), np.float32)
+        hC = apk_b200.pinned_empty((M, N), np.float32)
+        hA[:] = 0
+        hB[:] = 0
+        hC[:] = 0
+    finally:
+        if prev:
+            os.sched_setaffinity(0, prev)
+
     hA[:] = A
     hB[:] = B
     for _ in range(2):
@@ -553,9 +586,9 @@ def run_ours(args, world, rank, local):
         "clocks": clk,
         "e2e": {"value": sum(r["e2e_tf"] for r in allr), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": 2 * M * K * 4, "d2h_bytes_per_step": M * N * 4,
-                "copy_ceiling": r3(copy_ceiling),
+                "copy_ceiling": r3(copy_ceiling), "numa_local": bool(near),
                 "copy_ms": {k: r3(r0["copy"][k]) for k in ("h2d_ms", "d2h_ms", "both_ms")}},
-        "gpu": gpu_identity(local),
+        "gpu": gpu,
         "extras": allr[0]["extras"],
     }
     if world == 1 and not args.no_extras:
