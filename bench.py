@@ -55,12 +55,19 @@ METRIC = "urgent-task p50/p99 preempt latency (us); background GEMM TFLOPS (% of
 SMS_B200 = 148
 # DRAM bytes (read + write) per 128x128x4096 tile of the warp-specialized
 # fp32 kernel: one ncu capture of a 4096^3 drain (1024 tiles) measured
-# 363.2 MB read + 54.8 MB written, i.e. 417.9 MB / 1024 tiles.  Command:
+# 350.1 MB read + 53.0 MB written, i.e. 403.1 MB / 1024 tiles.  Command:
 #   ncu --set full --clock-control none -k regex:sgemm_ws -s 1 -c 1 \
 #       python bench.py --case drain-f32 --n 4096
 # A constant, so a stale value shows up beside the profile it came from
 # rather than silently; re-capture after any change to the kernel.
 F32WS_DRAM_BYTES_PER_TILE = 393618
+# DRAM bytes (read + write) per TFLOP of the configs[4] task kernel: one ncu
+# capture of a 2^16-task list of the same generator measured 70.97 GB read +
+# 94.84 GB written for 87.50 TFLOP.  Traffic grows with the work, so a full
+# shard's launch is scaled by its TFLOP.  Command:
+#   ncu --set full --clock-control none -k regex:gemm_bf16_persistent -s 1 -c 1 \
+#       python bench.py --case tasks-bf16 --tasks 65536 --reps 2
+C4_DRAM_BYTES_PER_TFLOP = (70.97e9 + 94.84e9) / 87.50
 
 
 def parse():
@@ -533,6 +540,15 @@ def run_ours(args, world, rank, local):
         c4_all = allgather_obj(world, c4_res)
         if rank == 0:
             c4 = config4.summarize(c4_all, counts, args.config4_tasks)
+            # by GPU time the configs[4] drains are the run's dominant kernel
+            # (the one-CTA bf16 task kernel): its roofline per GPU, against
+            # the sustained tensor peak (a ~1.6 s drain runs at the power cap)
+            per_gpu = c4["tflops_undisturbed"] / world
+            peak_s = measured_peaks().get("bf16_tflops_sustained", 1400.0)
+            c4["roofline"] = {"bound": "tensor", "achieved": r3(per_gpu), "peak": peak_s, "unit": "TFLOP/s",
+                              "frac": r3(per_gpu / peak_s),
+                              "traffic": r3(C4_DRAM_BYTES_PER_TFLOP * c4["pflop"] * 1e3 / world),
+                              "kernel": "bf16::gemm_bf16_persistent<POLL_STAGE,DRAIN,oracle,STD64> (task list)"}
 
     res = {"flops": flops, "launch_s": sum(launch_ms) / 1e3, "lats": lats, "clk": clk,
            "e2e_tf": e2e_tf, "copy": cp, "extras": extras, "info": info, "yields": yields,
