@@ -22,3 +22,19 @@ def test_reference_arm_prints_its_line():
     assert line["all_cores"]["cores"] >= 1 and line["all_cores"]["value"] > 0
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
     assert line["gpu_launches"] == 0
+
+
+def test_numa_local_cpus_reads_sysfs_or_declines():
+    """The e2e buffers are allocated on the GPU's NUMA node: the helper maps
+    a PCI address (nvidia-smi form) to the CPUs this process may use there,
+    and answers None for an address sysfs does not know."""
+    import os
+    import sys
+    sys.path.insert(0, ROOT)
+    import bench
+    allowed = os.sched_getaffinity(0)
+    host_bridge = bench.numa_local_cpus("00000000:00:00.0")
+    if os.path.exists("/sys/bus/pci/devices/0000:00:00.0/local_cpulist"):
+        assert host_bridge is not None and host_bridge <= allowed
+    assert bench.numa_local_cpus("not-a-bus-id") is None
+    assert bench.numa_local_cpus("0000FFFF:FF:1F.7") is None
