@@ -176,3 +176,22 @@ def test_pair_and_single_kernels_checksums_bitwise(whole_run):
         assert np.all(ex == 1), kern
         assert st["tiles_done"] == n_chk and st["device_status"] == 0, kern
     assert np.array_equal(out["pair"].view(np.uint64), out["single"].view(np.uint64))
+
+
+@pytest.mark.parametrize("kern", ["pair", "single"])
+def test_task_list_exit_is_prompt(libapk, kern):
+    """A 2^16-task list drains in ~0.1 s on either kernel.  At exit a
+    producer waits out only the loads of its last ring slots: waiting from a
+    lagging consumed count reused a slot's barrier parity and held the pair
+    kernel at exit for the whole bounded-wait limit (2 s, no device status)
+    -- so the launch time must stay far below that limit."""
+    from apk_b200.runtime import gen_tasks
+    A, B, pool = _pools()
+    tasks, n_chk = gen_tasks(1 << 16, SEED)
+    import apk_b200
+    with _ctx(poll="stage", bf16_kernel=kern) as c:
+        c.set_urgent(apk_b200.fill_normal_bf16((256, 256), 31), apk_b200.fill_normal_bf16((256, 256), 32))
+        _run(c, A, B, pool, tasks, n_chk)
+        st = c.run_stats()
+    assert st["device_status"] == 0 and st["tiles_done"] == n_chk
+    assert st["launch_ms"] < 1000.0, st["launch_ms"]
