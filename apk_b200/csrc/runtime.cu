@@ -530,7 +530,7 @@ apk_status apk_create(const apk_config* cfg, apk_ctx** out) {
                 "every SM in a co-resident pair (grid %d, %d SMs)", ctx->grid, ctx->sms);
   if (c.dtype == APK_F32 && c.f32_kernel == APK_F32_WARP_SPECIALIZED && !use_ws(ctx))
     return fail(ctx, APK_EUNSUPPORTED,
-                "the warp-specialized fp32 kernel needs the queue scheduler, K-tile 32 and two workers per SM "
+                "the warp-specialized fp32 kernel needs the queue scheduler, 128x128 tiles on 32-deep slots and two workers per SM "
                 "(grid %d, %d SMs)", ctx->grid, ctx->sms);
   if (ctx->grid > ctx->sms * ctx->max_ctas_per_sm)
     return fail(ctx, APK_EINVAL,

@@ -86,10 +86,11 @@ typedef enum apk_scheduler { APK_SCHED_QUEUE = 0, APK_SCHED_CLC = 1 } apk_schedu
 
 /* fp32 kernel.  WARP_SPECIALIZED: one 384-thread CTA per SM runs two
  * 128x128 workers (compute warps fed by a TMA producer warp per worker, a
- * control warp for the flag); it serves the queue scheduler at K-tile 32
- * with exactly two workers per SM.  BLOCK_SYNC: 128-thread CTAs, one block
- * barrier per stage; it serves every configuration (CLC, K-tile 64, one CTA
- * per SM, reduced grids).  AUTO picks WARP_SPECIALIZED where it applies.
+ * control warp for the flag); it serves the queue scheduler with exactly
+ * two workers per SM (32-deep ring slots, a yield site every k_tile / 32
+ * slots).  BLOCK_SYNC: 128-thread CTAs, one block barrier per stage; it
+ * serves every configuration (CLC, one CTA per SM with 64-deep slots at
+ * K-tile 64 or 128, 4 and 8 CTAs per SM, reduced grids).  AUTO picks WARP_SPECIALIZED where it applies.
  * Both compute every C element with the same FMA sequence: bitwise-equal
  * outputs.  In the warp-specialized kernel a "CTA" of the grid, the event
  * log, tile counters and checkpoint slabs is a worker. */
