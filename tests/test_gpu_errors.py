@@ -1,6 +1,7 @@
-"""The runtime's error contract on a B200 (include/apk.h "Error behaviour"):
-bad shapes, configurations the kernels do not serve, launches that could
-not end, and an empty or oversized task list come back as status codes --
+"""The runtime's error contract on a B200 (the apk_status codes of
+include/apk.h): bad shapes, configurations the kernels do not serve,
+launches that could not end, an empty task list and a launch longer than
+the task list come back as status codes --
 APK_EINVAL for arguments, APK_EUNSUPPORTED for variants that are not built,
 APK_ESTATE for calls out of order -- and the context stays usable after
 each (the reference's CUDA_CHECK -> exit(1) becomes a returned status)."""
